@@ -1,0 +1,345 @@
+/*
+ * conv.cu — host side of the fused conv kernels: weight packing and upload, TMA tensor maps,
+ * shape checks, instantiation dispatch and launch (the C ABI in include/aji_b200.h).
+ *
+ * Counterparts in the reference: src/native/conv.cu (kConv table :60-61, key_of :89-147,
+ * upload :183-204, launch :231-270) and src/native/pack.cpp (pack_fragments :9). The packing
+ * here targets a different consumer: the tcgen05 B operand, K-major without swizzle, stored
+ * per tap as [K/8 chunks][N/8 row groups][8 rows][8 fp16] so that one MMA's B (N x 16) is two
+ * K-adjacent chunks at a fixed leading-byte offset.
+ */
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <new>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "conv_tc.cuh"
+#include "../../include/aji_b200.h"
+
+struct ajib_weights {
+    void *img = nullptr;     // packed B image (9 or 1 taps)
+    float *bias = nullptr;   // npad floats
+    float *slope = nullptr;  // npad floats or null
+    int taps = 0, cin = 0, cout = 0, kpad = 0, npad = 0;
+    size_t bytes = 0;
+};
+
+namespace ajib {
+
+int pad_k(int cin) { return cin <= 16 ? 16 : (cin + 15) / 16 * 16; }
+int pad_n(int cout) { return (cout + 15) / 16 * 16; }
+
+// [tap][kc][ng][n8][k8] fp16 bits; entries past cin / cout are zero
+std::vector<uint16_t> pack_b_image(const uint16_t *w, int taps, int cin, int cout, int kpad, int npad)
+{
+    const int KC = kpad / 8, NG = npad / 8;
+    std::vector<uint16_t> img((size_t)taps * kpad * npad, 0);
+    for (int t = 0; t < taps; t++)
+        for (int kc = 0; kc < KC; kc++)
+            for (int ng = 0; ng < NG; ng++)
+                for (int n8 = 0; n8 < 8; n8++)
+                    for (int k8 = 0; k8 < 8; k8++) {
+                        const int k = kc * 8 + k8, n = ng * 8 + n8;
+                        if (k < cin && n < cout)
+                            img[((((size_t)t * KC + kc) * NG + ng) * 8 + n8) * 8 + k8] = w[((size_t)t * cin + k) * cout + n];
+                    }
+    return img;
+}
+
+// ---- per-device status word (kernels record pipeline timeouts here) ----
+namespace {
+std::mutex g_status_mu;
+int *g_status[64] = {};
+}  // namespace
+
+int *status_word()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    if (!g_status[dev]) {
+        int *p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+            cudaFree(p);
+            return nullptr;
+        }
+        g_status[dev] = p;
+    }
+    return g_status[dev];
+}
+
+// ---- TMA tensor maps ----
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+}  // namespace
+
+// The staged-row view of an NHWC fp16 tensor [H][W][C]: 4-D (8 channels, W, C/8, H) so that one
+// box {8, 130, C/8, 1} lands in shared memory as [C/8][130][8]. *split = 0. If the driver
+// refuses that view, the 3-D (C, W, H) view with box {8, 130, 1} (one copy per chunk), *split = 1.
+bool make_row_map(CUtensorMap *m, const void *base, int H, int W, int C, int *split)
+{
+    auto enc = encode_fn();
+    if (!enc) return false;
+    {
+        cuuint64_t dims[4] = {8, (cuuint64_t)W, (cuuint64_t)(C / 8), (cuuint64_t)H};
+        cuuint64_t strides[3] = {(cuuint64_t)C * 2, 16, (cuuint64_t)W * C * 2};
+        cuuint32_t box[4] = {8, (cuuint32_t)kHalo, (cuuint32_t)(C / 8), 1};
+        cuuint32_t es[4] = {1, 1, 1, 1};
+        if (enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            *split = 0;
+            return true;
+        }
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H};
+    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2};
+    cuuint32_t box[3] = {8, (cuuint32_t)kHalo, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    *split = 1;
+    return true;
+}
+
+int sm_count()
+{
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return n;
+}
+
+namespace {
+
+using ConvFn = cudaError_t (*)(const CUtensorMap &, const ConvDev &, int grid, cudaStream_t);
+
+template <int KPAD, int NPAD>
+cudaError_t run_conv(const CUtensorMap &tm, const ConvDev &p, int grid, cudaStream_t s)
+{
+    using Cf = ConvCfg<KPAD, NPAD>;
+    static_assert(Cf::SMEM <= kMaxSmem, "shared memory budget");
+    // the shared-memory opt-in is per device: set it once on each
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load() & bit)) {
+        const cudaError_t attr =
+            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+        if (attr != cudaSuccess) return attr;
+        done.fetch_or(bit);
+    }
+    k_conv3x3_tc<KPAD, NPAD><<<grid, kConvThreads, Cf::SMEM, s>>>(tm, p);
+    return cudaGetLastError();
+}
+
+ConvFn find_fn(int kpad, int npad)
+{
+#define AJIB_K(KP, NP) \
+    if (kpad == KP && npad == NP) return &run_conv<KP, NP>;
+#define AJIB_KN(KP) AJIB_K(KP, 16) AJIB_K(KP, 32) AJIB_K(KP, 48) AJIB_K(KP, 64)
+    AJIB_KN(16)
+    AJIB_KN(32)
+    AJIB_KN(48)
+    AJIB_KN(64)
+#undef AJIB_KN
+#undef AJIB_K
+    return nullptr;
+}
+
+int d2s_factor(int out) { return out == 1 ? 2 : out == 2 ? 4 : out == 3 ? 1 : out == 4 ? 3 : 0; }
+
+bool fail(char *why, size_t n, const char *msg)
+{
+    if (why && n) std::snprintf(why, n, "%s", msg);
+    return false;
+}
+
+// The shape checks of the reference key_of (src/native/conv.cu:89-147), for this engine's kernels.
+bool check(const ajib_conv *op, char *why, size_t n)
+{
+    if (!op) return fail(why, n, "no op");
+    if (!op->w) return fail(why, n, "no weights");
+    if (op->w->taps != 9) return fail(why, n, "weights are not 3x3");
+    if (op->w->cin != op->cin || op->w->cout != op->cout) return fail(why, n, "weights do not match the op's channels");
+    switch (op->in) {
+    case AJIB_IN_NHWC:
+        if (op->cin % 8 || op->cin < 8 || op->cin > 64) return fail(why, n, "NHWC input channels must be a multiple of 8, 8..64");
+        break;
+    case AJIB_IN_NCHW3:
+        if (op->cin != 3) return fail(why, n, "NCHW3 input has 3 channels");
+        break;
+    default:
+        return fail(why, n, "pixel-unshuffled inputs are not supported by this engine");
+    }
+    switch (op->out) {
+    case AJIB_OUT_NHWC:
+        if (op->cout % 8 || op->cout < 8 || op->cout > 64) return fail(why, n, "NHWC output channels must be a multiple of 8, 8..64");
+        break;
+    case AJIB_OUT_D2S2:
+        if (op->cout != 12) return fail(why, n, "depth-to-space 2 output has 12 channels");
+        break;
+    case AJIB_OUT_D2S4:
+        if (op->cout != 48) return fail(why, n, "depth-to-space 4 output has 48 channels");
+        break;
+    case AJIB_OUT_D2S1:
+        if (op->cout != 3) return fail(why, n, "depth-to-space 1 output has 3 channels");
+        break;
+    case AJIB_OUT_D2S3:
+        if (op->cout != 27) return fail(why, n, "depth-to-space 3 output has 27 channels");
+        break;
+    default:
+        return fail(why, n, "unknown output mode");
+    }
+    if (op->act < 0 || op->act > 3) return fail(why, n, "unknown activation");
+    if (op->gate < 0 || op->gate > 3) return fail(why, n, "unknown gate");
+    if (op->gate != AJIB_GATE_NONE) {
+        if (op->act != AJIB_ACT_NONE) return fail(why, n, "gates take no activation");
+        if (op->in != AJIB_IN_NHWC || op->out != AJIB_OUT_NHWC || op->cin != op->cout)
+            return fail(why, n, "gates need NHWC input and output with cin == cout");
+        if (op->gate == AJIB_GATE_TANH1X1) return fail(why, n, "the tanh 1x1 gate is not supported by this engine");
+    }
+    if (op->act == AJIB_ACT_PRELU && !op->w->slope) return fail(why, n, "PReLU without slopes");
+    if (!find_fn(op->w->kpad, op->w->npad)) return fail(why, n, "no kernel for these channel counts");
+    return true;
+}
+
+}  // namespace
+}  // namespace ajib
+
+using namespace ajib;
+
+extern "C" int ajib_weights_upload(ajib_weights **out, const uint16_t *w, const float *bias, const float *slope, int taps,
+                                   int cin, int cout)
+{
+    if (!out || !w || !bias || (taps != 9 && taps != 1) || cin < 1 || cout < 1 || cin > 256 || cout > 64) return AJIB_ERR_ARGS;
+    *out = nullptr;
+    auto *r = new (std::nothrow) ajib_weights();
+    if (!r) return AJIB_ERR_NO_MEM;
+    r->taps = taps;
+    r->cin = cin;
+    r->cout = cout;
+    r->kpad = taps == 9 ? pad_k(cin) : (cin + 15) / 16 * 16;
+    r->npad = pad_n(cout);
+    const std::vector<uint16_t> img = pack_b_image(w, taps, cin, cout, r->kpad, r->npad);
+    std::vector<float> b(r->npad, 0.f), s(r->npad, 0.f);
+    for (int i = 0; i < cout; i++) {
+        b[i] = bias[i];
+        if (slope) s[i] = slope[i];
+    }
+    cudaError_t e = cudaMalloc(&r->img, img.size() * 2);
+    if (e == cudaSuccess) e = cudaMemcpy(r->img, img.data(), img.size() * 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&r->bias, r->npad * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(r->bias, b.data(), r->npad * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && slope) e = cudaMalloc(&r->slope, r->npad * 4);
+    if (e == cudaSuccess && slope) e = cudaMemcpy(r->slope, s.data(), r->npad * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        ajib_weights_release(&r);
+        cudaGetLastError();
+        return e == cudaErrorMemoryAllocation ? AJIB_ERR_NO_MEM : AJIB_ERR_CUDA;
+    }
+    r->bytes = img.size() * 2 + r->npad * 4 * (slope ? 2 : 1);
+    *out = r;
+    return AJIB_OK;
+}
+
+extern "C" void ajib_weights_release(ajib_weights **w)
+{
+    if (!w || !*w) return;
+    cudaFree((*w)->img);
+    cudaFree((*w)->bias);
+    cudaFree((*w)->slope);
+    delete *w;
+    *w = nullptr;
+}
+
+extern "C" size_t ajib_weights_bytes(const ajib_weights *w) { return w ? w->bytes : 0; }
+
+extern "C" int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_size)
+{
+    return check(op, why, why_size) ? 1 : 0;
+}
+
+extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
+                                   int row_begin, int row_end, void *stream)
+{
+    if (!check(op, nullptr, 0)) return AJIB_ERR_UNSUPPORTED;
+    if (!src || !dst || H < 1 || W < 1) return AJIB_ERR_ARGS;
+    if (op->gate != AJIB_GATE_NONE && !resid) return AJIB_ERR_ARGS;
+    if (row_end <= 0 || row_end > H) row_end = H;
+    if (row_begin < 0 || row_begin >= row_end) return row_begin == row_end ? AJIB_OK : AJIB_ERR_ARGS;
+    // NHWC rows must start on 16-byte boundaries for the TMA loads and the vector stores
+    if (((uintptr_t)src & 15) || ((uintptr_t)dst & 15) || (resid && op->gate && ((uintptr_t)resid & 15)))
+        return AJIB_ERR_ARGS;
+
+    ConvDev p{};
+    p.src = (const __half *)src;
+    p.resid = (const __half *)resid;
+    p.dst = (__half *)dst;
+    p.wimg = (const unsigned char *)op->w->img;
+    p.bias = op->w->bias;
+    p.slope = op->w->slope;
+    p.err = status_word();
+    if (!p.err) return AJIB_ERR_CUDA;
+    p.H = H;
+    p.W = W;
+    p.cin = op->cin;
+    p.cout = op->cout;
+    p.in_mode = op->in;
+    p.act = op->act;
+    p.gate = op->gate;
+    p.R = d2s_factor(op->out);
+    p.in_norm = op->in_norm && op->in != AJIB_IN_NHWC;
+    p.out_clamp = op->out_clamp && op->out != AJIB_OUT_NHWC;
+    for (int c = 0; c < 3; c++) {
+        p.in_mean[c] = op->in_mean[c];
+        p.in_scale[c] = op->in_scale[c];
+    }
+    p.row_begin = row_begin;
+    p.row_end = row_end;
+
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    if (op->in == AJIB_IN_NHWC) {
+        if (!make_row_map(&tm, src, H, W, op->cin, &p.tma_split)) return AJIB_ERR_CUDA;
+    }
+    const long strips = (W + kTileM - 1) / kTileM;
+    const long tiles = strips * (row_end - row_begin);
+    const int grid = (int)std::min<long>(sm_count(), tiles);
+    ConvFn fn = find_fn(op->w->kpad, op->w->npad);
+    const cudaError_t e = fn(tm, p, grid, (cudaStream_t)stream);
+    return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+extern "C" int ajib_kernel_status(int clear)
+{
+    int *w = status_word();
+    if (!w) return AJIB_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return AJIB_ERR_CUDA;
+    if (clear && v && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return AJIB_ERR_CUDA;
+    return v;
+}

@@ -1,0 +1,93 @@
+/*
+ * aji_b200.h — the native hot path of this engine as a C ABI: the fused 3x3 conv kernels, the
+ * 1x1 concat kernel, the colour pre/post passes, the on-device image tiler, the native model
+ * (a plan of fused conv steps) and its executor. Plain pointers and sizes only; device pointers
+ * are CUDA device addresses on the current device, `stream` is a cudaStream_t (NULL = legacy
+ * default stream).
+ *
+ * Each declaration names the reference interface it replaces (the-database/animejanai-inference,
+ * file:line). The reference exposes these as C++ functions inside its backend library; a caller
+ * that wants the kernels alone (a test, a benchmark, another front-end) binds them here.
+ *
+ * Return codes: AJIB_OK (0) or a negative AJIB_ERR_*.
+ */
+#ifndef AJI_B200_H
+#define AJI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "aji.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AJIB_EXPORT __attribute__((visibility("default")))
+
+enum ajib_status {
+    AJIB_OK = 0,
+    AJIB_ERR = -1,
+    AJIB_ERR_ARGS = -2,        /* a bad pointer, size or shape */
+    AJIB_ERR_UNSUPPORTED = -3, /* no kernel for this combination */
+    AJIB_ERR_CUDA = -4,        /* a CUDA call failed */
+    AJIB_ERR_NO_MEM = -5,      /* a device or host allocation failed */
+    AJIB_ERR_TIMEOUT = -6,     /* a kernel gave up waiting on its own pipeline (ajib_kernel_status) */
+};
+
+/* ---- op vocabulary (reference src/native/ops.h:13-21; same integer values) ---- */
+enum ajib_input { AJIB_IN_NHWC = 0, AJIB_IN_NCHW3 = 1, AJIB_IN_NCHW3_UNSHUFFLE2 = 2 };
+enum ajib_act { AJIB_ACT_NONE = 0, AJIB_ACT_RELU = 1, AJIB_ACT_PRELU = 2, AJIB_ACT_SILU = 3 };
+enum ajib_gate { AJIB_GATE_NONE = 0, AJIB_GATE_RESIDUAL = 1, AJIB_GATE_TANH1X1 = 2, AJIB_GATE_SIGMOID_HALF = 3 };
+enum ajib_output { AJIB_OUT_NHWC = 0, AJIB_OUT_D2S2 = 1, AJIB_OUT_D2S4 = 2, AJIB_OUT_D2S1 = 3, AJIB_OUT_D2S3 = 4 };
+
+/* ---- conv weights (reference src/native/conv.h:34-49, upload/release) ----
+ * w: [taps][cin][cout] fp16 bit patterns (ONNX OIHW transposed to HWIO), bias: cout floats,
+ * slope: cout floats (PReLU) or NULL. taps is 9 (3x3) or 1 (1x1). Packed on the host into the
+ * tensor-core operand image the kernels copy to shared memory, and uploaded to the current
+ * device. */
+typedef struct ajib_weights ajib_weights;
+AJIB_EXPORT int ajib_weights_upload(ajib_weights **out, const uint16_t *w, const float *bias, const float *slope,
+                                    int taps, int cin, int cout);
+AJIB_EXPORT void ajib_weights_release(ajib_weights **w);
+AJIB_EXPORT size_t ajib_weights_bytes(const ajib_weights *w);
+
+/* ---- one fused 3x3 conv (reference src/native/conv.h:53-66, struct Conv3x3) ----
+ * Logical channel counts: an NCHW3 input has cin 3; a D2S1/2/3/4 output has cout 3/12/27/48. */
+typedef struct ajib_conv {
+    int in, act, gate, out; /* enum ajib_input / ajib_act / ajib_gate / ajib_output */
+    int cin, cout;
+    const ajib_weights *w;
+    const ajib_weights *att; /* AJIB_GATE_TANH1X1: the 1x1 cout -> cout attention conv */
+    int in_norm;             /* NCHW3 input: load (x - in_mean[c]) * in_scale[c] */
+    float in_mean[3], in_scale[3];
+    int out_clamp; /* depth-to-space outputs: clamp to [0, 1] after the model input is added */
+} ajib_conv;
+
+/* Whether a kernel exists for op (reference src/native/conv.h:86, supported); why (may be NULL)
+ * receives the reason for a refusal. Returns 1 or 0. */
+AJIB_EXPORT int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_size);
+
+/* Launch op at conv resolution H x W on output rows [row_begin, row_end) (row_end <= 0: all
+ * rows) (reference src/native/conv.h:91, launch). src: NHWC [H][W][cin] or NCHW [3][H][W].
+ * resid: gates read the block input x as NHWC [H][W][cout]; depth-to-space outputs add the NCHW
+ * model input [3][H][W] (nearest upsampled) when resid is not NULL. dst: NHWC [H][W][cout] or
+ * NCHW [3][R*H][R*W]. Rows outside the range are neither read beyond the one-row halo nor
+ * written, so a frame can be run as bands. */
+AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
+                                    int row_begin, int row_end, void *stream);
+
+/* Reads and optionally clears the current device's kernel status word: 0, or the code of the
+ * first pipeline wait that timed out in a kernel of this library. */
+AJIB_EXPORT int ajib_kernel_status(int clear);
+
+/* A one-CTA check of the tensor-core operand encodings the conv kernels use (a: [130][32] fp16,
+ * b: [2n][32] fp16, out: [2][128][n] fp32 = A[shift:shift+128] x B-halves^T). For tests. */
+AJIB_EXPORT int ajib_selftest_umma(const void *a, const void *b, float *out, int n, int shift, int collector, int *err,
+                                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AJI_B200_H */

@@ -1,0 +1,51 @@
+/*
+ * oracle.h — CPU restatement of the reference's algorithms on the native conv path, in plain C.
+ *
+ * TEST INFRASTRUCTURE ONLY. The product (animejanai-inference_b200/) never links, loads or calls
+ * this code; tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it as the
+ * checker. Pinned against the reference itself: tests/golden/ holds vectors produced by the
+ * reference's own sources compiled here (oracle/_ref, recipe in oracle/ref/), and the CPU tests
+ * compare this restatement against them.
+ *
+ * Every function cites the reference file:line it follows (the-database/animejanai-inference).
+ */
+#ifndef AJI_ORACLE_H
+#define AJI_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* fp32 <-> fp16 bits, round to nearest even (src/native/pack.cpp:69-111). */
+uint16_t orc_f2h(float f);
+float orc_h2f(uint16_t h);
+/* x[i] = fp16(x[i]) for n values (sanity/native_ref.h:22, f16r). */
+void orc_round_f16(float *x, size_t n);
+void orc_f2h_array(const float *x, uint16_t *out, size_t n);
+void orc_h2f_array(const uint16_t *h, float *out, size_t n);
+
+/* One fused 3x3 conv step of a lowered plan (sanity/native_ref.h:53-118), at conv resolution
+ * H x W. in_mode 0: src NHWC [H][W][cin]; 1: src NCHW [3][H][W] (the model input, cin 3).
+ * w: [9][cin][cout] (fp16-valued floats), bias [cout], slope [cout] (act 2) or NULL.
+ * act 0 none, 1 ReLU, 2 PReLU, 3 SiLU; gate 0 none, 1 residual, 2 (not supported here),
+ * 3 sigmoid-half with resid NHWC [H][W][cout]. R == 0: dst NHWC [H][W][cout], each value
+ * rounded to fp16. R in 1..4: depth-to-space (CRD) into dst NCHW [3][R*H][R*W] plus model_in
+ * NCHW [3][H][W] (nearest upsampled) when not NULL, clamped to [0,1] if out_clamp, rounded to
+ * fp16. Accumulates in double. nthreads <= 0: all cores. Returns 0, or -1 on bad arguments. */
+int orc_conv3x3(int in_mode, const float *src, int H, int W, int cin, const float *w, const float *bias,
+                const float *slope, int cout, int act, int gate, const float *resid, int R, const float *model_in,
+                int out_clamp, float *dst, int nthreads);
+
+/* 1x1 conv over the channel concat of nsrc NHWC [npx][c] maps (sanity/native_ref.h:41-52):
+ * w [nsrc*c][c], bias [c]; dst NHWC [npx][c] rounded to fp16. */
+int orc_concat1x1(const float *const *srcs, int nsrc, int npx, int c, const float *w, const float *bias, float *dst,
+                  int nthreads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,177 @@
+"""GPU parity of the fused 3x3 conv kernels (ajib_conv3x3_launch, the tcgen05 path) against the
+CPU oracle (oracle/oracle_conv.c, the reference's sanity/native_ref.h semantics).
+
+Tolerances: the north_star's max-abs 2e-2 on every output, and the reference conv test's RMS
+limit 3e-3 (sanity/native_conv_test.cu:195). Guard bands around every output catch writes out of
+bounds (the reference's DevBuf pattern, native_conv_test.cu:49-76)."""
+import numpy as np
+import pytest
+
+from util import conv_weights, f16r, oracle_conv, to_f16_bits
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+GUARD = 4096
+GUARD_BITS = 0x7BAB  # an fp16 pattern no kernel writes
+
+
+def dev_f16(x):
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32).astype(np.float16)).cuda()
+
+
+class Guarded:
+    """A device fp16 buffer with GUARD elements of a fixed pattern on each side."""
+
+    def __init__(self, shape):
+        n = int(np.prod(shape))
+        self.shape = shape
+        self.n = n
+        self.t = torch.full((n + 2 * GUARD,), 0, dtype=torch.int16, device="cuda")
+        self.t.fill_(GUARD_BITS)
+        self.ptr = self.t.data_ptr() + GUARD * 2
+
+    def value(self):
+        h = self.t.cpu().numpy()
+        assert (h[:GUARD] == GUARD_BITS).all(), "write before the output"
+        assert (h[GUARD + self.n:] == GUARD_BITS).all(), "write past the output"
+        return h[GUARD:GUARD + self.n].view(np.float16).astype(np.float32).reshape(self.shape)
+
+
+def run_conv(op, src, resid, dst_shape, H, W, rows=None):
+    import ajib
+    dst = Guarded(dst_shape)
+    s = torch.cuda.current_stream().cuda_stream
+    if rows is None:
+        rc = ajib.conv3x3(op, src.data_ptr(), 0 if resid is None else resid.data_ptr(), dst.ptr, H, W, 0, 0, s)
+        assert rc == 0, f"launch failed: {rc}"
+    else:
+        for (a, b) in rows:
+            rc = ajib.conv3x3(op, src.data_ptr(), 0 if resid is None else resid.data_ptr(), dst.ptr, H, W, a, b, s)
+            assert rc == 0, f"launch failed: {rc}"
+    torch.cuda.synchronize()
+    assert ajib.kernel_status() == 0, "a kernel pipeline wait timed out"
+    return dst.value()
+
+
+def check_close(got, want, max_abs=2e-2, rms=3e-3):
+    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert np.isfinite(got).all()
+    assert d.max() <= max_abs, f"max abs {d.max()}"
+    assert np.sqrt((d ** 2).mean()) <= rms, f"rms {np.sqrt((d ** 2).mean())}"
+
+
+def test_config0_conv64_prelu():
+    """NCHW 1x64x128x128 U[-1,1], 3x3 64->64, W~N(0,sqrt(2/576)), b~N(0,0.01),
+    PReLU slopes U[0.1,0.3]."""
+    import ajib
+    rng = np.random.default_rng(12345)
+    H = W = 128
+    x_nchw = f16r(rng.uniform(-1, 1, size=(64, H, W)))
+    x = np.ascontiguousarray(x_nchw.transpose(1, 2, 0))
+    w, b, s = conv_weights(rng, 64, 64, prelu=True)
+    want = oracle_conv(x, 0, H, W, 64, w, b, s, 64, act=2)
+    wt = ajib.Weights(to_f16_bits(w), b, s)
+    op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
+    got = run_conv(op, dev_f16(x), None, (H, W, 64), H, W)
+    check_close(got, want)
+
+
+SHAPES = [(19, 37), (32, 48), (7, 300), (1, 5), (130, 129), (3, 256)]
+
+
+@pytest.mark.parametrize("H,W", SHAPES)
+@pytest.mark.parametrize("c,act", [(64, 2), (48, 3), (24, 2), (32, 1), (64, 0)])
+def test_body(H, W, c, act):
+    import ajib
+    rng = np.random.default_rng(H * 1000 + W + c + act)
+    x = f16r(rng.uniform(-1, 1, size=(H, W, c)))
+    w, b, s = conv_weights(rng, c, c, prelu=act == 2)
+    want = oracle_conv(x, 0, H, W, c, w, b, s, c, act=act)
+    wt = ajib.Weights(to_f16_bits(w), b, s)
+    got = run_conv(ajib.conv_op(wt, act=act), dev_f16(x), None, (H, W, c), H, W)
+    check_close(got, want)
+
+
+@pytest.mark.parametrize("H,W", [(19, 37), (9, 200)])
+@pytest.mark.parametrize("gate", [1, 3])
+@pytest.mark.parametrize("c", [48, 24])
+def test_gates(H, W, gate, c):
+    import ajib
+    rng = np.random.default_rng(77 + gate + c + H)
+    x = f16r(rng.uniform(-1, 1, size=(H, W, c)))
+    r = f16r(rng.uniform(-1, 1, size=(H, W, c)))
+    w, b, _ = conv_weights(rng, c, c)
+    want = oracle_conv(x, 0, H, W, c, w, b, None, c, gate=gate, resid=r)
+    wt = ajib.Weights(to_f16_bits(w), b)
+    got = run_conv(ajib.conv_op(wt, gate=gate), dev_f16(x), dev_f16(r), (H, W, c), H, W)
+    check_close(got, want)
+
+
+@pytest.mark.parametrize("H,W", [(19, 37), (16, 130)])
+@pytest.mark.parametrize("cout,act", [(64, 2), (48, 0), (24, 2)])
+def test_head_nchw3(H, W, cout, act):
+    import ajib
+    rng = np.random.default_rng(5 + H + cout)
+    x = f16r(rng.uniform(0, 1, size=(3, H, W)))
+    w, b, s = conv_weights(rng, 3, cout, prelu=act == 2)
+    want = oracle_conv(x, 1, H, W, 3, w, b, s, cout, act=act)
+    wt = ajib.Weights(to_f16_bits(w), b, s)
+    got = run_conv(ajib.conv_op(wt, in_=ajib.IN_NCHW3, act=act), dev_f16(x), None, (H, W, cout), H, W)
+    check_close(got, want)
+
+
+@pytest.mark.parametrize("H,W", [(19, 37), (8, 129)])
+@pytest.mark.parametrize("cin,out,cout", [(64, 1, 12), (48, 1, 12), (24, 2, 48), (64, 2, 48), (32, 3, 3), (32, 4, 27)])
+@pytest.mark.parametrize("skip", [True, False])
+def test_tail_depth_to_space(H, W, cin, out, cout, skip):
+    import ajib
+    R = ajib.D2S_FACTOR[out]
+    rng = np.random.default_rng(9 + H + cin + out)
+    x = f16r(rng.uniform(-1, 1, size=(H, W, cin)))
+    mi = f16r(rng.uniform(0, 1, size=(3, H, W))) if skip else None
+    w, b, _ = conv_weights(rng, cin, cout)
+    want = oracle_conv(x, 0, H, W, cin, w, b, None, cout, R=R, model_in=mi)
+    wt = ajib.Weights(to_f16_bits(w), b)
+    got = run_conv(ajib.conv_op(wt, out=out), dev_f16(x), None if mi is None else dev_f16(mi), (3, R * H, R * W), H, W)
+    check_close(got, want)
+
+
+def test_tail_clamp():
+    import ajib
+    rng = np.random.default_rng(31)
+    H, W = 11, 140
+    x = f16r(rng.uniform(-1, 1, size=(H, W, 64)))
+    mi = f16r(rng.uniform(0, 1, size=(3, H, W)))
+    w, b, _ = conv_weights(rng, 64, 12, std=0.2)
+    want = oracle_conv(x, 0, H, W, 64, w, b, None, 12, R=2, model_in=mi, out_clamp=True)
+    wt = ajib.Weights(to_f16_bits(w), b)
+    got = run_conv(ajib.conv_op(wt, out=ajib.OUT_D2S2, out_clamp=True), dev_f16(x), dev_f16(mi), (3, 2 * H, 2 * W), H, W)
+    assert got.min() >= 0 and got.max() <= 1
+    check_close(got, want)
+
+
+def test_bands_match_whole_frame():
+    """Launching a frame as row bands gives exactly the whole-frame result (the band schedule)."""
+    import ajib
+    rng = np.random.default_rng(4)
+    H, W = 45, 260
+    x = dev_f16(f16r(rng.uniform(-1, 1, size=(H, W, 64))))
+    w, b, s = conv_weights(rng, 64, 64, prelu=True)
+    op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b, s), act=ajib.ACT_PRELU)
+    whole = run_conv(op, x, None, (H, W, 64), H, W)
+    bands = run_conv(op, x, None, (H, W, 64), H, W, rows=[(0, 7), (7, 8), (8, 30), (30, 45)])
+    assert np.array_equal(whole, bands)
+
+
+def test_refusals():
+    import ajib
+    rng = np.random.default_rng(0)
+    w, b, _ = conv_weights(rng, 64, 64)
+    wt = ajib.Weights(to_f16_bits(w), b)
+    ok, why = ajib.supported(ajib.conv_op(wt, act=ajib.ACT_PRELU))
+    assert not ok and "PReLU" in why
+    ok, why = ajib.supported(ajib.conv_op(wt, gate=ajib.GATE_SIGMOID_HALF, act=ajib.ACT_RELU))
+    assert not ok and "activation" in why
+    ok, why = ajib.supported(ajib.conv_op(wt, out=ajib.OUT_D2S2))
+    assert not ok

@@ -1,0 +1,91 @@
+"""Test helpers: the CPU oracle (oracle/liboracle.so) through ctypes, seeded inputs and weights,
+and comparison metrics. The oracle is the checker only; the engine under test is libaji.so."""
+import ctypes as C
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_PATH = os.path.join(ROOT, "oracle", "liboracle.so")
+
+_orc = None
+
+
+def oracle():
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORACLE_PATH):
+            raise RuntimeError(f"{ORACLE_PATH} is not built (make -C oracle)")
+        o = C.CDLL(ORACLE_PATH)
+        fp = C.POINTER(C.c_float)
+        o.orc_conv3x3.argtypes = [C.c_int, fp, C.c_int, C.c_int, C.c_int, fp, fp, fp, C.c_int, C.c_int, C.c_int,
+                                  fp, C.c_int, fp, C.c_int, fp, C.c_int]
+        o.orc_conv3x3.restype = C.c_int
+        o.orc_concat1x1.argtypes = [C.POINTER(fp), C.c_int, C.c_int, C.c_int, fp, fp, fp, C.c_int]
+        o.orc_concat1x1.restype = C.c_int
+        o.orc_f2h.argtypes = [C.c_float]
+        o.orc_f2h.restype = C.c_uint16
+        o.orc_h2f.argtypes = [C.c_uint16]
+        o.orc_h2f.restype = C.c_float
+        _orc = o
+    return _orc
+
+
+def _fp(a):
+    return None if a is None else a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def f16r(x):
+    """Round to fp16 and back (numpy's conversion is IEEE round-to-nearest-even)."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def oracle_conv(src, in_mode, H, W, cin, w, bias, slope, cout, act=0, gate=0, resid=None, R=0, model_in=None,
+                out_clamp=False, nthreads=0):
+    """One fused conv step on the CPU (oracle/oracle_conv.c, sanity/native_ref.h semantics).
+    w: [9][cin][cout] fp16-valued float32."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    bias = np.ascontiguousarray(bias, dtype=np.float32)
+    slope = None if slope is None else np.ascontiguousarray(slope, dtype=np.float32)
+    resid = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
+    model_in = None if model_in is None else np.ascontiguousarray(model_in, dtype=np.float32)
+    if R == 0:
+        dst = np.zeros((H, W, cout), np.float32)
+    else:
+        dst = np.zeros((3, R * H, R * W), np.float32)
+    rc = oracle().orc_conv3x3(in_mode, _fp(src), H, W, cin, _fp(w), _fp(bias), _fp(slope), cout, act, gate,
+                              _fp(resid), R, _fp(model_in), 1 if out_clamp else 0, _fp(dst), nthreads)
+    assert rc == 0, "oracle rejected the arguments"
+    return dst
+
+
+def oracle_concat(srcs, c, w, bias, nthreads=0):
+    srcs = [np.ascontiguousarray(s, dtype=np.float32) for s in srcs]
+    npx = srcs[0].size // c
+    arr = (C.POINTER(C.c_float) * len(srcs))(*[_fp(s) for s in srcs])
+    dst = np.zeros((npx, c), np.float32)
+    rc = oracle().orc_concat1x1(arr, len(srcs), npx, c, _fp(np.ascontiguousarray(w, np.float32)),
+                                _fp(np.ascontiguousarray(bias, np.float32)), _fp(dst), nthreads)
+    assert rc == 0
+    return dst
+
+
+def conv_weights(rng, cin, cout, prelu=False, std=None):
+    """He-init 3x3 weights as BASELINE config 0 specifies: W ~ N(0, sqrt(2/(9 cin))) rounded to
+    fp16, bias ~ N(0, 0.01), PReLU slopes ~ U[0.1, 0.3]. Returns (w [9][cin][cout] fp16-valued
+    float32, bias, slope or None)."""
+    std = np.sqrt(2.0 / (9 * cin)) if std is None else std
+    w = f16r(rng.normal(0.0, std, size=(9, cin, cout)))
+    b = rng.normal(0.0, 0.01, size=cout).astype(np.float32)
+    s = rng.uniform(0.1, 0.3, size=cout).astype(np.float32) if prelu else None
+    return w, b, s
+
+
+def to_f16_bits(x):
+    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def psnr(a, b, peak=1.0):
+    mse = float(np.mean((np.asarray(a, np.float64) - np.asarray(b, np.float64)) ** 2))
+    return float("inf") if mse == 0 else 10.0 * np.log10(peak * peak / mse)
