@@ -128,3 +128,332 @@ def conv3x3(op, src, resid, dst, H, W, row_begin=0, row_end=0, stream=0):
 
 def kernel_status(clear=True):
     return lib.ajib_kernel_status(1 if clear else 0)
+
+
+# ---------------------------------------------------------------------------------------------
+# native model files (format documented in csrc/model.cpp) and the architectures of the
+# BASELINE configs, as plans of fused steps (the structures the reference's lowering produces:
+# sanity/native_lower_test.cpp compact() / span_s()).
+
+MODEL_INPUT, MODEL_OUTPUT = -2, -3
+
+
+def _conv_step(w, bias, slope=None, in_=IN_NHWC, act=ACT_NONE, gate=GATE_NONE, out=OUT_NHWC, src=-1, resid=-1,
+               dst=-1, out_clamp=False, in_norm=None):
+    """w: [9][cin][cout] float (rounded to fp16 when written)."""
+    import numpy as np
+    w = np.asarray(w, np.float32)
+    return dict(kind=0, in_=in_, act=act, gate=gate, out=out, cin=w.shape[1], cout=w.shape[2], src=src, resid=resid,
+                dst=dst, w=w, bias=np.asarray(bias, np.float32), slope=None if slope is None else np.asarray(slope, np.float32),
+                out_clamp=out_clamp, in_norm=in_norm)
+
+
+def _concat_step(w, bias, srcs, c, dst):
+    import numpy as np
+    return dict(kind=1, c=c, nsrc=len(srcs), srcs=list(srcs), dst=dst, w=np.asarray(w, np.float32).reshape(1, len(srcs) * c, c),
+                bias=np.asarray(bias, np.float32), slope=None)
+
+
+def model_bytes(plan):
+    """Serialise a plan dict {name, steps, channels, depth_to_space} to the native model format."""
+    import struct
+
+    import numpy as np
+    out = [b"AJNM", struct.pack("<I", 1)]
+    name = plan.get("name", "").encode()
+    out.append(struct.pack("<IIIII", len(plan["steps"]), len(plan["channels"]), 1, plan["depth_to_space"], len(name)))
+    out.append(name)
+    out.append(np.asarray(plan["channels"], np.int32).tobytes())
+
+    def weights(w, b, s):
+        taps, cin, cout = w.shape
+        parts = [struct.pack("<iii", taps, cin, cout), w.astype(np.float16).view(np.uint16).tobytes(),
+                 np.asarray(b, np.float32).tobytes(), struct.pack("<i", 0 if s is None else 1)]
+        if s is not None:
+            parts.append(np.asarray(s, np.float32).tobytes())
+        return b"".join(parts)
+
+    for s in plan["steps"]:
+        srcs = list(s.get("srcs", [])) + [-1] * (4 - len(s.get("srcs", [])))
+        norm = s.get("in_norm")
+        mean, scale = (norm if norm is not None else ((0.0, 0.0, 0.0), (1.0, 1.0, 1.0)))
+        out.append(struct.pack("<12i4i", s["kind"], s.get("in_", 0), s.get("act", 0), s.get("gate", 0), s.get("out", 0),
+                               s.get("cin", 0), s.get("cout", 0), s.get("src", -1), s.get("resid", -1), s["dst"],
+                               s.get("c", 0), s.get("nsrc", 0), *srcs))
+        out.append(struct.pack("<i3f3fi", 1 if norm is not None else 0, *mean, *scale, 1 if s.get("out_clamp") else 0))
+        out.append(weights(s["w"], s["bias"], s.get("slope")))
+    return b"".join(out)
+
+
+def _he(rng, cin, cout, taps=9):
+    import numpy as np
+    return (rng.normal(0.0, np.sqrt(2.0 / (taps * cin)), size=(taps, cin, cout))).astype(np.float16).astype(np.float32)
+
+
+def compact_plan(seed, c=64, body=16, scale=2, name=None):
+    """SRVGGNetCompact: conv_first 3->c + PReLU, `body` x (c->c + PReLU), c->3*scale^2,
+    pixel_shuffle(scale), + nearest-upsampled input. He-init weights, bias N(0, 0.01), PReLU
+    slopes U[0.1, 0.3], all from `seed`."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    steps = []
+
+    def bias(n):
+        return rng.normal(0.0, 0.01, size=n).astype(np.float32)
+
+    def slope(n):
+        return rng.uniform(0.1, 0.3, size=n).astype(np.float32)
+
+    steps.append(_conv_step(_he(rng, 3, c), bias(c), slope(c), in_=IN_NCHW3, act=ACT_PRELU, src=MODEL_INPUT, dst=0))
+    for i in range(body):
+        steps.append(_conv_step(_he(rng, c, c), bias(c), slope(c), act=ACT_PRELU, src=i, dst=i + 1))
+    out_mode = {1: OUT_D2S1, 2: OUT_D2S2, 3: OUT_D2S3, 4: OUT_D2S4}[scale]
+    steps.append(_conv_step(_he(rng, c, 3 * scale * scale), bias(3 * scale * scale), out=out_mode, src=body,
+                            resid=MODEL_INPUT, dst=MODEL_OUTPUT))
+    return dict(name=name or f"compact-{c}x{body}-{scale}x", steps=steps, channels=[c] * (body + 1),
+                depth_to_space=scale)
+
+
+def span_plan(seed, c=48, blocks=6, scale=2, name=None):
+    """SPAN: conv_first 3->c; `blocks` SPABs (c1+SiLU, c2+SiLU, c3 with (c3 + x)(sigmoid(c3) - 0.5));
+    conv_2; concat[feat, conv_2, block 1 out, last block's c1 pre-activation] -> 1x1 4c->c;
+    c->3*scale^2 3x3; pixel_shuffle(scale). The last block's c1 is recomputed as a plain conv for the
+    concat, as the reference's lowering does (23 steps for 6 blocks)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    steps, channels = [], []
+
+    def bias(n):
+        return rng.normal(0.0, 0.01, size=n).astype(np.float32)
+
+    def new_feat():
+        channels.append(c)
+        return len(channels) - 1
+
+    feat = new_feat()
+    steps.append(_conv_step(_he(rng, 3, c), bias(c), in_=IN_NCHW3, src=MODEL_INPUT, dst=feat))
+    x, out_b1, mid = feat, None, None
+    for b in range(blocks):
+        w1, b1 = _he(rng, c, c), bias(c)
+        if b == blocks - 1:
+            mid = new_feat()
+            steps.append(_conv_step(w1, b1, src=x, dst=mid))
+        a1 = new_feat()
+        steps.append(_conv_step(w1, b1, act=ACT_SILU, src=x, dst=a1))
+        a2 = new_feat()
+        steps.append(_conv_step(_he(rng, c, c), bias(c), act=ACT_SILU, src=a1, dst=a2))
+        o = new_feat()
+        steps.append(_conv_step(_he(rng, c, c), bias(c), gate=GATE_SIGMOID_HALF, src=a2, resid=x, dst=o))
+        x = o
+        if b == 0:
+            out_b1 = o
+    o2 = new_feat()
+    steps.append(_conv_step(_he(rng, c, c), bias(c), src=x, dst=o2))
+    cat = new_feat()
+    steps.append(_concat_step(_he(rng, 4 * c, c, taps=1), bias(c), [feat, o2, out_b1, mid], c, cat))
+    out_mode = {1: OUT_D2S1, 2: OUT_D2S2, 3: OUT_D2S3, 4: OUT_D2S4}[scale]
+    steps.append(_conv_step(_he(rng, c, 3 * scale * scale), bias(3 * scale * scale), out=out_mode, src=cat,
+                            dst=MODEL_OUTPUT))
+    return dict(name=name or f"span-{c}x{blocks}-{scale}x", steps=steps, channels=channels, depth_to_space=scale)
+
+
+lib.ajib_model_load.argtypes = [C.c_char_p, C.POINTER(_vp), C.c_char_p, C.c_size_t]
+lib.ajib_model_load.restype = C.c_int
+lib.ajib_model_from_memory.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(_vp), C.c_char_p, C.c_size_t]
+lib.ajib_model_from_memory.restype = C.c_int
+lib.ajib_model_release.argtypes = [C.POINTER(_vp)]
+lib.ajib_model_release.restype = None
+lib.ajib_model_info.argtypes = [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_double), C.c_char_p,
+                                C.c_size_t]
+lib.ajib_model_info.restype = C.c_int
+lib.ajib_exec_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp), C.c_char_p, C.c_size_t]
+lib.ajib_exec_create.restype = C.c_int
+lib.ajib_exec_release.argtypes = [C.POINTER(_vp)]
+lib.ajib_exec_release.restype = None
+lib.ajib_exec_run.argtypes = [_vp, _vp, _vp, _vp]
+lib.ajib_exec_run.restype = C.c_int
+lib.ajib_exec_set_bands.argtypes = [_vp, C.c_int]
+lib.ajib_exec_set_bands.restype = C.c_int
+lib.ajib_exec_info.argtypes = [_vp, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.POINTER(C.c_int)]
+lib.ajib_exec_info.restype = C.c_int
+
+
+class Model:
+    def __init__(self, plan=None, path=None):
+        self.handle = _vp()
+        err = C.create_string_buffer(512)
+        if path is not None:
+            rc = lib.ajib_model_load(path.encode(), C.byref(self.handle), err, 512)
+        else:
+            data = model_bytes(plan)
+            rc = lib.ajib_model_from_memory(data, len(data), C.byref(self.handle), err, 512)
+        if rc != AJIB_OK:
+            raise AjibError(f"model load failed: {err.value.decode()}")
+        scale, steps, fpp = C.c_int(), C.c_int(), C.c_double()
+        desc = C.create_string_buffer(256)
+        lib.ajib_model_info(self.handle, C.byref(scale), C.byref(steps), C.byref(fpp), desc, 256)
+        self.scale, self.steps, self.flops_per_px, self.desc = scale.value, steps.value, fpp.value, desc.value.decode()
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib.ajib_model_release(C.byref(self.handle))
+        except Exception:
+            pass
+
+
+class Exec:
+    def __init__(self, model, w, h, bands=1):
+        self.handle = _vp()
+        self.model = model
+        err = C.create_string_buffer(512)
+        rc = lib.ajib_exec_create(model.handle, w, h, C.byref(self.handle), err, 512)
+        if rc != AJIB_OK:
+            raise AjibError(f"executor creation failed: {err.value.decode()}")
+        if bands != 1:
+            check(lib.ajib_exec_set_bands(self.handle, bands), "ajib_exec_set_bands")
+        self.w, self.h = w, h
+
+    def run(self, src, dst, stream=0):
+        return lib.ajib_exec_run(self.handle, src, dst, stream)
+
+    def info(self):
+        a, b, n = C.c_size_t(), C.c_size_t(), C.c_int()
+        lib.ajib_exec_info(self.handle, C.byref(a), C.byref(b), C.byref(n))
+        return dict(device_bytes=a.value, weight_bytes=b.value, launches=n.value)
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib.ajib_exec_release(C.byref(self.handle))
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------------------------
+# the video ABI (include/aji.h)
+
+AJI_API_VERSION = 9
+FMT_NV12, FMT_P010, FMT_YUV444P16, FMT_RGB10A2, FMT_YUV444P10MSB, FMT_YUV444P12MSB = 1, 2, 3, 4, 5, 6
+MATRIX_BT601, MATRIX_BT709, MATRIX_BT2020 = 1, 2, 3
+RANGE_LIMITED, RANGE_FULL = 1, 2
+SITING_LEFT, SITING_CENTER, SITING_TOPLEFT = 1, 2, 3
+AJI_OK, AJI_ERR = 0, -1
+
+LOG_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_char_p)
+
+
+class CreateParams(C.Structure):
+    _fields_ = [("api_version", C.c_uint32), ("cuda_context", C.c_void_p), ("conf_path", C.c_char_p),
+                ("model_dir", C.c_char_p), ("trtexec", C.c_char_p), ("trtexec_env", C.c_char_p), ("slot", C.c_int),
+                ("rife_model_dir", C.c_char_p), ("async_build", C.c_int), ("d3d11_device", C.c_void_p),
+                ("engine_path", C.c_char_p), ("max_width", C.c_int), ("max_height", C.c_int), ("log", LOG_FN),
+                ("log_opaque", C.c_void_p)]
+
+
+class Frame(C.Structure):
+    _fields_ = [("width", C.c_int), ("height", C.c_int), ("format", C.c_int), ("matrix", C.c_int), ("range", C.c_int),
+                ("siting", C.c_int), ("plane", C.c_void_p * 3), ("stride", C.c_ssize_t * 3)]
+
+
+def frame(w, h, fmt, planes, strides, matrix=MATRIX_BT709, range_=RANGE_LIMITED, siting=SITING_LEFT):
+    f = Frame()
+    f.width, f.height, f.format, f.matrix, f.range, f.siting = w, h, fmt, matrix, range_, siting
+    for i in range(3):
+        f.plane[i] = planes[i] if i < len(planes) else None
+        f.stride[i] = strides[i] if i < len(strides) else 0
+    return f
+
+
+lib.aji_create.argtypes = [C.POINTER(CreateParams)]
+lib.aji_create.restype = C.c_void_p
+lib.aji_configure.argtypes = [_vp, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+lib.aji_configure.restype = C.c_int
+lib.aji_infer.argtypes = [_vp, C.POINTER(Frame), C.POINTER(Frame), _vp]
+lib.aji_infer.restype = C.c_int
+lib.aji_flush.argtypes = [_vp, _vp]
+lib.aji_flush.restype = C.c_uint64
+lib.aji_done.argtypes = [_vp, C.c_uint64]
+lib.aji_done.restype = C.c_int
+lib.aji_wait.argtypes = [_vp, C.c_uint64]
+lib.aji_wait.restype = C.c_int
+lib.aji_last_error.argtypes = [_vp]
+lib.aji_last_error.restype = C.c_char_p
+lib.aji_current_log.argtypes = [_vp]
+lib.aji_current_log.restype = C.c_char_p
+lib.aji_scale_factor.argtypes = [_vp]
+lib.aji_scale_factor.restype = C.c_int
+lib.aji_destroy.argtypes = [C.POINTER(_vp)]
+lib.aji_destroy.restype = None
+
+
+class Video:
+    """A direct-mode aji_ctx on a native model file."""
+
+    def __init__(self, model_path, max_w, max_h, cuda_context=None):
+        p = CreateParams()
+        p.api_version = AJI_API_VERSION
+        p.cuda_context = cuda_context
+        p.engine_path = model_path.encode()
+        p.max_width, p.max_height = max_w, max_h
+        self._p = p
+        h = lib.aji_create(C.byref(p))
+        if not h:
+            raise AjibError("aji_create failed")
+        self.handle = _vp(h)
+
+    def configure(self, w, h, fps=24.0):
+        ow, oh = C.c_int(), C.c_int()
+        rc = lib.aji_configure(self.handle, w, h, fps, C.byref(ow), C.byref(oh))
+        if rc != 1:
+            raise AjibError(f"aji_configure: {rc} {self.error()}")
+        return ow.value, oh.value
+
+    def infer(self, fin, fout, stream=0):
+        return lib.aji_infer(self.handle, C.byref(fin), C.byref(fout), stream)
+
+    def flush(self, stream=0):
+        return lib.aji_flush(self.handle, stream)
+
+    def wait(self, ticket):
+        return lib.aji_wait(self.handle, ticket)
+
+    def error(self):
+        return (lib.aji_last_error(self.handle) or b"").decode()
+
+    def close(self):
+        if self.handle:
+            lib.aji_destroy(C.byref(self.handle))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# colour passes (aji_b200.h, named as the reference's src/kernels.h)
+class Csp(C.Structure):
+    _fields_ = [("kr", C.c_float), ("kb", C.c_float), ("yoff", C.c_float), ("yscale", C.c_float), ("coff", C.c_float),
+                ("cscale", C.c_float)]
+
+
+lib.aji_make_csp.argtypes = [C.c_int, C.c_int, C.c_int]
+lib.aji_make_csp.restype = Csp
+for _n in ("aji_pre_plan_create", "aji_post_plan_create"):
+    getattr(lib, _n).argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+    getattr(lib, _n).restype = C.c_void_p
+lib.aji_plan_destroy.argtypes = [_vp]
+lib.aji_plan_destroy.restype = None
+lib.aji_run_pre.argtypes = [_vp, _vp, C.c_ssize_t, _vp, C.c_ssize_t, C.POINTER(Csp), _vp, _vp]
+lib.aji_run_pre.restype = C.c_int
+lib.aji_run_post.argtypes = [_vp, _vp, C.POINTER(Csp), _vp, C.c_ssize_t, _vp, C.c_ssize_t, _vp]
+lib.aji_run_post.restype = C.c_int
+lib.aji_run_post444.argtypes = [C.c_int, C.c_int, C.c_int, _vp, C.POINTER(Csp), _vp, C.c_ssize_t, _vp, C.c_ssize_t,
+                                _vp, C.c_ssize_t, _vp]
+lib.aji_run_post444.restype = C.c_int
+lib.aji_run_pre444.argtypes = [C.c_int, C.c_int, _vp, C.c_ssize_t, _vp, C.c_ssize_t, _vp, C.c_ssize_t, C.POINTER(Csp),
+                               _vp, _vp]
+lib.aji_run_pre444.restype = C.c_int
+lib.ajib_plan_table.argtypes = [_vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float), C.c_int]
+lib.ajib_plan_table.restype = C.c_int

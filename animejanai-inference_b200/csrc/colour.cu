@@ -1,0 +1,434 @@
+/*
+ * colour.cu — the YUV <-> RGB passes around the conv net: NV12/P010 -> fp16 NCHW RGB before the
+ * first conv and fp16 NCHW RGB -> NV12/P010 after the last one, plus the 4:4:4 matrix-only
+ * variants (C ABI in include/aji_b200.h, named as the reference's src/kernels.h).
+ *
+ * The reference runs the pre-pass as two kernels with an fp32 chroma plane between them and the
+ * post-pass as three kernels with two fp32 planes between them (src/kernels.cu:105-231,
+ * :441-497). Here each pass is one kernel over a 2-D tile: the separable filter's first pass is
+ * computed for the tile's halo into shared memory and the second pass reads it from there, so
+ * the intermediate planes never reach HBM. Every output keeps the same fp32 operation sequence
+ * as the reference (taps accumulated in order with fused multiply-adds, IEEE divisions in the
+ * normalisation, rintf quantisation), which is what makes the results bit-identical.
+ */
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <new>
+
+#include "resample.h"
+#include "../../include/aji_b200.h"
+
+using namespace ajib;
+
+struct DevPass {
+    int taps, src, dst;
+    const int *start;
+    const float *wt;
+};
+
+struct aji_plan {
+    enum Kind { PRE, POST } kind;
+    int format = 0, w = 0, h = 0;
+    FilterTable th, tv;  // host copies (tests)
+    DevPass ph{}, pv{};
+    int max_rows = 0, max_cols = 0;  // staged halo extents (checked against the kernel's capacity)
+};
+
+extern "C" aji_csp aji_make_csp(int format, int matrix, int range)
+{
+    aji_csp c{};
+    switch (matrix) {
+    case AJI_MATRIX_BT601:
+        c.kr = 0.299f;
+        c.kb = 0.114f;
+        break;
+    case AJI_MATRIX_BT2020:
+        c.kr = 0.2627f;
+        c.kb = 0.0593f;
+        break;
+    default:
+        c.kr = 0.2126f;
+        c.kb = 0.0722f;
+        break;
+    }
+    // 16-bit containers hold MSB-aligned samples: limited-range points scale by 256; full-range
+    // peaks are the container's largest value at the sample depth.
+    const bool wide = format == AJI_FMT_P010 || aji_format_is_444(format);
+    const float m = wide ? 256.0f : 1.0f;
+    const float maxraw = (format == AJI_FMT_P010 || format == AJI_FMT_YUV444P10MSB) ? 65472.0f
+                         : format == AJI_FMT_YUV444P12MSB                           ? 65520.0f
+                         : format == AJI_FMT_YUV444P16                              ? 65535.0f
+                                                                                    : 255.0f;
+    if (range == AJI_RANGE_FULL) {
+        c.yoff = 0.0f;
+        c.yscale = maxraw;
+        c.coff = wide ? 32768.0f : 128.0f;
+        c.cscale = maxraw;
+    } else {
+        c.yoff = 16.0f * m;
+        c.yscale = 219.0f * m;
+        c.coff = 128.0f * m;
+        c.cscale = 224.0f * m;
+    }
+    return c;
+}
+
+namespace {
+
+// mirror an index into [0, n): -1 -> 0, -2 -> 1, n -> n - 1 (then clamp for far-out indices)
+__device__ __forceinline__ int mirror_index(int i, int n)
+{
+    i = i < 0 ? -i - 1 : i;
+    i = i >= n ? 2 * n - 1 - i : i;
+    return min(max(i, 0), n - 1);
+}
+
+__device__ __forceinline__ float quantize(float v, float qdiv, float qmax)
+{
+    return __fmul_rn(fminf(fmaxf(rintf(__fdiv_rn(v, qdiv)), 0.0f), qmax), qdiv);
+}
+
+// ---------------- pre: NV12/P010 -> fp16 NCHW RGB ----------------
+constexpr int kPreTW = 64, kPreTH = 16, kPreRows = 24;
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
+                                             DevPass ph, DevPass pv, aji_csp csp, __half *dst, int w, int h)
+{
+    __shared__ float2 uvh[kPreRows][kPreTW];  // horizontally resampled (u, v) per staged chroma row
+    const int x0 = blockIdx.x * kPreTW, y0 = blockIdx.y * kPreTH;
+    const int tid = threadIdx.x;
+    const int ylast = min(y0 + kPreTH, h) - 1;
+    const int lo = pv.start[y0], hi = pv.start[ylast] + pv.taps - 1;
+    const int nrows = hi - lo + 1;  // <= kPreRows (checked at plan creation)
+    const int ch = pv.src;
+
+    // pass 1: horizontal resample of the staged chroma rows (interleaved CbCr)
+    for (int i = tid; i < nrows * kPreTW; i += 256) {
+        const int rr = i / kPreTW, tx = i % kPreTW, x = x0 + tx;
+        if (x >= w) continue;
+        const T *row = reinterpret_cast<const T *>(uvp + (size_t)mirror_index(lo + rr, ch) * uvs);
+        const float *wt = ph.wt + (size_t)x * ph.taps;
+        const int s0 = ph.start[x];
+        float u = 0.0f, v = 0.0f;
+        for (int j = 0; j < ph.taps; j++) {
+            const int sx = mirror_index(s0 + j, ph.src);
+            u = __fmaf_rn(wt[j], (float)row[2 * sx], u);
+            v = __fmaf_rn(wt[j], (float)row[2 * sx + 1], v);
+        }
+        uvh[rr][tx] = make_float2(u, v);
+    }
+    __syncthreads();
+
+    // pass 2: vertical resample + matrix, one pixel per thread and row
+    const int tx = tid % kPreTW, x = x0 + tx;
+    if (x >= w) return;
+    const size_t plane = (size_t)w * h;
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float cr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));   // 2 (1 - kr)
+    const float cb = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));   // 2 (1 - kb)
+    const float gb = __fmul_rn(__fmul_rn(2.0f, csp.kb), __fsub_rn(1.0f, csp.kb));  // 2 kb (1 - kb)
+    const float gr = __fmul_rn(__fmul_rn(2.0f, csp.kr), __fsub_rn(1.0f, csp.kr));  // 2 kr (1 - kr)
+    for (int ty = tid / kPreTW; ty < kPreTH; ty += 256 / kPreTW) {
+        const int y = y0 + ty;
+        if (y >= h) break;
+        const float *wt = pv.wt + (size_t)y * pv.taps;
+        const int s0 = pv.start[y];
+        float u = 0.0f, v = 0.0f;
+        for (int j = 0; j < pv.taps; j++) {
+            const float2 q = uvh[s0 + j - lo][tx];
+            u = __fmaf_rn(wt[j], q.x, u);
+            v = __fmaf_rn(wt[j], q.y, v);
+        }
+        const float raw = (float)reinterpret_cast<const T *>(yp + (size_t)y * ys)[x];
+        const float Y = __fdiv_rn(__fsub_rn(raw, csp.yoff), csp.yscale);
+        const float U = __fdiv_rn(__fsub_rn(u, csp.coff), csp.cscale);
+        const float V = __fdiv_rn(__fsub_rn(v, csp.coff), csp.cscale);
+        const float r = __fmaf_rn(cr, V, Y);
+        const float b = __fmaf_rn(cb, U, Y);
+        const float g = __fsub_rn(Y, __fdiv_rn(__fmaf_rn(gb, U, __fmul_rn(gr, V)), kg));
+        const size_t idx = (size_t)y * w + x;
+        dst[idx] = __float2half_rn(r);
+        dst[plane + idx] = __float2half_rn(g);
+        dst[2 * plane + idx] = __float2half_rn(b);
+    }
+}
+
+// ---------------- post: fp16 NCHW RGB -> NV12/P010 ----------------
+constexpr int kPostTW = 32, kPostTH = 8;          // chroma samples per tile
+constexpr int kPostRows = 40, kPostCols = 96;      // staged luma halo capacity
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, DevPass ph, DevPass pv, aji_csp csp,
+                                              float qdiv, float qmax, uint8_t *yp, ptrdiff_t ys, uint8_t *uvp,
+                                              ptrdiff_t uvs)
+{
+    extern __shared__ float2 post_sm[];
+    float2 *cuv = post_sm;                              // [kPostRows][kPostCols] (U, V) of staged luma pixels
+    float2 *huv = post_sm + kPostRows * kPostCols;      // [kPostRows][kPostTW] after the horizontal pass
+    const int cx0 = blockIdx.x * kPostTW, cy0 = blockIdx.y * kPostTH;
+    const int cw = ph.dst, chh = pv.dst;
+    const int tid = threadIdx.x;
+    const int cxl = min(cx0 + kPostTW, cw) - 1, cyl = min(cy0 + kPostTH, chh) - 1;
+    const int xlo = ph.start[cx0], xhi = ph.start[cxl] + ph.taps - 1;
+    const int ylo = pv.start[cy0], yhi = pv.start[cyl] + pv.taps - 1;
+    const int ncols = xhi - xlo + 1, nrows = yhi - ylo + 1;
+    const size_t plane = (size_t)w * h;
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float db = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
+    const float dr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));
+
+    // luma of the tile's own pixels, quantised
+    for (int i = tid; i < 4 * kPostTW * kPostTH; i += 256) {
+        const int ly = 2 * cy0 + i / (2 * kPostTW), lx = 2 * cx0 + i % (2 * kPostTW);
+        if (lx >= w || ly >= h) continue;
+        const size_t idx = (size_t)ly * w + lx;
+        const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+        const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
+        reinterpret_cast<T *>(yp + (size_t)ly * ys)[lx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+    }
+    // chroma difference planes of the staged (mirrored) luma pixels
+    for (int i = tid; i < nrows * ncols; i += 256) {
+        const int rr = i / ncols, cc = i % ncols;
+        const size_t idx = (size_t)mirror_index(ylo + rr, h) * w + mirror_index(xlo + cc, w);
+        const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+        const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
+        cuv[rr * kPostCols + cc] = make_float2(__fdiv_rn(__fsub_rn(b, Y), db), __fdiv_rn(__fsub_rn(r, Y), dr));
+    }
+    __syncthreads();
+    // horizontal pass
+    for (int i = tid; i < nrows * kPostTW; i += 256) {
+        const int rr = i / kPostTW, tx = i % kPostTW, cx = cx0 + tx;
+        if (cx >= cw) continue;
+        const float *wt = ph.wt + (size_t)cx * ph.taps;
+        const int s0 = ph.start[cx] - xlo;
+        float u = 0.0f, v = 0.0f;
+        for (int j = 0; j < ph.taps; j++) {
+            const float2 q = cuv[rr * kPostCols + s0 + j];
+            u = __fmaf_rn(wt[j], q.x, u);
+            v = __fmaf_rn(wt[j], q.y, v);
+        }
+        huv[rr * kPostTW + tx] = make_float2(u, v);
+    }
+    __syncthreads();
+    // vertical pass, quantise, interleave
+    for (int i = tid; i < kPostTW * kPostTH; i += 256) {
+        const int ty = i / kPostTW, tx = i % kPostTW, cx = cx0 + tx, cy = cy0 + ty;
+        if (cx >= cw || cy >= chh) continue;
+        const float *wt = pv.wt + (size_t)cy * pv.taps;
+        const int s0 = pv.start[cy] - ylo;
+        float u = 0.0f, v = 0.0f;
+        for (int j = 0; j < pv.taps; j++) {
+            const float2 q = huv[(s0 + j) * kPostTW + tx];
+            u = __fmaf_rn(wt[j], q.x, u);
+            v = __fmaf_rn(wt[j], q.y, v);
+        }
+        T *row = reinterpret_cast<T *>(uvp + (size_t)cy * uvs);
+        row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qmax);
+        row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qmax);
+    }
+}
+
+// ---------------- 4:4:4 16-bit planar, matrix only ----------------
+__global__ void k_post444(const __half *src, int w, int h, aji_csp csp, float qdiv, float qmax, uint8_t *yp,
+                          ptrdiff_t ys, uint8_t *cbp, ptrdiff_t cbs, uint8_t *crp, ptrdiff_t crs)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= w || y >= h) return;
+    const size_t plane = (size_t)w * h, idx = (size_t)y * w + x;
+    const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
+    const float U = __fdiv_rn(__fsub_rn(b, Y), __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb)));
+    const float V = __fdiv_rn(__fsub_rn(r, Y), __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr)));
+    reinterpret_cast<uint16_t *>(yp + (size_t)y * ys)[x] = (uint16_t)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+    reinterpret_cast<uint16_t *>(cbp + (size_t)y * cbs)[x] = (uint16_t)quantize(__fmaf_rn(U, csp.cscale, csp.coff), qdiv, qmax);
+    reinterpret_cast<uint16_t *>(crp + (size_t)y * crs)[x] = (uint16_t)quantize(__fmaf_rn(V, csp.cscale, csp.coff), qdiv, qmax);
+}
+
+__global__ void k_pre444(const uint8_t *yp, ptrdiff_t ys, const uint8_t *cbp, ptrdiff_t cbs, const uint8_t *crp,
+                         ptrdiff_t crs, int w, int h, aji_csp csp, __half *dst)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= w || y >= h) return;
+    const size_t plane = (size_t)w * h, idx = (size_t)y * w + x;
+    const float Y = __fdiv_rn(__fsub_rn((float)reinterpret_cast<const uint16_t *>(yp + (size_t)y * ys)[x], csp.yoff), csp.yscale);
+    const float U = __fdiv_rn(__fsub_rn((float)reinterpret_cast<const uint16_t *>(cbp + (size_t)y * cbs)[x], csp.coff), csp.cscale);
+    const float V = __fdiv_rn(__fsub_rn((float)reinterpret_cast<const uint16_t *>(crp + (size_t)y * crs)[x], csp.coff), csp.cscale);
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float cr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr)), cb = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
+    const float gb = __fmul_rn(__fmul_rn(2.0f, csp.kb), __fsub_rn(1.0f, csp.kb));
+    const float gr = __fmul_rn(__fmul_rn(2.0f, csp.kr), __fsub_rn(1.0f, csp.kr));
+    dst[idx] = __float2half_rn(__fmaf_rn(cr, V, Y));
+    dst[2 * plane + idx] = __float2half_rn(__fmaf_rn(cb, U, Y));
+    dst[plane + idx] = __float2half_rn(__fsub_rn(Y, __fdiv_rn(__fmaf_rn(gb, U, __fmul_rn(gr, V)), kg)));
+}
+
+bool upload_pass(DevPass *d, const FilterTable &t)
+{
+    int *s = nullptr;
+    float *w = nullptr;
+    if (cudaMalloc(&s, t.start.size() * sizeof(int)) != cudaSuccess) return false;
+    if (cudaMalloc(&w, t.wt.size() * sizeof(float)) != cudaSuccess) {
+        cudaFree(s);
+        return false;
+    }
+    if (cudaMemcpy(s, t.start.data(), t.start.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(w, t.wt.data(), t.wt.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(s);
+        cudaFree(w);
+        return false;
+    }
+    d->taps = t.taps;
+    d->src = t.src;
+    d->dst = t.dst;
+    d->start = s;
+    d->wt = w;
+    return true;
+}
+
+// largest number of source indices a tile of `tile` consecutive outputs spans
+int span_of(const FilterTable &t, int tile)
+{
+    int m = 0;
+    for (int i0 = 0; i0 < t.dst; i0 += tile) {
+        const int i1 = std::min(i0 + tile, t.dst) - 1;
+        m = std::max(m, t.start[i1] + t.taps - t.start[i0]);
+    }
+    return m;
+}
+
+aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting, int filter)
+{
+    if ((format != AJI_FMT_NV12 && format != AJI_FMT_P010) || w < 2 || h < 2 || (w & 1) || (h & 1)) return nullptr;
+    auto *p = new (std::nothrow) aji_plan();
+    if (!p) return nullptr;
+    p->kind = kind;
+    p->format = format;
+    p->w = w;
+    p->h = h;
+    const int cw = w / 2, ch = h / 2;
+    double sx, sy;
+    chroma_shift(siting, kind == aji_plan::PRE, &sx, &sy);
+    if (kind == aji_plan::PRE) {
+        p->th = make_filter(cw, w, sx, filter);
+        p->tv = make_filter(ch, h, sy, filter);
+        p->max_rows = span_of(p->tv, kPreTH);
+        if (p->max_rows > kPreRows) {
+            delete p;
+            return nullptr;
+        }
+    } else {
+        p->th = make_filter(w, cw, sx, filter);
+        p->tv = make_filter(h, ch, sy, filter);
+        p->max_rows = span_of(p->tv, kPostTH);
+        p->max_cols = span_of(p->th, kPostTW);
+        if (p->max_rows > kPostRows || p->max_cols > kPostCols) {
+            delete p;
+            return nullptr;
+        }
+    }
+    if (!upload_pass(&p->ph, p->th) || !upload_pass(&p->pv, p->tv)) {
+        aji_plan_destroy(p);
+        return nullptr;
+    }
+    return p;
+}
+
+}  // namespace
+
+extern "C" aji_plan *aji_pre_plan_create(int format, int w, int h, int siting, int filter)
+{
+    return plan_create(aji_plan::PRE, format, w, h, siting, filter);
+}
+
+extern "C" aji_plan *aji_post_plan_create(int format, int w, int h, int siting, int filter)
+{
+    return plan_create(aji_plan::POST, format, w, h, siting, filter);
+}
+
+extern "C" void aji_plan_destroy(aji_plan *p)
+{
+    if (!p) return;
+    cudaFree((void *)p->ph.start);
+    cudaFree((void *)p->ph.wt);
+    cudaFree((void *)p->pv.start);
+    cudaFree((void *)p->pv.wt);
+    delete p;
+}
+
+extern "C" int ajib_plan_table(const aji_plan *p, int which, int *start, float *wt, int max_dst)
+{
+    if (!p) return -1;
+    const FilterTable &t = which ? p->tv : p->th;
+    const int n = std::min(max_dst, t.dst);
+    if (start) std::memcpy(start, t.start.data(), n * sizeof(int));
+    if (wt) std::memcpy(wt, t.wt.data(), (size_t)n * t.taps * sizeof(float));
+    return t.taps;
+}
+
+extern "C" int aji_run_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane,
+                           ptrdiff_t uv_stride, const aji_csp *csp, void *dst_f16, void *stream)
+{
+    if (!p || p->kind != aji_plan::PRE || !y_plane || !uv_plane || !csp || !dst_f16) return (int)cudaErrorInvalidValue;
+    const dim3 grid((p->w + kPreTW - 1) / kPreTW, (p->h + kPreTH - 1) / kPreTH);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (p->format == AJI_FMT_NV12)
+        k_pre<uint8_t><<<grid, 256, 0, s>>>((const uint8_t *)y_plane, y_stride, (const uint8_t *)uv_plane, uv_stride, p->ph,
+                                            p->pv, *csp, (__half *)dst_f16, p->w, p->h);
+    else
+        k_pre<uint16_t><<<grid, 256, 0, s>>>((const uint8_t *)y_plane, y_stride, (const uint8_t *)uv_plane, uv_stride,
+                                             p->ph, p->pv, *csp, (__half *)dst_f16, p->w, p->h);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int aji_run_post(aji_plan *p, const void *src_f16, const aji_csp *csp, void *y_plane, ptrdiff_t y_stride,
+                            void *uv_plane, ptrdiff_t uv_stride, void *stream)
+{
+    if (!p || p->kind != aji_plan::POST || !src_f16 || !csp || !y_plane || !uv_plane) return (int)cudaErrorInvalidValue;
+    const int cw = p->w / 2, ch = p->h / 2;
+    const dim3 grid((cw + kPostTW - 1) / kPostTW, (ch + kPostTH - 1) / kPostTH);
+    const size_t smem = (size_t)(kPostRows * kPostCols + kPostRows * kPostTW) * sizeof(float2);
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool p010 = p->format == AJI_FMT_P010;
+    const float qdiv = p010 ? 64.0f : 1.0f, qmax = p010 ? 1023.0f : 255.0f;
+    cudaError_t e;
+    if (p010) {
+        e = cudaFuncSetAttribute(k_post<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        k_post<uint16_t><<<grid, 256, smem, s>>>((const __half *)src_f16, p->w, p->h, p->ph, p->pv, *csp, qdiv, qmax,
+                                                 (uint8_t *)y_plane, y_stride, (uint8_t *)uv_plane, uv_stride);
+    } else {
+        e = cudaFuncSetAttribute(k_post<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        k_post<uint8_t><<<grid, 256, smem, s>>>((const __half *)src_f16, p->w, p->h, p->ph, p->pv, *csp, qdiv, qmax,
+                                                (uint8_t *)y_plane, y_stride, (uint8_t *)uv_plane, uv_stride);
+    }
+    return (int)cudaGetLastError();
+}
+
+extern "C" int aji_run_post444(int format, int w, int h, const void *src_f16, const aji_csp *csp, void *y_plane,
+                               ptrdiff_t y_stride, void *cb_plane, ptrdiff_t cb_stride, void *cr_plane,
+                               ptrdiff_t cr_stride, void *stream)
+{
+    if (w < 1 || h < 1 || !src_f16 || !csp || !y_plane || !cb_plane || !cr_plane) return (int)cudaErrorInvalidValue;
+    const float qdiv = format == AJI_FMT_YUV444P10MSB ? 64.0f : format == AJI_FMT_YUV444P12MSB ? 16.0f : 1.0f;
+    const float qmax = format == AJI_FMT_YUV444P10MSB ? 1023.0f : format == AJI_FMT_YUV444P12MSB ? 4095.0f : 65535.0f;
+    k_post444<<<dim3((w + 31) / 32, (h + 7) / 8), dim3(32, 8), 0, (cudaStream_t)stream>>>(
+        (const __half *)src_f16, w, h, *csp, qdiv, qmax, (uint8_t *)y_plane, y_stride, (uint8_t *)cb_plane, cb_stride,
+        (uint8_t *)cr_plane, cr_stride);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int aji_run_pre444(int w, int h, const void *y_plane, ptrdiff_t y_stride, const void *cb_plane,
+                              ptrdiff_t cb_stride, const void *cr_plane, ptrdiff_t cr_stride, const aji_csp *csp,
+                              void *dst_f16, void *stream)
+{
+    if (w < 1 || h < 1 || !y_plane || !cb_plane || !cr_plane || !csp || !dst_f16) return (int)cudaErrorInvalidValue;
+    k_pre444<<<dim3((w + 31) / 32, (h + 7) / 8), dim3(32, 8), 0, (cudaStream_t)stream>>>(
+        (const uint8_t *)y_plane, y_stride, (const uint8_t *)cb_plane, cb_stride, (const uint8_t *)cr_plane, cr_stride, w,
+        h, *csp, (__half *)dst_f16);
+    return (int)cudaGetLastError();
+}

@@ -1,0 +1,209 @@
+/*
+ * executor.cpp — see plan.h. Reference: src/native/executor.cpp:23-127 (create/run) and
+ * src/native/layout.cpp:10-77 (buffer assignment with lifetime reuse).
+ */
+#include "plan.h"
+
+#include <algorithm>
+#include <cstring>
+#include <utility>
+
+namespace ajib {
+
+Executor::~Executor()
+{
+    for (cudaEvent_t e : prof_ev_)
+        if (e) cudaEventDestroy(e);
+    for (void *b : buffers_) cudaFree(b);
+    for (Step &s : steps_) {
+        ajib_weights_release(&s.w);
+        ajib_weights_release(&s.att);
+    }
+}
+
+const void *Executor::ptr(int t, const void *in, void *out) const
+{
+    if (t == kModelInput) return in;
+    if (t == kModelOutput) return out;
+    return t >= 0 ? tensor_[t] : nullptr;
+}
+
+int Executor::launches_per_run() const { return (int)steps_.size() * bands_; }
+
+std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h, std::string *why)
+{
+    auto fail = [&](const std::string &m) -> std::unique_ptr<Executor> {
+        if (why) *why = m;
+        return nullptr;
+    };
+    std::string reason;
+    if (!validate_plan(plan, &reason)) return fail(reason);
+    if (in_w < 1 || in_h < 1) return fail("bad input size");
+    std::unique_ptr<Executor> e(new Executor());
+    e->W_ = in_w;
+    e->H_ = in_h;
+    e->R_ = plan.depth_to_space;
+    const size_t px = (size_t)in_w * in_h;
+
+    for (size_t i = 0; i < plan.steps.size(); i++) {
+        const PlanStep &ps = plan.steps[i];
+        Step st;
+        st.src = ps.src;
+        st.resid = ps.resid;
+        st.dst = ps.dst;
+        const PlanWeights &pw = ps.w;
+        int rc = ajib_weights_upload(&st.w, pw.w.data(), pw.bias.data(), pw.slope.empty() ? nullptr : pw.slope.data(),
+                                     pw.taps, pw.cin, pw.cout);
+        if (rc != AJIB_OK) return fail("weight upload failed (step " + std::to_string(i) + ")");
+        e->weight_bytes_ += ajib_weights_bytes(st.w);
+        if (ps.kind == PlanStep::CONCAT) {
+            st.concat = true;
+            st.c = ps.c;
+            st.nsrc = ps.nsrc;
+            for (int k = 0; k < 4; k++) st.srcs[k] = ps.srcs[k];
+            e->steps_.push_back(st);
+            return fail("concat steps are not supported by this engine yet");
+        }
+        ajib_conv &op = st.op;
+        op.in = ps.in;
+        op.act = ps.act;
+        op.gate = ps.gate;
+        op.out = ps.out;
+        op.cin = ps.cin;
+        op.cout = ps.cout;
+        op.w = st.w;
+        op.in_norm = ps.in_norm;
+        op.out_clamp = ps.out_clamp;
+        for (int c = 0; c < 3; c++) {
+            op.in_mean[c] = ps.in_mean[c];
+            op.in_scale[c] = ps.in_scale[c];
+        }
+        e->steps_.push_back(st);
+        char buf[256] = {0};
+        if (!ajib_conv_supported(&e->steps_.back().op, buf, sizeof(buf)))
+            return fail("conv " + std::to_string(ps.cin) + "->" + std::to_string(ps.cout) + ": " + buf);
+    }
+
+    // feature buffers: a buffer of the same size is reused once its tensor's last reader has run
+    const int ns = (int)plan.steps.size(), nt = (int)plan.channels.size();
+    std::vector<int> last(nt, -1), born(nt, -1), buffer(nt, -1);
+    for (int i = 0; i < ns; i++) {
+        const PlanStep &s = plan.steps[i];
+        auto read = [&](int t) {
+            if (t >= 0) last[t] = i;
+        };
+        read(s.src);
+        read(s.resid);
+        if (s.kind == PlanStep::CONCAT)
+            for (int t : s.srcs) read(t);
+        if (s.dst >= 0) born[s.dst] = i;
+    }
+    std::vector<size_t> sizes;
+    std::vector<std::pair<size_t, int>> free_list;
+    for (int i = 0; i < ns; i++) {
+        const int d = plan.steps[i].dst;
+        if (d >= 0 && buffer[d] < 0) {
+            const size_t need = px * plan.channels[d] * 2;
+            int b = -1;
+            for (size_t k = 0; k < free_list.size(); k++)
+                if (free_list[k].first == need) {
+                    b = free_list[k].second;
+                    free_list.erase(free_list.begin() + k);
+                    break;
+                }
+            if (b < 0) {
+                b = (int)sizes.size();
+                sizes.push_back(need);
+            }
+            buffer[d] = b;
+        }
+        for (int t = 0; t < nt; t++)
+            if (buffer[t] >= 0 && (last[t] == i || (last[t] < 0 && born[t] == i)))
+                free_list.push_back({px * plan.channels[t] * 2, buffer[t]});
+    }
+    for (size_t need : sizes) {
+        void *b = nullptr;
+        if (cudaMalloc(&b, need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail("feature buffer allocation failed (" + std::to_string(need >> 20) + " MB)");
+        }
+        e->buffers_.push_back(b);
+        e->bytes_ += need;
+    }
+    e->bytes_ += e->weight_bytes_;
+    e->tensor_.assign(nt, nullptr);
+    for (int t = 0; t < nt; t++)
+        if (buffer[t] >= 0) e->tensor_[t] = e->buffers_[buffer[t]];
+    return e;
+}
+
+int Executor::profile(bool on)
+{
+    if (on && prof_ev_.empty()) {
+        prof_ev_.assign((size_t)kProfRuns * steps_.size() * 2, nullptr);
+        for (cudaEvent_t &e : prof_ev_)
+            if (cudaEventCreate(&e) != cudaSuccess) return AJIB_ERR_CUDA;
+    }
+    prof_on_ = on;
+    prof_runs_ = 0;
+    return AJIB_OK;
+}
+
+int Executor::profile_read(double *ms, int *counts, int nsteps) const
+{
+    const int ns = (int)steps_.size();
+    for (int k = 0; k < nsteps; k++) {
+        ms[k] = 0.0;
+        counts[k] = 0;
+    }
+    const int runs = std::min(prof_runs_, kProfRuns);
+    for (int r = 0; r < runs; r++)
+        for (int k = 0; k < std::min(ns, nsteps); k++) {
+            cudaEvent_t a = prof_ev_[((size_t)r * ns + k) * 2], b = prof_ev_[((size_t)r * ns + k) * 2 + 1];
+            if (cudaEventSynchronize(b) != cudaSuccess) return AJIB_ERR_CUDA;
+            float t = 0.f;
+            if (cudaEventElapsedTime(&t, a, b) != cudaSuccess) return AJIB_ERR_CUDA;
+            ms[k] += t;
+            counts[k]++;
+        }
+    return AJIB_OK;
+}
+
+int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
+{
+    if (w < 1 || h < 1 || w > W_ || h > H_ || !in || !out) return AJIB_ERR_ARGS;
+    const int ns = (int)steps_.size();
+    // profiling brackets whole steps (all of a step's bands), so it runs unbanded
+    const bool prof = prof_on_ && !prof_ev_.empty();
+    const int slot = prof ? prof_runs_ % kProfRuns : 0;
+    if (prof) {
+        for (int k = 0; k < ns; k++) {
+            const Step &st = steps_[k];
+            cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2], s);
+            const int rc = ajib_conv3x3_launch(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                               const_cast<void *>(ptr(st.dst, in, out)), h, w, 0, h, s);
+            cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2 + 1], s);
+            if (rc != AJIB_OK) return rc;
+        }
+        prof_runs_++;
+        return AJIB_OK;
+    }
+    // band boundaries over the shifted row space [0, h + ns - 1): step k of band b covers rows
+    // [B_b - k, B_{b+1} - k) clipped to the frame
+    const int nb = std::max(1, std::min(bands_, h));
+    for (int b = 0; b < nb; b++) {
+        const int span = h + ns - 1;
+        const int B0 = (int)((long)span * b / nb), B1 = (int)((long)span * (b + 1) / nb);
+        for (int k = 0; k < ns; k++) {
+            const Step &st = steps_[k];
+            int r0 = nb == 1 ? 0 : std::max(0, B0 - k), r1 = nb == 1 ? h : std::min(h, B1 - k);
+            if (r0 >= r1) continue;
+            const int rc = ajib_conv3x3_launch(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                               const_cast<void *>(ptr(st.dst, in, out)), h, w, r0, r1, s);
+            if (rc != AJIB_OK) return rc;
+        }
+    }
+    return AJIB_OK;
+}
+
+}  // namespace ajib

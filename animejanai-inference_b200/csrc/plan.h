@@ -1,0 +1,121 @@
+/*
+ * plan.h — the native model: a conv net as a plan of fused steps, and the executor that runs it
+ * at one input size. Host C++ (internal; the C ABI is in include/aji_b200.h).
+ *
+ * A Plan is what the reference's lowering produces (src/native/lower.h:38-77): conv steps that
+ * read a feature map or the NCHW RGB model input and fold their activation, SPAN gate or
+ * depth-to-space output, and concat steps (a 1x1 conv over 2-4 feature maps). Feature ids >= 0
+ * are NHWC fp16 maps at the conv resolution; kModelInput / kModelOutput are the NCHW fp16 RGB
+ * model input and output. Models are read from this engine's model file (model.cpp) until the
+ * ONNX lowering lands.
+ *
+ * The Executor (reference src/native/executor.cpp:23-127) uploads the weights, assigns feature
+ * buffers with lifetime reuse (reference src/native/layout.cpp:10-77) and launches one kernel
+ * per step on a stream, so a run can be captured into a CUDA graph. Unlike the reference it can
+ * run the net as horizontal bands: all steps over band 0, then band 1, ..., each step's rows
+ * shifted down by one per step so every row a step reads was written by the previous step of the
+ * same or an earlier band. A band's activations stay in L2 between the steps.
+ */
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/aji_b200.h"
+
+struct ajib_concat_weights;
+
+namespace ajib {
+
+constexpr int kModelInput = -2, kModelOutput = -3;
+
+struct PlanWeights {
+    int taps = 0, cin = 0, cout = 0;
+    std::vector<uint16_t> w;   // [taps][cin][cout] fp16 bits
+    std::vector<float> bias;   // cout
+    std::vector<float> slope;  // cout or empty
+};
+
+struct PlanStep {
+    enum Kind { CONV = 0, CONCAT = 1 } kind = CONV;
+    int in = 0, act = 0, gate = 0, out = 0;
+    int cin = 0, cout = 0;
+    PlanWeights w, att;
+    int src = -1, resid = -1, dst = -1;
+    bool in_norm = false;
+    float in_mean[3] = {0.f, 0.f, 0.f}, in_scale[3] = {1.f, 1.f, 1.f};
+    bool out_clamp = false;
+    int c = 0, nsrc = 0;
+    int srcs[4] = {-1, -1, -1, -1};
+};
+
+struct Plan {
+    std::vector<PlanStep> steps;
+    std::vector<int> channels;  // per feature id
+    int unshuffle = 1;
+    int depth_to_space = 1;
+    std::string name;
+};
+
+// Parse this engine's model file (layout documented in model.cpp). *why on failure.
+bool parse_model(const void *data, size_t size, Plan *out, std::string *why);
+bool load_model_file(const std::string &path, Plan *out, std::string *why);
+bool validate_plan(const Plan &p, std::string *why);
+std::string describe(const Plan &p);
+// FLOPs per input pixel (algorithmic: 2 * taps * cin * cout per conv output pixel).
+double flops_per_pixel(const Plan &p);
+
+class Executor {
+public:
+    static std::unique_ptr<Executor> create(const Plan &plan, int in_w, int in_h, std::string *why);
+    ~Executor();
+    Executor(const Executor &) = delete;
+    Executor &operator=(const Executor &) = delete;
+
+    int in_w() const { return W_; }
+    int in_h() const { return H_; }
+    int out_w() const { return W_ * R_; }
+    int out_h() const { return H_ * R_; }
+    int scale() const { return R_; }
+    size_t device_bytes() const { return bytes_; }
+    size_t weight_bytes() const { return weight_bytes_; }
+    int launches_per_run() const;
+    // bands <= 1: one launch per step over the whole frame; else the banded schedule.
+    void set_bands(int bands) { bands_ = bands < 1 ? 1 : bands; }
+    int bands() const { return bands_; }
+    // in: NCHW fp16 [3][h][w], out: NCHW fp16 [3][R*h][R*w]; w <= in_w(), h <= in_h().
+    int run(const void *in, void *out, int w, int h, cudaStream_t s) const;
+    int run(const void *in, void *out, cudaStream_t s) const { return run(in, out, W_, H_, s); }
+    // Step timing: while enabled, every launch is bracketed by CUDA events on its stream (a ring of
+    // kProfRuns runs); profile_read synchronises and returns per-step summed milliseconds and
+    // counts of the runs recorded since enabling.
+    int profile(bool on);
+    int profile_read(double *ms, int *counts, int nsteps) const;
+
+private:
+    Executor() = default;
+    struct Step {
+        bool concat = false;
+        ajib_conv op{};
+        ajib_weights *w = nullptr, *att = nullptr;
+        int c = 0, nsrc = 0;
+        int src = -1, resid = -1, dst = -1;
+        int srcs[4] = {-1, -1, -1, -1};
+    };
+    const void *ptr(int t, const void *in, void *out) const;
+    static constexpr int kProfRuns = 64;
+    mutable std::vector<cudaEvent_t> prof_ev_;  // [kProfRuns][steps][2]
+    mutable int prof_runs_ = 0;
+    bool prof_on_ = false;
+    std::vector<Step> steps_;
+    std::vector<void *> buffers_;
+    std::vector<void *> tensor_;
+    int W_ = 0, H_ = 0, R_ = 1, bands_ = 1;
+    size_t bytes_ = 0, weight_bytes_ = 0;
+};
+
+}  // namespace ajib

@@ -1,0 +1,380 @@
+"""Benchmark: BASELINE config 1 — SRVGGNetCompact 2x video, 1920x1080 P010 -> 3840x2160 P010,
+fp16 net with random-init seeded weights, through the engine's video C ABI (include/aji.h:
+aji_create / aji_configure / aji_infer).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one frame through pre-pass -> 18 fused convs -> post-pass. `value` is frames/s over all
+ranks with frames already resident in HBM (device-timed with CUDA events on the launching
+stream, max over ranks); `e2e` is the same through aji_infer with the frame copied from pinned
+host memory and the result read back every step. N > 1: one process per GPU (torchrun), each
+rank upscales its own frames, no collectives on the data path ("scaling": "weak"); a gloo group
+only carries the barrier and the max of the per-rank times.
+
+--impl reference times the reference's own CPU implementation of this path (the fp32 reference
+net sanity/native_ref.h:run_plan, compiled from the reference sources into oracle/_ref) on the
+host cores, on a bounded sample of the same frame (a band of rows through all 18 steps); where
+that build is absent, the oracle's restatement of it.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "animejanai-inference_b200"))
+
+W_IN, H_IN, SCALE = 1920, 1080, 2
+MODEL_SEED = 1
+METRIC = "frames/s 1080p->4K 2x Compact fp16 at 1/2/4/8 B200; % tensor-core peak"
+
+
+def value_noise(rng, h, w, lo, hi, cell=32):
+    """Seeded smooth value noise in [lo, hi]: random values on a coarse grid, bilinear between."""
+    gh, gw = h // cell + 2, w // cell + 2
+    g = rng.uniform(lo, hi, size=(gh, gw))
+    ys = np.arange(h) / cell
+    xs = np.arange(w) / cell
+    y0, x0 = np.floor(ys).astype(int), np.floor(xs).astype(int)
+    fy, fx = (ys - y0)[:, None], (xs - x0)[None, :]
+    a = g[y0][:, x0]
+    b = g[y0][:, x0 + 1]
+    c = g[y0 + 1][:, x0]
+    d = g[y0 + 1][:, x0 + 1]
+    return (a * (1 - fy) * (1 - fx) + b * (1 - fy) * fx + c * fy * (1 - fx) + d * fy * fx)
+
+
+def p010_frame(seed, w=W_IN, h=H_IN):
+    """One P010 frame: Y and interleaved CbCr from smooth value noise spanning 64..940 (10-bit),
+    stored in the high bits of 16."""
+    rng = np.random.default_rng(seed)
+    y = np.rint(value_noise(rng, h, w, 64, 940)).astype(np.uint16) << 6
+    u = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
+    v = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
+    uv = np.stack([u, v], axis=-1).reshape(h // 2, w)
+    return y, uv
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 7:
+                    continue
+                try:
+                    sm.append(float(parts[0]))
+                    mx = max(mx, float(parts[1]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[3:7]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline_sample(rows=16, nthreads=0):
+    """The reference CPU path on a bounded sample: a W_IN x rows band of the Compact net (all 18
+    steps), timed on the host cores. Uses oracle/_ref (the reference's run_plan compiled from its
+    own sources) when built, else the oracle's restatement. Returns (frames/s, cores, kind, sample)."""
+    import ajib
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    plan = ajib.compact_plan(MODEL_SEED)
+    rng = np.random.default_rng(7)
+    x = rng.uniform(0, 1, size=(3, rows, W_IN)).astype(np.float16).astype(np.float32)
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_net.so")
+    if os.path.exists(ref_lib):
+        import refnet
+        t0 = time.perf_counter()
+        refnet.run_plan(ref_lib, plan, x, nthreads)
+        dt = time.perf_counter() - t0
+        cores = refnet.threads(ref_lib, nthreads)
+        kind = "reference"
+    else:
+        from util import oracle_conv
+        import oracle_net
+        t0 = time.perf_counter()
+        oracle_net.run_plan(plan, x, nthreads)
+        dt = time.perf_counter() - t0
+        cores = nthreads if nthreads > 0 else os.cpu_count()
+        kind = "port"
+    fps = (rows * W_IN) / (H_IN * W_IN) / dt
+    return fps, cores, kind, f"{W_IN}x{rows} band of the 1080p frame through all 18 steps ({dt:.2f} s)"
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        fps, cores, kind, sample = cpu_baseline_sample(rows=16)
+        if i >= args.warmup:
+            vals.append(fps)
+        info = (cores, kind, sample)
+    v = float(np.mean(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1 (Compact 2x 1080p P010 -> 4K), CPU reference net on a band sample",
+                       "model": "SRVGGNetCompact 64x16 2x random-init"},
+            "cpu_baseline": {"value": v, "unit": "frames/s", "cores": info[0], "kind": info[1], "sample": info[2]},
+            "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def current_context():
+    """The CUDA driver context torch made current on this rank's device (passed to aji_create)."""
+    import torch
+    torch.cuda.current_stream().synchronize()
+    cuda = C.CDLL("libcuda.so.1")
+    ctx = C.c_void_p()
+    cuda.cuCtxGetCurrent(C.byref(ctx))
+    return ctx.value
+
+
+def run_ours(args, rank, world, local_rank, dist):
+    import torch
+    import ajib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
+
+    # model file (seeded random init, the config-1 architecture)
+    plan = ajib.compact_plan(MODEL_SEED)
+    mdir = tempfile.mkdtemp(prefix="ajib_bench_")
+    mpath = os.path.join(mdir, "compact_2x.ajnm")
+    with open(mpath, "wb") as f:
+        f.write(ajib.model_bytes(plan))
+    torch.zeros(1, device=dev)
+    vid = ajib.Video(mpath, W_IN, H_IN, cuda_context=current_context())
+    ow, oh = vid.configure(W_IN, H_IN)
+    if args.bands > 1:
+        os.environ["AJIB_BANDS"] = str(args.bands)
+
+    nfr = 4
+    frames_in = []
+    for i in range(nfr):
+        y, uv = p010_frame(1000 * rank + i)
+        frames_in.append((torch.from_numpy(y.view(np.int16)).to(dev), torch.from_numpy(uv.view(np.int16)).to(dev)))
+    outs = [(torch.empty((oh, ow), dtype=torch.int16, device=dev), torch.empty((oh // 2, ow), dtype=torch.int16, device=dev))
+            for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+
+    def fr(i):
+        yi, uvi = frames_in[i % nfr]
+        return ajib.frame(W_IN, H_IN, ajib.FMT_P010, [yi.data_ptr(), uvi.data_ptr()], [W_IN * 2, W_IN * 2])
+
+    def fo(i):
+        yo, uvo = outs[i % 2]
+        return ajib.frame(ow, oh, ajib.FMT_P010, [yo.data_ptr(), uvo.data_ptr()], [ow * 2, ow * 2])
+
+    fins = [fr(i) for i in range(nfr)]
+    fouts = [fo(i) for i in range(2)]
+
+    def step(i):
+        rc = vid.infer(fins[i % nfr], fouts[i % 2], sp)
+        if rc != 0:
+            raise RuntimeError(f"aji_infer failed: {rc} {vid.error()}")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    stream.synchronize()
+    assert ajib.kernel_status() == 0, "a kernel pipeline wait timed out during warm-up"
+
+    # ---- device-timed region (frames resident in HBM)
+    prof = args.bands <= 1
+    if prof:
+        ajib.lib.ajib_video_profile(vid.handle, 1)
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    assert ajib.kernel_status() == 0, "a kernel pipeline wait timed out"
+    step_ms = np.zeros(64)
+    step_n = np.zeros(64, dtype=np.int32)
+    if prof:
+        ajib.lib.ajib_video_profile_read(vid.handle, step_ms.ctypes.data_as(C.POINTER(C.c_double)),
+                                         step_n.ctypes.data_as(C.POINTER(C.c_int)), 64)
+        ajib.lib.ajib_video_profile(vid.handle, 0)
+
+    # ---- e2e: pinned host frame in, result read back, every step
+    hy = [torch.from_numpy(p010_frame(5000 + rank * 10 + i)[0].view(np.int16)).pin_memory() for i in range(2)]
+    huv = [torch.from_numpy(p010_frame(5000 + rank * 10 + i)[1].view(np.int16)).pin_memory() for i in range(2)]
+    hoy = torch.empty((oh, ow), dtype=torch.int16).pin_memory()
+    houv = torch.empty((oh // 2, ow), dtype=torch.int16).pin_memory()
+    din_y, din_uv = frames_in[0]
+    dout_y, dout_uv = outs[0]
+    h2d = (hy[0].numel() + huv[0].numel()) * 2
+    d2h = (hoy.numel() + houv.numel()) * 2
+
+    def e2e_step(i):
+        with torch.cuda.stream(stream):
+            din_y.copy_(hy[i % 2], non_blocking=True)
+            din_uv.copy_(huv[i % 2], non_blocking=True)
+            step(0)
+            hoy.copy_(dout_y, non_blocking=True)
+            houv.copy_(dout_uv, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    f1.record(stream)
+    f1.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    # max over ranks
+    times = np.array([t_ms, e2e_ms], dtype=np.float64)
+    if dist is not None:
+        import torch as _t
+        tt = _t.from_numpy(times)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        times = tt.numpy()
+    t_ms, e2e_ms = float(times[0]), float(times[1])
+
+    if rank != 0:
+        vid.close()
+        return
+    frames_total = args.steps * world
+    value = frames_total / (t_ms / 1000.0)
+    e2e_value = frames_total / (e2e_ms / 1000.0)
+
+    # roofline of the dominant kernel: the 16 body convs (64 -> 64 + PReLU, steps 1..16)
+    flops_body = 2.0 * 9 * 64 * 64 * W_IN * H_IN
+    body_ms = None
+    if prof and step_n[1] > 0:
+        body_ms = float(np.sum(step_ms[1:17]) / np.sum(step_n[1:17]))
+    roof = None
+    if body_ms:
+        achieved = flops_body / (body_ms / 1000.0) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_sus, "unit": "TFLOP/s",
+                "frac": achieved / tflops_sus, "traffic": None,
+                "kernel": "k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)",
+                "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json)",
+                "flops_per_launch": flops_body,
+                "frame_tflops": plan_flops(plan) / (t_ms / args.steps / 1000.0) / 1e12}
+
+    line = {"metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1: Compact 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010",
+                       "model": "SRVGGNetCompact 64 feat x 16 body, PReLU, pixel_shuffle 2, random-init (seed 1)",
+                       "global_batch": world, "parallelism": f"frame-parallel x{world} (replicas, no collectives)",
+                       "l2": "inputs larger than L2 (two 265 MB activation buffers per frame)",
+                       "bands": args.bands},
+            "roofline": roof,
+            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * (2 + 18 * max(1, args.bands)),
+            "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        fps, cores, kind, sample = cpu_baseline_sample(rows=16)
+        line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": kind, "sample": sample}
+    vid.close()
+    print(json.dumps(line), flush=True)
+
+
+def plan_flops(plan):
+    return sum(2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2] for s in plan["steps"]) * W_IN * H_IN
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--bands", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as td
+        td.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        dist = td
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -77,6 +77,85 @@ AJIB_EXPORT int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_s
 AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                     int row_begin, int row_end, void *stream);
 
+/* ---- colour passes (reference src/kernels.h:12-78; same names, arguments and semantics) ----
+ * Normalisation constants in raw container units (P010 samples are 10 bits in the high bits of
+ * 16, so its scales include the << 6): y = (raw - yoff) / yscale, c = (raw - coff) / cscale. */
+typedef struct aji_csp {
+    float kr, kb;
+    float yoff, yscale;
+    float coff, cscale;
+} aji_csp;
+
+/* reference src/kernels.h:21 (constants: src/resample.h:100-129) */
+AJIB_EXPORT aji_csp aji_make_csp(int format, int matrix, int range);
+
+typedef struct aji_plan aji_plan;
+enum { AJI_FILTER_SPLINE36 = 0, AJI_FILTER_BILINEAR = 1 };
+
+/* Resampling plans (reference src/kernels.h:46-49): the filter tables of zimg's compute_filter
+ * for 4:2:0 chroma at luma size w x h and the given siting, uploaded to the current device.
+ * Runs must use the same device. NULL on failure. */
+AJIB_EXPORT aji_plan *aji_pre_plan_create(int format, int w, int h, int siting, int filter);
+AJIB_EXPORT aji_plan *aji_post_plan_create(int format, int w, int h, int siting, int filter);
+AJIB_EXPORT void aji_plan_destroy(aji_plan *p);
+
+/* NV12/P010 -> fp16 NCHW RGB [3][h][w] (reference src/kernels.h:52-55): chroma upsampled with
+ * the plan's filter, then the matrix; fp32 throughout, one rounding to fp16. One kernel. Returns
+ * 0 or a cudaError_t. */
+AJIB_EXPORT int aji_run_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane,
+                            ptrdiff_t uv_stride, const aji_csp *csp, void *dst_f16, void *stream);
+
+/* fp16 NCHW RGB [3][h][w] -> NV12/P010 (reference src/kernels.h:58-60): matrix, luma quantised,
+ * chroma downsampled (horizontal then vertical, fp32) and quantised. P010 quantises at 10 bits
+ * then shifts. One kernel. Returns 0 or a cudaError_t. */
+AJIB_EXPORT int aji_run_post(aji_plan *p, const void *src_f16, const aji_csp *csp, void *y_plane, ptrdiff_t y_stride,
+                             void *uv_plane, ptrdiff_t uv_stride, void *stream);
+
+/* 4:4:4 16-bit planar variants, matrix only (reference src/kernels.h:64-75). */
+AJIB_EXPORT int aji_run_post444(int format, int w, int h, const void *src_f16, const aji_csp *csp, void *y_plane,
+                                ptrdiff_t y_stride, void *cb_plane, ptrdiff_t cb_stride, void *cr_plane,
+                                ptrdiff_t cr_stride, void *stream);
+AJIB_EXPORT int aji_run_pre444(int w, int h, const void *y_plane, ptrdiff_t y_stride, const void *cb_plane,
+                               ptrdiff_t cb_stride, const void *cr_plane, ptrdiff_t cr_stride, const aji_csp *csp,
+                               void *dst_f16, void *stream);
+
+/* The plan's filter tables as the host computed them (for tests): which = 0 horizontal, 1
+ * vertical. Copies up to max_dst entries of start and max_dst * taps weights; returns taps. */
+AJIB_EXPORT int ajib_plan_table(const aji_plan *p, int which, int *start, float *wt, int max_dst);
+
+/* ---- the native model and its executor ----
+ * A model is a plan of fused conv steps (reference src/native/lower.h:38-77, Plan), read from
+ * this engine's model file (format: animejanai-inference_b200/csrc/model.cpp). An executor is
+ * the model instantiated for one input size on the current device (reference
+ * src/native/executor.h:21-60): weights uploaded, feature buffers allocated, run() only launches
+ * kernels (capturable in a CUDA graph). */
+typedef struct ajib_model ajib_model;
+typedef struct ajib_exec ajib_exec;
+
+AJIB_EXPORT int ajib_model_load(const char *path, ajib_model **out, char *err, size_t err_size);
+AJIB_EXPORT int ajib_model_from_memory(const void *data, size_t size, ajib_model **out, char *err, size_t err_size);
+AJIB_EXPORT void ajib_model_release(ajib_model **m);
+/* scale (depth-to-space), steps, algorithmic FLOPs per input pixel; description into desc */
+AJIB_EXPORT int ajib_model_info(const ajib_model *m, int *scale, int *steps, double *flops_per_px, char *desc,
+                                size_t desc_size);
+
+AJIB_EXPORT int ajib_exec_create(const ajib_model *m, int w, int h, ajib_exec **out, char *err, size_t err_size);
+AJIB_EXPORT void ajib_exec_release(ajib_exec **e);
+/* in: NCHW fp16 [3][h][w]; out: NCHW fp16 [3][R*h][R*w] (device pointers). */
+AJIB_EXPORT int ajib_exec_run(ajib_exec *e, const void *in, void *out, void *stream);
+/* Run the net as `bands` horizontal bands (1 = whole frame per step): each band runs every step,
+ * its rows shifted down one per step, so a band's activations stay in L2 between steps. */
+AJIB_EXPORT int ajib_exec_set_bands(ajib_exec *e, int bands);
+/* Step timing for benchmarks: while on, each step's launch is bracketed by CUDA events on the run's
+ * stream; profile_read synchronises and fills per-step summed milliseconds and run counts. */
+AJIB_EXPORT int ajib_exec_profile(ajib_exec *e, int on);
+AJIB_EXPORT int ajib_exec_profile_read(ajib_exec *e, double *ms, int *counts, int nsteps);
+/* The same for the executor inside a configured video context (aji.h). */
+AJIB_EXPORT int ajib_video_profile(aji_ctx *c, int on);
+AJIB_EXPORT int ajib_video_profile_read(aji_ctx *c, double *ms, int *counts, int nsteps);
+/* device bytes held, launches per run */
+AJIB_EXPORT int ajib_exec_info(const ajib_exec *e, size_t *device_bytes, size_t *weight_bytes, int *launches);
+
 /* Reads and optionally clears the current device's kernel status word: 0, or the code of the
  * first pipeline wait that timed out in a kernel of this library. */
 AJIB_EXPORT int ajib_kernel_status(int clear);

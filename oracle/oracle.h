@@ -44,6 +44,24 @@ int orc_conv3x3(int in_mode, const float *src, int H, int W, int cin, const floa
 int orc_concat1x1(const float *const *srcs, int nsrc, int npx, int c, const float *w, const float *bias, float *dst,
                   int nthreads);
 
+/* ---- colour passes (src/resample.h, src/kernels.cu) ---- */
+/* zimg filter table (src/resample.h:53-84): returns taps; start [dst] and wt [dst][taps] filled
+ * when both are given. filter 0 Spline36, 1 bilinear. */
+int orc_filter(int src, int dst, double shift, int filter, int *start, float *wt);
+void orc_chroma_shift(int siting, int up, double *sx, double *sy);
+/* csp = {kr, kb, yoff, yscale, coff, cscale} (src/resample.h:100-129) */
+void orc_make_csp(int format, int matrix, int range, float *csp);
+/* NV12/P010 -> fp16 bits NCHW [3][h][w] (src/kernels.cu:105-164, :441-465) */
+int orc_pre(int format, int w, int h, int siting, int filter, const void *y_plane, ptrdiff_t ys, const void *uv_plane,
+            ptrdiff_t uvs, const float *csp, uint16_t *dst);
+/* fp16 bits NCHW [3][h][w] -> NV12/P010 (src/kernels.cu:170-231, :467-497) */
+int orc_post(int format, int w, int h, int siting, int filter, const uint16_t *src, const float *csp, void *y_plane,
+             ptrdiff_t ys, void *uv_plane, ptrdiff_t uvs);
+int orc_post444(int format, int w, int h, const uint16_t *src, const float *csp, uint16_t *yp, uint16_t *cbp,
+                uint16_t *crp);
+int orc_pre444(int w, int h, const uint16_t *yp, const uint16_t *cbp, const uint16_t *crp, const float *csp,
+               uint16_t *dst);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,34 @@
+#!/usr/bin/env bash
+# Compiles the reference's own sources (the-database/animejanai-inference, read-only at $1) into
+# oracle/_ref/: the checkers and the CPU baseline. Nothing here is part of the product, and no
+# reference source is copied: each library is built from the files where they lie, plus the thin
+# C shims in this directory. Only the compilers run (no reference build system).
+set -euo pipefail
+REF=${1:-/root/reference}
+HERE=$(cd "$(dirname "$0")" && pwd)
+OUT=$HERE/../_ref
+mkdir -p "$OUT"
+CXX=${CXX:-g++}
+NVCC=${NVCC:-nvcc}
+ARCH="-gencode arch=compute_100a,code=sm_100a"
+
+# CPU reference net (sanity/native_ref.h + src/native/pack.cpp)
+$CXX -O3 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/sanity" -I"$REF/include" \
+    "$HERE/refnet_shim.cpp" "$REF/src/native/pack.cpp" -o "$OUT/libref_net.so" -lpthread
+# CPU tiler (src/core/tiling.cpp)
+$CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/src/core" -I"$REF/include" \
+    "$HERE/reftiling_shim.cpp" "$REF/src/core/tiling.cpp" -o "$OUT/libref_tiling.so" -lpthread
+# host resampling tables and colour constants (src/resample.h)
+$CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/include" \
+    "$HERE/refresample_shim.cpp" -o "$OUT/libref_resample.so"
+# GPU: the reference colour kernels (src/kernels.cu), GPU tiler (src/core/tiling_gpu.cu) and conv
+# kernels (src/native/conv.cu + pack.cpp) for sm_100a — bit-exact checkers and the GPU bar
+if command -v "$NVCC" >/dev/null; then
+    $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" \
+        "$REF/src/kernels.cu" -o "$OUT/libref_kernels.so"
+    $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/src/core" -I"$REF/include" \
+        "$REF/src/core/tiling_gpu.cu" -o "$OUT/libref_tiling_gpu.so"
+    $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" \
+        "$HERE/refconv_shim.cu" "$REF/src/native/conv.cu" "$REF/src/native/pack.cpp" -o "$OUT/libref_conv.so"
+fi
+echo "oracle/_ref built from $REF"

@@ -1,0 +1,155 @@
+"""GPU: the colour passes (aji_run_pre / aji_run_post / 4:4:4) against the CPU oracle, bit for bit
+(0 mismatches, the reference's own criterion for its fused pre-pass: sanity/pre_fusion.cu:71-99),
+over formats, matrices, ranges, sitings and ragged sizes; and, when the reference's kernels were
+built into oracle/_ref, against those kernels run on the same GPU."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from util import ROOT, oracle_csp, oracle_post, oracle_pre, yuv420_frame
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+REF_KERNELS = os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so")
+
+CASES = [(2, 2, 1, 1, 1920, 1080), (1, 2, 1, 1, 1280, 720), (2, 1, 2, 2, 130, 66), (1, 3, 1, 3, 62, 46),
+         (2, 3, 2, 3, 258, 34), (1, 1, 2, 1, 6, 4), (2, 2, 1, 2, 2, 2)]
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16 if a.dtype == np.uint16 else np.uint8)).cuda()
+
+
+def gpu_pre(fmt, y, uv, matrix, rng_, siting):
+    import ajib
+    h, w = y.shape
+    p = ajib.lib.aji_pre_plan_create(fmt, w, h, siting, 0)
+    assert p
+    dy, duv = dev(y), dev(uv)
+    out = torch.empty((3, h, w), dtype=torch.float16, device="cuda")
+    csp = ajib.lib.aji_make_csp(fmt, matrix, rng_)
+    rc = ajib.lib.aji_run_pre(p, dy.data_ptr(), y.strides[0], duv.data_ptr(), uv.strides[0], C.byref(csp),
+                              out.data_ptr(), None)
+    torch.cuda.synchronize()
+    ajib.lib.aji_plan_destroy(p)
+    assert rc == 0
+    return out.cpu().numpy().view(np.uint16)
+
+
+def gpu_post(fmt, rgb_bits, matrix, rng_, siting=1):
+    import ajib
+    _, h, w = rgb_bits.shape
+    p = ajib.lib.aji_post_plan_create(fmt, w, h, siting, 0)
+    assert p
+    src = torch.from_numpy(rgb_bits.view(np.float16)).cuda()
+    dt = torch.int16 if fmt == 2 else torch.uint8
+    oy = torch.empty((h, w), dtype=dt, device="cuda")
+    ouv = torch.empty((h // 2, w), dtype=dt, device="cuda")
+    es = 2 if fmt == 2 else 1
+    csp = ajib.lib.aji_make_csp(fmt, matrix, rng_)
+    rc = ajib.lib.aji_run_post(p, src.data_ptr(), C.byref(csp), oy.data_ptr(), w * es, ouv.data_ptr(), w * es, None)
+    torch.cuda.synchronize()
+    ajib.lib.aji_plan_destroy(p)
+    assert rc == 0
+    npdt = np.uint16 if fmt == 2 else np.uint8
+    return oy.cpu().numpy().view(npdt), ouv.cpu().numpy().view(npdt)
+
+
+@pytest.mark.parametrize("fmt,matrix,rng_,siting,w,h", CASES)
+def test_pre_bit_exact(fmt, matrix, rng_, siting, w, h):
+    rng = np.random.default_rng(w * 7 + h + fmt)
+    y, uv = yuv420_frame(rng, w, h, fmt)
+    want = oracle_pre(fmt, y, uv, matrix, rng_, siting)
+    got = gpu_pre(fmt, y, uv, matrix, rng_, siting)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} mismatches"
+
+
+@pytest.mark.parametrize("fmt,matrix,rng_,siting,w,h", CASES)
+def test_post_bit_exact(fmt, matrix, rng_, siting, w, h):
+    rng = np.random.default_rng(w * 3 + h + fmt)
+    rgb = rng.uniform(-0.1, 1.1, size=(3, h, w)).astype(np.float16).view(np.uint16)
+    wy, wuv = oracle_post(fmt, rgb, matrix, rng_, siting)
+    gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting)
+    assert np.array_equal(gy, wy), f"luma: {int((gy != wy).sum())} mismatches"
+    assert np.array_equal(guv, wuv), f"chroma: {int((guv != wuv).sum())} mismatches"
+
+
+@pytest.mark.parametrize("fmt", [3, 5, 6])
+def test_444_bit_exact(fmt):
+    import ajib
+    rng = np.random.default_rng(fmt)
+    h, w = 37, 53
+    rgb = rng.uniform(-0.1, 1.1, size=(3, h, w)).astype(np.float16).view(np.uint16)
+    o = __import__("util")._colour_sigs()
+    csp_o = oracle_csp(fmt, 2, 1)
+    wy, wcb, wcr = (np.zeros((h, w), np.uint16) for _ in range(3))
+    o.orc_post444(fmt, w, h, rgb.ctypes.data, csp_o, wy.ctypes.data, wcb.ctypes.data, wcr.ctypes.data)
+    src = torch.from_numpy(rgb.view(np.float16)).cuda()
+    planes = [torch.empty((h, w), dtype=torch.int16, device="cuda") for _ in range(3)]
+    csp = ajib.lib.aji_make_csp(fmt, 2, 1)
+    rc = ajib.lib.aji_run_post444(fmt, w, h, src.data_ptr(), C.byref(csp), planes[0].data_ptr(), w * 2,
+                                  planes[1].data_ptr(), w * 2, planes[2].data_ptr(), w * 2, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    got = [p.cpu().numpy().view(np.uint16) for p in planes]
+    for g, want in zip(got, (wy, wcb, wcr)):
+        assert np.array_equal(g, want)
+    # and back: 4:4:4 -> RGB
+    want_rgb = np.zeros((3, h, w), np.uint16)
+    o.orc_pre444(w, h, wy.ctypes.data, wcb.ctypes.data, wcr.ctypes.data, csp_o, want_rgb.ctypes.data)
+    out = torch.empty((3, h, w), dtype=torch.float16, device="cuda")
+    rc = ajib.lib.aji_run_pre444(w, h, planes[0].data_ptr(), w * 2, planes[1].data_ptr(), w * 2, planes[2].data_ptr(),
+                                 w * 2, C.byref(csp), out.data_ptr(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), want_rgb)
+
+
+@pytest.mark.skipif(not os.path.exists(REF_KERNELS), reason="reference kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("fmt,matrix,rng_,siting,w,h", CASES[:5])
+def test_against_reference_kernels(fmt, matrix, rng_, siting, w, h):
+    """The reference's own src/kernels.cu, compiled for sm_100a, on the same inputs: 0 mismatches."""
+    import ajib
+    ref = C.CDLL(REF_KERNELS)
+    ref.aji_pre_plan_create.restype = C.c_void_p
+    ref.aji_post_plan_create.restype = C.c_void_p
+    ref.aji_pre_plan_create.argtypes = [C.c_int] * 5
+    ref.aji_post_plan_create.argtypes = [C.c_int] * 5
+    ref.aji_run_pre.argtypes = [C.c_void_p, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_void_p,
+                                C.c_void_p]
+    ref.aji_run_post.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_ssize_t,
+                                 C.c_void_p]
+    ref.aji_plan_destroy.argtypes = [C.c_void_p]
+    rng = np.random.default_rng(w + h)
+    y, uv = yuv420_frame(rng, w, h, fmt)
+    csp = ajib.lib.aji_make_csp(fmt, matrix, rng_)
+    # pre
+    p = ref.aji_pre_plan_create(fmt, w, h, siting, 0)
+    dy, duv = dev(y), dev(uv)
+    out = torch.empty((3, h, w), dtype=torch.float16, device="cuda")
+    assert ref.aji_run_pre(p, dy.data_ptr(), y.strides[0], duv.data_ptr(), uv.strides[0], C.addressof(csp),
+                           out.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    ref.aji_plan_destroy(p)
+    want = out.cpu().numpy().view(np.uint16)
+    got = gpu_pre(fmt, y, uv, matrix, rng_, siting)
+    assert np.array_equal(got, want), f"pre: {int((got != want).sum())} mismatches vs the reference kernels"
+    # post
+    rgb = want
+    p = ref.aji_post_plan_create(fmt, w, h, siting, 0)
+    src = torch.from_numpy(rgb.view(np.float16)).cuda()
+    dt = torch.int16 if fmt == 2 else torch.uint8
+    es = 2 if fmt == 2 else 1
+    oy = torch.empty((h, w), dtype=dt, device="cuda")
+    ouv = torch.empty((h // 2, w), dtype=dt, device="cuda")
+    assert ref.aji_run_post(p, src.data_ptr(), C.addressof(csp), oy.data_ptr(), w * es, ouv.data_ptr(), w * es,
+                            None) == 0
+    torch.cuda.synchronize()
+    ref.aji_plan_destroy(p)
+    npdt = np.uint16 if fmt == 2 else np.uint8
+    gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting)
+    assert np.array_equal(gy, oy.cpu().numpy().view(npdt))
+    assert np.array_equal(guv, ouv.cpu().numpy().view(npdt))

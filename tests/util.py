@@ -89,3 +89,85 @@ def to_f16_bits(x):
 def psnr(a, b, peak=1.0):
     mse = float(np.mean((np.asarray(a, np.float64) - np.asarray(b, np.float64)) ** 2))
     return float("inf") if mse == 0 else 10.0 * np.log10(peak * peak / mse)
+
+
+# ---- colour oracle (oracle/oracle_colour.c) ----
+def _colour_sigs():
+    o = oracle()
+    if getattr(o, "_colour", False):
+        return o
+    vp, sz = C.c_void_p, C.c_ssize_t
+    o.orc_filter.argtypes = [C.c_int, C.c_int, C.c_double, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float)]
+    o.orc_filter.restype = C.c_int
+    o.orc_make_csp.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
+    o.orc_make_csp.restype = None
+    o.orc_pre.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, sz, vp, sz, C.POINTER(C.c_float), vp]
+    o.orc_pre.restype = C.c_int
+    o.orc_post.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, C.POINTER(C.c_float), vp, sz, vp, sz]
+    o.orc_post.restype = C.c_int
+    o.orc_post444.argtypes = [C.c_int, C.c_int, C.c_int, vp, C.POINTER(C.c_float), vp, vp, vp]
+    o.orc_post444.restype = C.c_int
+    o.orc_pre444.argtypes = [C.c_int, C.c_int, vp, vp, vp, C.POINTER(C.c_float), vp]
+    o.orc_pre444.restype = C.c_int
+    o._colour = True
+    return o
+
+
+def oracle_csp(fmt, matrix, rng_):
+    o = _colour_sigs()
+    c = (C.c_float * 6)()
+    o.orc_make_csp(fmt, matrix, rng_, c)
+    return c
+
+
+def oracle_filter(src, dst, shift, filt=0):
+    o = _colour_sigs()
+    taps = o.orc_filter(src, dst, shift, filt, None, None)
+    start = np.zeros(dst, np.int32)
+    wt = np.zeros(dst * taps, np.float32)
+    o.orc_filter(src, dst, shift, filt, start.ctypes.data_as(C.POINTER(C.c_int)), wt.ctypes.data_as(C.POINTER(C.c_float)))
+    return taps, start, wt.reshape(dst, taps)
+
+
+def oracle_pre(fmt, y, uv, matrix, rng_, siting, filt=0):
+    """y: [h][w], uv: [h/2][w] interleaved (uint8 NV12 or uint16 P010). Returns fp16 bits [3][h][w]."""
+    o = _colour_sigs()
+    h, w = y.shape
+    y = np.ascontiguousarray(y)
+    uv = np.ascontiguousarray(uv)
+    dst = np.zeros((3, h, w), np.uint16)
+    csp = oracle_csp(fmt, matrix, rng_)
+    rc = o.orc_pre(fmt, w, h, siting, filt, y.ctypes.data, y.strides[0], uv.ctypes.data, uv.strides[0], csp,
+                   dst.ctypes.data)
+    assert rc == 0
+    return dst
+
+
+def oracle_post(fmt, rgb_bits, matrix, rng_, siting=1, filt=0):
+    """rgb_bits: fp16 bits [3][h][w]. Returns (y [h][w], uv [h/2][w]) uint8 or uint16."""
+    o = _colour_sigs()
+    _, h, w = rgb_bits.shape
+    dt = np.uint16 if fmt == 2 else np.uint8
+    y = np.zeros((h, w), dt)
+    uv = np.zeros((h // 2, w), dt)
+    src = np.ascontiguousarray(rgb_bits, np.uint16)
+    csp = oracle_csp(fmt, matrix, rng_)
+    rc = o.orc_post(fmt, w, h, siting, filt, src.ctypes.data, csp, y.ctypes.data, y.strides[0], uv.ctypes.data,
+                    uv.strides[0])
+    assert rc == 0
+    return y, uv
+
+
+def yuv420_frame(rng, w, h, fmt, lo=None, hi=None):
+    """Random 4:2:0 planes: P010 samples are 10 bits in the high bits of 16."""
+    if fmt == 2:
+        lo = 0 if lo is None else lo
+        hi = 1023 if hi is None else hi
+        y = (rng.integers(lo, hi + 1, size=(h, w)).astype(np.uint16) << 6)
+        uv = (rng.integers(lo, hi + 1, size=(h // 2, w)).astype(np.uint16) << 6)
+    else:
+        lo = 0 if lo is None else lo
+        hi = 255 if hi is None else hi
+        y = rng.integers(lo, hi + 1, size=(h, w)).astype(np.uint8)
+        uv = rng.integers(lo, hi + 1, size=(h // 2, w)).astype(np.uint8)
+    return y, uv
