@@ -50,6 +50,10 @@ lib.ajib_conv_supported.argtypes = [C.POINTER(ConvOp), C.c_char_p, C.c_size_t]
 lib.ajib_conv_supported.restype = C.c_int
 lib.ajib_conv3x3_launch.argtypes = [C.POINTER(ConvOp), _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp]
 lib.ajib_conv3x3_launch.restype = C.c_int
+lib.ajib_feature_pitch.argtypes = [C.c_int]
+lib.ajib_feature_pitch.restype = C.c_int
+lib.ajib_feature_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
+lib.ajib_feature_bytes.restype = C.c_size_t
 lib.ajib_kernel_status.argtypes = [C.c_int]
 lib.ajib_kernel_status.restype = C.c_int
 lib.ajib_selftest_umma.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp]
@@ -457,3 +461,15 @@ lib.aji_run_pre444.argtypes = [C.c_int, C.c_int, _vp, C.c_ssize_t, _vp, C.c_ssiz
 lib.aji_run_pre444.restype = C.c_int
 lib.ajib_plan_table.argtypes = [_vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float), C.c_int]
 lib.ajib_plan_table.restype = C.c_int
+lib.ajib_filter_table.argtypes = [C.c_int, C.c_int, C.c_double, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float)]
+lib.ajib_filter_table.restype = C.c_int
+
+
+def filter_table(src, dst, shift, filt=0):
+    import numpy as np
+    taps = lib.ajib_filter_table(src, dst, shift, filt, None, None)
+    start = np.zeros(dst, np.int32)
+    wt = np.zeros(dst * taps, np.float32)
+    lib.ajib_filter_table(src, dst, shift, filt, start.ctypes.data_as(C.POINTER(C.c_int)),
+                          wt.ctypes.data_as(C.POINTER(C.c_float)))
+    return taps, start, wt.reshape(dst, taps)

@@ -359,6 +359,17 @@ extern "C" void aji_plan_destroy(aji_plan *p)
     delete p;
 }
 
+extern "C" int ajib_filter_table(int src, int dst, double shift, int filter, int *start, float *wt)
+{
+    if (src < 1 || dst < 1) return -1;
+    const FilterTable t = make_filter(src, dst, shift, filter);
+    if (start && wt) {
+        std::memcpy(start, t.start.data(), t.start.size() * sizeof(int));
+        std::memcpy(wt, t.wt.data(), t.wt.size() * sizeof(float));
+    }
+    return t.taps;
+}
+
 extern "C" int ajib_plan_table(const aji_plan *p, int which, int *start, float *wt, int max_dst)
 {
     if (!p) return -1;

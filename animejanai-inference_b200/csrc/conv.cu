@@ -9,7 +9,6 @@
  * K-adjacent chunks at a fixed leading-byte offset.
  */
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -35,22 +34,31 @@ struct ajib_weights {
 namespace ajib {
 
 int pad_k(int cin) { return cin <= 16 ? 16 : (cin + 15) / 16 * 16; }
-int pad_n(int cout) { return (cout + 15) / 16 * 16; }
+// 3x3 outputs pad to 32 or 64: the accumulator ring's slots then start on 32-column TMEM
+// boundaries (TMEM's allocation granularity)
+int pad_n(int cout) { return cout <= 32 ? 32 : 64; }
 
-// [tap][kc][ng][n8][k8] fp16 bits; entries past cin / cout are zero
+// The B operand image. 3x3 weights (taps == 9) are stacked by tap row so that one MMA covers all
+// three vertical taps of a horizontal tap dx: [dx][kc][ty][ng][n8][k8], B row ty * npad + n of
+// (dx, K chunk kc) holding w[tap ty * 3 + dx][kc * 8 + k8][n]. 1x1 weights: [kc][ng][n8][k8].
+// Entries past cin / cout are zero.
 std::vector<uint16_t> pack_b_image(const uint16_t *w, int taps, int cin, int cout, int kpad, int npad)
 {
     const int KC = kpad / 8, NG = npad / 8;
     std::vector<uint16_t> img((size_t)taps * kpad * npad, 0);
-    for (int t = 0; t < taps; t++)
+    for (int t = 0; t < taps; t++) {
+        const int ty = taps == 9 ? t / 3 : 0, dx = taps == 9 ? t % 3 : 0;
         for (int kc = 0; kc < KC; kc++)
             for (int ng = 0; ng < NG; ng++)
                 for (int n8 = 0; n8 < 8; n8++)
                     for (int k8 = 0; k8 < 8; k8++) {
                         const int k = kc * 8 + k8, n = ng * 8 + n8;
-                        if (k < cin && n < cout)
-                            img[((((size_t)t * KC + kc) * NG + ng) * 8 + n8) * 8 + k8] = w[((size_t)t * cin + k) * cout + n];
+                        if (k >= cin || n >= cout) continue;
+                        const size_t at = taps == 9 ? ((((size_t)dx * KC + kc) * 3 + ty) * NG + ng) * 64 + n8 * 8 + k8
+                                                    : (((size_t)kc * NG + ng) * 64) + n8 * 8 + k8;
+                        img[at] = w[((size_t)t * cin + k) * cout + n];
                     }
+    }
     return img;
 }
 
@@ -77,53 +85,6 @@ int *status_word()
     return g_status[dev];
 }
 
-// ---- TMA tensor maps ----
-namespace {
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            p = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }();
-    return fn;
-}
-}  // namespace
-
-// The staged-row view of an NHWC fp16 tensor [H][W][C]: 4-D (8 channels, W, C/8, H) so that one
-// box {8, 130, C/8, 1} lands in shared memory as [C/8][130][8]. *split = 0. If the driver
-// refuses that view, the 3-D (C, W, H) view with box {8, 130, 1} (one copy per chunk), *split = 1.
-bool make_row_map(CUtensorMap *m, const void *base, int H, int W, int C, int *split)
-{
-    auto enc = encode_fn();
-    if (!enc) return false;
-    {
-        cuuint64_t dims[4] = {8, (cuuint64_t)W, (cuuint64_t)(C / 8), (cuuint64_t)H};
-        cuuint64_t strides[3] = {(cuuint64_t)C * 2, 16, (cuuint64_t)W * C * 2};
-        cuuint32_t box[4] = {8, (cuuint32_t)kHalo, (cuuint32_t)(C / 8), 1};
-        cuuint32_t es[4] = {1, 1, 1, 1};
-        if (enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-            *split = 0;
-            return true;
-        }
-    }
-    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H};
-    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2};
-    cuuint32_t box[3] = {8, (cuuint32_t)kHalo, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    if (enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return false;
-    *split = 1;
-    return true;
-}
-
 int sm_count()
 {
     int dev = 0, n = 0;
@@ -134,10 +95,10 @@ int sm_count()
 
 namespace {
 
-using ConvFn = cudaError_t (*)(const CUtensorMap &, const ConvDev &, int grid, cudaStream_t);
+using ConvFn = cudaError_t (*)(const ConvDev &, int grid, cudaStream_t);
 
 template <int KPAD, int NPAD>
-cudaError_t run_conv(const CUtensorMap &tm, const ConvDev &p, int grid, cudaStream_t s)
+cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
     using Cf = ConvCfg<KPAD, NPAD>;
     static_assert(Cf::SMEM <= kMaxSmem, "shared memory budget");
@@ -152,7 +113,7 @@ cudaError_t run_conv(const CUtensorMap &tm, const ConvDev &p, int grid, cudaStre
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    k_conv3x3_tc<KPAD, NPAD><<<grid, kConvThreads, Cf::SMEM, s>>>(tm, p);
+    k_conv3x3_tc<KPAD, NPAD><<<grid, kConvThreads, Cf::SMEM, s>>>(p);
     return cudaGetLastError();
 }
 
@@ -160,7 +121,7 @@ ConvFn find_fn(int kpad, int npad)
 {
 #define AJIB_K(KP, NP) \
     if (kpad == KP && npad == NP) return &run_conv<KP, NP>;
-#define AJIB_KN(KP) AJIB_K(KP, 16) AJIB_K(KP, 32) AJIB_K(KP, 48) AJIB_K(KP, 64)
+#define AJIB_KN(KP) AJIB_K(KP, 32) AJIB_K(KP, 64)
     AJIB_KN(16)
     AJIB_KN(32)
     AJIB_KN(48)
@@ -243,7 +204,7 @@ extern "C" int ajib_weights_upload(ajib_weights **out, const uint16_t *w, const 
     r->cin = cin;
     r->cout = cout;
     r->kpad = taps == 9 ? pad_k(cin) : (cin + 15) / 16 * 16;
-    r->npad = pad_n(cout);
+    r->npad = taps == 9 ? pad_n(cout) : (cout + 15) / 16 * 16;
     const std::vector<uint16_t> img = pack_b_image(w, taps, cin, cout, r->kpad, r->npad);
     std::vector<float> b(r->npad, 0.f), s(r->npad, 0.f);
     for (int i = 0; i < cout; i++) {
@@ -291,7 +252,7 @@ extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const v
     if (op->gate != AJIB_GATE_NONE && !resid) return AJIB_ERR_ARGS;
     if (row_end <= 0 || row_end > H) row_end = H;
     if (row_begin < 0 || row_begin >= row_end) return row_begin == row_end ? AJIB_OK : AJIB_ERR_ARGS;
-    // NHWC rows must start on 16-byte boundaries for the TMA loads and the vector stores
+    // row-chunked maps are read by bulk copies and written by 16-byte stores
     if (((uintptr_t)src & 15) || ((uintptr_t)dst & 15) || (resid && op->gate && ((uintptr_t)resid & 15)))
         return AJIB_ERR_ARGS;
 
@@ -320,18 +281,21 @@ extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const v
     }
     p.row_begin = row_begin;
     p.row_end = row_end;
-
-    CUtensorMap tm;
-    std::memset(&tm, 0, sizeof(tm));
-    if (op->in == AJIB_IN_NHWC) {
-        if (!make_row_map(&tm, src, H, W, op->cin, &p.tma_split)) return AJIB_ERR_CUDA;
-    }
+    p.pitch = feature_pitch(W);
     const long strips = (W + kTileM - 1) / kTileM;
     const long tiles = strips * (row_end - row_begin);
     const int grid = (int)std::min<long>(sm_count(), tiles);
     ConvFn fn = find_fn(op->w->kpad, op->w->npad);
-    const cudaError_t e = fn(tm, p, grid, (cudaStream_t)stream);
+    const cudaError_t e = fn(p, grid, (cudaStream_t)stream);
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+extern "C" int ajib_feature_pitch(int W) { return W > 0 ? feature_pitch(W) : 0; }
+
+extern "C" size_t ajib_feature_bytes(int H, int W, int C)
+{
+    if (H < 1 || W < 1 || C < 8 || C % 8) return 0;
+    return (size_t)H * (C / 8) * feature_pitch(W) * 16;
 }
 
 extern "C" int ajib_kernel_status(int clear)

@@ -2,23 +2,36 @@
  * conv_tc.cuh — the fused 3x3 convolution on Blackwell tensor cores (sm_100a), device code.
  *
  * Implicit GEMM with the output pixels as M: a tile is 128 consecutive pixels of one output row,
- * N is cout (padded to a multiple of 16), K is 9 taps x cin (padded to a multiple of 16). One
- * staged input row (130 pixels: the tile plus a one-pixel halo on each side) feeds every tap of
- * the three output rows it touches: for tap (ty, tx) the A operand is the staged row starting
- * tx pixels in, which is just a 16-byte-unit shift of the shared-memory descriptor's start
- * address, because the row is staged K-major without swizzle as [cin/8][130][8 fp16].
+ * K is 9 taps x cin (cin padded to a multiple of 16). One staged input row (130 pixels: the tile
+ * plus a one-pixel halo on each side) feeds every tap of the three output rows it touches. For
+ * horizontal tap dx the A operand is the staged row starting dx pixels in: a 16-byte shift of the
+ * shared-memory descriptor's start address, because the row is staged K-major without swizzle as
+ * [cin/8][130][8 fp16].
+ *
+ * The three vertical taps share that A, so one MMA computes all three at once: B stacks the
+ * weights of tap rows 0, 1, 2 along N (N = 3 x cout_pad, 192 for 64 channels), and the MMA's D
+ * is three adjacent accumulators — those of output rows r+1, r and r-1 for input row r. The
+ * accumulators live in a ring of TMEM slots in descending order (output j in slot S-1-(j mod S)),
+ * so those three outputs are adjacent slots; where the window wraps around the ring the MMA is
+ * split in two. A tensor-core MMA of N >= 128 runs at the full rate, while N = cout alone would
+ * be bound by the operand fetch (about 48 cycles for an N = 64 MMA against 32 of math). Each
+ * slot is zeroed by the epilogue after it reads it, so every MMA accumulates.
+ *
+ * Feature maps live in HBM as row-chunked, padded NHWC: element (y, x, c) of a C-channel map is
+ * at ((y * C/8 + c/8) * Wp + x + 1) * 8 + c % 8 (fp16), Wp = 128 * ceil(W / 128) + 2, with the
+ * pad columns (x = -1 and x >= W) zero. So the staged row's 8-channel chunk k is one contiguous
+ * 2080-byte run, fetched by one bulk copy (the TMA unit) with the zero padding already in place,
+ * and the epilogue's stores of one chunk for 32 consecutive pixels are one coalesced 512-byte
+ * write.
  *
  * A CTA is persistent on one SM and walks a contiguous run of (strip, row) tiles down a
- * 128-pixel-wide vertical strip, so each input row is fetched once and used by up to three
- * output rows (A is kept in the tensor core's collector buffer across those MMAs). Roles:
- *   warps 0-3  producer: one thread issues the TMA load of each input row (NHWC inputs), or all
- *              128 threads convert the NCHW RGB model input into the same layout;
+ * 128-pixel-wide vertical strip, so each input row is fetched once. Roles:
+ *   warps 0-3  producer: one thread issues the bulk copies of each input row (row-chunked
+ *              inputs), or all 128 threads convert the NCHW RGB model input into the same layout;
  *   warps 4-7  epilogue: TMEM -> registers (one pixel per thread), bias, activation, SPAN gate or
- *              depth-to-space with the model-input skip, fp16 store;
+ *              depth-to-space with the model-input skip, fp16 store; then zero the slot;
  *   warp 8     MMA issuer (one thread) and TMEM owner.
- * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime. Accumulators are
- * fp32 in TMEM: four 128 x NPAD slots, so three output rows accumulate while the epilogue drains
- * the fourth.
+ * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime.
  *
  * The semantics are those of the reference kernel k_conv3x3 (src/native/conv_kernels.cuh:100-350)
  * with fp32 accumulation and an fp32 epilogue instead of fp16 ones (one rounding to fp16 at the
@@ -32,11 +45,10 @@
 
 namespace ajib {
 
-constexpr int kTileM = 128;            // output pixels per tile (the MMA's M)
-constexpr int kHalo = kTileM + 2;      // staged input pixels per row
-constexpr int kAccSlots = 4;           // TMEM accumulators
-constexpr int kAccStride = 64;         // TMEM columns per accumulator slot
-constexpr int kConvThreads = 288;      // 9 warps
+constexpr int kTileM = 128;        // output pixels per tile (the MMA's M)
+constexpr int kHalo = kTileM + 2;  // staged input pixels per row
+constexpr int kTmemCols = 512;     // the whole TMEM: the accumulator ring
+constexpr int kConvThreads = 288;  // 9 warps
 constexpr int kMaxSmem = 227 * 1024;
 
 // error codes written to the status word (which wait timed out)
@@ -44,42 +56,44 @@ enum { kErrProdEmpty = 101, kErrMmaFull = 102, kErrMmaAccEmpty = 103, kErrEpiAcc
        kErrDrain = 106 };
 
 struct ConvDev {
-    const __half *src;    // NHWC [H][W][cin] or NCHW [3][H][W]
-    const __half *resid;  // gate: NHWC [H][W][cout]; depth-to-space: NCHW model input [3][H][W] or null
-    __half *dst;          // NHWC [H][W][cout] or NCHW [3][R*H][R*W]
+    const __half *src;    // row-chunked map [H][cin] or NCHW [3][H][W]
+    const __half *resid;  // gate: row-chunked [H][cout]; depth-to-space: NCHW model input [3][H][W] or null
+    __half *dst;          // row-chunked [H][cout] or NCHW [3][R*H][R*W]
     const unsigned char *wimg;  // packed B operand image, all taps
     const float *bias;    // NPAD floats
     const float *slope;   // NPAD floats or null
     int *err;             // status word
     int H, W, cin, cout;
-    int in_mode, act, gate, R;  // R = 0: NHWC output, else depth-to-space factor
+    int in_mode, act, gate, R;  // R = 0: row-chunked output, else depth-to-space factor
     int in_norm, out_clamp;
     float in_mean[3], in_scale[3];
     int row_begin, row_end;
-    int tma_split;        // 1: a 3-D tensor map, one TMA copy per 8-channel chunk
+    int pitch;            // Wp: padded pixels per chunk row of the row-chunked maps
 };
+
+// Padded pixels per chunk row of a row-chunked feature map of width W.
+__host__ __device__ constexpr int feature_pitch(int W) { return (W + kTileM - 1) / kTileM * kTileM + 2; }
 
 template <int KPAD, int NPAD>
 struct ConvCfg {
     static_assert(KPAD % 16 == 0 && NPAD % 16 == 0 && KPAD <= 64 && NPAD <= 64, "padded channel counts");
-    static constexpr int KC = KPAD / 8;     // 8-channel chunks per pixel
-    static constexpr int KS = KPAD / 16;    // MMA K steps per tap
-    static constexpr int NG = NPAD / 8;     // 8-row core-matrix groups of B
+    static constexpr int KC = KPAD / 8;       // 8-channel chunks per pixel
+    static constexpr int KS = KPAD / 16;      // MMA K steps per tap
+    static constexpr int NG = NPAD / 8;       // 8-row core-matrix groups of one tap's B
+    static constexpr int S = kTmemCols / NPAD;  // accumulator ring slots
     static constexpr int LBO_A = kHalo * 16;  // bytes between K chunks of a staged row
+    static constexpr int LBO_B = 3 * NG * 128;  // bytes between K chunks of a stacked-tap B
     static constexpr int SLOT = (KC * LBO_A + 1023) / 1024 * 1024;
     static constexpr int WBYTES = 9 * KPAD * NPAD * 2;
     static constexpr int AOFF = (WBYTES + 1023) / 1024 * 1024;
-    static constexpr int CC = NPAD / 8;                   // 16-byte chunks per output pixel (max)
-    static constexpr int SC = (CC % 2) ? CC : CC + 1;      // staging row stride in chunks (odd: no bank conflicts)
-    static constexpr int EPI_WARP = 32 * SC * 16;
-    static constexpr int FIXED = AOFF + 4 * EPI_WARP + 2 * 64 * 4 + 512 + 1024;
+    static constexpr int FIXED = AOFF + 2 * 64 * 4 + 1024 + 1024;
     static constexpr int NS_FIT = (kMaxSmem - FIXED) / SLOT;
     static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;
-    static_assert(NS >= 2, "at least double-buffered input rows");
-    static constexpr int EOFF = AOFF + NS * SLOT;
-    static constexpr int POFF = EOFF + 4 * EPI_WARP;   // bias[64], slope[64] floats
-    static constexpr int BOFF = POFF + 2 * 64 * 4;     // mbarriers
-    static constexpr int SMEM = BOFF + 512 + 1024;     // + alignment slack for the base
+    static_assert(NS >= 2 && S >= 4, "pipeline depth");
+    static constexpr int POFF = AOFF + NS * SLOT;  // bias[64], slope[64] floats
+    static constexpr int BOFF = POFF + 2 * 64 * 4;  // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar
+    static constexpr int SMEM = BOFF + 1024 + 1024;  // + alignment slack for the base
+    static_assert((2 * NS + 2 * S + 2) * 8 + 8 <= 1024, "barrier area");
 };
 
 // The run of tiles a CTA owns, split into per-strip segments. All roles walk the same sequence.
@@ -153,34 +167,57 @@ __device__ __forceinline__ void store_d2s(const float (&v)[NPAD], const ConvDev 
     }
 }
 
+// The ring slot of the j-th output row a CTA produces, and its mbarrier phase parity.
+template <int S>
+__device__ __forceinline__ int ring_slot(uint32_t j) { return S - 1 - (int)(j % S); }
+template <int S>
+__device__ __forceinline__ uint32_t ring_phase(uint32_t j) { return (j / S) & 1u; }
+
+// One staged row's MMAs: for every horizontal tap dx and K step kk, one MMA per piece (a run of
+// adjacent accumulators with consecutive tap rows). NP pieces, unrolled straight-line.
+template <int NP, int KS, int KC, int NG, int LBO_A>
+__device__ __forceinline__ void issue_row(uint64_t adesc0, uint64_t bdesc0, const uint32_t (&pd)[3],
+                                          const uint32_t (&pb)[3], const uint32_t (&pi)[3])
+{
+#pragma unroll
+    for (int dx = 0; dx < 3; dx++) {
+#pragma unroll
+        for (int kk = 0; kk < KS; kk++) {
+            const uint64_t ad = adesc0 + (uint64_t)((kk * 2 * LBO_A + dx * 16) >> 4);
+            const uint64_t bd = bdesc0 + (uint64_t)(((dx * KC + 2 * kk) * 3 * NG * 128) >> 4);
+#pragma unroll
+            for (int p = 0; p < NP; p++) dev::mma_f16(pd[p], ad, bd + pb[p], pi[p], 1u, 0);
+        }
+    }
+}
+
 template <int KPAD, int NPAD>
-__global__ void __launch_bounds__(kConvThreads, 1)
-    k_conv3x3_tc(const __grid_constant__ CUtensorMap tin, const __grid_constant__ ConvDev a)
+__global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ ConvDev a)
 {
     using C = ConvCfg<KPAD, NPAD>;
+    constexpr int S = C::S;
     extern __shared__ unsigned char smraw[];
-    // 1024-byte aligned base (TMA destinations and descriptor bases)
+    // 1024-byte aligned base (bulk-copy destinations and descriptor bases)
     unsigned char *sm = smraw + ((1024 - (dev::smem_u32(smraw) & 1023)) & 1023);
     const uint32_t sbase = dev::smem_u32(sm);
     const uint32_t wbase = sbase, abase = sbase + C::AOFF;
     float *sbias = reinterpret_cast<float *>(sm + C::POFF), *sslope = sbias + 64;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::BOFF);
-    // barrier indices
     const uint32_t full0 = dev::smem_u32(bars), empty0 = full0 + 8 * C::NS, accf0 = empty0 + 8 * C::NS,
-                   acce0 = accf0 + 8 * kAccSlots, wbar = acce0 + 8 * kAccSlots, dbar = wbar + 8;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * kAccSlots + 2);
+                   acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * S + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool tma_in = a.in_mode == 0;
+    const bool bulk_in = a.in_mode == 0;
     const int H = a.H, W = a.W;
 
     // ---- set-up
     if (tid == 0) {
         for (int s = 0; s < C::NS; s++) {
-            dev::mbar_init(full0 + 8 * s, tma_in ? 1 : 128);
+            dev::mbar_init(full0 + 8 * s, bulk_in ? 1 : 128);
             dev::mbar_init(empty0 + 8 * s, 1);
         }
-        for (int s = 0; s < kAccSlots; s++) {
+        for (int s = 0; s < S; s++) {
             dev::mbar_init(accf0 + 8 * s, 1);
             dev::mbar_init(acce0 + 8 * s, 4);
         }
@@ -188,11 +225,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         dev::mbar_init(dbar, 1);
         dev::fence_mbar_init();
     }
-    if (warp == 8) dev::tmem_alloc(dev::smem_u32(tslot), kAccSlots * kAccStride);
+    if (warp == 8) dev::tmem_alloc(dev::smem_u32(tslot), kTmemCols);
     // K chunks the producer never writes (channel padding) are zero for the kernel's lifetime
     {
-        const int written = tma_in ? a.cin / 8 : 1;
-        const int nz = (C::KC - written) * (kHalo * 16 / 16);
+        const int written = bulk_in ? a.cin / 8 : 1;
+        const int nz = (C::KC - written) * kHalo;
         for (int s = 0; s < C::NS; s++)
             for (int i = tid; i < nz; i += kConvThreads)
                 reinterpret_cast<uint4 *>(sm + C::AOFF + s * C::SLOT + written * C::LBO_A)[i] = make_uint4(0, 0, 0, 0);
@@ -209,12 +246,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
     if (warp < 4) {
         // ================= producer
-        if (tma_in) {
+        if (tid == 0) {
+            dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
+            dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
+        }
+        if (bulk_in) {
             if (tid == 0) {
-                dev::tma_prefetch_desc(&tin);
-                dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
-                dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
-                const uint32_t bytes = (uint32_t)(a.cin / 8) * kHalo * 16;
+                const int kcin = a.cin / 8;
+                const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
+                const size_t chunk_row = (size_t)a.pitch * 8;  // halves per chunk row
                 SegIter seg(W, a.row_begin, a.row_end);
                 uint32_t it = 0;
                 int strip, ya, yb;
@@ -226,12 +266,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
                         dev::mbar_arrive_expect_tx(full0 + 8 * s, bytes);
                         const uint32_t dst = abase + s * C::SLOT;
-                        if (!a.tma_split) {
-                            dev::tma_load_4d(dst, &tin, full0 + 8 * s, 0, x0 - 1, 0, r);
-                        } else {
-                            for (int kc = 0; kc < a.cin / 8; kc++)
-                                dev::tma_load_3d(dst + kc * C::LBO_A, &tin, full0 + 8 * s, kc * 8, x0 - 1, r);
-                        }
+                        // padded column x0 is pixel x0 - 1: the left halo
+                        const __half *row = a.src + (size_t)r * kcin * chunk_row + (size_t)x0 * 8;
+                        for (int kc = 0; kc < kcin; kc++)
+                            dev::bulk_load(dst + kc * C::LBO_A, row + kc * chunk_row, kHalo * 16, full0 + 8 * s);
                     }
                 }
                 // on an error exit, let the last copy land before the CTA can leave
@@ -242,10 +280,6 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
         } else {
             // NCHW RGB model input -> chunk 0 of the staged row: {r, g, b, 0, 0, 0, 0, 0} per pixel
-            if (tid == 0) {
-                dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
-                dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
-            }
             SegIter seg(W, a.row_begin, a.row_end);
             uint32_t it = 0;
             int strip, ya, yb;
@@ -283,8 +317,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     } else if (warp < 8) {
         // ================= epilogue
         const int q = warp & 3;
-        unsigned char *stage = sm + C::EOFF + q * C::EPI_WARP;
-        const int ccout = a.cout / 8;  // NHWC outputs: 16-byte chunks per pixel
+        const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        // every ring slot starts at zero; the MMA warp waits on named barrier 1 for this
+        for (int c = 0; c < S * NPAD; c += 16) dev::tmem_zero16(tmem + lanes + c);
+        dev::tmem_wait_st();
+        dev::tc_fence_before();
+        dev::named_bar_sync(1, 160);
+
+        const int ccout = a.cout / 8;  // row-chunked outputs: 16-byte chunks per pixel
         SegIter seg(W, a.row_begin, a.row_end);
         uint32_t ot = 0;
         int strip, ya, yb;
@@ -293,11 +333,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const int x0 = strip * kTileM;
             const int x = x0 + q * 32 + lane;
             for (int o = ya; o < yb; o++, ot++) {
-                const uint32_t slot = ot % kAccSlots, ph = (ot / kAccSlots) & 1;
-                if (!(ok = dev::mbar_wait(accf0 + 8 * slot, ph, a.err, kErrEpiAccFull))) break;
+                const int slot = ring_slot<S>(ot);
+                if (!(ok = dev::mbar_wait(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                __syncwarp();
                 dev::tc_fence_after();
                 float v[NPAD];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + slot * kAccStride;
+                const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
 #pragma unroll
                 for (int c = 0; c < NPAD / 16; c++) {
                     float t[16];
@@ -306,30 +347,47 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     for (int j = 0; j < 16; j++) v[c * 16 + j] = t[j];
                 }
                 dev::tmem_wait_ld();
+                // hand the slot back zeroed: the MMAs accumulate into it from scratch
+#pragma unroll
+                for (int c = 0; c < NPAD / 16; c++) dev::tmem_zero16(taddr + c * 16);
+                dev::tmem_wait_st();
                 dev::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
 
 #pragma unroll
-                for (int n = 0; n < NPAD; n++) v[n] += sbias[n];
+                for (int n = 0; n < NPAD; n += 4) {
+                    const float4 b4 = *reinterpret_cast<const float4 *>(sbias + n);
+                    v[n] += b4.x;
+                    v[n + 1] += b4.y;
+                    v[n + 2] += b4.z;
+                    v[n + 3] += b4.w;
+                }
                 if (a.R == 0) {
-                    // NHWC output (+ activation or gate)
+                    // row-chunked output (+ activation or gate)
                     if (a.act == 1) {
 #pragma unroll
                         for (int n = 0; n < NPAD; n++) v[n] = fmaxf(v[n], 0.f);
                     } else if (a.act == 2) {
 #pragma unroll
-                        for (int n = 0; n < NPAD; n++) v[n] = v[n] >= 0.f ? v[n] : v[n] * sslope[n];
+                        for (int n = 0; n < NPAD; n += 4) {
+                            const float4 s4 = *reinterpret_cast<const float4 *>(sslope + n);
+                            v[n] = v[n] >= 0.f ? v[n] : v[n] * s4.x;
+                            v[n + 1] = v[n + 1] >= 0.f ? v[n + 1] : v[n + 1] * s4.y;
+                            v[n + 2] = v[n + 2] >= 0.f ? v[n + 2] : v[n + 2] * s4.z;
+                            v[n + 3] = v[n + 3] >= 0.f ? v[n + 3] : v[n + 3] * s4.w;
+                        }
                     } else if (a.act == 3) {
 #pragma unroll
                         for (int n = 0; n < NPAD; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
                     }
+                    const size_t chunk_row = (size_t)a.pitch * 8;
                     if (a.gate != 0 && x < W) {
-                        const uint4 *xr = reinterpret_cast<const uint4 *>(a.resid + ((size_t)o * W + x) * a.cout);
+                        const __half *xr = a.resid + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
 #pragma unroll
                         for (int c = 0; c < NPAD / 8; c++) {
                             if (c < ccout) {
-                                const uint4 rv = __ldg(xr + c);
+                                const uint4 rv = __ldg(reinterpret_cast<const uint4 *>(xr + c * chunk_row));
                                 const __half2 *h = reinterpret_cast<const __half2 *>(&rv);
 #pragma unroll
                                 for (int j = 0; j < 4; j++) {
@@ -346,27 +404,21 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                             }
                         }
                     }
-                    // stage [32 px][SC chunks] then copy out coalesced
-                    uint4 *st = reinterpret_cast<uint4 *>(stage);
+                    // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
+                    if (x < W) {
+                        __half *drow = a.dst + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
 #pragma unroll
-                    for (int c = 0; c < NPAD / 8; c++) {
-                        if (c < ccout) {
-                            uint4 w4;
-                            w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
-                            w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
-                            w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
-                            w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
-                            st[lane * C::SC + c] = w4;
+                        for (int c = 0; c < NPAD / 8; c++) {
+                            if (c < ccout) {
+                                uint4 w4;
+                                w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
+                                w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
+                                w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
+                                w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
+                                *reinterpret_cast<uint4 *>(drow + c * chunk_row) = w4;
+                            }
                         }
                     }
-                    __syncwarp();
-                    const int xw = x0 + q * 32;
-                    uint4 *drow = reinterpret_cast<uint4 *>(a.dst + ((size_t)o * W + xw) * a.cout);
-                    for (int i = lane; i < 32 * ccout; i += 32) {
-                        const int p = i / ccout, c = i - p * ccout;
-                        if (xw + p < W) drow[i] = st[p * C::SC + c];
-                    }
-                    __syncwarp();
                 } else if (x < W) {
                     switch (a.R) {
                     case 1: store_d2s<1>(v, a, o, x); break;
@@ -379,50 +431,70 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
     } else {
         // ================= MMA issuer (warp 8)
+        dev::named_bar_sync(1, 160);
+        dev::tc_fence_after();
         if (lane == 0) {
-            constexpr uint32_t idesc = dev::idesc_f16_f32(kTileM, NPAD);
             bool ok = dev::mbar_wait(wbar, 0, a.err, kErrWeights);
             SegIter seg(W, a.row_begin, a.row_end);
             uint32_t it = 0, ot = 0;
             int strip, ya, yb;
+            // descriptor templates: the start address is the low 14 bits (16-byte units), so a byte
+            // offset d is added as d >> 4
+            const uint64_t bdesc0 = dev::sdesc(wbase, C::LBO_B, 128);
+            const uint64_t adesc_base = dev::sdesc(abase, C::LBO_A, 128);
             while (ok && seg.next(strip, ya, yb)) {
                 const int r0 = max(ya - 1, 0), r1 = min(yb, H - 1);
-                for (int r = r0; r <= r1 && ok; r++, it++) {
+                for (int r = r0; r <= r1; r++, it++) {
                     const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
                     if (!(ok = dev::mbar_wait(full0 + 8 * s, ph, a.err, kErrMmaFull))) break;
-                    const int olo = max(r - 1, ya), ohi = min(r + 1, yb - 1);
-                    // output rows whose first input row is r take a fresh accumulator
-                    for (int o = olo; o <= ohi && ok; o++) {
-                        if (max(o - 1, 0) == r) {
-                            const uint32_t j = ot + (uint32_t)(o - ya);
-                            ok = dev::mbar_wait(acce0 + 8 * (j % kAccSlots), ((j / kAccSlots) & 1) ^ 1, a.err,
-                                                kErrMmaAccEmpty);
-                        }
+                    // the outputs this row feeds: r+1 (tap row 0), r (1), r-1 (2), those in [ya, yb),
+                    // grouped into pieces: runs of adjacent ring slots, one MMA each
+                    bool v[3];
+                    int sl[3];
+#pragma unroll
+                    for (int ty = 0; ty < 3; ty++) {
+                        const int o = r + 1 - ty;
+                        v[ty] = o >= ya && o < yb;
+                        const uint32_t j = ot + (uint32_t)(o - ya);
+                        sl[ty] = ring_slot<S>(j);
+                        // an output's first input row is max(o - 1, 0): its slot must be free
+                        if (v[ty] && max(o - 1, 0) == r && ok)
+                            ok = dev::mbar_wait(acce0 + 8 * sl[ty], ring_phase<S>(j) ^ 1u, a.err, kErrMmaAccEmpty);
                     }
                     if (!ok) break;
-                    dev::tc_fence_after();
-                    const uint32_t arow = abase + s * C::SLOT;
-                    const int n = ohi - olo + 1;
-#pragma unroll 1
-                    for (int dx = 0; dx < 3; dx++) {
-#pragma unroll
-                        for (int kk = 0; kk < C::KS; kk++) {
-                            const uint64_t ad = dev::sdesc(arow + kk * 2 * C::LBO_A + dx * 16, C::LBO_A, 128);
-                            for (int i = 0; i < n; i++) {
-                                const int o = ohi - i, ty = r - o + 1, tap = ty * 3 + dx;
-                                const uint64_t bd =
-                                    dev::sdesc(wbase + (uint32_t)((tap * C::KC + 2 * kk) * C::NG) * 128, C::NG * 128, 128);
-                                const uint32_t j = ot + (uint32_t)(o - ya);
-                                const uint32_t d = tmem + (j % kAccSlots) * kAccStride;
-                                const bool first = (r == max(o - 1, 0)) && dx == 0 && kk == 0;
-                                const int cm = n == 1 ? 0 : (i == 0 ? 1 : (i == n - 1 ? 3 : 2));
-                                dev::mma_f16(d, ad, bd, idesc, first ? 0u : 1u, cm);
-                            }
-                        }
+                    const bool c01 = v[0] && v[1] && sl[1] == sl[0] + 1, c12 = v[1] && v[2] && sl[2] == sl[1] + 1;
+                    const bool st0 = v[0], st1 = v[1] && !c01, st2 = v[2] && !c12;
+                    const int len0 = 1 + (c01 ? 1 : 0) + ((c01 && c12) ? 1 : 0), len1 = 1 + (c12 ? 1 : 0);
+                    // the three candidate pieces (start slot, first tap row, length)
+                    const uint32_t D0 = tmem + (uint32_t)(sl[0] * NPAD), D1 = tmem + (uint32_t)(sl[1] * NPAD),
+                                   D2 = tmem + (uint32_t)(sl[2] * NPAD);
+                    constexpr uint32_t B1 = (uint32_t)(1 * C::NG * 128) >> 4, B2 = (uint32_t)(2 * C::NG * 128) >> 4;
+                    const uint32_t I0 = dev::idesc_f16_f32(kTileM, len0 * NPAD), I1 = dev::idesc_f16_f32(kTileM, len1 * NPAD),
+                                   I2 = dev::idesc_f16_f32(kTileM, NPAD);
+                    uint32_t pd[3] = {D0, D1, D2}, pb[3] = {0u, B1, B2}, pi[3] = {I0, I1, I2};
+                    const int mask = (st0 ? 1 : 0) | (st1 ? 2 : 0) | (st2 ? 4 : 0);
+                    int np = 3;
+                    switch (mask) {
+                    case 1: np = 1; break;
+                    case 2: pd[0] = D1; pb[0] = B1; pi[0] = I1; np = 1; break;
+                    case 3: np = 2; break;
+                    case 4: pd[0] = D2; pb[0] = B2; pi[0] = I2; np = 1; break;
+                    case 5: pd[1] = D2; pb[1] = B2; pi[1] = I2; np = 2; break;
+                    case 6: pd[0] = D1; pb[0] = B1; pi[0] = I1; pd[1] = D2; pb[1] = B2; pi[1] = I2; np = 2; break;
+                    default: break;
                     }
+                    dev::tc_fence_after();
+                    const uint64_t adesc0 = adesc_base + (uint64_t)((s * C::SLOT) >> 4);
+                    if (np == 1)
+                        issue_row<1, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
+                    else if (np == 2)
+                        issue_row<2, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
+                    else
+                        issue_row<3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
                     dev::mma_commit(empty0 + 8 * s);
-                    if (r - 1 >= ya && r - 1 < yb) dev::mma_commit(accf0 + 8 * ((ot + (uint32_t)(r - 1 - ya)) % kAccSlots));
-                    if (r == H - 1 && r >= ya && r < yb) dev::mma_commit(accf0 + 8 * ((ot + (uint32_t)(r - ya)) % kAccSlots));
+                    // outputs complete at their last input row min(o + 1, H - 1)
+                    if (r - 1 >= ya && r - 1 < yb) dev::mma_commit(accf0 + 8 * ring_slot<S>(ot + (uint32_t)(r - 1 - ya)));
+                    if (r == H - 1 && r >= ya && r < yb) dev::mma_commit(accf0 + 8 * ring_slot<S>(ot + (uint32_t)(r - ya)));
                 }
                 ot += (uint32_t)(yb - ya);
             }
@@ -437,7 +509,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     __syncthreads();
     if (warp == 8) {
         dev::tc_fence_after();
-        dev::tmem_dealloc(tmem, kAccSlots * kAccStride);
+        dev::tmem_dealloc(tmem, kTmemCols);
     }
 }
 

@@ -43,7 +43,6 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
     e->W_ = in_w;
     e->H_ = in_h;
     e->R_ = plan.depth_to_space;
-    const size_t px = (size_t)in_w * in_h;
 
     for (size_t i = 0; i < plan.steps.size(); i++) {
         const PlanStep &ps = plan.steps[i];
@@ -103,7 +102,7 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
     for (int i = 0; i < ns; i++) {
         const int d = plan.steps[i].dst;
         if (d >= 0 && buffer[d] < 0) {
-            const size_t need = px * plan.channels[d] * 2;
+            const size_t need = ajib_feature_bytes(in_h, in_w, plan.channels[d]);
             int b = -1;
             for (size_t k = 0; k < free_list.size(); k++)
                 if (free_list[k].first == need) {
@@ -119,11 +118,13 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
         }
         for (int t = 0; t < nt; t++)
             if (buffer[t] >= 0 && (last[t] == i || (last[t] < 0 && born[t] == i)))
-                free_list.push_back({px * plan.channels[t] * 2, buffer[t]});
+                free_list.push_back({ajib_feature_bytes(in_h, in_w, plan.channels[t]), buffer[t]});
     }
     for (size_t need : sizes) {
         void *b = nullptr;
-        if (cudaMalloc(&b, need) != cudaSuccess) {
+        // the pad columns of row-chunked maps must read as zero: clear once, kernels never write them
+        if (cudaMalloc(&b, need) != cudaSuccess || cudaMemset(b, 0, need) != cudaSuccess) {
+            cudaFree(b);
             cudaGetLastError();
             return fail("feature buffer allocation failed (" + std::to_string(need >> 20) + " MB)");
         }

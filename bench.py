@@ -343,6 +343,63 @@ def run_ours(args, rank, world, local_rank, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel(args):
+    """The dominant kernel alone: the body conv (64 -> 64 + PReLU) at --size, K launches timed with
+    CUDA events on the launching stream. --impl ours: this engine's tcgen05 kernel through
+    ajib_conv3x3_launch; --impl refgpu: the reference's k_conv3x3 (mma.sync, fp16 accumulation)
+    compiled for sm_100a from its own sources (oracle/_ref/libref_conv.so) with its own tile pick,
+    the GPU bar the new kernel is measured against."""
+    import torch
+    import ajib
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from util import conv_weights, to_f16_bits, to_rows
+    w_, h_ = (int(v) for v in args.size.split("x"))
+    hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, size=(h_, w_, 64)).astype(np.float16).astype(np.float32)
+    w, b, sl = conv_weights(rng, 64, 64, prelu=True)
+    s = torch.cuda.current_stream()
+    if args.impl == "refgpu":
+        ref = C.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_conv.so"))
+        ref.ref_conv_upload.restype = C.c_void_p
+        ref.ref_conv_upload.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]
+        ref.ref_conv_launch.argtypes = [C.c_void_p] + [C.c_int] * 6 + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p]
+        wb = to_f16_bits(w)
+        hw = ref.ref_conv_upload(wb.ctypes.data, b.ctypes.data, sl.ctypes.data, 64, 64, 64, 64)
+        src = torch.from_numpy(x.astype(np.float16)).cuda()
+        dst = torch.empty_like(src)
+
+        def launch():
+            return ref.ref_conv_launch(hw, 0, 2, 0, 0, 64, 64, src.data_ptr(), None, dst.data_ptr(), h_, w_, -1,
+                                       s.cuda_stream)
+        kname = "reference k_conv3x3<64,64,...,PReLU> (mma.sync m16n8k16 fp16-acc) recompiled for sm_100a"
+    else:
+        wt = ajib.Weights(to_f16_bits(w), b, sl)
+        op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
+        src = torch.from_numpy(to_rows(x).astype(np.float16)).cuda()
+        dst = torch.zeros_like(src)
+
+        def launch():
+            return ajib.conv3x3(op, src.data_ptr(), 0, dst.data_ptr(), h_, w_, 0, 0, s.cuda_stream)
+        kname = "k_conv3x3_tc<64,64> (tcgen05, fp32 TMEM accumulation)"
+    for _ in range(args.warmup):
+        assert launch() == 0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        assert launch() == 0
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 2.0 * 9 * 64 * 64 * w_ * h_
+    tf = flops / (ms / 1000.0) / 1e12
+    print(json.dumps({"kernel": kname, "impl": args.impl, "size": args.size, "ms_per_launch": ms, "tflops": tf,
+                      "frac_of_burst_peak": tf / tflops_burst, "peak_source": peak_src,
+                      "algorithmic_bytes": 2 * 2 * 64 * w_ * h_,
+                      "hbm_gbs_algorithmic": 2 * 2 * 64 * w_ * h_ / (ms / 1000.0) / 1e9}), flush=True)
+
+
 def plan_flops(plan):
     return sum(2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2] for s in plan["steps"]) * W_IN * H_IN
 
@@ -352,13 +409,19 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "refgpu"])
+    ap.add_argument("--kernel", default=None, choices=[None, "conv64"],
+                    help="time the dominant kernel alone instead of the whole frame")
+    ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -68,12 +68,21 @@ typedef struct ajib_conv {
  * receives the reason for a refusal. Returns 1 or 0. */
 AJIB_EXPORT int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_size);
 
+/* Feature maps (the NHWC tensors between steps) are stored row-chunked and padded: element
+ * (y, x, c) of a C-channel map (C a multiple of 8) is the fp16 at index
+ *   ((y * C/8 + c/8) * pitch + x + 1) * 8 + c % 8,   pitch = ajib_feature_pitch(W),
+ * and the pad columns (x = -1 and x >= W) must hold zeros (clear the buffer once; the kernels never
+ * write them). Each 8-channel chunk of a row is then one contiguous run the kernels copy in one
+ * piece. ajib_feature_bytes gives the buffer size. */
+AJIB_EXPORT int ajib_feature_pitch(int W);
+AJIB_EXPORT size_t ajib_feature_bytes(int H, int W, int C);
+
 /* Launch op at conv resolution H x W on output rows [row_begin, row_end) (row_end <= 0: all
- * rows) (reference src/native/conv.h:91, launch). src: NHWC [H][W][cin] or NCHW [3][H][W].
- * resid: gates read the block input x as NHWC [H][W][cout]; depth-to-space outputs add the NCHW
- * model input [3][H][W] (nearest upsampled) when resid is not NULL. dst: NHWC [H][W][cout] or
- * NCHW [3][R*H][R*W]. Rows outside the range are neither read beyond the one-row halo nor
- * written, so a frame can be run as bands. */
+ * rows) (reference src/native/conv.h:91, launch). src: a row-chunked map [H][cin] or the NCHW
+ * fp16 model input [3][H][W]. resid: gates read the block input x as a row-chunked map
+ * [H][cout]; depth-to-space outputs add the NCHW model input [3][H][W] (nearest upsampled) when
+ * resid is not NULL. dst: a row-chunked map [H][cout] or NCHW [3][R*H][R*W]. Rows outside the
+ * range are neither read beyond the one-row halo nor written, so a frame can be run as bands. */
 AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                     int row_begin, int row_end, void *stream);
 
@@ -118,6 +127,11 @@ AJIB_EXPORT int aji_run_post444(int format, int w, int h, const void *src_f16, c
 AJIB_EXPORT int aji_run_pre444(int w, int h, const void *y_plane, ptrdiff_t y_stride, const void *cb_plane,
                                ptrdiff_t cb_stride, const void *cr_plane, ptrdiff_t cr_stride, const aji_csp *csp,
                                void *dst_f16, void *stream);
+
+/* The filter table the plans upload, computed on the host alone (no device): zimg's
+ * compute_filter (reference src/resample.h:53-84) for src -> dst samples with the given shift.
+ * Returns taps; start [dst] and wt [dst][taps] are filled when both are not NULL. */
+AJIB_EXPORT int ajib_filter_table(int src, int dst, double shift, int filter, int *start, float *wt);
 
 /* The plan's filter tables as the host computed them (for tests): which = 0 horizontal, 1
  * vertical. Copies up to max_dst entries of start and max_dst * taps weights; returns taps. */

@@ -7,7 +7,7 @@ bounds (the reference's DevBuf pattern, native_conv_test.cu:49-76)."""
 import numpy as np
 import pytest
 
-from util import conv_weights, f16r, oracle_conv, to_f16_bits
+from util import conv_weights, f16r, from_rows, oracle_conv, rows_pad_mask, to_f16_bits, to_rows
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -17,15 +17,28 @@ GUARD_BITS = 0x7BAB  # an fp16 pattern no kernel writes
 
 
 def dev_f16(x):
+    """NCHW planes as they are (the model input)."""
     return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32).astype(np.float16)).cuda()
 
 
-class Guarded:
-    """A device fp16 buffer with GUARD elements of a fixed pattern on each side."""
+def dev_rows(x):
+    """An NHWC map in the engine's row-chunked layout (zero pad columns)."""
+    return torch.from_numpy(to_rows(x).astype(np.float16)).cuda()
 
-    def __init__(self, shape):
-        n = int(np.prod(shape))
+
+class Guarded:
+    """A device fp16 buffer with GUARD elements of a fixed pattern on each side. An NHWC shape
+    (H, W, C) is allocated row-chunked, its pad columns also holding the pattern: the kernels must
+    never write them."""
+
+    def __init__(self, shape, nhwc=False):
+        self.nhwc = nhwc
         self.shape = shape
+        if nhwc:
+            H, W, Cc = shape
+            n = H * (Cc // 8) * ((W + 127) // 128 * 128 + 2) * 8
+        else:
+            n = int(np.prod(shape))
         self.n = n
         self.t = torch.full((n + 2 * GUARD,), 0, dtype=torch.int16, device="cuda")
         self.t.fill_(GUARD_BITS)
@@ -35,12 +48,17 @@ class Guarded:
         h = self.t.cpu().numpy()
         assert (h[:GUARD] == GUARD_BITS).all(), "write before the output"
         assert (h[GUARD + self.n:] == GUARD_BITS).all(), "write past the output"
-        return h[GUARD:GUARD + self.n].view(np.float16).astype(np.float32).reshape(self.shape)
+        body = h[GUARD:GUARD + self.n]
+        if not self.nhwc:
+            return body.view(np.float16).astype(np.float32).reshape(self.shape)
+        H, W, Cc = self.shape
+        assert (body[rows_pad_mask(H, W, Cc).ravel()] == GUARD_BITS).all(), "write into a pad column"
+        return from_rows(body.view(np.float16).astype(np.float32), H, W, Cc)
 
 
 def run_conv(op, src, resid, dst_shape, H, W, rows=None):
     import ajib
-    dst = Guarded(dst_shape)
+    dst = Guarded(dst_shape, nhwc=op.out == ajib.OUT_NHWC)
     s = torch.cuda.current_stream().cuda_stream
     if rows is None:
         rc = ajib.conv3x3(op, src.data_ptr(), 0 if resid is None else resid.data_ptr(), dst.ptr, H, W, 0, 0, s)
@@ -73,7 +91,7 @@ def test_config0_conv64_prelu():
     want = oracle_conv(x, 0, H, W, 64, w, b, s, 64, act=2)
     wt = ajib.Weights(to_f16_bits(w), b, s)
     op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
-    got = run_conv(op, dev_f16(x), None, (H, W, 64), H, W)
+    got = run_conv(op, dev_rows(x), None, (H, W, 64), H, W)
     check_close(got, want)
 
 
@@ -89,7 +107,7 @@ def test_body(H, W, c, act):
     w, b, s = conv_weights(rng, c, c, prelu=act == 2)
     want = oracle_conv(x, 0, H, W, c, w, b, s, c, act=act)
     wt = ajib.Weights(to_f16_bits(w), b, s)
-    got = run_conv(ajib.conv_op(wt, act=act), dev_f16(x), None, (H, W, c), H, W)
+    got = run_conv(ajib.conv_op(wt, act=act), dev_rows(x), None, (H, W, c), H, W)
     check_close(got, want)
 
 
@@ -104,7 +122,7 @@ def test_gates(H, W, gate, c):
     w, b, _ = conv_weights(rng, c, c)
     want = oracle_conv(x, 0, H, W, c, w, b, None, c, gate=gate, resid=r)
     wt = ajib.Weights(to_f16_bits(w), b)
-    got = run_conv(ajib.conv_op(wt, gate=gate), dev_f16(x), dev_f16(r), (H, W, c), H, W)
+    got = run_conv(ajib.conv_op(wt, gate=gate), dev_rows(x), dev_rows(r), (H, W, c), H, W)
     check_close(got, want)
 
 
@@ -133,7 +151,7 @@ def test_tail_depth_to_space(H, W, cin, out, cout, skip):
     w, b, _ = conv_weights(rng, cin, cout)
     want = oracle_conv(x, 0, H, W, cin, w, b, None, cout, R=R, model_in=mi)
     wt = ajib.Weights(to_f16_bits(w), b)
-    got = run_conv(ajib.conv_op(wt, out=out), dev_f16(x), None if mi is None else dev_f16(mi), (3, R * H, R * W), H, W)
+    got = run_conv(ajib.conv_op(wt, out=out), dev_rows(x), None if mi is None else dev_f16(mi), (3, R * H, R * W), H, W)
     check_close(got, want)
 
 
@@ -146,7 +164,7 @@ def test_tail_clamp():
     w, b, _ = conv_weights(rng, 64, 12, std=0.2)
     want = oracle_conv(x, 0, H, W, 64, w, b, None, 12, R=2, model_in=mi, out_clamp=True)
     wt = ajib.Weights(to_f16_bits(w), b)
-    got = run_conv(ajib.conv_op(wt, out=ajib.OUT_D2S2, out_clamp=True), dev_f16(x), dev_f16(mi), (3, 2 * H, 2 * W), H, W)
+    got = run_conv(ajib.conv_op(wt, out=ajib.OUT_D2S2, out_clamp=True), dev_rows(x), dev_f16(mi), (3, 2 * H, 2 * W), H, W)
     assert got.min() >= 0 and got.max() <= 1
     check_close(got, want)
 
@@ -156,7 +174,7 @@ def test_bands_match_whole_frame():
     import ajib
     rng = np.random.default_rng(4)
     H, W = 45, 260
-    x = dev_f16(f16r(rng.uniform(-1, 1, size=(H, W, 64))))
+    x = dev_rows(f16r(rng.uniform(-1, 1, size=(H, W, 64))))
     w, b, s = conv_weights(rng, 64, 64, prelu=True)
     op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b, s), act=ajib.ACT_PRELU)
     whole = run_conv(op, x, None, (H, W, 64), H, W)

@@ -171,3 +171,30 @@ def yuv420_frame(rng, w, h, fmt, lo=None, hi=None):
         y = rng.integers(lo, hi + 1, size=(h, w)).astype(np.uint8)
         uv = rng.integers(lo, hi + 1, size=(h // 2, w)).astype(np.uint8)
     return y, uv
+
+
+# ---- row-chunked padded feature maps (the engine's layout for maps between steps) ----
+def feature_pitch(W):
+    return (W + 127) // 128 * 128 + 2
+
+
+def to_rows(x, pad_value=0.0):
+    """NHWC [H][W][C] -> row-chunked [H][C/8][pitch][8] with pad columns = pad_value."""
+    H, W, Cc = x.shape
+    KC, P = Cc // 8, feature_pitch(W)
+    out = np.full((H, KC, P, 8), pad_value, dtype=np.float32)
+    out[:, :, 1:W + 1, :] = np.asarray(x, np.float32).reshape(H, W, KC, 8).transpose(0, 2, 1, 3)
+    return out
+
+
+def from_rows(buf, H, W, Cc):
+    KC, P = Cc // 8, feature_pitch(W)
+    return np.asarray(buf).reshape(H, KC, P, 8)[:, :, 1:W + 1, :].transpose(0, 2, 1, 3).reshape(H, W, Cc)
+
+
+def rows_pad_mask(H, W, Cc):
+    """True at the pad columns of a row-chunked map."""
+    KC, P = Cc // 8, feature_pitch(W)
+    m = np.ones((H, KC, P, 8), bool)
+    m[:, :, 1:W + 1, :] = False
+    return m
