@@ -50,6 +50,9 @@ lib.ajib_conv_supported.argtypes = [C.POINTER(ConvOp), C.c_char_p, C.c_size_t]
 lib.ajib_conv_supported.restype = C.c_int
 lib.ajib_conv3x3_launch.argtypes = [C.POINTER(ConvOp), _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp]
 lib.ajib_conv3x3_launch.restype = C.c_int
+lib.ajib_conv3x3_launch_images.argtypes = [C.POINTER(ConvOp), _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                           _vp]
+lib.ajib_conv3x3_launch_images.restype = C.c_int
 lib.ajib_feature_pitch.argtypes = [C.c_int]
 lib.ajib_feature_pitch.restype = C.c_int
 lib.ajib_feature_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
@@ -128,6 +131,10 @@ def supported(op):
 
 def conv3x3(op, src, resid, dst, H, W, row_begin=0, row_end=0, stream=0):
     return lib.ajib_conv3x3_launch(C.byref(op), src, resid, dst, H, W, row_begin, row_end, stream)
+
+
+def conv3x3_images(op, src, resid, dst, nimg, img_h, W, row_begin=0, row_end=0, stream=0):
+    return lib.ajib_conv3x3_launch_images(C.byref(op), src, resid, dst, nimg, img_h, W, row_begin, row_end, stream)
 
 
 def kernel_status(clear=True):
@@ -473,3 +480,142 @@ def filter_table(src, dst, shift, filt=0):
     lib.ajib_filter_table(src, dst, shift, filt, start.ctypes.data_as(C.POINTER(C.c_int)),
                           wt.ctypes.data_as(C.POINTER(C.c_float)))
     return taps, start, wt.reshape(dst, taps)
+
+
+# ---------------------------------------------------------------------------------------------
+# the image ABI (include/aji_image.h) and the GPU tiler (aji_b200.h, ajib_tiler_*)
+
+AJI_IMAGE_API_VERSION = 1
+IMG_TENSORRT, IMG_DIRECTML, IMG_TENSORRT_RTX, IMG_VULKAN = 1, 2, 3, 4
+IMG_OK, IMG_ERR, IMG_ERR_ARGS, IMG_NOT_READY, IMG_CANCELLED, IMG_ERR_NO_MEM = 0, -1, -2, -3, -4, -5
+IMG_LOAD_EVEN_TILES = 2
+IMG_LOG_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_char_p)
+PROGRESS_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int)
+
+
+class ImgDevice(C.Structure):
+    _fields_ = [("id", C.c_uint64), ("name", C.c_char * 128), ("vram_bytes", C.c_uint64), ("sm_major", C.c_int),
+                ("sm_minor", C.c_int)]
+
+
+class ImgCreateParams(C.Structure):
+    _fields_ = [("api_version", C.c_uint32), ("backend", C.c_int), ("device_id", C.c_uint64), ("cache_dir", C.c_char_p),
+                ("trtexec", C.c_char_p), ("trtexec_env", C.c_char_p), ("log", IMG_LOG_FN), ("log_opaque", C.c_void_p)]
+
+
+class ImgModelParams(C.Structure):
+    _fields_ = [("onnx_path", C.c_char_p), ("tile_w", C.c_int), ("tile_h", C.c_int), ("overlap", C.c_int),
+                ("flags", C.c_int)]
+
+
+class ImgModelInfo(C.Structure):
+    _fields_ = [("scale", C.c_int), ("in_channels", C.c_int), ("out_channels", C.c_int), ("tile_w", C.c_int),
+                ("tile_h", C.c_int), ("overlap", C.c_int)]
+
+
+class ImgBuffer(C.Structure):
+    _fields_ = [("width", C.c_int), ("height", C.c_int), ("channels", C.c_int), ("stride", C.c_ssize_t),
+                ("data", C.c_void_p)]
+
+
+class ImgMemory(C.Structure):
+    _fields_ = [("device_free", C.c_uint64), ("device_total", C.c_uint64), ("ctx_activations", C.c_uint64),
+                ("ctx_scratch", C.c_uint64), ("model_weights", C.c_uint64), ("model_activations", C.c_uint64),
+                ("model_buffers", C.c_uint64), ("activations_shared", C.c_int)]
+
+
+lib.aji_img_enum_devices.argtypes = [C.c_int, C.POINTER(ImgDevice), C.c_int]
+lib.aji_img_enum_devices.restype = C.c_int
+lib.aji_img_create.argtypes = [C.POINTER(ImgCreateParams), C.c_char_p, C.c_size_t]
+lib.aji_img_create.restype = C.c_void_p
+lib.aji_img_load.argtypes = [_vp, C.POINTER(ImgModelParams)]
+lib.aji_img_load.restype = C.c_void_p
+lib.aji_img_model_state.argtypes = [_vp]
+lib.aji_img_model_state.restype = C.c_int
+lib.aji_img_model_info_get.argtypes = [_vp, C.POINTER(ImgModelInfo)]
+lib.aji_img_model_info_get.restype = C.c_int
+lib.aji_img_upscale.argtypes = [_vp, C.POINTER(ImgBuffer), C.POINTER(ImgBuffer), PROGRESS_FN, C.c_void_p]
+lib.aji_img_upscale.restype = C.c_int
+lib.aji_img_release.argtypes = [C.POINTER(_vp)]
+lib.aji_img_release.restype = None
+lib.aji_img_last_error.argtypes = [_vp]
+lib.aji_img_last_error.restype = C.c_char_p
+lib.aji_img_destroy.argtypes = [C.POINTER(_vp)]
+lib.aji_img_destroy.restype = None
+lib.aji_img_release_device.argtypes = [C.c_int, C.c_uint64]
+lib.aji_img_release_device.restype = C.c_int
+lib.aji_img_memory_get.argtypes = [_vp, _vp, C.POINTER(ImgMemory)]
+lib.aji_img_memory_get.restype = C.c_int
+lib.aji_img_native_probe.argtypes = [_vp, C.POINTER(ImgModelParams), C.POINTER(ImgMemory)]
+lib.aji_img_native_probe.restype = C.c_int
+lib.ajib_tiler_create.argtypes = [C.c_int] * 8 + [C.POINTER(_vp)]
+lib.ajib_tiler_create.restype = C.c_int
+lib.ajib_tiler_info.argtypes = [_vp] + [C.POINTER(C.c_int)] * 4
+lib.ajib_tiler_info.restype = C.c_int
+lib.ajib_tiler_extract.argtypes = [_vp, _vp, C.c_int, C.c_int, _vp, _vp]
+lib.ajib_tiler_extract.restype = C.c_int
+lib.ajib_tiler_compose.argtypes = [_vp, _vp, _vp, _vp]
+lib.ajib_tiler_compose.restype = C.c_int
+lib.ajib_tiler_release.argtypes = [C.POINTER(_vp)]
+lib.ajib_tiler_release.restype = None
+
+
+def img_buffer(arr):
+    """An aji_img_buffer over a uint8 numpy array [h][w][c] (kept alive by the caller)."""
+    h, w, c = arr.shape
+    b = ImgBuffer()
+    b.width, b.height, b.channels = w, h, c
+    b.stride = arr.strides[0]
+    b.data = arr.ctypes.data
+    return b
+
+
+class Image:
+    """An aji_img_ctx (CUDA backend) on device `device_id` (0 = first)."""
+
+    def __init__(self, device_id=0):
+        p = ImgCreateParams()
+        p.api_version = AJI_IMAGE_API_VERSION
+        p.backend = IMG_TENSORRT
+        p.device_id = device_id
+        err = C.create_string_buffer(512)
+        h = lib.aji_img_create(C.byref(p), err, 512)
+        if not h:
+            raise AjibError(f"aji_img_create: {err.value.decode()}")
+        self.handle = _vp(h)
+
+    def load(self, path, tile=512, overlap=0, flags=0):
+        mp = ImgModelParams()
+        mp.onnx_path = path.encode()
+        mp.tile_w = mp.tile_h = tile
+        mp.overlap = overlap
+        mp.flags = flags
+        m = lib.aji_img_load(self.handle, C.byref(mp))
+        if not m:
+            raise AjibError(f"aji_img_load: {self.error()}")
+        return _vp(m)
+
+    def upscale(self, model, img, scale, progress=None):
+        h, w, c = img.shape
+        img = np.ascontiguousarray(img)
+        out = np.zeros((h * scale, w * scale, c), np.uint8)
+        bi, bo = img_buffer(img), img_buffer(out)
+        cb = PROGRESS_FN(progress) if progress else PROGRESS_FN()
+        rc = lib.aji_img_upscale(model, C.byref(bi), C.byref(bo), cb, None)
+        return rc, out
+
+    def error(self):
+        return (lib.aji_img_last_error(self.handle) or b"").decode()
+
+    def close(self):
+        if self.handle:
+            lib.aji_img_destroy(C.byref(self.handle))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+import numpy as np  # noqa: E402  (used by the helpers above)

@@ -247,7 +247,15 @@ extern "C" int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_si
 extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                    int row_begin, int row_end, void *stream)
 {
+    return ajib_conv3x3_launch_images(op, src, resid, dst, 1, H, W, row_begin, row_end, stream);
+}
+
+extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, const void *resid, void *dst, int nimg,
+                                          int img_h, int W, int row_begin, int row_end, void *stream)
+{
     if (!check(op, nullptr, 0)) return AJIB_ERR_UNSUPPORTED;
+    if (nimg < 1 || img_h < 1 || (long)nimg * img_h > (1l << 30)) return AJIB_ERR_ARGS;
+    const int H = nimg * img_h;
     if (!src || !dst || H < 1 || W < 1) return AJIB_ERR_ARGS;
     if (op->gate != AJIB_GATE_NONE && !resid) return AJIB_ERR_ARGS;
     if (row_end <= 0 || row_end > H) row_end = H;
@@ -282,6 +290,7 @@ extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const v
     p.row_begin = row_begin;
     p.row_end = row_end;
     p.pitch = feature_pitch(W);
+    p.img_h = img_h;
     const long strips = (W + kTileM - 1) / kTileM;
     const long tiles = strips * (row_end - row_begin);
     const int grid = (int)std::min<long>(sm_count(), tiles);

@@ -69,7 +69,16 @@ struct ConvDev {
     float in_mean[3], in_scale[3];
     int row_begin, row_end;
     int pitch;            // Wp: padded pixels per chunk row of the row-chunked maps
+    int img_h;            // rows per image: H = n * img_h images stacked along H, convolved apart
 };
+
+// The input rows a segment of output rows [ya, yb) reads: one-row halos that stay inside the
+// image (a stack of images of img_h rows each).
+__device__ __forceinline__ void segment_rows(int ya, int yb, int img_h, int &r0, int &r1)
+{
+    r0 = (ya % img_h == 0) ? ya : ya - 1;
+    r1 = (yb % img_h == 0) ? yb - 1 : yb;
+}
 
 // Padded pixels per chunk row of a row-chunked feature map of width W.
 __host__ __device__ constexpr int feature_pitch(int W) { return (W + kTileM - 1) / kTileM * kTileM + 2; }
@@ -260,7 +269,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 int strip, ya, yb;
                 bool ok = true;
                 while (ok && seg.next(strip, ya, yb)) {
-                    const int x0 = strip * kTileM, r0 = max(ya - 1, 0), r1 = min(yb, H - 1);
+                    const int x0 = strip * kTileM;
+                    int r0, r1;
+                    segment_rows(ya, yb, a.img_h, r0, r1);
                     for (int r = r0; r <= r1; r++, it++) {
                         const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
                         if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
@@ -286,7 +297,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             bool ok = true;
             const size_t plane = (size_t)H * W;
             while (ok && seg.next(strip, ya, yb)) {
-                const int x0 = strip * kTileM, r0 = max(ya - 1, 0), r1 = min(yb, H - 1);
+                const int x0 = strip * kTileM;
+                int r0, r1;
+                segment_rows(ya, yb, a.img_h, r0, r1);
                 for (int r = r0; r <= r1; r++, it++) {
                     const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
                     if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
@@ -443,24 +456,29 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             const uint64_t bdesc0 = dev::sdesc(wbase, C::LBO_B, 128);
             const uint64_t adesc_base = dev::sdesc(abase, C::LBO_A, 128);
             while (ok && seg.next(strip, ya, yb)) {
-                const int r0 = max(ya - 1, 0), r1 = min(yb, H - 1);
+                int r0, r1;
+                segment_rows(ya, yb, a.img_h, r0, r1);
                 for (int r = r0; r <= r1; r++, it++) {
                     const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
                     if (!(ok = dev::mbar_wait(full0 + 8 * s, ph, a.err, kErrMmaFull))) break;
-                    // the outputs this row feeds: r+1 (tap row 0), r (1), r-1 (2), those in [ya, yb),
-                    // grouped into pieces: runs of adjacent ring slots, one MMA each
+                    // the outputs this row feeds: r+1 (tap row 0), r (1), r-1 (2), those in [ya, yb)
+                    // and in r's image, grouped into pieces: runs of adjacent ring slots, one MMA each
+                    const int first = r / a.img_h * a.img_h, last = first + a.img_h - 1;
                     bool v[3];
                     int sl[3];
+                    v[0] = r + 1 <= last && r + 1 >= ya && r + 1 < yb;
+                    v[1] = r >= ya && r < yb;
+                    v[2] = r - 1 >= first && r - 1 >= ya && r - 1 < yb;
 #pragma unroll
-                    for (int ty = 0; ty < 3; ty++) {
-                        const int o = r + 1 - ty;
-                        v[ty] = o >= ya && o < yb;
-                        const uint32_t j = ot + (uint32_t)(o - ya);
-                        sl[ty] = ring_slot<S>(j);
-                        // an output's first input row is max(o - 1, 0): its slot must be free
-                        if (v[ty] && max(o - 1, 0) == r && ok)
-                            ok = dev::mbar_wait(acce0 + 8 * sl[ty], ring_phase<S>(j) ^ 1u, a.err, kErrMmaAccEmpty);
-                    }
+                    for (int ty = 0; ty < 3; ty++) sl[ty] = ring_slot<S>(ot + (uint32_t)(r + 1 - ty - ya));
+                    // an output's first input row must find its slot free: r+1 always starts at r, and
+                    // r starts at r when r is its image's first row
+                    if (v[0] && ok)
+                        ok = dev::mbar_wait(acce0 + 8 * sl[0], ring_phase<S>(ot + (uint32_t)(r + 1 - ya)) ^ 1u, a.err,
+                                            kErrMmaAccEmpty);
+                    if (v[1] && r == first && ok)
+                        ok = dev::mbar_wait(acce0 + 8 * sl[1], ring_phase<S>(ot + (uint32_t)(r - ya)) ^ 1u, a.err,
+                                            kErrMmaAccEmpty);
                     if (!ok) break;
                     const bool c01 = v[0] && v[1] && sl[1] == sl[0] + 1, c12 = v[1] && v[2] && sl[2] == sl[1] + 1;
                     const bool st0 = v[0], st1 = v[1] && !c01, st2 = v[2] && !c12;
@@ -492,9 +510,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     else
                         issue_row<3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
                     dev::mma_commit(empty0 + 8 * s);
-                    // outputs complete at their last input row min(o + 1, H - 1)
-                    if (r - 1 >= ya && r - 1 < yb) dev::mma_commit(accf0 + 8 * ring_slot<S>(ot + (uint32_t)(r - 1 - ya)));
-                    if (r == H - 1 && r >= ya && r < yb) dev::mma_commit(accf0 + 8 * ring_slot<S>(ot + (uint32_t)(r - ya)));
+                    // outputs complete at their last input row: o + 1, or o at the image's last row
+                    if (v[2]) dev::mma_commit(accf0 + 8 * sl[2]);
+                    if (v[1] && r == last) dev::mma_commit(accf0 + 8 * sl[1]);
                 }
                 ot += (uint32_t)(yb - ya);
             }

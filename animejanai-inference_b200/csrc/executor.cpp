@@ -170,9 +170,12 @@ int Executor::profile_read(double *ms, int *counts, int nsteps) const
     return AJIB_OK;
 }
 
-int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
+int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const { return run_images(in, out, w, h, 1, s); }
+
+int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const
 {
-    if (w < 1 || h < 1 || w > W_ || h > H_ || !in || !out) return AJIB_ERR_ARGS;
+    const int h = img_h * nimg;
+    if (w < 1 || img_h < 1 || nimg < 1 || w > W_ || h > H_ || !in || !out) return AJIB_ERR_ARGS;
     const int ns = (int)steps_.size();
     // profiling brackets whole steps (all of a step's bands), so it runs unbanded
     const bool prof = prof_on_ && !prof_ev_.empty();
@@ -181,8 +184,8 @@ int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
         for (int k = 0; k < ns; k++) {
             const Step &st = steps_[k];
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2], s);
-            const int rc = ajib_conv3x3_launch(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
-                                               const_cast<void *>(ptr(st.dst, in, out)), h, w, 0, h, s);
+            const int rc = ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, 0, h, s);
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2 + 1], s);
             if (rc != AJIB_OK) return rc;
         }
@@ -199,8 +202,8 @@ int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
             const Step &st = steps_[k];
             int r0 = nb == 1 ? 0 : std::max(0, B0 - k), r1 = nb == 1 ? h : std::min(h, B1 - k);
             if (r0 >= r1) continue;
-            const int rc = ajib_conv3x3_launch(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
-                                               const_cast<void *>(ptr(st.dst, in, out)), h, w, r0, r1, s);
+            const int rc = ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, r0, r1, s);
             if (rc != AJIB_OK) return rc;
         }
     }

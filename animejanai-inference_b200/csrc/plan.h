@@ -90,6 +90,9 @@ public:
     // in: NCHW fp16 [3][h][w], out: NCHW fp16 [3][R*h][R*w]; w <= in_w(), h <= in_h().
     int run(const void *in, void *out, int w, int h, cudaStream_t s) const;
     int run(const void *in, void *out, cudaStream_t s) const { return run(in, out, W_, H_, s); }
+    // nimg images of img_h rows each, stacked along H (nimg * img_h <= in_h()), each convolved on
+    // its own: in [3][nimg * img_h][w], out [3][R * nimg * img_h][R * w].
+    int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const;
     // Step timing: while enabled, every launch is bracketed by CUDA events on its stream (a ring of
     // kProfRuns runs); profile_read synchronises and returns per-step summed milliseconds and
     // counts of the runs recorded since enabling.

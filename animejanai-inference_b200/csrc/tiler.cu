@@ -1,0 +1,129 @@
+// tiler.cu — device side of the image tiler (see tiler.h): batched tile extraction and the
+// gather composition of the blended 8-bit output.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "tiler.h"
+
+namespace ajib {
+namespace {
+
+__device__ __forceinline__ int d_reflect(int i, int n)
+{
+    if (n == 1) return 0;
+    const int period = 2 * (n - 1);
+    i %= period;
+    if (i < 0) i += period;
+    return i < n ? i : period - i;
+}
+
+// tile k0 + blockIdx.z: pixel (x, y) of the reflect-padded tile, as the net's fp16 input
+// v * (1/255) (the reference's k_extract, src/core/tiling_gpu.cu:71-96, 3-channel model)
+__global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *ox, const int *oy, int nx, int tw,
+                          int th, int k0, int n, float inv255, __half *dst)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, k = blockIdx.z;
+    if (x >= tw || y >= th) return;
+    const int t = k0 + k, i = t % nx, j = t / nx;
+    const uint8_t *p = img + ((size_t)d_reflect(oy[j] + y, H) * W + d_reflect(ox[i] + x, W)) * ci;
+    const size_t plane = (size_t)n * th * tw, at = ((size_t)k * th + y) * tw + x;
+    const int g = ci == 1;
+#pragma unroll
+    for (int c = 0; c < 3; c++) dst[c * plane + at] = __float2half_rn(__fmul_rn((float)p[g ? 0 : c], inv255));
+}
+
+// out[Y][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
+// multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134)
+__global__ void k_compose(const __half *tiles, int ntiles, int toh, int tow, int nx, const int *ox, const int *oy,
+                          const float *wx, const float *wy, int cols, int rows, const int2 *cx, const int2 *cy, int s,
+                          int co, int OW, int OH, uint8_t *out)
+{
+    const int X = blockIdx.x * blockDim.x + threadIdx.x, Y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (X >= OW || Y >= OH) return;
+    const int2 rx = cx[X], ry = cy[Y];
+    const size_t plane = (size_t)ntiles * toh * tow;
+    for (int c = 0; c < co; c++) {
+        float b = 0.0f;
+        for (int jj = 0; jj < ry.y; jj++) {
+            const int j = ry.x + jj, v = Y - oy[j] * s;
+            const float wv = wy[(size_t)j * rows + v];
+            for (int ii = 0; ii < rx.y; ii++) {
+                const int i = rx.x + ii, u = X - ox[i] * s, k = j * nx + i;
+                const float w = __fmul_rn(wv, wx[(size_t)i * cols + u]);
+                const float t = __half2float(tiles[(co == 1 ? 0 : c) * plane + ((size_t)k * toh + v) * tow + u]);
+                b = __fadd_rn(b, __fmul_rn(w, t));
+            }
+        }
+        const float f = __fadd_rn(__fmul_rn(b, 255.0f), 0.5f);
+        out[((size_t)Y * OW + X) * co + c] = f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
+    }
+}
+
+// per output coordinate along one axis: the first tile covering it and how many do
+std::vector<int2> cover(const std::vector<int> &org, int span, int s, int len)
+{
+    std::vector<int2> c((size_t)len * s);
+    for (int X = 0; X < len * s; X++) {
+        int first = -1, n = 0;
+        for (int t = 0; t < (int)org.size(); t++)
+            if (X >= org[t] * s && X < (org[t] + span) * s) {
+                if (first < 0) first = t;
+                n++;
+            }
+        c[X] = make_int2(first, n);
+    }
+    return c;
+}
+
+template <typename T>
+bool upload(T **d, const std::vector<T> &h, size_t *bytes)
+{
+    if (cudaMalloc(d, h.size() * sizeof(T)) != cudaSuccess) return false;
+    *bytes += h.size() * sizeof(T);
+    return cudaMemcpy(*d, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+}  // namespace
+
+DeviceTiler::~DeviceTiler()
+{
+    cudaFree(d_ox_);
+    cudaFree(d_oy_);
+    cudaFree(d_wx_);
+    cudaFree(d_wy_);
+    cudaFree(d_cx_);
+    cudaFree(d_cy_);
+}
+
+bool DeviceTiler::init(const TileGeometry &g)
+{
+    g_ = g;
+    const int s = g.scale;
+    const int spw = std::min(g.tw, g.W), sph = std::min(g.th, g.H);
+    return upload(&d_ox_, g.ox, &bytes_) && upload(&d_oy_, g.oy, &bytes_) &&
+           upload(&d_wx_, axis_weights(g.ox, g.W, g.tw, s), &bytes_) &&
+           upload(&d_wy_, axis_weights(g.oy, g.H, g.th, s), &bytes_) && upload(&d_cx_, cover(g.ox, spw, s, g.W), &bytes_) &&
+           upload(&d_cy_, cover(g.oy, sph, s, g.H), &bytes_);
+}
+
+cudaError_t DeviceTiler::extract(const uint8_t *img, int k0, int n, void *dst, cudaStream_t s) const
+{
+    if (n < 1) return cudaSuccess;
+    const dim3 block(32, 8), grid((g_.tw + 31) / 32, (g_.th + 7) / 8, n);
+    k_extract<<<grid, block, 0, s>>>(img, g_.W, g_.H, g_.ci, d_ox_, d_oy_, g_.nx(), g_.tw, g_.th, k0, n, 1.0f / 255.0f,
+                                     (__half *)dst);
+    return cudaGetLastError();
+}
+
+cudaError_t DeviceTiler::compose(const void *tiles, uint8_t *out, cudaStream_t st) const
+{
+    const int s = g_.scale, OW = g_.W * s, OH = g_.H * s;
+    const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
+    const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
+    k_compose<<<grid, block, 0, st>>>((const __half *)tiles, g_.count(), g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
+                                      d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, OH, out);
+    return cudaGetLastError();
+}
+
+}  // namespace ajib

@@ -86,6 +86,13 @@ AJIB_EXPORT size_t ajib_feature_bytes(int H, int W, int C);
 AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                     int row_begin, int row_end, void *stream);
 
+/* The same over nimg images of img_h rows stacked along H (H = nimg * img_h): each image is
+ * convolved on its own, zero-padded at its own top and bottom rows. One launch for a batch of
+ * equal-size tiles (the image tiler); no reference counterpart (the reference runs tiles one by
+ * one, src/aji_img_trt.cpp:980-1011). */
+AJIB_EXPORT int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, const void *resid, void *dst,
+                                           int nimg, int img_h, int W, int row_begin, int row_end, void *stream);
+
 /* ---- colour passes (reference src/kernels.h:12-78; same names, arguments and semantics) ----
  * Normalisation constants in raw container units (P010 samples are 10 bits in the high bits of
  * 16, so its scales include the << 6): y = (raw - yoff) / yscale, c = (raw - coff) / cscale. */
@@ -136,6 +143,24 @@ AJIB_EXPORT int ajib_filter_table(int src, int dst, double shift, int filter, in
 /* The plan's filter tables as the host computed them (for tests): which = 0 horizontal, 1
  * vertical. Copies up to max_dst entries of start and max_dst * taps weights; returns taps. */
 AJIB_EXPORT int ajib_plan_table(const aji_plan *p, int which, int *start, float *wt, int max_dst);
+
+/* ---- the image tiler on the GPU ----
+ * Geometry of the reference's cover (src/core/tiling.cpp:17-103: tile origins flush to the far
+ * edge or even tiles, reflect padding, linear blend ramps across a 16-pixel band at the centre of
+ * each overlap, normalised per axis), uploaded for one image shape. Replaces the reference's
+ * gpu_tile_extract / gpu_tile_blend / gpu_band_flush (src/core/tiling_gpu.h:49-67):
+ *  - extract cuts tiles [k0, k0 + n) (k = tile row * nx + tile column) of the device image
+ *    (W x H x ci, packed, 8-bit) into fp16 [3][n * th][tw] (tiles stacked along H), v / 255;
+ *  - compose blends the model outputs of all tiles, fp16 [3][nx * ny * th * S][tw * S], into the
+ *    8-bit output (H * S) x (W * S) x ci, bit-identical to blending each tile into an fp32 band
+ *    in tile order and flushing it. */
+typedef struct ajib_tiler ajib_tiler;
+AJIB_EXPORT int ajib_tiler_create(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, int even,
+                                  ajib_tiler **out);
+AJIB_EXPORT int ajib_tiler_info(const ajib_tiler *t, int *nx, int *ny, int *tw, int *th);
+AJIB_EXPORT int ajib_tiler_extract(ajib_tiler *t, const uint8_t *img, int k0, int n, void *dst, void *stream);
+AJIB_EXPORT int ajib_tiler_compose(ajib_tiler *t, const void *tiles, uint8_t *out, void *stream);
+AJIB_EXPORT void ajib_tiler_release(ajib_tiler **t);
 
 /* ---- the native model and its executor ----
  * A model is a plan of fused conv steps (reference src/native/lower.h:38-77, Plan), read from

@@ -62,6 +62,17 @@ int orc_post444(int format, int w, int h, const uint16_t *src, const float *csp,
 int orc_pre444(int w, int h, const uint16_t *yp, const uint16_t *cbp, const uint16_t *crp, const float *csp,
                uint16_t *dst);
 
+/* ---- the still-image tiler (src/core/tiling.cpp) ---- */
+int orc_tile_origins(int len, int tile, int overlap, int *out, int max);
+int orc_even_origins(int n, int max_tile, int overlap, int *tile, int *out, int max);
+int orc_reflect(int i, int n);
+/* w[t][u] for n tiles, u < min(tile, len) * scale */
+int orc_axis_weights(const int *org, int n, int len, int tile, int scale, float *w);
+/* upscale_tiled with the model as a callback (3-channel model): see oracle_tiling.c */
+int orc_upscale_tiled(int (*run)(void *opaque, const float *in, float *out), void *opaque, int tw, int th, int s,
+                      int overlap, int even, const uint8_t *in, int W, int H, int ci, ptrdiff_t in_stride,
+                      uint8_t *out, ptrdiff_t out_stride);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,7 +27,7 @@ if command -v "$NVCC" >/dev/null; then
     $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" \
         "$REF/src/kernels.cu" -o "$OUT/libref_kernels.so"
     $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/src/core" -I"$REF/include" \
-        "$REF/src/core/tiling_gpu.cu" -o "$OUT/libref_tiling_gpu.so"
+        "$HERE/reftiling_gpu_shim.cu" "$REF/src/core/tiling_gpu.cu" -o "$OUT/libref_tiling_gpu.so"
     $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" \
         "$HERE/refconv_shim.cu" "$REF/src/native/conv.cu" "$REF/src/native/pack.cpp" -o "$OUT/libref_conv.so"
 fi

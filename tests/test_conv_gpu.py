@@ -182,6 +182,47 @@ def test_bands_match_whole_frame():
     assert np.array_equal(whole, bands)
 
 
+@pytest.mark.parametrize("kind", ["body", "head", "tail"])
+def test_stacked_images(kind):
+    """Images stacked along H (the tiler's batches) convolve each on its own: equal to each image
+    convolved alone, whole and as row bands that cross image boundaries."""
+    import ajib
+    rng = np.random.default_rng(8)
+    n, h, W, c = 5, 7, 140, 48
+    s_ = torch.cuda.current_stream().cuda_stream
+    if kind == "head":
+        x = f16r(rng.uniform(0, 1, size=(3, n * h, W)))
+        w, b, sl = conv_weights(rng, 3, c, prelu=True)
+        op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b, sl), in_=ajib.IN_NCHW3, act=ajib.ACT_PRELU)
+        src, shape = dev_f16(x), (n * h, W, c)
+        want = np.concatenate([oracle_conv(np.ascontiguousarray(x[:, i * h:(i + 1) * h]), 1, h, W, 3, w, b, sl, c,
+                                           act=2) for i in range(n)])
+    elif kind == "body":
+        x = f16r(rng.uniform(-1, 1, size=(n * h, W, c)))
+        w, b, sl = conv_weights(rng, c, c, prelu=True)
+        op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b, sl), act=ajib.ACT_PRELU)
+        src, shape = dev_rows(x), (n * h, W, c)
+        want = np.concatenate([oracle_conv(x[i * h:(i + 1) * h], 0, h, W, c, w, b, sl, c, act=2) for i in range(n)])
+    else:
+        x = f16r(rng.uniform(-1, 1, size=(n * h, W, c)))
+        R = 4
+        w, b, _ = conv_weights(rng, c, 3 * R * R)
+        op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b), out=ajib.OUT_D2S4)
+        src, shape = dev_rows(x), (3, R * n * h, R * W)
+        want = np.concatenate([oracle_conv(x[i * h:(i + 1) * h], 0, h, W, c, w, b, None, 3 * R * R, R=R)
+                               for i in range(n)], axis=1)
+    outs = []
+    for bands in [[(0, 0)], [(0, 3), (3, 14), (14, 15), (15, n * h)]]:
+        dst = Guarded(shape, nhwc=op.out == ajib.OUT_NHWC)
+        for (a, b_) in bands:
+            assert ajib.conv3x3_images(op, src.data_ptr(), 0, dst.ptr, n, h, W, a, b_, s_) == 0
+        torch.cuda.synchronize()
+        assert ajib.kernel_status() == 0
+        outs.append(dst.value())
+    check_close(outs[0], want)
+    assert np.array_equal(outs[0], outs[1])
+
+
 def test_refusals():
     import ajib
     rng = np.random.default_rng(0)

@@ -24,6 +24,7 @@ REQUIRED_IMAGE = ["aji_img_enum_devices", "aji_img_create", "aji_img_load", "aji
 def declared(header):
     text = open(os.path.join(ROOT, "include", header)).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = "\n".join(line for line in text.splitlines() if not line.lstrip().startswith("#"))
     return re.findall(r"(?:AJI_EXPORT|AJI_IMG_EXPORT|AJIB_EXPORT)[^;(]*?\b(\w+)\s*\(", text)
 
 

@@ -198,3 +198,71 @@ def rows_pad_mask(H, W, Cc):
     m = np.ones((H, KC, P, 8), bool)
     m[:, :, 1:W + 1, :] = False
     return m
+
+
+# ---- tiler oracle (oracle/oracle_tiling.c) ----
+TILE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float))
+
+
+def _tiling_sigs():
+    o = oracle()
+    if getattr(o, "_tiling", False):
+        return o
+    ip = C.POINTER(C.c_int)
+    o.orc_tile_origins.argtypes = [C.c_int, C.c_int, C.c_int, ip, C.c_int]
+    o.orc_even_origins.argtypes = [C.c_int, C.c_int, C.c_int, ip, ip, C.c_int]
+    o.orc_reflect.argtypes = [C.c_int, C.c_int]
+    o.orc_axis_weights.argtypes = [ip, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
+    o.orc_upscale_tiled.argtypes = [TILE_FN, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                    C.c_int, C.c_int, C.c_int, C.c_ssize_t, C.c_void_p, C.c_ssize_t]
+    o._tiling = True
+    return o
+
+
+def oracle_origins(n, tile, overlap):
+    o = _tiling_sigs()
+    buf = (C.c_int * 4096)()
+    k = o.orc_tile_origins(n, tile, overlap, buf, 4096)
+    return np.array(buf[:k], np.int32)
+
+
+def oracle_even_origins(n, tile, overlap):
+    o = _tiling_sigs()
+    buf = (C.c_int * 4096)()
+    t = C.c_int()
+    k = o.orc_even_origins(n, tile, overlap, C.byref(t), buf, 4096)
+    return np.array(buf[:k], np.int32), t.value
+
+
+def oracle_axis_weights(org, n, tile, scale):
+    o = _tiling_sigs()
+    org = np.ascontiguousarray(org, np.int32)
+    span = min(tile, n)
+    w = np.zeros((len(org), span * scale), np.float32)
+    o.orc_axis_weights(org.ctypes.data_as(C.POINTER(C.c_int)), len(org), n, tile, scale,
+                       w.ctypes.data_as(C.POINTER(C.c_float)))
+    return w
+
+
+def oracle_upscale_tiled(model, tw, th, s, overlap, img, even=False):
+    """img: uint8 [h][w][c]; model(in [3][th][tw] float32) -> [3][th*s][tw*s] float32. With even,
+    tw / th are the largest tile and the tiles take the even-tile sides."""
+    o = _tiling_sigs()
+    h, w, c = img.shape
+    img = np.ascontiguousarray(img)
+    if even:
+        tw0, th0 = tw, th
+        tw = oracle_even_origins(w, tw0, overlap)[1]
+        th = oracle_even_origins(h, th0, overlap)[1]
+    out = np.zeros((h * s, w * s, c), np.uint8)
+
+    def run(_, pin, pout):
+        x = np.ctypeslib.as_array(pin, shape=(3, th, tw)).copy()
+        y = np.asarray(model(x), np.float32).reshape(3 * th * s * tw * s)
+        C.memmove(pout, y.ctypes.data, y.nbytes)
+        return 0
+    cb = TILE_FN(run)
+    rc = o.orc_upscale_tiled(cb, None, tw0 if even else tw, th0 if even else th, s, overlap, int(even), img.ctypes.data,
+                             w, h, c, w * c, out.ctypes.data, w * s * c)
+    assert rc == 0
+    return out
