@@ -97,7 +97,7 @@ namespace {
 
 using ConvFn = cudaError_t (*)(const ConvDev &, int grid, cudaStream_t);
 
-template <int KPAD, int NPAD>
+template <int KPAD, int NPAD, int EK, bool IN3>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
     using Cf = ConvCfg<KPAD, NPAD>;
@@ -109,27 +109,51 @@ cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done.load() & bit)) {
         const cudaError_t attr =
-            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD, EK, IN3>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    k_conv3x3_tc<KPAD, NPAD><<<grid, kConvThreads, Cf::SMEM, s>>>(p);
+    k_conv3x3_tc<KPAD, NPAD, EK, IN3><<<grid, kConvThreads, Cf::SMEM, s>>>(p);
     return cudaGetLastError();
 }
 
-ConvFn find_fn(int kpad, int npad)
+// The kernel instantiation for padded channel counts, epilogue kind and input mode. Built: every
+// K x N with the activation and depth-to-space epilogues; SPAN gates (cin == cout) at the four
+// K x N pairs that cin == cout gives; the NCHW RGB model input (K 16) with activation or
+// depth-to-space.
+ConvFn find_fn(int kpad, int npad, int ek, bool in3)
 {
-#define AJIB_K(KP, NP) \
-    if (kpad == KP && npad == NP) return &run_conv<KP, NP>;
-#define AJIB_KN(KP) AJIB_K(KP, 32) AJIB_K(KP, 64)
-    AJIB_KN(16)
-    AJIB_KN(32)
-    AJIB_KN(48)
-    AJIB_KN(64)
+#define AJIB_K(KP, NP, EK, IN3) \
+    if (kpad == KP && npad == NP && ek == EK && in3 == IN3) return &run_conv<KP, NP, EK, IN3>;
+#define AJIB_KN(KP, EK) AJIB_K(KP, 32, EK, false) AJIB_K(KP, 64, EK, false)
+    AJIB_KN(16, kEpiAct)
+    AJIB_KN(32, kEpiAct)
+    AJIB_KN(48, kEpiAct)
+    AJIB_KN(64, kEpiAct)
+    AJIB_KN(16, kEpiD2S)
+    AJIB_KN(32, kEpiD2S)
+    AJIB_KN(48, kEpiD2S)
+    AJIB_KN(64, kEpiD2S)
+    AJIB_K(16, 32, kEpiGate, false)
+    AJIB_K(32, 32, kEpiGate, false)
+    AJIB_K(48, 64, kEpiGate, false)
+    AJIB_K(64, 64, kEpiGate, false)
+    AJIB_K(16, 32, kEpiAct, true)
+    AJIB_K(16, 64, kEpiAct, true)
+    AJIB_K(16, 32, kEpiD2S, true)
+    AJIB_K(16, 64, kEpiD2S, true)
 #undef AJIB_KN
 #undef AJIB_K
     return nullptr;
 }
+
+int epi_kind(const ajib_conv *op)
+{
+    if (op->out != AJIB_OUT_NHWC) return kEpiD2S;
+    return op->gate != AJIB_GATE_NONE ? kEpiGate : kEpiAct;
+}
+
+ConvFn op_fn(const ajib_conv *op) { return find_fn(op->w->kpad, op->w->npad, epi_kind(op), op->in == AJIB_IN_NCHW3); }
 
 int d2s_factor(int out) { return out == 1 ? 2 : out == 2 ? 4 : out == 3 ? 1 : out == 4 ? 3 : 0; }
 
@@ -184,7 +208,7 @@ bool check(const ajib_conv *op, char *why, size_t n)
         if (op->gate == AJIB_GATE_TANH1X1) return fail(why, n, "the tanh 1x1 gate is not supported by this engine");
     }
     if (op->act == AJIB_ACT_PRELU && !op->w->slope) return fail(why, n, "PReLU without slopes");
-    if (!find_fn(op->w->kpad, op->w->npad)) return fail(why, n, "no kernel for these channel counts");
+    if (!op_fn(op)) return fail(why, n, "no kernel for these channel counts");
     return true;
 }
 
@@ -294,7 +318,7 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     const long strips = (W + kTileM - 1) / kTileM;
     const long tiles = strips * (row_end - row_begin);
     const int grid = (int)std::min<long>(sm_count(), tiles);
-    ConvFn fn = find_fn(op->w->kpad, op->w->npad);
+    ConvFn fn = op_fn(op);
     const cudaError_t e = fn(p, grid, (cudaStream_t)stream);
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
 }

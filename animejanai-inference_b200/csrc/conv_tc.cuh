@@ -26,11 +26,16 @@
  *
  * A CTA is persistent on one SM and walks a contiguous run of (strip, row) tiles down a
  * 128-pixel-wide vertical strip, so each input row is fetched once. Roles:
- *   warps 0-3  producer: one thread issues the bulk copies of each input row (row-chunked
- *              inputs), or all 128 threads convert the NCHW RGB model input into the same layout;
- *   warps 4-7  epilogue: TMEM -> registers (one pixel per thread), bias, activation, SPAN gate or
- *              depth-to-space with the model-input skip, fp16 store; then zero the slot;
- *   warp 8     MMA issuer (one thread) and TMEM owner.
+ *   warps 0-3   producer: one thread issues the bulk copies of each input row (row-chunked
+ *               inputs), or all 128 threads convert the NCHW RGB model input into the same layout;
+ *               it also waits for the accumulators a row starts to be free and writes the row's
+ *               MMA plan beside the staged row;
+ *   warps 4-11  epilogue: TMEM -> registers (one pixel per thread, half a slot's channels per
+ *               warp), bias, activation, SPAN gate or depth-to-space with the model-input skip,
+ *               fp16 store; then zero the half slot;
+ *   warp 12     MMA issuer (one thread) and TMEM owner. The tensor pipe queues only a few MMAs
+ *               and a lone thread's bookkeeping is slow, so this thread only waits for a staged
+ *               row, reads its plan and issues; the next row's wait sits between this row's MMAs.
  * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime.
  *
  * The semantics are those of the reference kernel k_conv3x3 (src/native/conv_kernels.cuh:100-350)
@@ -48,11 +53,19 @@ namespace ajib {
 constexpr int kTileM = 128;        // output pixels per tile (the MMA's M)
 constexpr int kHalo = kTileM + 2;  // staged input pixels per row
 constexpr int kTmemCols = 512;     // the whole TMEM: the accumulator ring
-constexpr int kConvThreads = 288;  // 9 warps
+constexpr int kProdWarps = 4;      // producer warps (all of them convert an NCHW model input)
+constexpr int kEpiWarps = 8;       // epilogue warps: two per TMEM lane quarter, one per half slot
+constexpr int kMmaWarp = kProdWarps + kEpiWarps;
+constexpr int kConvThreads = (kMmaWarp + 1) * 32;
 constexpr int kMaxSmem = 227 * 1024;
 
+// Epilogue kinds, one kernel instantiation each (so each layer runs only the code it needs):
+// row-chunked output with an activation; row-chunked output through a SPAN gate; depth-to-space
+// into NCHW (with the model-input skip).
+enum { kEpiAct = 0, kEpiGate = 1, kEpiD2S = 2 };
+
 // error codes written to the status word (which wait timed out)
-enum { kErrProdEmpty = 101, kErrMmaFull = 102, kErrMmaAccEmpty = 103, kErrEpiAccFull = 104, kErrWeights = 105,
+enum { kErrProdEmpty = 101, kErrMmaFull = 102, kErrProdAccEmpty = 103, kErrEpiAccFull = 104, kErrWeights = 105,
        kErrDrain = 106 };
 
 struct ConvDev {
@@ -95,14 +108,17 @@ struct ConvCfg {
     static constexpr int SLOT = (KC * LBO_A + 1023) / 1024 * 1024;
     static constexpr int WBYTES = 9 * KPAD * NPAD * 2;
     static constexpr int AOFF = (WBYTES + 1023) / 1024 * 1024;
+    static constexpr int RP = 2;                     // staged rows per pipeline stage
+    static constexpr int STAGE = RP * SLOT;
     static constexpr int FIXED = AOFF + 2 * 64 * 4 + 1024 + 1024;
-    static constexpr int NS_FIT = (kMaxSmem - FIXED) / SLOT;
-    static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;
+    static constexpr int NS_FIT = (kMaxSmem - FIXED) / STAGE;
+    static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;
     static_assert(NS >= 2 && S >= 4, "pipeline depth");
-    static constexpr int POFF = AOFF + NS * SLOT;  // bias[64], slope[64] floats
+    static constexpr int POFF = AOFF + NS * STAGE;  // bias[64], slope[64] floats
     static constexpr int BOFF = POFF + 2 * 64 * 4;  // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar
+    static constexpr int PLOFF = BOFF + 512;        // RowPlan per staged row
     static constexpr int SMEM = BOFF + 1024 + 1024;  // + alignment slack for the base
-    static_assert((2 * NS + 2 * S + 2) * 8 + 8 <= 1024, "barrier area");
+    static_assert((2 * NS + 2 * S + 2) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
 };
 
 // The run of tiles a CTA owns, split into per-strip segments. All roles walk the same sequence.
@@ -140,38 +156,148 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
 
 // Depth-to-space by R into NCHW [3][R*H][R*W] (PixelShuffle / DepthToSpace CRD: channel
 // c*R*R + ry*R + rx -> [c][R*y + ry][R*x + rx]), plus the nearest-upsampled model input when
-// given, optionally clamped to [0, 1]; one rounding to fp16.
-template <int R, int NPAD>
-__device__ __forceinline__ void store_d2s(const float (&v)[NPAD], const ConvDev &a, int o, int x)
+// given, optionally clamped to [0, 1]; one rounding to fp16. v holds channels [C0, C0 + CW): the
+// groups of R channels that lie wholly inside it are stored here.
+template <int R, int CW, int C0>
+__device__ __forceinline__ void store_d2s(const float (&v)[CW], const ConvDev &a, int o, int x, const float (&skip)[3])
 {
-    if constexpr (3 * R * R <= NPAD) {
-        const int W = a.W, H = a.H;
-        const size_t OW = (size_t)R * W, OH = (size_t)R * H;
+    const int W = a.W, H = a.H;
+    const size_t OW = (size_t)R * W, OH = (size_t)R * H;
 #pragma unroll
-        for (int c3 = 0; c3 < 3; c3++) {
-            const float add = a.resid ? __half2float(a.resid[((size_t)c3 * H + o) * W + x]) : 0.f;
+    for (int c3 = 0; c3 < 3; c3++) {
+        // skip the colour planes with no channel group inside [C0, C0 + CW)
+        if (c3 * R * R + R > C0 + CW || c3 * R * R + R * R <= C0) continue;
+        const float add = skip[c3];
 #pragma unroll
-            for (int ry = 0; ry < R; ry++) {
-                __half *d = a.dst + ((size_t)c3 * OH + (size_t)R * o + ry) * OW + (size_t)R * x;
-                float t[R];
+        for (int ry = 0; ry < R; ry++) {
+            const int n0 = c3 * R * R + ry * R - C0;
+            if (n0 < 0 || n0 + R > CW) continue;
+            __half *d = a.dst + ((size_t)c3 * OH + (size_t)R * o + ry) * OW + (size_t)R * x;
+            float t[R];
 #pragma unroll
-                for (int rx = 0; rx < R; rx++) {
-                    float val = v[c3 * R * R + ry * R + rx] + add;
-                    if (a.out_clamp) val = fminf(fmaxf(val, 0.f), 1.f);
-                    t[rx] = val;
-                }
-                if constexpr (R == 2) {
-                    *reinterpret_cast<uint32_t *>(d) = pack_h2(t[0], t[1]);
-                } else if constexpr (R == 4) {
-                    uint2 u;
-                    u.x = pack_h2(t[0], t[1]);
-                    u.y = pack_h2(t[2], t[3]);
-                    *reinterpret_cast<uint2 *>(d) = u;
-                } else {
+            for (int rx = 0; rx < R; rx++) {
+                float val = v[n0 + rx] + add;
+                if (a.out_clamp) val = fminf(fmaxf(val, 0.f), 1.f);
+                t[rx] = val;
+            }
+            if constexpr (R == 2) {
+                *reinterpret_cast<uint32_t *>(d) = pack_h2(t[0], t[1]);
+            } else if constexpr (R == 4) {
+                uint2 u;
+                u.x = pack_h2(t[0], t[1]);
+                u.y = pack_h2(t[2], t[3]);
+                *reinterpret_cast<uint2 *>(d) = u;
+            } else {
 #pragma unroll
-                    for (int rx = 0; rx < R; rx++) d[rx] = __float2half_rn(t[rx]);
+                for (int rx = 0; rx < R; rx++) d[rx] = __float2half_rn(t[rx]);
+            }
+        }
+    }
+}
+
+// The global inputs of one output row's epilogue, for pixel x and channels [C0, C0 + CW). They
+// are loaded before the wait for the accumulator, so their latency overlaps it.
+template <int CW>
+struct EpiIn {
+    float skip[3];       // depth-to-space: the model-input pixel (nearest-upsampled skip), or zeros
+    uint4 gate[CW / 8];  // SPAN gate: the block input's chunks of this half
+};
+
+template <int EK, int CW, int C0>
+__device__ __forceinline__ void epi_prefetch(EpiIn<CW> &in, const ConvDev &a, int o, int x)
+{
+    const int W = a.W, H = a.H;
+    if constexpr (EK == kEpiD2S) {
+#pragma unroll
+        for (int c3 = 0; c3 < 3; c3++)
+            in.skip[c3] = (a.resid && x < W) ? __half2float(__ldg(a.resid + ((size_t)c3 * H + o) * W + x)) : 0.f;
+    } else if constexpr (EK == kEpiGate) {
+        const int ccout = a.cout / 8;
+        const size_t chunk_row = (size_t)a.pitch * 8;
+        const __half *xr = a.resid + (size_t)o * ccout * chunk_row + (size_t)((x < W ? x : 0) + 1) * 8;
+#pragma unroll
+        for (int c = 0; c < CW / 8; c++)
+            in.gate[c] = (C0 / 8 + c < ccout) ? __ldg(reinterpret_cast<const uint4 *>(xr + (C0 / 8 + c) * chunk_row))
+                                              : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// The epilogue of one output row for pixel x and channels [C0, C0 + CW): bias, then activation
+// and SPAN gate into the row-chunked map, or depth-to-space into NCHW. (Staging the row in shared
+// memory for bulk stores measured slower than these coalesced 512-byte warp stores.)
+template <int EK, int CW, int C0>
+__device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, const float *sbias, const float *sslope,
+                                          int o, int x, const EpiIn<CW> &in)
+{
+    if (x >= a.W) return;
+#pragma unroll
+    for (int n = 0; n < CW; n += 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(sbias + C0 + n);
+        v[n] += b4.x;
+        v[n + 1] += b4.y;
+        v[n + 2] += b4.z;
+        v[n + 3] += b4.w;
+    }
+    if constexpr (EK == kEpiD2S) {
+        switch (a.R) {
+        case 1: store_d2s<1, CW, C0>(v, a, o, x, in.skip); break;
+        case 2: store_d2s<2, CW, C0>(v, a, o, x, in.skip); break;
+        case 3: store_d2s<3, CW, C0>(v, a, o, x, in.skip); break;
+        default: store_d2s<4, CW, C0>(v, a, o, x, in.skip); break;
+        }
+        return;
+    }
+    if constexpr (EK == kEpiAct) {
+    if (a.act == 1) {
+#pragma unroll
+        for (int n = 0; n < CW; n++) v[n] = fmaxf(v[n], 0.f);
+    } else if (a.act == 2) {
+#pragma unroll
+        for (int n = 0; n < CW; n += 4) {
+            const float4 s4 = *reinterpret_cast<const float4 *>(sslope + C0 + n);
+            v[n] = v[n] >= 0.f ? v[n] : v[n] * s4.x;
+            v[n + 1] = v[n + 1] >= 0.f ? v[n + 1] : v[n + 1] * s4.y;
+            v[n + 2] = v[n + 2] >= 0.f ? v[n + 2] : v[n + 2] * s4.z;
+            v[n + 3] = v[n + 3] >= 0.f ? v[n + 3] : v[n + 3] * s4.w;
+        }
+    } else if (a.act == 3) {
+#pragma unroll
+        for (int n = 0; n < CW; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
+    }
+    }
+    const int ccout = a.cout / 8;  // 16-byte chunks per pixel
+    const size_t chunk_row = (size_t)a.pitch * 8;
+    if constexpr (EK == kEpiGate) {
+#pragma unroll
+        for (int c = 0; c < CW / 8; c++) {
+            if (C0 / 8 + c < ccout) {
+                const __half2 *h = reinterpret_cast<const __half2 *>(&in.gate[c]);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float2 f = __half22float2(h[j]);
+                    const int n0 = c * 8 + 2 * j;
+                    if (a.gate == 1) {
+                        v[n0] = f.x + v[n0];
+                        v[n0 + 1] = f.y + v[n0 + 1];
+                    } else if (a.gate == 3) {
+                        v[n0] = (f.x + v[n0]) * (0.5f * dev::tanh_fast(0.5f * v[n0]));
+                        v[n0 + 1] = (f.y + v[n0 + 1]) * (0.5f * dev::tanh_fast(0.5f * v[n0 + 1]));
+                    }
                 }
             }
+        }
+    }
+    // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
+    __half *drow = a.dst + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
+#pragma unroll
+    for (int c = 0; c < CW / 8; c++) {
+        if (C0 / 8 + c < ccout) {
+            uint4 w4;
+            w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
+            w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
+            w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
+            w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
+            *reinterpret_cast<uint4 *>(drow + (C0 / 8 + c) * chunk_row) = w4;
         }
     }
 }
@@ -182,29 +308,141 @@ __device__ __forceinline__ int ring_slot(uint32_t j) { return S - 1 - (int)(j % 
 template <int S>
 __device__ __forceinline__ uint32_t ring_phase(uint32_t j) { return (j / S) & 1u; }
 
-// One staged row's MMAs: for every horizontal tap dx and K step kk, one MMA per piece (a run of
-// adjacent accumulators with consecutive tap rows). NP pieces, unrolled straight-line.
-template <int NP, int KS, int KC, int NG, int LBO_A>
-__device__ __forceinline__ void issue_row(uint64_t adesc0, uint64_t bdesc0, const uint32_t (&pd)[3],
-                                          const uint32_t (&pb)[3], const uint32_t (&pi)[3])
+// The input rows a CTA stages, in the order the producer and the MMA thread walk them: per
+// segment (strip, output rows [ya, yb)) its input rows r0..r1, with the first row of the image
+// that holds the current row.
+struct RowWalk {
+    SegIter seg;
+    int img_h;
+    int r = 0, r1 = -1, ya = 0, yb = 0, first = 0, strip = 0;
+    uint32_t ot = 0, ot_next = 0;  // output index of row ya; of the next segment's first row
+    __device__ RowWalk(int W, int row_begin, int row_end, int img_h_) : seg(W, row_begin, row_end), img_h(img_h_) {}
+    __device__ bool next()
+    {
+        if (r < r1) {
+            r++;
+            if (r - first == img_h) first = r;
+            return true;
+        }
+        int a_, b_;
+        if (!seg.next(strip, a_, b_)) return false;
+        ot = ot_next;
+        ot_next += (uint32_t)(b_ - a_);
+        ya = a_;
+        yb = b_;
+        int r0;
+        segment_rows(ya, yb, img_h, r0, r1);
+        r = r0;
+        first = r0 / img_h * img_h;
+        return true;
+    }
+};
+
+// What one staged row's MMAs do: up to three pieces (runs of adjacent accumulators, one MMA each
+// per tap column and K step) and the accumulator-full barriers the row completes. The producer
+// writes it into shared memory beside the staged row, so the MMA thread only reads it.
+struct RowPlan {
+    uint32_t pd[3], pb[3], pi[3];
+    uint32_t np;
+    uint32_t commit_a, commit_b;  // accumulator-full mbarrier addresses to commit after the row, or 0
+};
+static_assert(sizeof(RowPlan) == 48, "row plan layout");
+
+// The accumulator-free waits a row's plan depends on: up to two (mbarrier, parity) pairs.
+struct RowWaits {
+    bool w0 = false, w1 = false;
+    uint32_t bar0 = 0, par0 = 0, bar1 = 0, par1 = 0;
+    __device__ bool wait(int *err) const
+    {
+        bool ok = true;
+        if (w0) ok = dev::mbar_wait(bar0, par0, err, kErrProdAccEmpty);
+        if (w1 && ok) ok = dev::mbar_wait(bar1, par1, err, kErrProdAccEmpty);
+        return ok;
+    }
+};
+
+// The plan of the walk's current row, and the waits that must pass before its MMAs may run (the
+// accumulators the row starts must be free).
+template <int S, int NPAD, int NG>
+__device__ __forceinline__ void plan_row(const RowWalk &w, uint32_t tmem, uint32_t accf0, uint32_t acce0, RowPlan &p,
+                                         RowWaits &wt)
+{
+    const int r = w.r, ya = w.ya, yb = w.yb, first = w.first, last = first + w.img_h - 1;
+    // the outputs this row feeds: r+1 (tap row 0), r (1), r-1 (2), those in [ya, yb) and in r's
+    // image, grouped into pieces: runs of adjacent ring slots, one MMA each
+    const bool v0 = r + 1 <= last && r + 1 >= ya && r + 1 < yb, v1 = r >= ya && r < yb,
+               v2 = r - 1 >= first && r - 1 >= ya && r - 1 < yb;
+    const uint32_t j0 = w.ot + (uint32_t)(r + 1 - ya);
+    const int sl0 = ring_slot<S>(j0), sl1 = ring_slot<S>(j0 - 1u), sl2 = ring_slot<S>(j0 - 2u);
+    // an output's first input row must find its slot free: r+1 always starts at r, and r starts at
+    // r when r is its image's first row
+    wt.w0 = v0;
+    wt.bar0 = acce0 + 8 * sl0;
+    wt.par0 = ring_phase<S>(j0) ^ 1u;
+    wt.w1 = v1 && r == first;
+    wt.bar1 = acce0 + 8 * sl1;
+    wt.par1 = ring_phase<S>(j0 - 1u) ^ 1u;
+    const bool c01 = v0 && v1 && sl1 == sl0 + 1, c12 = v1 && v2 && sl2 == sl1 + 1;
+    const bool st0 = v0, st1 = v1 && !c01, st2 = v2 && !c12;
+    const int len0 = 1 + (c01 ? 1 : 0) + ((c01 && c12) ? 1 : 0), len1 = 1 + (c12 ? 1 : 0);
+    const uint32_t D0 = tmem + (uint32_t)(sl0 * NPAD), D1 = tmem + (uint32_t)(sl1 * NPAD), D2 = tmem + (uint32_t)(sl2 * NPAD);
+    constexpr uint32_t B1 = (uint32_t)(1 * NG * 128) >> 4, B2 = (uint32_t)(2 * NG * 128) >> 4;
+    const uint32_t I0 = dev::idesc_f16_f32(kTileM, len0 * NPAD), I1 = dev::idesc_f16_f32(kTileM, len1 * NPAD),
+                   I2 = dev::idesc_f16_f32(kTileM, NPAD);
+    p.pd[0] = D0; p.pb[0] = 0u; p.pi[0] = I0;
+    p.pd[1] = D1; p.pb[1] = B1; p.pi[1] = I1;
+    p.pd[2] = D2; p.pb[2] = B2; p.pi[2] = I2;
+    const int mask = (st0 ? 1 : 0) | (st1 ? 2 : 0) | (st2 ? 4 : 0);
+    // mask 7 (three pieces) would need two wraps in three adjacent slots: impossible for S >= 2;
+    // mask 5 (r+1 and r-1 without r) cannot occur either: a staged row outside [ya, yb) feeds
+    // only one output
+    static_assert(S >= 2, "ring");
+    p.np = 1;
+    switch (mask) {
+    case 1: break;
+    case 2: p.pd[0] = D1; p.pb[0] = B1; p.pi[0] = I1; break;
+    case 3: p.np = 2; break;
+    case 4: p.pd[0] = D2; p.pb[0] = B2; p.pi[0] = I2; break;
+    default: p.pd[0] = D1; p.pb[0] = B1; p.pi[0] = I1; p.pd[1] = D2; p.pb[1] = B2; p.pi[1] = I2; p.np = 2; break;
+    }
+    // outputs complete at their last input row: o + 1, or o at the image's last row
+    p.commit_a = v2 ? accf0 + 8 * sl2 : 0u;
+    p.commit_b = (v1 && r == last) ? accf0 + 8 * sl1 : 0u;
+}
+
+// One staged row's MMAs for tap columns [DX0, DX1): for each K step, one MMA per piece.
+template <int NP, int DX0, int DX1, int KS, int KC, int NG, int LBO_A>
+__device__ __forceinline__ void issue_taps(uint64_t adesc0, uint64_t bdesc0, const RowPlan &p)
 {
 #pragma unroll
-    for (int dx = 0; dx < 3; dx++) {
+    for (int dx = DX0; dx < DX1; dx++) {
 #pragma unroll
         for (int kk = 0; kk < KS; kk++) {
             const uint64_t ad = adesc0 + (uint64_t)((kk * 2 * LBO_A + dx * 16) >> 4);
             const uint64_t bd = bdesc0 + (uint64_t)(((dx * KC + 2 * kk) * 3 * NG * 128) >> 4);
 #pragma unroll
-            for (int p = 0; p < NP; p++) dev::mma_f16(pd[p], ad, bd + pb[p], pi[p], 1u, 0);
+            for (int q = 0; q < NP; q++) dev::mma_f16(p.pd[q], ad, bd + p.pb[q], p.pi[q], 1u, 0);
         }
     }
 }
 
-template <int KPAD, int NPAD>
+// A row's pieces are one or two: its (up to) three accumulators are adjacent ring slots except
+// across the ring's one wrap.
+template <int DX0, int DX1, int KS, int KC, int NG, int LBO_A>
+__device__ __forceinline__ void issue_plan(uint64_t adesc0, uint64_t bdesc0, const RowPlan &p)
+{
+    if (p.np == 1)
+        issue_taps<1, DX0, DX1, KS, KC, NG, LBO_A>(adesc0, bdesc0, p);
+    else
+        issue_taps<2, DX0, DX1, KS, KC, NG, LBO_A>(adesc0, bdesc0, p);
+}
+
+template <int KPAD, int NPAD, int EK, bool IN3>
 __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ ConvDev a)
 {
     using C = ConvCfg<KPAD, NPAD>;
     constexpr int S = C::S;
+    constexpr int HW = NPAD / 2;  // accumulator columns per epilogue warp (half a slot)
     extern __shared__ unsigned char smraw[];
     // 1024-byte aligned base (bulk-copy destinations and descriptor bases)
     unsigned char *sm = smraw + ((1024 - (dev::smem_u32(smraw) & 1023)) & 1023);
@@ -215,31 +453,32 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     const uint32_t full0 = dev::smem_u32(bars), empty0 = full0 + 8 * C::NS, accf0 = empty0 + 8 * C::NS,
                    acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * S + 2);
+    RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool bulk_in = a.in_mode == 0;
+    constexpr bool bulk_in = !IN3;  // row-chunked input by bulk copies, else the NCHW RGB model input
     const int H = a.H, W = a.W;
 
     // ---- set-up
     if (tid == 0) {
         for (int s = 0; s < C::NS; s++) {
-            dev::mbar_init(full0 + 8 * s, bulk_in ? 1 : 128);
+            dev::mbar_init(full0 + 8 * s, bulk_in ? 1 : kProdWarps * 32);
             dev::mbar_init(empty0 + 8 * s, 1);
         }
         for (int s = 0; s < S; s++) {
             dev::mbar_init(accf0 + 8 * s, 1);
-            dev::mbar_init(acce0 + 8 * s, 4);
+            dev::mbar_init(acce0 + 8 * s, kEpiWarps);
         }
         dev::mbar_init(wbar, 1);
         dev::mbar_init(dbar, 1);
         dev::fence_mbar_init();
     }
-    if (warp == 8) dev::tmem_alloc(dev::smem_u32(tslot), kTmemCols);
+    if (warp == kMmaWarp) dev::tmem_alloc(dev::smem_u32(tslot), kTmemCols);
     // K chunks the producer never writes (channel padding) are zero for the kernel's lifetime
     {
         const int written = bulk_in ? a.cin / 8 : 1;
         const int nz = (C::KC - written) * kHalo;
-        for (int s = 0; s < C::NS; s++)
+        for (int s = 0; s < C::NS * C::RP; s++)
             for (int i = tid; i < nz; i += kConvThreads)
                 reinterpret_cast<uint4 *>(sm + C::AOFF + s * C::SLOT + written * C::LBO_A)[i] = make_uint4(0, 0, 0, 0);
     }
@@ -253,67 +492,113 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     dev::tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp < 4) {
-        // ================= producer
+    if (warp < kProdWarps) {
+        // ================= producer: stages each input row and writes its MMA plan beside it,
+        // after waiting for the accumulators the row starts to be free
         if (tid == 0) {
             dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
             dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
         }
-        if (bulk_in) {
+        if constexpr (bulk_in) {
             if (tid == 0) {
                 const int kcin = a.cin / 8;
                 const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
                 const size_t chunk_row = (size_t)a.pitch * 8;  // halves per chunk row
-                SegIter seg(W, a.row_begin, a.row_end);
-                uint32_t it = 0;
-                int strip, ya, yb;
+                RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
+                uint32_t pi = 0;  // stage fills so far (pairs of rows)
                 bool ok = true;
-                while (ok && seg.next(strip, ya, yb)) {
-                    const int x0 = strip * kTileM;
-                    int r0, r1;
-                    segment_rows(ya, yb, a.img_h, r0, r1);
-                    for (int r = r0; r <= r1; r++, it++) {
-                        const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
-                        if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
-                        dev::mbar_arrive_expect_tx(full0 + 8 * s, bytes);
-                        const uint32_t dst = abase + s * C::SLOT;
+                while (ok && walk.next()) {
+                    const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                    if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
+                    // each row's copies go out once the accumulators it starts are free (issuing them
+                    // earlier, as soon as the stage is free, measured slower: more reads in flight
+                    // against the epilogue's writes)
+                    int h = 0;
+                    for (; h < C::RP; h++) {
+                        if (h > 0 && !walk.next()) break;
+                        RowWaits wt;
+                        RowPlan p;
+                        plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, p, wt);
+                        if (!(ok = wt.wait(a.err))) break;
+                        plans[s * C::RP + h] = p;
+                        dev::mbar_expect_tx(full0 + 8 * s, bytes);
+                        const uint32_t dst = abase + s * C::STAGE + h * C::SLOT;
                         // padded column x0 is pixel x0 - 1: the left halo
-                        const __half *row = a.src + (size_t)r * kcin * chunk_row + (size_t)x0 * 8;
+                        const __half *row = a.src + (size_t)walk.r * kcin * chunk_row + (size_t)walk.strip * kTileM * 8;
                         for (int kc = 0; kc < kcin; kc++)
                             dev::bulk_load(dst + kc * C::LBO_A, row + kc * chunk_row, kHalo * 16, full0 + 8 * s);
                     }
+                    // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
+                    // empty: the MMA thread skips rows whose plan has no pieces
+                    for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
+                    // one arrival per stage; it completes once the copies above have landed
+                    dev::mbar_arrive(full0 + 8 * s);
+                    pi++;
                 }
-                // on an error exit, let the last copy land before the CTA can leave
-                if (!ok && it > 0) {
-                    const uint32_t s = (it - 1) % C::NS, ph = ((it - 1) / C::NS) & 1;
+                // on an error exit, let the last copies land before the CTA can leave
+                if (!ok && pi > 0) {
+                    const uint32_t s = (pi - 1) % C::NS, ph = ((pi - 1) / C::NS) & 1;
                     dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
                 }
             }
         } else {
-            // NCHW RGB model input -> chunk 0 of the staged row: {r, g, b, 0, 0, 0, 0, 0} per pixel
-            SegIter seg(W, a.row_begin, a.row_end);
-            uint32_t it = 0;
-            int strip, ya, yb;
-            bool ok = true;
+            // NCHW RGB model input -> chunk 0 of the staged row: {r, g, b, 0, 0, 0, 0, 0} per pixel.
+            // Each thread holds pixels tid and tid + 128 of a row. Two stages' pixels are kept in
+            // registers, loaded one stage ahead of their use, so the load latency overlaps a
+            // whole stage of work.
+            RowWalk wl(W, a.row_begin, a.row_end, a.img_h), wp(W, a.row_begin, a.row_end, a.img_h);
             const size_t plane = (size_t)H * W;
-            while (ok && seg.next(strip, ya, yb)) {
-                const int x0 = strip * kTileM;
-                int r0, r1;
-                segment_rows(ya, yb, a.img_h, r0, r1);
-                for (int r = r0; r <= r1; r++, it++) {
-                    const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
-                    if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
-                    unsigned char *dst = sm + C::AOFF + s * C::SLOT;
-                    for (int p = tid; p < kHalo; p += 128) {
-                        const int x = x0 - 1 + p;
-                        float v[3] = {0.f, 0.f, 0.f};
-                        if (x >= 0 && x < W) {
-                            const __half *px = a.src + (size_t)r * W + x;
+            typedef __half StagePix[C::RP][2][3];
+            // the next stage's pixels (walk wl), as raw fp16; returns its row count
+            auto prefetch = [&](StagePix &pv) -> int {
+                int n = 0;
 #pragma unroll
-                            for (int c = 0; c < 3; c++) {
-                                v[c] = __half2float(px[c * plane]);
-                                if (a.in_norm) v[c] = __half2float(__float2half_rn((v[c] - a.in_mean[c]) * a.in_scale[c]));
-                            }
+                for (int h = 0; h < C::RP; h++) {
+                    if (n < h || !wl.next()) break;
+                    const int x0 = wl.strip * kTileM, r = wl.r;
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        const int p = tid + k * kProdWarps * 32, x = x0 - 1 + p;
+                        const bool in = p < kHalo && x >= 0 && x < W;
+                        const __half *px = a.src + (size_t)r * W + (in ? x : 0);
+#pragma unroll
+                        for (int c = 0; c < 3; c++) pv[h][k][c] = in ? __ldg(px + c * plane) : __float2half_rn(0.f);
+                    }
+                    n = h + 1;
+                }
+                return n;
+            };
+            uint32_t pi = 0;
+            bool ok = true;
+            // stage pi from pv (n rows, walk wp): its plans, its pixels, one arrival
+            auto fill = [&](const StagePix &pv, int n) {
+                const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) return;
+#pragma unroll
+                for (int h = 0; h < C::RP; h++) {
+                    if (h >= n) break;
+                    wp.next();
+                    if (tid == 0) {
+                        RowPlan p;
+                        RowWaits wt;
+                        plan_row<S, NPAD, C::NG>(wp, tmem, accf0, acce0, p, wt);
+                        ok = wt.wait(a.err) && ok;
+                        if (!ok) p.np = 0;
+                        plans[s * C::RP + h] = p;
+                    }
+                    unsigned char *dst = sm + C::AOFF + s * C::STAGE + h * C::SLOT;
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        const int p = tid + k * kProdWarps * 32;
+                        if (p >= kHalo) continue;
+                        // normalisation applies to image pixels; the zero padding stays zero
+                        const int x = wp.strip * kTileM - 1 + p;
+                        float v[3];
+#pragma unroll
+                        for (int c = 0; c < 3; c++) {
+                            v[c] = __half2float(pv[h][k][c]);
+                            if (a.in_norm && x >= 0 && x < W)
+                                v[c] = __half2float(__float2half_rn((v[c] - a.in_mean[c]) * a.in_scale[c]));
                         }
                         uint4 q;
                         q.x = pack_h2(v[0], v[1]);
@@ -322,22 +607,39 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         q.w = 0u;
                         reinterpret_cast<uint4 *>(dst)[p] = q;
                     }
-                    dev::fence_proxy_async();
-                    dev::mbar_arrive(full0 + 8 * s);
                 }
+                if (tid == 0)
+                    for (int e = n; e < C::RP; e++) plans[s * C::RP + e].np = 0;
+                dev::fence_proxy_async();
+                dev::mbar_arrive(full0 + 8 * s);
+                pi++;
+            };
+            StagePix pa, pb;
+            int na = prefetch(pa), nb = prefetch(pb);
+            while (ok && na > 0) {
+                fill(pa, na);
+                if (!ok || nb == 0) break;
+                na = prefetch(pa);
+                fill(pb, nb);
+                if (!ok) break;
+                nb = prefetch(pb);
             }
         }
-    } else if (warp < 8) {
-        // ================= epilogue
-        const int q = warp & 3;
+    } else if (warp < kMmaWarp) {
+        // ================= epilogue: warp (q, h) takes TMEM lanes 32q.. (pixels) and half h of
+        // each slot's columns; depth-to-space by 3 (groups of 3 channels across the halves) has
+        // half 0 take the whole slot
+        const int q = warp & 3, h = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        const bool whole = EK == kEpiD2S && a.R == 3;
         // every ring slot starts at zero; the MMA warp waits on named barrier 1 for this
-        for (int c = 0; c < S * NPAD; c += 16) dev::tmem_zero16(tmem + lanes + c);
+        for (int sl = 0; sl < S; sl++)
+#pragma unroll
+            for (int c = 0; c < HW; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + h * HW + c));
         dev::tmem_wait_st();
         dev::tc_fence_before();
-        dev::named_bar_sync(1, 160);
+        dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
 
-        const int ccout = a.cout / 8;  // row-chunked outputs: 16-byte chunks per pixel
         SegIter seg(W, a.row_begin, a.row_end);
         uint32_t ot = 0;
         int strip, ya, yb;
@@ -347,174 +649,126 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             const int x = x0 + q * 32 + lane;
             for (int o = ya; o < yb; o++, ot++) {
                 const int slot = ring_slot<S>(ot);
-                if (!(ok = dev::mbar_wait(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                EpiIn<HW> in;
+                EpiIn<NPAD> inw;
+                if (!whole) {
+                    if (h == 0)
+                        epi_prefetch<EK, HW, 0>(in, a, o, x);
+                    else
+                        epi_prefetch<EK, HW, HW>(in, a, o, x);
+                } else if (h == 0) {
+                    epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
+                }
+                if (!(ok = dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
                 __syncwarp();
                 dev::tc_fence_after();
-                float v[NPAD];
                 const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
+                if (!whole) {
+                    float v[HW];
 #pragma unroll
-                for (int c = 0; c < NPAD / 16; c++) {
-                    float t[16];
-                    dev::tmem_ld16(taddr + c * 16, t);
+                    for (int c = 0; c < HW; c += 16) {
+                        float t[16];
+                        dev::tmem_ld16(taddr + h * HW + c, t);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[c * 16 + j] = t[j];
-                }
-                dev::tmem_wait_ld();
-                // hand the slot back zeroed: the MMAs accumulate into it from scratch
-#pragma unroll
-                for (int c = 0; c < NPAD / 16; c++) dev::tmem_zero16(taddr + c * 16);
-                dev::tmem_wait_st();
-                dev::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
-
-#pragma unroll
-                for (int n = 0; n < NPAD; n += 4) {
-                    const float4 b4 = *reinterpret_cast<const float4 *>(sbias + n);
-                    v[n] += b4.x;
-                    v[n + 1] += b4.y;
-                    v[n + 2] += b4.z;
-                    v[n + 3] += b4.w;
-                }
-                if (a.R == 0) {
-                    // row-chunked output (+ activation or gate)
-                    if (a.act == 1) {
-#pragma unroll
-                        for (int n = 0; n < NPAD; n++) v[n] = fmaxf(v[n], 0.f);
-                    } else if (a.act == 2) {
-#pragma unroll
-                        for (int n = 0; n < NPAD; n += 4) {
-                            const float4 s4 = *reinterpret_cast<const float4 *>(sslope + n);
-                            v[n] = v[n] >= 0.f ? v[n] : v[n] * s4.x;
-                            v[n + 1] = v[n + 1] >= 0.f ? v[n + 1] : v[n + 1] * s4.y;
-                            v[n + 2] = v[n + 2] >= 0.f ? v[n + 2] : v[n + 2] * s4.z;
-                            v[n + 3] = v[n + 3] >= 0.f ? v[n + 3] : v[n + 3] * s4.w;
-                        }
-                    } else if (a.act == 3) {
-#pragma unroll
-                        for (int n = 0; n < NPAD; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
+                        for (int j = 0; j < 16; j++) v[c + j] = t[j];
                     }
-                    const size_t chunk_row = (size_t)a.pitch * 8;
-                    if (a.gate != 0 && x < W) {
-                        const __half *xr = a.resid + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
+                    dev::tmem_wait_ld();
+                    // hand the half slot back zeroed: the MMAs accumulate into it from scratch
 #pragma unroll
-                        for (int c = 0; c < NPAD / 8; c++) {
-                            if (c < ccout) {
-                                const uint4 rv = __ldg(reinterpret_cast<const uint4 *>(xr + c * chunk_row));
-                                const __half2 *h = reinterpret_cast<const __half2 *>(&rv);
+                    for (int c = 0; c < HW; c += 16) dev::tmem_zero16(taddr + h * HW + c);
+                    dev::tmem_wait_st();
+                    dev::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+                    if (h == 0)
+                        epi_store<EK, HW, 0>(v, a, sbias, sslope, o, x, in);
+                    else
+                        epi_store<EK, HW, HW>(v, a, sbias, sslope, o, x, in);
+                } else {
+                    // depth-to-space by 3 only comes with 27 output channels (NPAD 32)
+                    if constexpr (NPAD == 32 && EK == kEpiD2S) {
+                        float v[NPAD];
+                        if (h == 0) {
 #pragma unroll
-                                for (int j = 0; j < 4; j++) {
-                                    const float2 f = __half22float2(h[j]);
-                                    const int n0 = c * 8 + 2 * j;
-                                    if (a.gate == 1) {
-                                        v[n0] = f.x + v[n0];
-                                        v[n0 + 1] = f.y + v[n0 + 1];
-                                    } else if (a.gate == 3) {
-                                        v[n0] = (f.x + v[n0]) * (0.5f * dev::tanh_fast(0.5f * v[n0]));
-                                        v[n0 + 1] = (f.y + v[n0 + 1]) * (0.5f * dev::tanh_fast(0.5f * v[n0 + 1]));
-                                    }
-                                }
+                            for (int c = 0; c < NPAD; c += 16) {
+                                float t[16];
+                                dev::tmem_ld16(taddr + c, t);
+#pragma unroll
+                                for (int j = 0; j < 16; j++) v[c + j] = t[j];
                             }
-                        }
-                    }
-                    // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
-                    if (x < W) {
-                        __half *drow = a.dst + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
+                            dev::tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < NPAD / 8; c++) {
-                            if (c < ccout) {
-                                uint4 w4;
-                                w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
-                                w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
-                                w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
-                                w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
-                                *reinterpret_cast<uint4 *>(drow + c * chunk_row) = w4;
-                            }
+                            for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(taddr + c);
+                            dev::tmem_wait_st();
                         }
-                    }
-                } else if (x < W) {
-                    switch (a.R) {
-                    case 1: store_d2s<1>(v, a, o, x); break;
-                    case 2: store_d2s<2>(v, a, o, x); break;
-                    case 3: store_d2s<3>(v, a, o, x); break;
-                    default: store_d2s<4>(v, a, o, x); break;
+                        dev::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+                        if (h == 0) epi_store<EK, NPAD, 0>(v, a, sbias, sslope, o, x, inw);
+                    } else {
+                        __syncwarp();
+                        if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                     }
                 }
             }
         }
     } else {
-        // ================= MMA issuer (warp 8)
-        dev::named_bar_sync(1, 160);
+        // ================= MMA issuer (one thread). It takes a stage of RP rows per wait and
+        // commit, and waits for the next stage between the rows' MMAs.
+        dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
         dev::tc_fence_after();
         if (lane == 0) {
             bool ok = dev::mbar_wait(wbar, 0, a.err, kErrWeights);
-            SegIter seg(W, a.row_begin, a.row_end);
-            uint32_t it = 0, ot = 0;
-            int strip, ya, yb;
             // descriptor templates: the start address is the low 14 bits (16-byte units), so a byte
             // offset d is added as d >> 4
             const uint64_t bdesc0 = dev::sdesc(wbase, C::LBO_B, 128);
             const uint64_t adesc_base = dev::sdesc(abase, C::LBO_A, 128);
-            while (ok && seg.next(strip, ya, yb)) {
-                int r0, r1;
-                segment_rows(ya, yb, a.img_h, r0, r1);
-                for (int r = r0; r <= r1; r++, it++) {
-                    const uint32_t s = it % C::NS, ph = (it / C::NS) & 1;
-                    if (!(ok = dev::mbar_wait(full0 + 8 * s, ph, a.err, kErrMmaFull))) break;
-                    // the outputs this row feeds: r+1 (tap row 0), r (1), r-1 (2), those in [ya, yb)
-                    // and in r's image, grouped into pieces: runs of adjacent ring slots, one MMA each
-                    const int first = r / a.img_h * a.img_h, last = first + a.img_h - 1;
-                    bool v[3];
-                    int sl[3];
-                    v[0] = r + 1 <= last && r + 1 >= ya && r + 1 < yb;
-                    v[1] = r >= ya && r < yb;
-                    v[2] = r - 1 >= first && r - 1 >= ya && r - 1 < yb;
-#pragma unroll
-                    for (int ty = 0; ty < 3; ty++) sl[ty] = ring_slot<S>(ot + (uint32_t)(r + 1 - ty - ya));
-                    // an output's first input row must find its slot free: r+1 always starts at r, and
-                    // r starts at r when r is its image's first row
-                    if (v[0] && ok)
-                        ok = dev::mbar_wait(acce0 + 8 * sl[0], ring_phase<S>(ot + (uint32_t)(r + 1 - ya)) ^ 1u, a.err,
-                                            kErrMmaAccEmpty);
-                    if (v[1] && r == first && ok)
-                        ok = dev::mbar_wait(acce0 + 8 * sl[1], ring_phase<S>(ot + (uint32_t)(r - ya)) ^ 1u, a.err,
-                                            kErrMmaAccEmpty);
-                    if (!ok) break;
-                    const bool c01 = v[0] && v[1] && sl[1] == sl[0] + 1, c12 = v[1] && v[2] && sl[2] == sl[1] + 1;
-                    const bool st0 = v[0], st1 = v[1] && !c01, st2 = v[2] && !c12;
-                    const int len0 = 1 + (c01 ? 1 : 0) + ((c01 && c12) ? 1 : 0), len1 = 1 + (c12 ? 1 : 0);
-                    // the three candidate pieces (start slot, first tap row, length)
-                    const uint32_t D0 = tmem + (uint32_t)(sl[0] * NPAD), D1 = tmem + (uint32_t)(sl[1] * NPAD),
-                                   D2 = tmem + (uint32_t)(sl[2] * NPAD);
-                    constexpr uint32_t B1 = (uint32_t)(1 * C::NG * 128) >> 4, B2 = (uint32_t)(2 * C::NG * 128) >> 4;
-                    const uint32_t I0 = dev::idesc_f16_f32(kTileM, len0 * NPAD), I1 = dev::idesc_f16_f32(kTileM, len1 * NPAD),
-                                   I2 = dev::idesc_f16_f32(kTileM, NPAD);
-                    uint32_t pd[3] = {D0, D1, D2}, pb[3] = {0u, B1, B2}, pi[3] = {I0, I1, I2};
-                    const int mask = (st0 ? 1 : 0) | (st1 ? 2 : 0) | (st2 ? 4 : 0);
-                    int np = 3;
-                    switch (mask) {
-                    case 1: np = 1; break;
-                    case 2: pd[0] = D1; pb[0] = B1; pi[0] = I1; np = 1; break;
-                    case 3: np = 2; break;
-                    case 4: pd[0] = D2; pb[0] = B2; pi[0] = I2; np = 1; break;
-                    case 5: pd[1] = D2; pb[1] = B2; pi[1] = I2; np = 2; break;
-                    case 6: pd[0] = D1; pb[0] = B1; pi[0] = I1; pd[1] = D2; pb[1] = B2; pi[1] = I2; np = 2; break;
-                    default: break;
+            RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
+            // the rows of the next stage fill: up to RP rows of the walk
+            auto count = [&]() -> int {
+                int n = 0;
+                while (n < C::RP && walk.next()) n++;
+                return n;
+            };
+            // the pi-th stage fill: wait until it is full, then take its rows' plans
+            static_assert(C::RP == 2, "the loop below takes stages of two rows");
+            auto fetch = [&](uint32_t pi, RowPlan &p0, RowPlan &p1) -> bool {
+                const uint32_t s = pi % C::NS;
+                const bool good = dev::mbar_wait(full0 + 8 * s, (pi / C::NS) & 1, a.err, kErrMmaFull);
+                p0 = plans[s * C::RP];
+                p1 = plans[s * C::RP + 1];
+                dev::tc_fence_after();
+                return good;
+            };
+            RowPlan c0, c1, n0, n1;
+            uint32_t pi = 0;
+            int n = ok ? count() : 0;
+            if (n) ok = fetch(pi, c0, c1);
+            while (n && ok) {
+                const uint32_t s = pi % C::NS;
+                const uint64_t adesc0 = adesc_base + (uint64_t)((s * C::STAGE) >> 4);
+                int nn = 0;
+                bool okn = true;
+                // one copy of the row's MMA code for both rows; the next stage is fetched between them
+#pragma unroll 1
+                for (int h = 0; h < n; h++) {
+                    const RowPlan &p = h ? c1 : c0;
+                    if (p.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)((h * C::SLOT) >> 4), bdesc0, p);
+                    if (h == 0) {
+                        nn = count();
+                        if (nn) okn = fetch(pi + 1, n0, n1);
                     }
-                    dev::tc_fence_after();
-                    const uint64_t adesc0 = adesc_base + (uint64_t)((s * C::SLOT) >> 4);
-                    if (np == 1)
-                        issue_row<1, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
-                    else if (np == 2)
-                        issue_row<2, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
-                    else
-                        issue_row<3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, pd, pb, pi);
-                    dev::mma_commit(empty0 + 8 * s);
-                    // outputs complete at their last input row: o + 1, or o at the image's last row
-                    if (v[2]) dev::mma_commit(accf0 + 8 * sl[2]);
-                    if (v[1] && r == last) dev::mma_commit(accf0 + 8 * sl[1]);
                 }
-                ot += (uint32_t)(yb - ya);
+                dev::mma_commit(empty0 + 8 * s);
+                if (c0.np && c0.commit_a) dev::mma_commit(c0.commit_a);
+                if (c0.np && c0.commit_b) dev::mma_commit(c0.commit_b);
+                if (n > 1 && c1.np && c1.commit_a) dev::mma_commit(c1.commit_a);
+                if (n > 1 && c1.np && c1.commit_b) dev::mma_commit(c1.commit_b);
+                pi++;
+                n = nn;
+                ok = okn;
+                c0 = n0;
+                c1 = n1;
             }
             // every MMA issued has completed before TMEM can be released
             dev::mma_commit(dbar);
@@ -525,7 +779,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
 
     dev::tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == kMmaWarp) {
         dev::tc_fence_after();
         dev::tmem_dealloc(tmem, kTmemCols);
     }

@@ -43,6 +43,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
+// Raise the bytes the current phase waits for, without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
@@ -54,11 +59,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking test of the same condition (cheaper than try_wait when the phase is complete).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the phase of parity `parity` to complete. Gives up after ~2 s: writes `code` to *err
 // (first error wins) and returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code)
 {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -67,6 +84,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *er
             return false;
         }
     }
+}
+
+// mbar_wait by every lane of a warp, with one verdict for the whole warp (so that a wait giving
+// up at its deadline never splits the warp).
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int *err, int code)
+{
+    const bool ok = mbar_wait(bar, parity, err, code);
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---- TMA ---------------------------------------------------------------------------------------
