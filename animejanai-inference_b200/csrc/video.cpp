@@ -151,6 +151,14 @@ extern "C" aji_ctx *aji_create(const aji_create_params *params)
         CtxGuard g(c->cu);
         if (!g.ok) return nullptr;
         if (!c->owns_primary && d.ctx_get_device(&c->dev) != CUDA_SUCCESS) return nullptr;
+        // the kernels are built for sm_100a only: refuse any other device up front
+        int rdev = 0, major = 0;
+        if (cudaGetDevice(&rdev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, rdev) != cudaSuccess || major != 10) {
+            if (c->log) c->log(c->log_opaque, 2, "this engine runs on B200-class (sm_100) devices only");
+            if (c->owns_primary) d.primary_release(c->dev);
+            return nullptr;
+        }
         std::string why;
         if (!load_model_file(params->engine_path, &c->plan, &why)) {
             if (c->log) c->log(c->log_opaque, 2, why.c_str());

@@ -33,6 +33,9 @@ sys.path.insert(0, os.path.join(ROOT, "animejanai-inference_b200"))
 W_IN, H_IN, SCALE = 1920, 1080, 2
 MODEL_SEED = 1
 METRIC = "frames/s 1080p->4K 2x Compact fp16 at 1/2/4/8 B200; % tensor-core peak"
+# DRAM bytes (read + write) of one body-conv launch at 1920x1080, from the ncu capture summarised
+# in profiles/conv3x3_body_64x64_1080p.txt (the roofline's "traffic")
+BODY_TRAFFIC_BYTES = 498.3e6
 
 
 def value_noise(rng, h, w, lo, hi, cell=32):
@@ -160,7 +163,7 @@ def run_reference(args, rank, world):
             vals.append(fps)
         info = (cores, kind, sample)
     v = float(np.mean(vals))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": 0, "steps": args.steps,
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "BASELINE config 1 (Compact 2x 1080p P010 -> 4K), CPU reference net on a band sample",
@@ -318,7 +321,7 @@ def run_ours(args, rank, world, local_rank, dist):
     if body_ms:
         achieved = flops_body / (body_ms / 1000.0) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_sus, "unit": "TFLOP/s",
-                "frac": achieved / tflops_sus, "traffic": None,
+                "frac": achieved / tflops_sus, "traffic": BODY_TRAFFIC_BYTES,
                 "kernel": "k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)",
                 "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json)",
                 "flops_per_launch": flops_body,
