@@ -3,8 +3,11 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
+#include <mutex>
 
 #include "tiler.h"
+#include "../../include/aji_b200.h"
 
 namespace ajib {
 namespace {
@@ -127,3 +130,84 @@ cudaError_t DeviceTiler::compose(const void *tiles, uint8_t *out, cudaStream_t s
 }
 
 }  // namespace ajib
+
+// ---------------------------------------------------------------------------------------------
+// Composition that allocates no device memory (ajib_tiler_compose_static, include/aji_b200.h).
+//
+// For callers that may not call cudaMalloc: a host application whose device memory all comes
+// from its own allocator or budget, or a real-time frame path where cudaMalloc / cudaFree would
+// synchronise the device. The geometry tables that ajib_tiler_create keeps in memory it
+// allocates live here in one fixed area that every GPU loading this library holds until the
+// process exits. Each call rewrites every table byte it reads, so nothing has to start at zero;
+// but all calls on a device share the area, so calls that overlap on the GPU race.
+
+namespace ajib {
+namespace {
+
+constexpr size_t kStaticTableBytes = 1u << 20;  // 1 MiB: outputs up to about 24K x 24K pixels
+static __device__ __align__(256) unsigned char g_tiler_tables[kStaticTableBytes];
+
+// The area's device address on the current device. In host code g_tiler_tables names a host-side
+// stand-in, not the device memory, so the address comes from cudaGetSymbolAddress: once per
+// device, on the first call made with that device current.
+void *static_tables()
+{
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_tiler_tables) != cudaSuccess) return nullptr;
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+template <typename T>
+size_t put(std::vector<unsigned char> &buf, const std::vector<T> &v)
+{
+    const size_t at = buf.size();
+    buf.resize(align256(at + v.size() * sizeof(T)));
+    std::memcpy(buf.data() + at, v.data(), v.size() * sizeof(T));
+    return at;
+}
+
+}  // namespace
+
+}  // namespace ajib
+
+extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, int even,
+                                         const void *tiles, uint8_t *out, void *stream)
+{
+    using namespace ajib;
+    if (!tiles || !out || W < 1 || H < 1 || (ci != 1 && ci != 3) || scale < 1 || tile_w < 1 || tile_h < 1 || overlap < 0)
+        return AJIB_ERR_ARGS;
+    try {
+        const TileGeometry g = make_geometry(W, H, ci, scale, tile_w, tile_h, overlap, even != 0);
+        const int s = g.scale, spw = std::min(g.tw, g.W), sph = std::min(g.th, g.H);
+        // the tables of DeviceTiler::init, packed at 256-byte offsets into one host image
+        std::vector<unsigned char> img;
+        const size_t o_ox = put(img, g.ox), o_oy = put(img, g.oy);
+        const size_t o_wx = put(img, axis_weights(g.ox, g.W, g.tw, s)), o_wy = put(img, axis_weights(g.oy, g.H, g.th, s));
+        const size_t o_cx = put(img, cover(g.ox, spw, s, g.W)), o_cy = put(img, cover(g.oy, sph, s, g.H));
+        if (img.size() > kStaticTableBytes) return AJIB_ERR_UNSUPPORTED;  // tables beyond the fixed area
+        unsigned char *base = static_cast<unsigned char *>(static_tables());
+        if (!base) return AJIB_ERR_CUDA;
+        const cudaStream_t st = (cudaStream_t)stream;
+        // from pageable host memory: returns once the bytes are staged, so img may go
+        if (cudaMemcpyAsync(base, img.data(), img.size(), cudaMemcpyHostToDevice, st) != cudaSuccess) return AJIB_ERR_CUDA;
+        const int OW = g.W * s, OH = g.H * s;
+        const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
+        k_compose<<<grid, block, 0, st>>>((const __half *)tiles, g.count(), g.th * s, g.tw * s, g.nx(),
+                                          (const int *)(base + o_ox), (const int *)(base + o_oy),
+                                          (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
+                                          (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, OH, out);
+        return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+    } catch (...) {
+        return AJIB_ERR_NO_MEM;
+    }
+}

@@ -162,6 +162,23 @@ AJIB_EXPORT int ajib_tiler_extract(ajib_tiler *t, const uint8_t *img, int k0, in
 AJIB_EXPORT int ajib_tiler_compose(ajib_tiler *t, const void *tiles, uint8_t *out, void *stream);
 AJIB_EXPORT void ajib_tiler_release(ajib_tiler **t);
 
+/* Compose without allocating device memory. This entry point has no counterpart in the
+ * reference; it exists for callers that may not call cudaMalloc, such as a host application
+ * whose device memory all comes from its own allocator or budget, or a real-time frame path
+ * where cudaMalloc / cudaFree would synchronise the device. It does what ajib_tiler_create +
+ * ajib_tiler_compose + ajib_tiler_release do for one image shape (same arguments, same bytes
+ * out), but the geometry tables go into a fixed 1 MiB area inside this library that every GPU
+ * loading it holds until the process exits; the tables of outputs up to about 24K x 24K pixels
+ * fit. The caller passes the tiles and the output, both device memory.
+ * Returns AJIB_OK, AJIB_ERR_ARGS for bad arguments, AJIB_ERR_UNSUPPORTED when the shape's tables
+ * exceed the 1 MiB area, AJIB_ERR_CUDA on a CUDA error.
+ * The first call on a device looks up the area's device address (with that device current);
+ * make that first call before any stream capture. Every call on a device uses the same area and
+ * leaves its tables there: calls that overlap on the GPU (other streams, or the next call before
+ * this one's kernel has run on another stream) race. */
+AJIB_EXPORT int ajib_tiler_compose_static(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap,
+                                          int even, const void *tiles, uint8_t *out, void *stream);
+
 /* ---- the native model and its executor ----
  * A model is a plan of fused conv steps (reference src/native/lower.h:38-77, Plan), read from
  * this engine's model file (format: animejanai-inference_b200/csrc/model.cpp). An executor is
