@@ -133,6 +133,17 @@ def conv3x3(op, src, resid, dst, H, W, row_begin=0, row_end=0, stream=0):
     return lib.ajib_conv3x3_launch(C.byref(op), src, resid, dst, H, W, row_begin, row_end, stream)
 
 
+lib.ajib_concat1x1_launch.argtypes = [_vp, C.c_int, C.POINTER(_vp), C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                      _vp]
+lib.ajib_concat1x1_launch.restype = C.c_int
+
+
+def concat1x1(w, srcs, c, dst, H, W, row_begin=0, row_end=0, stream=0):
+    """SPAN's concat + 1x1 conv on row-chunked maps (ajib_concat1x1_launch); w: Weights(taps=1)."""
+    arr = (_vp * len(srcs))(*srcs)
+    return lib.ajib_concat1x1_launch(w.handle, len(srcs), arr, c, dst, H, W, row_begin, row_end, stream)
+
+
 def conv3x3_images(op, src, resid, dst, nimg, img_h, W, row_begin=0, row_end=0, stream=0):
     return lib.ajib_conv3x3_launch_images(C.byref(op), src, resid, dst, nimg, img_h, W, row_begin, row_end, stream)
 

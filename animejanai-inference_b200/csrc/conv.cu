@@ -20,6 +20,7 @@
 #include <string>
 #include <vector>
 
+#include "concat_tc.cuh"
 #include "conv_tc.cuh"
 #include "../../include/aji_b200.h"
 
@@ -320,6 +321,72 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     const int grid = (int)std::min<long>(sm_count(), tiles);
     ConvFn fn = op_fn(op);
     const cudaError_t e = fn(p, grid, (cudaStream_t)stream);
+    return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+namespace ajib {
+namespace {
+
+template <int NPAD>
+cudaError_t run_concat(const CatDev &p, int grid, int smem, cudaStream_t s)
+{
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load() & bit)) {
+        const cudaError_t attr = cudaFuncSetAttribute(k_concat1x1<NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (attr != cudaSuccess) return attr;
+        done.fetch_or(bit);
+    }
+    k_concat1x1<NPAD><<<grid, kCatThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace ajib
+
+extern "C" int ajib_concat1x1_launch(const ajib_weights *w, int nsrc, const void *const *srcs, int c, void *dst, int H,
+                                     int W, int row_begin, int row_end, void *stream)
+{
+    if (!w || !srcs || !dst || nsrc < 2 || nsrc > 4 || c < 8 || c > 64 || c % 8 || H < 1 || W < 1) return AJIB_ERR_ARGS;
+    if (w->taps != 1 || w->cin != nsrc * c || w->cout != c) return AJIB_ERR_ARGS;
+    if (((uintptr_t)dst & 15)) return AJIB_ERR_ARGS;
+    for (int k = 0; k < nsrc; k++)
+        if (!srcs[k] || ((uintptr_t)srcs[k] & 15)) return AJIB_ERR_ARGS;
+    if (row_end <= 0 || row_end > H) row_end = H;
+    if (row_begin < 0 || row_begin >= row_end) return row_begin == row_end ? AJIB_OK : AJIB_ERR_ARGS;
+    CatDev p{};
+    for (int k = 0; k < 4; k++) p.src[k] = k < nsrc ? (const __half *)srcs[k] : nullptr;
+    p.dst = (__half *)dst;
+    p.wimg = (const unsigned char *)w->img;
+    p.bias = w->bias;
+    p.err = status_word();
+    if (!p.err) return AJIB_ERR_CUDA;
+    p.nsrc = nsrc;
+    p.c = c;
+    p.H = H;
+    p.W = W;
+    p.pitch = feature_pitch(W);
+    p.kpad = w->kpad;
+    p.row_begin = row_begin;
+    p.row_end = row_end;
+    // as many stages as fit (2..4); at least 120 KB requested so that one CTA holds an SM (and its TMEM)
+    const CatSmem one(w->kpad, w->npad, 0);
+    const int fit = (kMaxSmem - one.total) / one.stage;
+    p.ns = std::min(kCatMaxStages, fit);
+    if (p.ns < 2) return AJIB_ERR_UNSUPPORTED;
+    const int smem = std::max(CatSmem(w->kpad, w->npad, p.ns).total, 120 * 1024);
+    const long tiles = (long)((W + kTileM - 1) / kTileM) * (row_end - row_begin);
+    const int grid = (int)std::min<long>(sm_count(), tiles);
+    cudaError_t e;
+    switch (w->npad) {
+    case 16: e = run_concat<16>(p, grid, smem, (cudaStream_t)stream); break;
+    case 32: e = run_concat<32>(p, grid, smem, (cudaStream_t)stream); break;
+    case 48: e = run_concat<48>(p, grid, smem, (cudaStream_t)stream); break;
+    case 64: e = run_concat<64>(p, grid, smem, (cudaStream_t)stream); break;
+    default: return AJIB_ERR_UNSUPPORTED;
+    }
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
 }
 

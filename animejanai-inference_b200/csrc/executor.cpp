@@ -61,7 +61,7 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
             st.nsrc = ps.nsrc;
             for (int k = 0; k < 4; k++) st.srcs[k] = ps.srcs[k];
             e->steps_.push_back(st);
-            return fail("concat steps are not supported by this engine yet");
+            continue;
         }
         ajib_conv &op = st.op;
         op.in = ps.in;
@@ -172,6 +172,19 @@ int Executor::profile_read(double *ms, int *counts, int nsteps) const
 
 int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const { return run_images(in, out, w, h, 1, s); }
 
+int Executor::launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1,
+                     cudaStream_t s) const
+{
+    if (st.concat) {
+        const void *srcs[4] = {nullptr, nullptr, nullptr, nullptr};
+        for (int k = 0; k < st.nsrc; k++) srcs[k] = ptr(st.srcs[k], in, out);
+        return ajib_concat1x1_launch(st.w, st.nsrc, srcs, st.c, const_cast<void *>(ptr(st.dst, in, out)), nimg * img_h, w,
+                                     r0, r1, s);
+    }
+    return ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, r0, r1, s);
+}
+
 int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const
 {
     const int h = img_h * nimg;
@@ -184,8 +197,7 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
         for (int k = 0; k < ns; k++) {
             const Step &st = steps_[k];
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2], s);
-            const int rc = ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
-                                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, 0, h, s);
+            const int rc = launch(st, in, out, nimg, img_h, w, 0, h, s);
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2 + 1], s);
             if (rc != AJIB_OK) return rc;
         }
@@ -202,8 +214,7 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
             const Step &st = steps_[k];
             int r0 = nb == 1 ? 0 : std::max(0, B0 - k), r1 = nb == 1 ? h : std::min(h, B1 - k);
             if (r0 >= r1) continue;
-            const int rc = ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
-                                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, r0, r1, s);
+            const int rc = launch(st, in, out, nimg, img_h, w, r0, r1, s);
             if (rc != AJIB_OK) return rc;
         }
     }

@@ -110,6 +110,7 @@ private:
         int srcs[4] = {-1, -1, -1, -1};
     };
     const void *ptr(int t, const void *in, void *out) const;
+    int launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1, cudaStream_t s) const;
     static constexpr int kProfRuns = 64;
     mutable std::vector<cudaEvent_t> prof_ev_;  // [kProfRuns][steps][2]
     mutable int prof_runs_ = 0;

@@ -74,6 +74,13 @@ AJIB_EXPORT int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_s
  * and the pad columns (x = -1 and x >= W) must hold zeros (clear the buffer once; the kernels never
  * write them). Each 8-channel chunk of a row is then one contiguous run the kernels copy in one
  * piece. ajib_feature_bytes gives the buffer size. */
+/* The 1x1 convolution over the concatenation of nsrc (2..4) row-chunked maps of c channels (c a
+ * multiple of 8, 8..64) into a row-chunked map of c channels, plus bias (SPAN's concat + conv;
+ * replaces the reference's ConcatConv1x1 / k_concat1x1, src/native/conv.h:38-102 and
+ * conv_kernels.cuh:351-407). w: 1x1 weights uploaded with taps 1, cin nsrc * c, cout c (K index
+ * k * c + i is channel i of source k). Rows [row_begin, row_end) (row_end <= 0: all). */
+AJIB_EXPORT int ajib_concat1x1_launch(const ajib_weights *w, int nsrc, const void *const *srcs, int c, void *dst,
+                                      int H, int W, int row_begin, int row_end, void *stream);
 AJIB_EXPORT int ajib_feature_pitch(int W);
 AJIB_EXPORT size_t ajib_feature_bytes(int H, int W, int C);
 

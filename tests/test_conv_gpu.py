@@ -7,7 +7,7 @@ bounds (the reference's DevBuf pattern, native_conv_test.cu:49-76)."""
 import numpy as np
 import pytest
 
-from util import conv_weights, f16r, from_rows, oracle_conv, rows_pad_mask, to_f16_bits, to_rows
+from util import conv_weights, f16r, from_rows, oracle_concat, oracle_conv, rows_pad_mask, to_f16_bits, to_rows
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -221,6 +221,48 @@ def test_stacked_images(kind):
         outs.append(dst.value())
     check_close(outs[0], want)
     assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("H,W", [(19, 37), (5, 300), (16, 128)])
+@pytest.mark.parametrize("nsrc,c", [(4, 48), (2, 16), (3, 24), (4, 64), (2, 8)])
+def test_concat1x1(H, W, nsrc, c):
+    """SPAN's concat + 1x1 conv (reference k_concat1x1) against the oracle, whole and as bands."""
+    import ajib
+    rng = np.random.default_rng(H + W + nsrc + c)
+    xs = [f16r(rng.uniform(-1, 1, size=(H, W, c))) for _ in range(nsrc)]
+    w = f16r(rng.normal(0.0, np.sqrt(1.0 / (nsrc * c)), size=(nsrc * c, c)))
+    b = rng.normal(0.0, 0.01, size=c).astype(np.float32)
+    want = oracle_concat([x.reshape(-1, c) for x in xs], c, w, b).reshape(H, W, c)
+    wt = ajib.Weights(to_f16_bits(w), b, taps=1)
+    srcs = [dev_rows(x) for x in xs]
+    s_ = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for bands in [[(0, 0)], [(0, 2), (2, 3), (3, H)]]:
+        dst = Guarded((H, W, c), nhwc=True)
+        for (a, b_) in bands:
+            if a >= H:
+                continue
+            assert ajib.concat1x1(wt, [t.data_ptr() for t in srcs], c, dst.ptr, H, W, a, b_, s_) == 0
+        torch.cuda.synchronize()
+        assert ajib.kernel_status() == 0
+        outs.append(dst.value())
+    check_close(outs[0], want)
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_concat1x1_refusals():
+    import ajib
+    rng = np.random.default_rng(0)
+    w = f16r(rng.normal(0.0, 0.1, size=(96, 48)))
+    wt = ajib.Weights(to_f16_bits(w), np.zeros(48, np.float32), taps=1)
+    x = dev_rows(np.zeros((4, 16, 48), np.float32))
+    ptrs = [x.data_ptr(), x.data_ptr()]
+    dst = Guarded((4, 16, 48), nhwc=True)
+    assert ajib.concat1x1(wt, ptrs, 48, dst.ptr, 4, 16) == 0
+    assert ajib.concat1x1(wt, ptrs + [x.data_ptr()], 48, dst.ptr, 4, 16) == ajib.AJIB_ERR_ARGS  # weights for 2 sources
+    assert ajib.concat1x1(wt, ptrs, 40, dst.ptr, 4, 16) == ajib.AJIB_ERR_ARGS
+    assert ajib.concat1x1(wt, [x.data_ptr() + 2, x.data_ptr()], 48, dst.ptr, 4, 16) == ajib.AJIB_ERR_ARGS  # misaligned
+    torch.cuda.synchronize()
 
 
 def test_refusals():

@@ -60,6 +60,23 @@ def test_super_ultra_compact_4x():
     check(run_exec(plan, x), run_plan(plan, x))
 
 
+@pytest.mark.parametrize("c,blocks,scale", [(48, 6, 2), (16, 2, 4)])
+def test_span(c, blocks, scale):
+    """SPAN (BASELINE config 3's architecture at 48 channels, 6 blocks): SiLU convs, sigmoid gates,
+    the concat + 1x1 conv, depth-to-space."""
+    import ajib
+    plan = ajib.span_plan(15 + c, c=c, blocks=blocks, scale=scale)
+    x = f16r(np.random.default_rng(6).uniform(0, 1, size=(3, 29, 150)))
+    check(run_exec(plan, x), run_plan(plan, x))
+
+
+def test_span_bands_bit_identical():
+    import ajib
+    plan = ajib.span_plan(16, c=16, blocks=2)
+    x = f16r(np.random.default_rng(7).uniform(0, 1, size=(3, 40, 70)))
+    assert np.array_equal(run_exec(plan, x, bands=1), run_exec(plan, x, bands=4))
+
+
 def test_video_p010_chain():
     """aji_infer (pre -> net -> post) against oracle pre -> oracle net -> oracle post. The net's
     fp16 tolerance can move a quantised sample by a level or two; everything else is exact."""
