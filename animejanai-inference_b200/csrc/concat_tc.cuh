@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
         dev::mbar_init(wbar, 1);
         dev::mbar_init(dbar, 1);
         dev::fence_mbar_init();
+        dev::mbar_arrive_expect_tx(wbar, (uint32_t)(a.kpad * NPAD * 2));
+        dev::bulk_load(wbase, a.wimg, (uint32_t)(a.kpad * NPAD * 2), wbar);
     }
     if (warp == 1) dev::tmem_alloc(dev::smem_u32(tslot), 512);
     // K chunks past the concatenation (padding to a multiple of 16) stay zero
@@ -94,14 +96,15 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
     __syncthreads();
     dev::tc_fence_after();
     const uint32_t tmem = *tslot;
+    // programmatic dependent launch: inputs are read only after the previous kernel completes
+    dev::griddep_launch_dependents();
+    dev::griddep_wait();
 
     const int H = a.H, W = a.W;
     (void)H;
     if (warp == 0) {
         // ================= producer
         if (lane == 0) {
-            dev::mbar_arrive_expect_tx(wbar, (uint32_t)(a.kpad * NPAD * 2));
-            dev::bulk_load(wbase, a.wimg, (uint32_t)(a.kpad * NPAD * 2), wbar);
             SegIter seg(W, a.row_begin, a.row_end);
             uint32_t it = 0;
             int strip, ya, yb;

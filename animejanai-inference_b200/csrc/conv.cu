@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <new>
 #include <cstring>
 #include <mutex>
@@ -98,6 +99,30 @@ namespace {
 
 using ConvFn = cudaError_t (*)(const ConvDev &, int grid, cudaStream_t);
 
+// Launch with programmatic stream serialisation: the kernel's set-up (barriers, TMEM, weight fetch)
+// may run while the previous kernel in the stream drains; the kernel waits (griddepcontrol.wait)
+// before it touches that kernel's outputs.
+template <typename Arg>
+cudaError_t launch_pdl(void (*kernel)(Arg), int grid, int threads, int smem, cudaStream_t s, const Arg &arg)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    // AJIB_PDL=0 in the environment launches without the attribute (plain stream order)
+    static const bool pdl = [] {
+        const char *e = std::getenv("AJIB_PDL");
+        return !(e && e[0] == '0');
+    }();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
 template <int KPAD, int NPAD, int EK, bool IN3>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
@@ -114,8 +139,7 @@ cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    k_conv3x3_tc<KPAD, NPAD, EK, IN3><<<grid, kConvThreads, Cf::SMEM, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(k_conv3x3_tc<KPAD, NPAD, EK, IN3>, grid, kConvThreads, Cf::SMEM, s, p);
 }
 
 // The kernel instantiation for padded channel counts, epilogue kind and input mode. Built: every
@@ -339,8 +363,7 @@ cudaError_t run_concat(const CatDev &p, int grid, int smem, cudaStream_t s)
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    k_concat1x1<NPAD><<<grid, kCatThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(k_concat1x1<NPAD>, grid, kCatThreads, smem, s, p);
 }
 
 }  // namespace

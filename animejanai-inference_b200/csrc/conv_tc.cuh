@@ -472,6 +472,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         dev::mbar_init(wbar, 1);
         dev::mbar_init(dbar, 1);
         dev::fence_mbar_init();
+        // the weights were uploaded long before any kernel ran: fetch them before the wait below
+        dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
+        dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
     }
     if (warp == kMmaWarp) dev::tmem_alloc(dev::smem_u32(tslot), kTmemCols);
     // K chunks the producer never writes (channel padding) are zero for the kernel's lifetime
@@ -491,14 +494,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     __syncthreads();
     dev::tc_fence_after();
     const uint32_t tmem = *tslot;
+    // launched with programmatic stream serialisation: the set-up above overlapped the previous
+    // kernel's tail; its outputs (this kernel's inputs) are read only after this wait
+    dev::griddep_launch_dependents();
+    dev::griddep_wait();
 
     if (warp < kProdWarps) {
         // ================= producer: stages each input row and writes its MMA plan beside it,
         // after waiting for the accumulators the row starts to be free
-        if (tid == 0) {
-            dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
-            dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
-        }
         if constexpr (bulk_in) {
             if (tid == 0) {
                 const int kcin = a.cin / 8;

@@ -94,6 +94,13 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, in
     return __all_sync(0xffffffffu, ok);
 }
 
+// ---- programmatic dependent launch ----
+// Let the next kernel in the stream start its prologue on SMs this grid frees.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Wait until the grids this one depends on have completed and their writes are visible. Nothing
+// that reads their outputs, and nothing that writes memory they may still read, comes before it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- TMA ---------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m)

@@ -198,10 +198,10 @@ def run_ours(args, rank, world, local_rank, dist):
     with open(mpath, "wb") as f:
         f.write(ajib.model_bytes(plan))
     torch.zeros(1, device=dev)
+    if args.bands > 1:
+        os.environ["AJIB_BANDS"] = str(args.bands)  # read by aji_create
     vid = ajib.Video(mpath, W_IN, H_IN, cuda_context=current_context())
     ow, oh = vid.configure(W_IN, H_IN)
-    if args.bands > 1:
-        os.environ["AJIB_BANDS"] = str(args.bands)
 
     nfr = 4
     frames_in = []
@@ -376,7 +376,7 @@ def run_kernel(args):
             return ref.ref_conv_launch(hw, 0, 2, 0, 0, 64, 64, src.data_ptr(), None, dst.data_ptr(), h_, w_, -1,
                                        s.cuda_stream)
         kname = "reference k_conv3x3<64,64,...,PReLU> (mma.sync m16n8k16 fp16-acc) recompiled for sm_100a"
-    else:
+    elif args.kernel == "conv64":
         wt = ajib.Weights(to_f16_bits(w), b, sl)
         op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
         src = torch.from_numpy(to_rows(x).astype(np.float16)).cuda()
@@ -385,6 +385,32 @@ def run_kernel(args):
         def launch():
             return ajib.conv3x3(op, src.data_ptr(), 0, dst.data_ptr(), h_, w_, 0, 0, s.cuda_stream)
         kname = "k_conv3x3_tc<64,64> (tcgen05, fp32 TMEM accumulation)"
+    else:
+        # the frame's other convs: head 3->64 from NCHW planes (or from an 8-channel row-chunked
+        # map, "head8"), tail 64->12 with depth-to-space 2 and the model-input skip
+        cin = {"head": 3, "head8": 8, "tail": 64}[args.kernel]
+        cout = 12 if args.kernel == "tail" else 64
+        wk, bk, sk = conv_weights(rng, cin, cout, prelu=args.kernel != "tail")
+        wt = ajib.Weights(to_f16_bits(wk), bk, sk)
+        mi = None
+        if args.kernel == "head":
+            op = ajib.conv_op(wt, in_=ajib.IN_NCHW3, act=ajib.ACT_PRELU)
+            src = torch.from_numpy(rng.uniform(0, 1, size=(3, h_, w_)).astype(np.float16)).cuda()
+            dst = torch.zeros(ajib.lib.ajib_feature_bytes(h_, w_, 64) // 2, dtype=torch.float16, device="cuda")
+        elif args.kernel == "head8":
+            op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
+            src = torch.from_numpy(to_rows(rng.uniform(0, 1, size=(h_, w_, 8)).astype(np.float32)).astype(np.float16)).cuda()
+            dst = torch.zeros(ajib.lib.ajib_feature_bytes(h_, w_, 64) // 2, dtype=torch.float16, device="cuda")
+        else:
+            op = ajib.conv_op(wt, out=ajib.OUT_D2S2)
+            src = torch.from_numpy(to_rows(x).astype(np.float16)).cuda()
+            mi = torch.from_numpy(rng.uniform(0, 1, size=(3, h_, w_)).astype(np.float16)).cuda()
+            dst = torch.zeros((3, 2 * h_, 2 * w_), dtype=torch.float16, device="cuda")
+
+        def launch():
+            return ajib.conv3x3(op, src.data_ptr(), 0 if mi is None else mi.data_ptr(), dst.data_ptr(), h_, w_, 0, 0,
+                                s.cuda_stream)
+        kname = f"k_conv3x3_tc {args.kernel} ({cin}->{cout})"
     for _ in range(args.warmup):
         assert launch() == 0
     torch.cuda.synchronize()
@@ -395,12 +421,17 @@ def run_kernel(args):
     e1.record(s)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    flops = 2.0 * 9 * 64 * 64 * w_ * h_
+    if args.kernel in ("conv64", None) or args.impl == "refgpu":
+        flops, nbytes = 2.0 * 9 * 64 * 64 * w_ * h_, 2 * 2 * 64 * w_ * h_
+    elif args.kernel in ("head", "head8"):
+        flops, nbytes = 2.0 * 9 * 3 * 64 * w_ * h_, (3 * 2 + 64 * 2) * w_ * h_
+    else:
+        flops, nbytes = 2.0 * 9 * 64 * 12 * w_ * h_, (64 * 2 + 3 * 2 + 12 * 2) * w_ * h_
     tf = flops / (ms / 1000.0) / 1e12
     print(json.dumps({"kernel": kname, "impl": args.impl, "size": args.size, "ms_per_launch": ms, "tflops": tf,
                       "frac_of_burst_peak": tf / tflops_burst, "peak_source": peak_src,
-                      "algorithmic_bytes": 2 * 2 * 64 * w_ * h_,
-                      "hbm_gbs_algorithmic": 2 * 2 * 64 * w_ * h_ / (ms / 1000.0) / 1e9}), flush=True)
+                      "algorithmic_bytes": nbytes, "hbm_gbs_algorithmic": nbytes / (ms / 1000.0) / 1e9,
+                      "frac_of_hbm_peak": nbytes / (ms / 1000.0) / 1e9 / hbm_peak}), flush=True)
 
 
 def plan_flops(plan):
@@ -413,7 +444,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "refgpu"])
-    ap.add_argument("--kernel", default=None, choices=[None, "conv64"],
+    ap.add_argument("--kernel", default=None, choices=[None, "conv64", "head", "head8", "tail"],
                     help="time the dominant kernel alone instead of the whole frame")
     ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)
