@@ -559,6 +559,8 @@ lib.aji_img_memory_get.argtypes = [_vp, _vp, C.POINTER(ImgMemory)]
 lib.aji_img_memory_get.restype = C.c_int
 lib.aji_img_native_probe.argtypes = [_vp, C.POINTER(ImgModelParams), C.POINTER(ImgMemory)]
 lib.aji_img_native_probe.restype = C.c_int
+lib.ajib_img_create_multi.argtypes = [C.POINTER(ImgCreateParams), C.POINTER(C.c_uint64), C.c_int, C.c_char_p, C.c_size_t]
+lib.ajib_img_create_multi.restype = C.c_void_p
 lib.ajib_tiler_create.argtypes = [C.c_int] * 8 + [C.POINTER(_vp)]
 lib.ajib_tiler_create.restype = C.c_int
 lib.ajib_tiler_info.argtypes = [_vp] + [C.POINTER(C.c_int)] * 4
@@ -584,13 +586,19 @@ def img_buffer(arr):
 class Image:
     """An aji_img_ctx (CUDA backend) on device `device_id` (0 = first)."""
 
-    def __init__(self, device_id=0):
+    def __init__(self, device_id=0, device_ids=None):
+        """device_ids: a list of aji_img_device ids for a context over several GPUs
+        (ajib_img_create_multi)."""
         p = ImgCreateParams()
         p.api_version = AJI_IMAGE_API_VERSION
         p.backend = IMG_TENSORRT
         p.device_id = device_id
         err = C.create_string_buffer(512)
-        h = lib.aji_img_create(C.byref(p), err, 512)
+        if device_ids is not None:
+            ids = (C.c_uint64 * len(device_ids))(*device_ids)
+            h = lib.ajib_img_create_multi(C.byref(p), ids, len(device_ids), err, 512)
+        else:
+            h = lib.aji_img_create(C.byref(p), err, 512)
         if not h:
             raise AjibError(f"aji_img_create: {err.value.decode()}")
         self.handle = _vp(h)

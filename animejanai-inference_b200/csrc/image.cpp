@@ -18,6 +18,8 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "plan.h"
 #include "tiler.h"
@@ -45,20 +47,26 @@ constexpr int kMaxBatch = 256;  // tiles per net launch
 
 struct aji_img_model;
 
-struct aji_img_ctx {
+// One device of a context: its stream, scratch and the tile tables of the last geometry.
+struct ImgDev {
     int device = 0;
+    cudaStream_t stream = nullptr;
+    uint8_t *d_img = nullptr, *d_out = nullptr;
+    void *d_tin = nullptr, *d_tout = nullptr;
+    size_t img_cap = 0, out_cap = 0, tin_cap = 0, tout_cap = 0;
+    std::unique_ptr<DeviceTiler> tiler;
+    int tiler_key[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    size_t scratch_bytes() const { return img_cap + out_cap + tin_cap + tout_cap + (tiler ? tiler->table_bytes() : 0); }
+};
+
+struct aji_img_ctx {
+    std::vector<ImgDev> devs;  // one for aji_img_create; several for ajib_img_create_multi
+    int device = 0;            // devs[0].device
     aji_img_log_fn log = nullptr;
     void *log_opaque = nullptr;
     std::string err;
     std::mutex run_mu;
-    cudaStream_t stream = nullptr;
     std::vector<aji_img_model *> models;
-    // scratch shared by the context's models, grown on demand
-    uint8_t *d_img = nullptr, *d_out = nullptr;
-    void *d_tin = nullptr, *d_tout = nullptr;
-    size_t img_cap = 0, out_cap = 0, tin_cap = 0, tout_cap = 0;
-    std::unique_ptr<DeviceTiler> tiler;  // the last geometry's tables
-    int tiler_key[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 
     void set_error(const char *fmt, ...)
     {
@@ -70,14 +78,24 @@ struct aji_img_ctx {
         err = b;
         if (log) log(log_opaque, 2, b);
     }
-    size_t scratch_bytes() const { return img_cap + out_cap + tin_cap + tout_cap + (tiler ? tiler->table_bytes() : 0); }
+    size_t scratch_bytes() const
+    {
+        size_t n = 0;
+        for (const ImgDev &d : devs) n += d.scratch_bytes();
+        return n;
+    }
+};
+
+// The model instantiated on each of the context's devices.
+struct ImgExec {
+    std::unique_ptr<Executor> exec;
+    int capacity = 0;  // tiles the executor holds at once
 };
 
 struct aji_img_model {
     aji_img_ctx *ctx = nullptr;
     Plan plan;
-    std::unique_ptr<Executor> exec;
-    int capacity = 0;  // tiles the executor holds at once
+    std::vector<ImgExec> execs;  // per device of the context
     int tile_w = 512, tile_h = 512, overlap = 128, flags = 0, scale = 1;
 };
 
@@ -97,19 +115,23 @@ bool grow(void **p, size_t *cap, size_t need)
     return true;
 }
 
-// The executor sized for n tiles of the model's tile (grown, never shrunk).
-bool ensure_exec(aji_img_model *m, int n)
+// The executor of device index di sized for n tiles of the model's tile (grown, never shrunk).
+// The device must be current. *why on failure.
+bool ensure_exec(aji_img_model *m, size_t di, int n, std::string *why)
 {
-    if (m->exec && m->capacity >= n) return true;
-    m->exec.reset();
-    std::string why;
-    m->exec = Executor::create(m->plan, m->tile_w, m->tile_h * n, &why);
-    if (!m->exec) {
-        m->ctx->set_error("native model refused at %d tiles of %dx%d: %s", n, m->tile_w, m->tile_h, why.c_str());
-        m->capacity = 0;
+    ImgExec &x = m->execs[di];
+    if (x.exec && x.capacity >= n) return true;
+    x.exec.reset();
+    std::string r;
+    x.exec = Executor::create(m->plan, m->tile_w, m->tile_h * n, &r);
+    if (!x.exec) {
+        char b[512];
+        std::snprintf(b, sizeof(b), "native model refused at %d tiles of %dx%d: %s", n, m->tile_w, m->tile_h, r.c_str());
+        *why = b;
+        x.capacity = 0;
         return false;
     }
-    m->capacity = n;
+    x.capacity = n;
     return true;
 }
 
@@ -125,6 +147,42 @@ int device_ordinal(uint64_t id, int *out)
         }
     }
     return -1;
+}
+
+// Open device ordinal d for a context: sm_100 only, a non-blocking stream. *why on failure.
+bool open_dev(int d, ImgDev *out, const char **why)
+{
+    cudaDeviceProp prop;
+    if (cudaSetDevice(d) != cudaSuccess || cudaGetDeviceProperties(&prop, d) != cudaSuccess) {
+        *why = "cannot use the CUDA device";
+        return false;
+    }
+    if (prop.major != 10) {
+        *why = "this engine runs on Blackwell datacenter GPUs (sm_100) only";
+        return false;
+    }
+    out->device = d;
+    if (cudaStreamCreateWithFlags(&out->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        *why = "cannot create a stream";
+        return false;
+    }
+    std::lock_guard<std::mutex> lk(g_open_mu);
+    g_open[d & 63]++;
+    return true;
+}
+
+void close_dev(ImgDev &d)
+{
+    cudaSetDevice(d.device);
+    d.tiler.reset();
+    cudaFree(d.d_img);
+    cudaFree(d.d_out);
+    cudaFree(d.d_tin);
+    cudaFree(d.d_tout);
+    if (d.stream) cudaStreamDestroy(d.stream);
+    d.stream = nullptr;
+    std::lock_guard<std::mutex> lk(g_open_mu);
+    g_open[d.device & 63]--;
 }
 
 }  // namespace
@@ -151,6 +209,37 @@ extern "C" int aji_img_enum_devices(int backend, aji_img_device *out, int max)
     return n;
 }
 
+namespace {
+
+aji_img_ctx *create_ctx(const aji_img_create_params *p, const int *ordinals, int n, char *err, size_t err_size)
+{
+    auto fail = [&](const char *m) -> aji_img_ctx * {
+        if (err && err_size) std::snprintf(err, err_size, "%s", m);
+        return nullptr;
+    };
+    auto c = std::make_unique<aji_img_ctx>();
+    c->log = p->log;
+    c->log_opaque = p->log_opaque;
+    for (int i = 0; i < n; i++) {
+        for (int k = 0; k < i; k++)
+            if (ordinals[k] == ordinals[i]) {
+                for (ImgDev &d : c->devs) close_dev(d);
+                return fail("a device is listed twice");
+            }
+        ImgDev d;
+        const char *why = nullptr;
+        if (!open_dev(ordinals[i], &d, &why)) {
+            for (ImgDev &o : c->devs) close_dev(o);
+            return fail(why);
+        }
+        c->devs.push_back(std::move(d));
+    }
+    c->device = c->devs[0].device;
+    return c.release();
+}
+
+}  // namespace
+
 extern "C" aji_img_ctx *aji_img_create(const aji_img_create_params *p, char *err, size_t err_size)
 {
     auto fail = [&](const char *m) -> aji_img_ctx * {
@@ -160,20 +249,29 @@ extern "C" aji_img_ctx *aji_img_create(const aji_img_create_params *p, char *err
     if (!p || p->api_version != AJI_IMAGE_API_VERSION) return fail("bad create params or API version");
     if (!backend_ok(p->backend)) return fail("this engine serves the CUDA backends only");
     try {
-        auto c = std::make_unique<aji_img_ctx>();
-        c->log = p->log;
-        c->log_opaque = p->log_opaque;
-        if (device_ordinal(p->device_id, &c->device) != 0) return fail("no such CUDA device");
-        cudaDeviceProp prop;
-        if (cudaSetDevice(c->device) != cudaSuccess || cudaGetDeviceProperties(&prop, c->device) != cudaSuccess)
-            return fail("cannot use the CUDA device");
-        if (prop.major != 10) return fail("this engine runs on Blackwell datacenter GPUs (sm_100) only");
-        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("cannot create a stream");
-        {
-            std::lock_guard<std::mutex> lk(g_open_mu);
-            g_open[c->device & 63]++;
-        }
-        return c.release();
+        int d = 0;
+        if (device_ordinal(p->device_id, &d) != 0) return fail("no such CUDA device");
+        return create_ctx(p, &d, 1, err, err_size);
+    } catch (...) {
+        return fail("out of host memory");
+    }
+}
+
+extern "C" aji_img_ctx *ajib_img_create_multi(const aji_img_create_params *p, const uint64_t *device_ids, int n, char *err,
+                                              size_t err_size)
+{
+    auto fail = [&](const char *m) -> aji_img_ctx * {
+        if (err && err_size) std::snprintf(err, err_size, "%s", m);
+        return nullptr;
+    };
+    if (!p || p->api_version != AJI_IMAGE_API_VERSION) return fail("bad create params or API version");
+    if (!backend_ok(p->backend)) return fail("this engine serves the CUDA backends only");
+    if (!device_ids || n < 1 || n > 64) return fail("need 1..64 device ids");
+    try {
+        std::vector<int> ord(n);
+        for (int i = 0; i < n; i++)
+            if (device_ordinal(device_ids[i], &ord[i]) != 0) return fail("no such CUDA device");
+        return create_ctx(p, ord.data(), n, err, err_size);
     } catch (...) {
         return fail("out of host memory");
     }
@@ -187,7 +285,6 @@ extern "C" aji_img_model *aji_img_load(aji_img_ctx *c, const aji_img_model_param
         return nullptr;
     }
     try {
-        cudaSetDevice(c->device);
         auto m = std::make_unique<aji_img_model>();
         m->ctx = c;
         std::string why;
@@ -200,7 +297,14 @@ extern "C" aji_img_model *aji_img_load(aji_img_ctx *c, const aji_img_model_param
         m->overlap = p->overlap > 0 ? p->overlap : 128;
         m->flags = p->flags;
         m->scale = m->plan.depth_to_space;
-        if (!ensure_exec(m.get(), 1)) return nullptr;
+        m->execs.resize(c->devs.size());
+        for (size_t i = 0; i < c->devs.size(); i++) {
+            cudaSetDevice(c->devs[i].device);
+            if (!ensure_exec(m.get(), i, 1, &why)) {
+                c->set_error("%s", why.c_str());
+                return nullptr;
+            }
+        }
         c->models.push_back(m.get());
         return m.release();
     } catch (...) {
@@ -222,6 +326,123 @@ extern "C" int aji_img_model_info_get(aji_img_model *m, aji_img_model_info *info
     info->overlap = m->overlap;
     return AJI_IMG_OK;
 }
+
+namespace {
+
+// One device's share of an upscale: the output rows [Y0, Y1), from tile rows [j0, j1]. Runs with
+// the device current; the first failure is reported through *why (and its status returned).
+struct Share {
+    int Y0 = 0, Y1 = 0, j0 = 0, j1 = -1;
+    int tiles() const { return j1 >= j0 ? j1 - j0 + 1 : 0; }
+};
+
+std::vector<Share> make_shares(const TileGeometry &g, int ndev)
+{
+    const int ny = g.ny(), nd = std::max(1, std::min(ndev, ny)), s = g.scale;
+    std::vector<Share> shares(nd);
+    for (int d = 0; d < nd; d++) {
+        const int ga = (int)((long)d * ny / nd), gb = (int)((long)(d + 1) * ny / nd) - 1;
+        Share &sh = shares[d];
+        sh.Y0 = d == 0 ? 0 : g.oy[ga] * s;
+        sh.Y1 = d == nd - 1 ? g.H * s : g.oy[gb + 1] * s;
+        tile_rows_covering(g, sh.Y0, sh.Y1, &sh.j0, &sh.j1);
+    }
+    return shares;
+}
+
+int run_share(aji_img_model *m, size_t di, const Share &sh, const aji_img_buffer *in, const aji_img_buffer *out,
+              bool even, aji_img_progress_fn progress, void *opaque, std::string *why)
+{
+    aji_img_ctx *c = m->ctx;
+    ImgDev &D = c->devs[di];
+    const int W = in->width, H = in->height, s = m->scale, ci = in->channels;
+    if (cudaSetDevice(D.device) != cudaSuccess) {
+        *why = "cannot use the CUDA device";
+        return AJI_IMG_ERR;
+    }
+    cudaStream_t st = D.stream;
+    const int key[8] = {W, H, ci, s, m->tile_w, m->tile_h, m->overlap, even ? 1 : 0};
+    if (!D.tiler || std::memcmp(key, D.tiler_key, sizeof(key)) != 0) {
+        auto t = std::make_unique<DeviceTiler>();
+        if (!t->init(make_geometry(W, H, ci, s, m->tile_w, m->tile_h, m->overlap, even))) {
+            cudaGetLastError();
+            *why = "out of device memory for the tile tables";
+            return AJI_IMG_ERR_NO_MEM;
+        }
+        D.tiler = std::move(t);
+        std::memcpy(D.tiler_key, key, sizeof(key));
+    }
+    const TileGeometry &g = D.tiler->geometry();
+    const int nx = g.nx(), k0 = sh.j0 * nx, count = sh.tiles() * nx, tw = g.tw, th = g.th;
+    const int batch = std::min(count, kMaxBatch);
+    const size_t tile_in = (size_t)3 * tw * th * 2, tile_out = tile_in * s * s;
+    const size_t OW = (size_t)W * s, rows = (size_t)(sh.Y1 - sh.Y0);
+    // with more tiles than one batch, each batch's output is staged after its input and then
+    // copied into its place in the share's stack
+    const size_t staging = batch < count ? tile_out * batch : 0;
+    if (!ensure_exec(m, di, batch, why)) return AJI_IMG_ERR_NO_MEM;
+    if (!grow((void **)&D.d_img, &D.img_cap, (size_t)W * H * ci) || !grow((void **)&D.d_out, &D.out_cap, OW * rows * ci) ||
+        !grow(&D.d_tin, &D.tin_cap, tile_in * batch + staging) || !grow(&D.d_tout, &D.tout_cap, tile_out * count)) {
+        *why = "out of device memory for the tiling buffers";
+        return AJI_IMG_ERR_NO_MEM;
+    }
+    // the whole input on every device (tiles reflect across the image edges)
+    if (cudaMemcpy2DAsync(D.d_img, (size_t)W * ci, in->data, in->stride, (size_t)W * ci, H, cudaMemcpyHostToDevice, st) !=
+        cudaSuccess) {
+        *why = "image upload failed";
+        return AJI_IMG_ERR;
+    }
+    // the share's tiles through the net, a batch at a time; a batch's output lands in its tiles'
+    // place of the share's stack ([3][count * th * s][tw * s])
+    Executor &ex = *m->execs[di].exec;
+    const size_t plane_all = (size_t)count * th * s * tw * s;
+    for (int b0 = 0; b0 < count; b0 += batch) {
+        const int n = std::min(batch, count - b0);
+        const bool direct = n == count;
+        void *dst = direct ? D.d_tout : (char *)D.d_tin + tile_in * batch;
+        if (D.tiler->extract(D.d_img, k0 + b0, n, D.d_tin, st) != cudaSuccess ||
+            ex.run_images(D.d_tin, dst, tw, th, n, st) != AJIB_OK) {
+            *why = "tile kernels failed";
+            return AJI_IMG_ERR;
+        }
+        if (!direct) {
+            const size_t plane_n = (size_t)n * th * s * tw * s;
+            for (int ch = 0; ch < 3; ch++)
+                if (cudaMemcpyAsync((uint16_t *)D.d_tout + ch * plane_all + (size_t)b0 * th * s * tw * s,
+                                    (const uint16_t *)dst + ch * plane_n, plane_n * 2, cudaMemcpyDeviceToDevice,
+                                    st) != cudaSuccess) {
+                    *why = "tile output copy failed";
+                    return AJI_IMG_ERR;
+                }
+        }
+        if (progress) {
+            if (cudaStreamSynchronize(st) != cudaSuccess) {
+                *why = "tile kernels failed";
+                return AJI_IMG_ERR;
+            }
+            if (progress(opaque, b0 + n, count)) {
+                *why = "cancelled";
+                return AJI_IMG_CANCELLED;
+            }
+        }
+    }
+    uint8_t *host_rows = (uint8_t *)out->data + (ptrdiff_t)sh.Y0 * out->stride;
+    if (D.tiler->compose_rows(D.d_tout, k0, count, sh.Y0, sh.Y1, D.d_out, st) != cudaSuccess ||
+        cudaMemcpy2DAsync(host_rows, out->stride, D.d_out, OW * ci, OW * ci, rows, cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        *why = std::string("compose or download failed: ") + cudaGetErrorString(cudaGetLastError());
+        return AJI_IMG_ERR;
+    }
+    const int ks = ajib_kernel_status(1);
+    if (ks != 0) {
+        *why = "a native kernel timed out waiting on its pipeline (code " + std::to_string(ks) + ")";
+        return AJI_IMG_ERR;
+    }
+    return AJI_IMG_OK;
+}
+
+}  // namespace
 
 extern "C" int aji_img_upscale(aji_img_model *m, const aji_img_buffer *in, const aji_img_buffer *out,
                                aji_img_progress_fn progress, void *opaque)
@@ -248,85 +469,42 @@ extern "C" int aji_img_upscale(aji_img_model *m, const aji_img_buffer *in, const
         return AJI_IMG_ERR_ARGS;
     }
     try {
-        if (cudaSetDevice(c->device) != cudaSuccess) {
-            c->set_error("cannot use the CUDA device");
-            return AJI_IMG_ERR;
-        }
-        cudaStream_t st = c->stream;
         const bool even = (m->flags & AJI_IMG_LOAD_EVEN_TILES) != 0;
-        const int key[8] = {W, H, ci, s, m->tile_w, m->tile_h, m->overlap, even ? 1 : 0};
-        if (!c->tiler || std::memcmp(key, c->tiler_key, sizeof(key)) != 0) {
-            auto t = std::make_unique<DeviceTiler>();
-            if (!t->init(make_geometry(W, H, ci, s, m->tile_w, m->tile_h, m->overlap, even))) {
-                cudaGetLastError();
-                c->set_error("out of device memory for the tile tables");
-                return AJI_IMG_ERR_NO_MEM;
+        const TileGeometry g = make_geometry(W, H, ci, s, m->tile_w, m->tile_h, m->overlap, even);
+        // shares: contiguous groups of tile rows per device; a device owns the output rows from
+        // the start of its first tile row to the start of the next device's, and also runs the
+        // tile row before its group whose blend reaches into those rows (no data crosses devices;
+        // every output pixel is blended in the one-device order, so the bytes are the same)
+        const std::vector<Share> shares = make_shares(g, (int)c->devs.size());
+        const int nd = (int)shares.size();
+        if (nd == 1) {
+            std::string why;
+            const int rc = run_share(m, 0, shares[0], in, out, even, progress, opaque, &why);
+            if (rc != AJI_IMG_OK) c->set_error("%s", why.c_str());
+            return rc;
+        }
+        // several devices: one host thread each; progress reports whole shares as they finish
+        std::vector<int> rcs(nd, AJI_IMG_OK);
+        std::vector<std::string> whys(nd);
+        std::vector<std::thread> threads;
+        for (int d = 0; d < nd; d++)
+            threads.emplace_back([&, d] { rcs[d] = run_share(m, d, shares[d], in, out, even, nullptr, nullptr, &whys[d]); });
+        int total = 0, done = 0;
+        for (const Share &sh : shares) total += sh.tiles() * g.nx();
+        bool cancel = false;
+        for (int d = 0; d < nd; d++) {
+            threads[d].join();
+            done += shares[d].tiles() * g.nx();
+            if (progress && !cancel && rcs[d] == AJI_IMG_OK && progress(opaque, done, total)) cancel = true;
+        }
+        for (int d = 0; d < nd; d++)
+            if (rcs[d] != AJI_IMG_OK) {
+                c->set_error("device %d: %s", c->devs[d].device, whys[d].c_str());
+                return rcs[d];
             }
-            c->tiler = std::move(t);
-            std::memcpy(c->tiler_key, key, sizeof(key));
-        }
-        const TileGeometry &g = c->tiler->geometry();
-        const int count = g.count(), tw = g.tw, th = g.th, batch = std::min(count, kMaxBatch);
-        const size_t tile_in = (size_t)3 * tw * th * 2, tile_out = tile_in * s * s;
-        const size_t OW = (size_t)W * s, OH = (size_t)H * s;
-        // with more tiles than one batch, each batch's output is staged after its input and then
-        // copied into its place in the full stack
-        const size_t staging = batch < count ? tile_out * batch : 0;
-        if (!ensure_exec(m, batch)) return AJI_IMG_ERR_NO_MEM;
-        if (!grow((void **)&c->d_img, &c->img_cap, (size_t)W * H * ci) || !grow((void **)&c->d_out, &c->out_cap, OW * OH * ci) ||
-            !grow(&c->d_tin, &c->tin_cap, tile_in * batch + staging) || !grow(&c->d_tout, &c->tout_cap, tile_out * count)) {
-            c->set_error("out of device memory for the tiling buffers");
-            return AJI_IMG_ERR_NO_MEM;
-        }
-        if (cudaMemcpy2DAsync(c->d_img, (size_t)W * ci, in->data, in->stride, (size_t)W * ci, H, cudaMemcpyHostToDevice,
-                              st) != cudaSuccess) {
-            c->set_error("image upload failed");
-            return AJI_IMG_ERR;
-        }
-        // every tile through the net, a batch at a time; a batch's output lands in its tiles'
-        // place of the full stack ([3][count * th * s][tw * s])
-        const size_t plane_all = (size_t)count * th * s * tw * s;
-        for (int k0 = 0; k0 < count; k0 += batch) {
-            const int n = std::min(batch, count - k0);
-            const bool direct = n == count;
-            void *dst = direct ? c->d_tout : (char *)c->d_tin + tile_in * batch;
-            if (c->tiler->extract(c->d_img, k0, n, c->d_tin, st) != cudaSuccess ||
-                m->exec->run_images(c->d_tin, dst, tw, th, n, st) != AJIB_OK) {
-                c->set_error("tile kernels failed");
-                return AJI_IMG_ERR;
-            }
-            if (!direct) {
-                const size_t plane_n = (size_t)n * th * s * tw * s;
-                for (int ch = 0; ch < 3; ch++)
-                    if (cudaMemcpyAsync((uint16_t *)c->d_tout + ch * plane_all + (size_t)k0 * th * s * tw * s,
-                                        (const uint16_t *)dst + ch * plane_n, plane_n * 2, cudaMemcpyDeviceToDevice,
-                                        st) != cudaSuccess) {
-                        c->set_error("tile output copy failed");
-                        return AJI_IMG_ERR;
-                    }
-            }
-            if (progress) {
-                if (cudaStreamSynchronize(st) != cudaSuccess) {
-                    c->set_error("tile kernels failed");
-                    return AJI_IMG_ERR;
-                }
-                if (progress(opaque, k0 + n, count)) {
-                    c->set_error("cancelled");
-                    return AJI_IMG_CANCELLED;
-                }
-            }
-        }
-        if (c->tiler->compose(c->d_tout, c->d_out, st) != cudaSuccess ||
-            cudaMemcpy2DAsync(out->data, out->stride, c->d_out, OW * ci, OW * ci, OH, cudaMemcpyDeviceToHost, st) !=
-                cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess) {
-            c->set_error("compose or download failed: %s", cudaGetErrorString(cudaGetLastError()));
-            return AJI_IMG_ERR;
-        }
-        const int ks = ajib_kernel_status(1);
-        if (ks != 0) {
-            c->set_error("a native kernel timed out waiting on its pipeline (code %d)", ks);
-            return AJI_IMG_ERR;
+        if (cancel) {
+            c->set_error("cancelled");
+            return AJI_IMG_CANCELLED;
         }
         return AJI_IMG_OK;
     } catch (...) {
@@ -342,8 +520,11 @@ extern "C" void aji_img_release(aji_img_model **pm)
     aji_img_ctx *c = m->ctx;
     {
         std::lock_guard<std::mutex> lk(c->run_mu);
-        cudaSetDevice(c->device);
         c->models.erase(std::remove(c->models.begin(), c->models.end(), m), c->models.end());
+        for (size_t i = 0; i < m->execs.size(); i++) {
+            cudaSetDevice(c->devs[i].device);
+            m->execs[i].exec.reset();
+        }
         delete m;
     }
     *pm = nullptr;
@@ -355,19 +536,11 @@ extern "C" void aji_img_destroy(aji_img_ctx **pc)
 {
     if (!pc || !*pc) return;
     aji_img_ctx *c = *pc;
-    cudaSetDevice(c->device);
-    for (aji_img_model *m : c->models) delete m;
-    c->models.clear();
-    c->tiler.reset();
-    cudaFree(c->d_img);
-    cudaFree(c->d_out);
-    cudaFree(c->d_tin);
-    cudaFree(c->d_tout);
-    if (c->stream) cudaStreamDestroy(c->stream);
-    {
-        std::lock_guard<std::mutex> lk(g_open_mu);
-        g_open[c->device & 63]--;
+    while (!c->models.empty()) {
+        aji_img_model *m = c->models.back();
+        aji_img_release(&m);
     }
+    for (ImgDev &d : c->devs) close_dev(d);
     delete c;
     *pc = nullptr;
 }
@@ -390,15 +563,16 @@ extern "C" int aji_img_memory_get(aji_img_ctx *c, aji_img_model *m, aji_img_memo
 {
     if (!c || !out) return AJI_IMG_ERR_ARGS;
     std::memset(out, 0, sizeof(*out));
-    cudaSetDevice(c->device);
+    // the first device's figures (the reference reports one device per context)
+    cudaSetDevice(c->devs[0].device);
     size_t fr = 0, tot = 0;
     if (cudaMemGetInfo(&fr, &tot) != cudaSuccess) return AJI_IMG_ERR;
     out->device_free = fr;
     out->device_total = tot;
-    out->ctx_scratch = c->scratch_bytes();
-    if (m && m->exec) {
-        out->model_weights = m->exec->weight_bytes();
-        out->model_activations = m->exec->device_bytes() - m->exec->weight_bytes();
+    out->ctx_scratch = c->devs[0].scratch_bytes();
+    if (m && !m->execs.empty() && m->execs[0].exec) {
+        out->model_weights = m->execs[0].exec->weight_bytes();
+        out->model_activations = m->execs[0].exec->device_bytes() - m->execs[0].exec->weight_bytes();
         out->activations_shared = 0;
     }
     return AJI_IMG_OK;
@@ -412,8 +586,27 @@ extern "C" int aji_img_native_probe(aji_img_ctx *c, const aji_img_model_params *
     int rc = AJI_IMG_OK;
     if (out) {
         rc = aji_img_memory_get(c, m, out);
-        if (rc == AJI_IMG_OK) out->device_free += m->exec ? m->exec->device_bytes() : 0;
+        if (rc == AJI_IMG_OK && m->execs[0].exec) out->device_free += m->execs[0].exec->device_bytes();
     }
     aji_img_release(&m);
     return rc;
+}
+
+extern "C" int ajib_img_shares(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, int even, int ndev,
+                               int *y0, int *y1, int *j0, int *j1)
+{
+    if (W < 1 || H < 1 || (ci != 1 && ci != 3) || scale < 1 || tile_w < 1 || tile_h < 1 || overlap < 0 || ndev < 1)
+        return -1;
+    try {
+        const std::vector<Share> sh = make_shares(make_geometry(W, H, ci, scale, tile_w, tile_h, overlap, even != 0), ndev);
+        for (size_t d = 0; d < sh.size(); d++) {
+            if (y0) y0[d] = sh[d].Y0;
+            if (y1) y1[d] = sh[d].Y1;
+            if (j0) j0[d] = sh[d].j0;
+            if (j1) j1[d] = sh[d].j1;
+        }
+        return (int)sh.size();
+    } catch (...) {
+        return -1;
+    }
 }

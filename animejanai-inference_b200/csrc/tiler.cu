@@ -36,14 +36,16 @@ __global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *o
     for (int c = 0; c < 3; c++) dst[c * plane + at] = __float2half_rn(__fmul_rn((float)p[g ? 0 : c], inv255));
 }
 
-// out[Y][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
-// multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134)
-__global__ void k_compose(const __half *tiles, int ntiles, int toh, int tow, int nx, const int *ox, const int *oy,
+// out[Y - Y0][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
+// multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134),
+// for output rows [Y0, Y0 + gridDim.y * blockDim.y) clipped to Y1; the tiles buffer holds tiles
+// [k0, k0 + ntiles) of the image's row-major tile order
+__global__ void k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx, const int *ox, const int *oy,
                           const float *wx, const float *wy, int cols, int rows, const int2 *cx, const int2 *cy, int s,
-                          int co, int OW, int OH, uint8_t *out)
+                          int co, int OW, int Y0, int Y1, uint8_t *out)
 {
-    const int X = blockIdx.x * blockDim.x + threadIdx.x, Y = blockIdx.y * blockDim.y + threadIdx.y;
-    if (X >= OW || Y >= OH) return;
+    const int X = blockIdx.x * blockDim.x + threadIdx.x, Y = Y0 + blockIdx.y * blockDim.y + threadIdx.y;
+    if (X >= OW || Y >= Y1) return;
     const int2 rx = cx[X], ry = cy[Y];
     const size_t plane = (size_t)ntiles * toh * tow;
     for (int c = 0; c < co; c++) {
@@ -52,14 +54,14 @@ __global__ void k_compose(const __half *tiles, int ntiles, int toh, int tow, int
             const int j = ry.x + jj, v = Y - oy[j] * s;
             const float wv = wy[(size_t)j * rows + v];
             for (int ii = 0; ii < rx.y; ii++) {
-                const int i = rx.x + ii, u = X - ox[i] * s, k = j * nx + i;
+                const int i = rx.x + ii, u = X - ox[i] * s, k = j * nx + i - k0;
                 const float w = __fmul_rn(wv, wx[(size_t)i * cols + u]);
                 const float t = __half2float(tiles[(co == 1 ? 0 : c) * plane + ((size_t)k * toh + v) * tow + u]);
                 b = __fadd_rn(b, __fmul_rn(w, t));
             }
         }
         const float f = __fadd_rn(__fmul_rn(b, 255.0f), 0.5f);
-        out[((size_t)Y * OW + X) * co + c] = f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
+        out[((size_t)(Y - Y0) * OW + X) * co + c] = f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
     }
 }
 
@@ -121,11 +123,18 @@ cudaError_t DeviceTiler::extract(const uint8_t *img, int k0, int n, void *dst, c
 
 cudaError_t DeviceTiler::compose(const void *tiles, uint8_t *out, cudaStream_t st) const
 {
-    const int s = g_.scale, OW = g_.W * s, OH = g_.H * s;
+    return compose_rows(tiles, 0, g_.count(), 0, g_.H * g_.scale, out, st);
+}
+
+cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int Y0, int Y1, uint8_t *out,
+                                      cudaStream_t st) const
+{
+    const int s = g_.scale, OW = g_.W * s;
+    if (Y1 <= Y0) return cudaSuccess;
     const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
-    const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
-    k_compose<<<grid, block, 0, st>>>((const __half *)tiles, g_.count(), g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
-                                      d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, OH, out);
+    const dim3 block(64, 4), grid((OW + 63) / 64, (Y1 - Y0 + 3) / 4);
+    k_compose<<<grid, block, 0, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
+                                      d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
     return cudaGetLastError();
 }
 
@@ -202,10 +211,10 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
         if (cudaMemcpyAsync(base, img.data(), img.size(), cudaMemcpyHostToDevice, st) != cudaSuccess) return AJIB_ERR_CUDA;
         const int OW = g.W * s, OH = g.H * s;
         const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
-        k_compose<<<grid, block, 0, st>>>((const __half *)tiles, g.count(), g.th * s, g.tw * s, g.nx(),
+        k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
                                           (const int *)(base + o_ox), (const int *)(base + o_oy),
                                           (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
-                                          (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, OH, out);
+                                          (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, 0, OH, out);
         return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
     } catch (...) {
         return AJIB_ERR_NO_MEM;

@@ -42,6 +42,8 @@ struct TileGeometry {
 };
 
 TileGeometry make_geometry(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, bool even);
+// The tile rows [*j0, *j1] whose outputs cover any of the output rows [Y0, Y1) (Y0 < Y1).
+void tile_rows_covering(const TileGeometry &g, int Y0, int Y1, int *j0, int *j1);
 
 // Device tables for one geometry (origins, weights, per-output-pixel covering tile ranges).
 class DeviceTiler {
@@ -53,6 +55,10 @@ public:
     cudaError_t extract(const uint8_t *img, int k0, int n, void *dst, cudaStream_t s) const;
     // all tiles' model outputs tiles fp16 [3][count * th * S][tw * S] -> out u8 [H*S][W*S][ci]
     cudaError_t compose(const void *tiles, uint8_t *out, cudaStream_t s) const;
+    // output rows [Y0, Y1) into out u8 [Y1 - Y0][W*S][ci], from the outputs of tiles
+    // [k0, k0 + ntiles) (fp16 [3][ntiles * th * S][tw * S]), which must hold every tile covering
+    // those rows
+    cudaError_t compose_rows(const void *tiles, int k0, int ntiles, int Y0, int Y1, uint8_t *out, cudaStream_t s) const;
     size_t table_bytes() const { return bytes_; }
 
 private:

@@ -98,4 +98,16 @@ TileGeometry make_geometry(int W, int H, int ci, int scale, int tile_w, int tile
     return g;
 }
 
+void tile_rows_covering(const TileGeometry &g, int Y0, int Y1, int *j0, int *j1)
+{
+    const int s = g.scale, span = std::min(g.th, g.H);
+    *j0 = g.ny();
+    *j1 = -1;
+    for (int j = 0; j < g.ny(); j++)
+        if (g.oy[j] * s < Y1 && (g.oy[j] + span) * s > Y0) {
+            *j0 = std::min(*j0, j);
+            *j1 = std::max(*j1, j);
+        }
+}
+
 }  // namespace ajib

@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include "aji.h"
+#include "aji_image.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -185,6 +186,24 @@ AJIB_EXPORT void ajib_tiler_release(ajib_tiler **t);
  * this one's kernel has run on another stream) race. */
 AJIB_EXPORT int ajib_tiler_compose_static(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap,
                                           int even, const void *tiles, uint8_t *out, void *stream);
+
+/* ---- several GPUs for one image ----
+ * An image context over n devices (aji_img_device.id values; 0 = the first device), used like one
+ * from aji_img_create with the rest of include/aji_image.h. The reference's image ABI has one
+ * device per context (aji_img_create, include/aji_image.h:124-125); this additive entry point is
+ * what its dispatcher would probe, like the reference's optional 0.24+ additions
+ * (aji_image.h:220-222). aji_img_upscale splits the output rows into one band per device at tile
+ * row boundaries: each device uploads the image, runs the tile rows covering its band (the tile
+ * row before the band, whose blend reaches into it, runs on both neighbours) and blends and
+ * downloads only its band, so no data crosses devices and the bytes equal the one-device result.
+ * Progress is reported per finished band. */
+AJIB_EXPORT aji_img_ctx *ajib_img_create_multi(const aji_img_create_params *p, const uint64_t *device_ids, int n,
+                                               char *err, size_t err_size);
+/* The bands ajib_img_create_multi's upscale gives ndev devices for one image shape (host only):
+ * returns the number of bands used (min(ndev, tile rows)); band d owns output rows
+ * [y0[d], y1[d]) and runs tile rows [j0[d], j1[d]]. Arrays hold ndev entries. -1: bad arguments. */
+AJIB_EXPORT int ajib_img_shares(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, int even, int ndev,
+                                int *y0, int *y1, int *j0, int *j1);
 
 /* ---- the native model and its executor ----
  * A model is a plan of fused conv steps (reference src/native/lower.h:38-77, Plan), read from

@@ -182,3 +182,51 @@ def test_image_api_errors_and_progress():
     assert ajib.lib.aji_img_enum_devices(ajib.IMG_DIRECTML, devs, 8) < 0
     ajib.lib.aji_img_release(C.byref(m))
     ctx.close()
+
+
+def _device_ids():
+    import ajib
+    devs = (ajib.ImgDevice * 16)()
+    n = ajib.lib.aji_img_enum_devices(ajib.IMG_TENSORRT, devs, 16)
+    return [devs[i].id for i in range(n)]
+
+
+def _upscale(ctx, path, img, tile, ov):
+    m = ctx.load(path, tile=tile, overlap=ov)
+    rc, out = ctx.upscale(m, img, 4)
+    assert rc == 0, ctx.error()
+    import ajib
+    ajib.lib.aji_img_release(C.byref(m))
+    return out
+
+
+def test_multi_context_one_device_equals_single():
+    import ajib
+    path = _model_file(ajib.compact_plan(23, c=24, body=2, scale=4))
+    img = np.random.default_rng(4).integers(0, 256, size=(150, 120, 3)).astype(np.uint8)
+    a = ajib.Image()
+    want = _upscale(a, path, img, 48, 8)
+    a.close()
+    b = ajib.Image(device_ids=[_device_ids()[0]])
+    got = _upscale(b, path, img, 48, 8)
+    b.close()
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_multi_device_bands_equal_single():
+    """Bands on two (or more) GPUs: the same bytes as one GPU, for a tall image of several tile rows."""
+    import ajib
+    path = _model_file(ajib.compact_plan(24, c=24, body=2, scale=4))
+    img = np.random.default_rng(5).integers(0, 256, size=(300, 90, 3)).astype(np.uint8)
+    a = ajib.Image()
+    want = _upscale(a, path, img, 64, 16)
+    a.close()
+    ids = _device_ids()[:min(4, torch.cuda.device_count())]
+    b = ajib.Image(device_ids=ids)
+    got = _upscale(b, path, img, 64, 16)
+    b.close()
+    assert np.array_equal(got, want)
+    # duplicates are refused
+    with pytest.raises(ajib.AjibError):
+        ajib.Image(device_ids=[ids[0], ids[0]])
