@@ -29,8 +29,9 @@ struct DevPass {
 };
 
 struct aji_plan {
-    enum Kind { PRE, POST } kind;
+    enum Kind { PRE, POST, RESIZE } kind;
     int format = 0, w = 0, h = 0;
+    int dw = 0, dh = 0;  // RESIZE: output size
     FilterTable th, tv;  // host copies (tests)
     DevPass ph{}, pv{};
     int max_rows = 0, max_cols = 0;  // staged halo extents (checked against the kernel's capacity)
@@ -231,6 +232,44 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
     }
 }
 
+// ---------------- resize: fp16 NCHW RGB -> fp16 NCHW RGB (Spline36) ----------------
+// The reference's k_rs_h + k_rs_v (src/kernels.cu:322-354) in one kernel: a tile of 32 x 16
+// output pixels of one plane runs the horizontal pass for the (mirrored) source rows its
+// vertical taps read into shared memory, then the vertical pass; each pass accumulates
+// fma(weight, sample, sum) in tap order in fp32 as the reference's, one rounding to fp16.
+constexpr int kRsTW = 32, kRsTH = 16;
+
+__global__ void __launch_bounds__(256) k_resize(const __half *src, int sw, int sh, DevPass ph, DevPass pv, __half *dst)
+{
+    extern __shared__ float rs_sm[];  // [rows][kRsTW]
+    const int c = blockIdx.z, tx = threadIdx.x, ty = threadIdx.y;
+    const int dw = ph.dst, dh = pv.dst;
+    const int x0 = blockIdx.x * kRsTW, y0 = blockIdx.y * kRsTH, x = x0 + tx;
+    const int ylo = pv.start[y0], yl = min(y0 + kRsTH, dh) - 1, nrows = pv.start[yl] + pv.taps - ylo;
+    const __half *plane = src + (size_t)c * sw * sh;
+    if (x < dw) {
+        const float *wt = ph.wt + (size_t)x * ph.taps;
+        const int s0 = ph.start[x];
+        for (int rr = ty; rr < nrows; rr += blockDim.y) {
+            const __half *row = plane + (size_t)mirror_index(ylo + rr, sh) * sw;
+            float a = 0.0f;
+            for (int j = 0; j < ph.taps; j++) a = __fmaf_rn(wt[j], __half2float(row[mirror_index(s0 + j, sw)]), a);
+            rs_sm[rr * kRsTW + tx] = a;
+        }
+    }
+    __syncthreads();
+    if (x >= dw) return;
+    for (int yy = ty; yy < kRsTH; yy += blockDim.y) {
+        const int y = y0 + yy;
+        if (y >= dh) break;
+        const float *wt = pv.wt + (size_t)y * pv.taps;
+        const int s0 = pv.start[y] - ylo;
+        float a = 0.0f;
+        for (int j = 0; j < pv.taps; j++) a = __fmaf_rn(wt[j], rs_sm[(s0 + j) * kRsTW + tx], a);
+        dst[(size_t)c * dw * dh + (size_t)y * dw + x] = __float2half_rn(a);
+    }
+}
+
 // ---------------- 4:4:4 16-bit planar, matrix only ----------------
 __global__ void k_post444(const __half *src, int w, int h, aji_csp csp, float qdiv, float qmax, uint8_t *yp,
                           ptrdiff_t ys, uint8_t *cbp, ptrdiff_t cbs, uint8_t *crp, ptrdiff_t crs)
@@ -347,6 +386,40 @@ extern "C" aji_plan *aji_pre_plan_create(int format, int w, int h, int siting, i
 extern "C" aji_plan *aji_post_plan_create(int format, int w, int h, int siting, int filter)
 {
     return plan_create(aji_plan::POST, format, w, h, siting, filter);
+}
+
+extern "C" aji_plan *aji_resize_plan_create(int sw, int sh, int dw, int dh)
+{
+    if (sw < 1 || sh < 1 || dw < 1 || dh < 1) return nullptr;
+    auto *p = new (std::nothrow) aji_plan();
+    if (!p) return nullptr;
+    p->kind = aji_plan::RESIZE;
+    p->w = sw;
+    p->h = sh;
+    p->dw = dw;
+    p->dh = dh;
+    p->th = make_filter(sw, dw, 0.0, kFilterSpline36);
+    p->tv = make_filter(sh, dh, 0.0, kFilterSpline36);
+    p->max_rows = span_of(p->tv, kRsTH);
+    // the tile's staged rows must fit the shared memory of one block (downscales beyond ~16x do not)
+    if ((size_t)p->max_rows * kRsTW * sizeof(float) > 96 * 1024 || !upload_pass(&p->ph, p->th) ||
+        !upload_pass(&p->pv, p->tv)) {
+        aji_plan_destroy(p);
+        return nullptr;
+    }
+    return p;
+}
+
+extern "C" int aji_run_resize(aji_plan *p, const void *src_f16, void *dst_f16, void *stream)
+{
+    if (!p || p->kind != aji_plan::RESIZE || !src_f16 || !dst_f16) return (int)cudaErrorInvalidValue;
+    const size_t smem = (size_t)p->max_rows * kRsTW * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    const dim3 grid((p->dw + kRsTW - 1) / kRsTW, (p->dh + kRsTH - 1) / kRsTH, 3), block(kRsTW, 8);
+    k_resize<<<grid, block, smem, (cudaStream_t)stream>>>((const __half *)src_f16, p->w, p->h, p->ph, p->pv,
+                                                         (__half *)dst_f16);
+    return (int)cudaGetLastError();
 }
 
 extern "C" void aji_plan_destroy(aji_plan *p)

@@ -122,6 +122,13 @@ enum { AJI_FILTER_SPLINE36 = 0, AJI_FILTER_BILINEAR = 1 };
 AJIB_EXPORT aji_plan *aji_pre_plan_create(int format, int w, int h, int siting, int filter);
 AJIB_EXPORT aji_plan *aji_post_plan_create(int format, int w, int h, int siting, int filter);
 AJIB_EXPORT void aji_plan_destroy(aji_plan *p);
+/* Spline36 resize plan, sw x sh -> dw x dh (reference src/kernels.h:48, zimg semantics: kernel
+ * stretched by 1/scale when downscaling, mirrored borders). NULL on failure. */
+AJIB_EXPORT aji_plan *aji_resize_plan_create(int sw, int sh, int dw, int dh);
+/* Resize fp16 NCHW RGB [3][sh][sw] -> [3][dh][dw] with a resize plan (reference src/kernels.h:
+ * 77-78): horizontal then vertical pass, fp32 between them, one rounding to fp16. One kernel.
+ * Returns 0 or a cudaError_t. */
+AJIB_EXPORT int aji_run_resize(aji_plan *p, const void *src_f16, void *dst_f16, void *stream);
 
 /* NV12/P010 -> fp16 NCHW RGB [3][h][w] (reference src/kernels.h:52-55): chroma upsampled with
  * the plan's filter, then the matrix; fp32 throughout, one rounding to fp16. One kernel. Returns

@@ -73,6 +73,8 @@ int orc_upscale_tiled(int (*run)(void *opaque, const float *in, float *out), voi
                       int overlap, int even, const uint8_t *in, int W, int H, int ci, ptrdiff_t in_stride,
                       uint8_t *out, ptrdiff_t out_stride);
 
+int orc_resize(const uint16_t *src, int sw, int sh, int dw, int dh, uint16_t *dst);
+
 #ifdef __cplusplus
 }
 #endif

@@ -293,3 +293,41 @@ int orc_pre444(int w, int h, const uint16_t *yp, const uint16_t *cbp, const uint
     }
     return 0;
 }
+
+/* src/kernels.cu:322-354 + :416-431, :499-508 (aji_resize_plan_create / aji_run_resize): Spline36
+ * resize of fp16 NCHW RGB [3][sh][sw] (bits) -> [3][dh][dw] (bits). Horizontal pass into an fp32
+ * plane, vertical pass, each sum accumulated as fmaf(weight, sample, sum) in tap order (the CUDA
+ * compiler contracts the reference's a += w * x), one rounding to fp16. Returns 0 or -1. */
+int orc_resize(const uint16_t *src, int sw, int sh, int dw, int dh, uint16_t *dst)
+{
+    if (!src || !dst || sw < 1 || sh < 1 || dw < 1 || dh < 1) return -1;
+    const int th = orc_filter(sw, dw, 0.0, 0, 0, 0), tv = orc_filter(sh, dh, 0.0, 0, 0, 0);
+    int *hs = malloc(sizeof(int) * dw), *vs = malloc(sizeof(int) * dh);
+    float *hw = malloc(sizeof(float) * (size_t)dw * th), *vw = malloc(sizeof(float) * (size_t)dh * tv);
+    float *tmp = malloc(sizeof(float) * (size_t)3 * dw * sh);
+    if (!hs || !vs || !hw || !vw || !tmp) return -1;
+    orc_filter(sw, dw, 0.0, 0, hs, hw);
+    orc_filter(sh, dh, 0.0, 0, vs, vw);
+    for (int c = 0; c < 3; c++)
+        for (int y = 0; y < sh; y++)
+            for (int x = 0; x < dw; x++) {
+                float a = 0.0f;
+                for (int j = 0; j < th; j++)
+                    a = fmaf(hw[(size_t)x * th + j], orc_h2f(src[((size_t)c * sh + y) * sw + mirr(hs[x] + j, sw)]), a);
+                tmp[((size_t)c * sh + y) * dw + x] = a;
+            }
+    for (int c = 0; c < 3; c++)
+        for (int y = 0; y < dh; y++)
+            for (int x = 0; x < dw; x++) {
+                float a = 0.0f;
+                for (int j = 0; j < tv; j++)
+                    a = fmaf(vw[(size_t)y * tv + j], tmp[((size_t)c * sh + mirr(vs[y] + j, sh)) * dw + x], a);
+                dst[((size_t)c * dh + y) * dw + x] = orc_f2h(a);
+            }
+    free(hs);
+    free(vs);
+    free(hw);
+    free(vw);
+    free(tmp);
+    return 0;
+}

@@ -153,3 +153,57 @@ def test_against_reference_kernels(fmt, matrix, rng_, siting, w, h):
     gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting)
     assert np.array_equal(gy, oy.cpu().numpy().view(npdt))
     assert np.array_equal(guv, ouv.cpu().numpy().view(npdt))
+
+
+RESIZE_CASES = [(64, 36, 96, 54), (97, 41, 50, 80), (40, 30, 40, 30), (128, 72, 32, 18), (33, 17, 131, 70)]
+
+
+def _resize_oracle(src_bits, sw, sh, dw, dh):
+    from util import oracle
+    o = oracle()
+    o.orc_resize.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    out = np.zeros((3, dh, dw), np.uint16)
+    assert o.orc_resize(np.ascontiguousarray(src_bits).ctypes.data, sw, sh, dw, dh, out.ctypes.data) == 0
+    return out
+
+
+def _resize_ours(src_bits, sw, sh, dw, dh):
+    import ajib
+    ajib.lib.aji_resize_plan_create.restype = C.c_void_p
+    ajib.lib.aji_resize_plan_create.argtypes = [C.c_int] * 4
+    ajib.lib.aji_run_resize.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    p = ajib.lib.aji_resize_plan_create(sw, sh, dw, dh)
+    assert p
+    src = torch.from_numpy(src_bits.view(np.int16)).cuda()
+    out = torch.empty((3, dh, dw), dtype=torch.int16, device="cuda")
+    assert ajib.lib.aji_run_resize(C.c_void_p(p), C.c_void_p(src.data_ptr()), C.c_void_p(out.data_ptr()), None) == 0
+    torch.cuda.synchronize()
+    ajib.lib.aji_plan_destroy(C.c_void_p(p))
+    return out.cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("sw,sh,dw,dh", RESIZE_CASES)
+def test_resize_spline36_against_oracle(sw, sh, dw, dh):
+    rng = np.random.default_rng(sw * dh)
+    src = rng.uniform(-0.1, 1.1, size=(3, sh, sw)).astype(np.float16).view(np.uint16)
+    assert np.array_equal(_resize_ours(src, sw, sh, dw, dh), _resize_oracle(src, sw, sh, dw, dh))
+
+
+@pytest.mark.skipif(not os.path.exists(REF_KERNELS), reason="reference kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("sw,sh,dw,dh", RESIZE_CASES)
+def test_resize_against_reference_kernels(sw, sh, dw, dh):
+    """aji_run_resize against the reference's own k_rs_h + k_rs_v on the B200: the same bits."""
+    ref = C.CDLL(REF_KERNELS)
+    ref.aji_resize_plan_create.restype = C.c_void_p
+    ref.aji_resize_plan_create.argtypes = [C.c_int] * 4
+    ref.aji_run_resize.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    ref.aji_plan_destroy.argtypes = [C.c_void_p]
+    rng = np.random.default_rng(sw + sh + dw)
+    src = rng.uniform(-0.1, 1.1, size=(3, sh, sw)).astype(np.float16).view(np.uint16)
+    p = ref.aji_resize_plan_create(sw, sh, dw, dh)
+    dsrc = torch.from_numpy(src.view(np.int16)).cuda()
+    out = torch.empty((3, dh, dw), dtype=torch.int16, device="cuda")
+    assert ref.aji_run_resize(p, dsrc.data_ptr(), out.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    ref.aji_plan_destroy(p)
+    assert np.array_equal(_resize_ours(src, sw, sh, dw, dh), out.cpu().numpy().view(np.uint16))
