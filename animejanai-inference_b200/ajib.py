@@ -424,12 +424,35 @@ class Video:
             raise AjibError("aji_create failed")
         self.handle = _vp(h)
 
-    def configure(self, w, h, fps=24.0):
+    @classmethod
+    def from_conf(cls, conf_path, model_dir=None, slot=1, cuda_context=None):
+        """A conf-mode aji_ctx: animejanai.conf chains of native model files (<model_dir>/<name>.ajnm)."""
+        self = cls.__new__(cls)
+        p = CreateParams()
+        p.api_version = AJI_API_VERSION
+        p.cuda_context = cuda_context
+        p.conf_path = conf_path.encode()
+        p.model_dir = None if model_dir is None else model_dir.encode()
+        p.slot = slot
+        self._p = p
+        h = lib.aji_create(C.byref(p))
+        if not h:
+            raise AjibError("aji_create (conf mode) failed")
+        self.handle = _vp(h)
+        return self
+
+    def configure(self, w, h, fps=24.0, allow_passthrough=False):
         ow, oh = C.c_int(), C.c_int()
         rc = lib.aji_configure(self.handle, w, h, fps, C.byref(ow), C.byref(oh))
-        if rc != 1:
+        if rc != 1 and not (allow_passthrough and rc == 0):
             raise AjibError(f"aji_configure: {rc} {self.error()}")
         return ow.value, oh.value
+
+    def log(self):
+        return (lib.aji_current_log(self.handle) or b"").decode()
+
+    def resize_frame(self, fin, fout, stream=0):
+        return lib.aji_resize_frame(self.handle, C.byref(fin), C.byref(fout), stream)
 
     def infer(self, fin, fout, stream=0):
         return lib.aji_infer(self.handle, C.byref(fin), C.byref(fout), stream)

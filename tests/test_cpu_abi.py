@@ -86,12 +86,14 @@ def _load_bytes(data):
     ajib.lib.ajib_model_release(C.byref(h))
 
 
-def test_video_create_refuses_conf_mode_and_bad_params():
+def test_video_create_refuses_bad_params():
     import ajib
     p = ajib.CreateParams()
     p.api_version = 8
     assert not ajib.lib.aji_create(C.byref(p))
     p.api_version = ajib.AJI_API_VERSION
+    # direct mode without a model file, and (here, without a GPU) conf mode too, give no context
+    assert not ajib.lib.aji_create(C.byref(p))
     p.conf_path = b"/nonexistent/animejanai.conf"
     assert not ajib.lib.aji_create(C.byref(p))
 

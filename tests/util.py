@@ -266,3 +266,13 @@ def oracle_upscale_tiled(model, tw, th, s, overlap, img, even=False):
                              w, h, c, w * c, out.ctypes.data, w * s * c)
     assert rc == 0
     return out
+
+
+def oracle_resize(src_bits, sw, sh, dw, dh):
+    """Spline36 resize of fp16 NCHW RGB bits [3][sh][sw] -> [3][dh][dw] (oracle/oracle_colour.c,
+    the reference's k_rs_h + k_rs_v)."""
+    o = oracle()
+    o.orc_resize.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    out = np.zeros((3, dh, dw), np.uint16)
+    assert o.orc_resize(np.ascontiguousarray(src_bits, dtype=np.uint16).ctypes.data, sw, sh, dw, dh, out.ctypes.data) == 0
+    return out
