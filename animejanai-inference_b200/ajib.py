@@ -207,6 +207,72 @@ def model_bytes(plan):
     return b"".join(out)
 
 
+def parse_model_bytes(b):
+    """The plan dict of a native model file (the inverse of model_bytes)."""
+    import struct
+
+    import numpy as np
+    assert b[:4] == b"AJNM"
+    at = 8
+    nsteps, nfeat, _unshuffle, d2s, name_len = struct.unpack_from("<IIIII", b, at)
+    at += 20
+    name = b[at:at + name_len].decode()
+    at += name_len
+    channels = list(np.frombuffer(b, np.int32, nfeat, at))
+    at += 4 * nfeat
+
+    def weights():
+        nonlocal at
+        taps, cin, cout = struct.unpack_from("<iii", b, at)
+        at += 12
+        w = np.frombuffer(b, np.uint16, taps * cin * cout, at).view(np.float16).astype(np.float32).reshape(taps, cin, cout)
+        at += 2 * taps * cin * cout
+        bias = np.frombuffer(b, np.float32, cout, at).copy()
+        at += 4 * cout
+        (has,) = struct.unpack_from("<i", b, at)
+        at += 4
+        slope = None
+        if has:
+            slope = np.frombuffer(b, np.float32, cout, at).copy()
+            at += 4 * cout
+        return w, bias, slope
+
+    steps = []
+    for _ in range(nsteps):
+        f = struct.unpack_from("<12i4i", b, at)
+        at += 64
+        norm_flag, m0, m1, m2, s0, s1, s2, clamp = struct.unpack_from("<i3f3fi", b, at)
+        at += 32
+        w, bias, slope = weights()
+        s = dict(kind=f[0], in_=f[1], act=f[2], gate=f[3], out=f[4], cin=f[5], cout=f[6], src=f[7], resid=f[8],
+                 dst=f[9], c=f[10], nsrc=f[11], srcs=[x for x in f[12:16] if x != -1], w=w, bias=bias)
+        if slope is not None:
+            s["slope"] = slope
+        if norm_flag:
+            s["in_norm"] = ((m0, m1, m2), (s0, s1, s2))
+        if clamp:
+            s["out_clamp"] = True
+        if f[0] == 0 and f[3] == 2:
+            s["att"] = weights()
+        steps.append(s)
+    return dict(name=name, steps=steps, channels=channels, depth_to_space=d2s)
+
+
+def model_from_bytes(b):
+    """ajib_model_from_memory on native or ONNX bytes; returns the model's native file bytes."""
+    h = _vp()
+    err = C.create_string_buffer(512)
+    rc = lib.ajib_model_from_memory(b, len(b), C.byref(h), err, 512)
+    if rc != 0:
+        raise AjibError(err.value.decode())
+    n = C.c_size_t()
+    lib.ajib_model_save(h, None, 0, C.byref(n))
+    buf = C.create_string_buffer(n.value)
+    assert lib.ajib_model_save(h, buf, n.value, C.byref(n)) == 0
+    lib.ajib_model_release(C.byref(h))
+    return buf.raw[:n.value]
+
+
 def _he(rng, cin, cout, taps=9):
     import numpy as np
     return (rng.normal(0.0, np.sqrt(2.0 / (taps * cin)), size=(taps, cin, cout))).astype(np.float16).astype(np.float32)
@@ -584,6 +650,8 @@ lib.aji_img_native_probe.argtypes = [_vp, C.POINTER(ImgModelParams), C.POINTER(I
 lib.aji_img_native_probe.restype = C.c_int
 lib.ajib_img_create_multi.argtypes = [C.POINTER(ImgCreateParams), C.POINTER(C.c_uint64), C.c_int, C.c_char_p, C.c_size_t]
 lib.ajib_img_create_multi.restype = C.c_void_p
+lib.ajib_model_save.argtypes = [_vp, _vp, C.c_size_t, C.POINTER(C.c_size_t)]
+lib.ajib_model_save.restype = C.c_int
 lib.ajib_tiler_create.argtypes = [C.c_int] * 8 + [C.POINTER(_vp)]
 lib.ajib_tiler_create.restype = C.c_int
 lib.ajib_tiler_info.argtypes = [_vp] + [C.POINTER(C.c_int)] * 4

@@ -65,7 +65,7 @@ extern "C" int ajib_model_from_memory(const void *data, size_t size, ajib_model 
     return guarded(err, err_size, [&] {
         auto m = std::make_unique<ajib_model>();
         std::string why;
-        if (!ajib::parse_model(data, size, &m->plan, &why)) {
+        if (!ajib::load_model_bytes(data, size, &m->plan, &why)) {
             put(err, err_size, why);
             return (int)AJIB_ERR;
         }
@@ -79,6 +79,17 @@ extern "C" void ajib_model_release(ajib_model **m)
     if (!m || !*m) return;
     delete *m;
     *m = nullptr;
+}
+
+extern "C" int ajib_model_save(const ajib_model *m, void *buf, size_t cap, size_t *size)
+{
+    if (!m) return AJIB_ERR_ARGS;
+    return guarded(nullptr, 0, [&] {
+        const std::vector<uint8_t> b = ajib::serialize_model(m->plan);
+        if (size) *size = b.size();
+        if (buf && cap >= b.size()) std::memcpy(buf, b.data(), b.size());
+        return (buf && cap < b.size()) ? (int)AJIB_ERR_ARGS : (int)AJIB_OK;
+    });
 }
 
 extern "C" int ajib_model_info(const ajib_model *m, int *scale, int *steps, double *flops_per_px, char *desc,

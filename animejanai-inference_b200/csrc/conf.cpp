@@ -125,7 +125,9 @@ std::string model_file(const std::string &model_dir, const std::string &name)
 {
     std::string d = model_dir;
     if (!d.empty() && d.back() != '/') d += '/';
-    return d + name + ".ajnm";
+    // this engine's model file if there is one, else the ONNX model (lowered when loaded)
+    const std::string native = d + name + ".ajnm", onnx = d + name + ".onnx";
+    return file_exists(native) || !file_exists(onnx) ? native : onnx;
 }
 
 bool load_conf(const std::string &path, Conf *out, std::string *err)

@@ -9,7 +9,8 @@
  *  - chain_C_model_M_name / _resize_factor_before_upscale (percent, default 100) /
  *    _resize_height_before_upscale (default 0 = none), M = 1 .. number of distinct M;
  *  - chain_C_upscale=no drops the chain's models.
- * Models are this engine's native model files: <model_dir>/<name>.ajnm. The reference's
+ * Models are <model_dir>/<name>.ajnm (this engine's model file) or else <name>.onnx (lowered to
+ * a native plan when loaded). The reference's
  * built-in default profiles (slots 1001+) name its shipped ONNX models and are not provided;
  * temporal-fix models and RIFE settings are parsed into flags that make the chain unsupported
  * (temporal) or report RIFE as inactive.
@@ -56,6 +57,8 @@ bool load_conf(const std::string &path, Conf *out, std::string *err);
 const ChainConf *select_chain(const Conf &conf, int slot, const std::string &model_dir, int w, int h, double fps,
                               std::vector<std::string> *skipped);
 
+// <model_dir>/<name>.ajnm if that file exists, else <model_dir>/<name>.onnx if that one does,
+// else the .ajnm path (reported as missing).
 std::string model_file(const std::string &model_dir, const std::string &name);
 
 // Size arithmetic of the reference's chain configuration (src/aji_trt.cpp:407-423): round to

@@ -15,6 +15,7 @@
  * writes it (animejanai-inference_b200/ajib.py, write_model) from the same structures the
  * reference's lowering produces for SRVGG Compact, SuperUltraCompact and SPAN.
  */
+#include "onnx.h"
 #include "plan.h"
 
 #include <cstdio>
@@ -120,12 +121,79 @@ bool parse_model(const void *data, size_t size, Plan *out, std::string *why)
     return true;
 }
 
+namespace {
+
+template <typename T>
+void put(std::vector<uint8_t> &b, const T &v)
+{
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(&v);
+    b.insert(b.end(), p, p + sizeof(T));
+}
+
+template <typename T>
+void put_all(std::vector<uint8_t> &b, const std::vector<T> &v)
+{
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(v.data());
+    b.insert(b.end(), p, p + v.size() * sizeof(T));
+}
+
+void put_weights(std::vector<uint8_t> &b, const PlanWeights &w)
+{
+    put<int32_t>(b, w.taps);
+    put<int32_t>(b, w.cin);
+    put<int32_t>(b, w.cout);
+    put_all(b, w.w);
+    put_all(b, w.bias);
+    put<int32_t>(b, w.slope.empty() ? 0 : 1);
+    put_all(b, w.slope);
+}
+
+}  // namespace
+
+std::vector<uint8_t> serialize_model(const Plan &p)
+{
+    std::vector<uint8_t> b = {'A', 'J', 'N', 'M'};
+    put<uint32_t>(b, 1);
+    put<uint32_t>(b, (uint32_t)p.steps.size());
+    put<uint32_t>(b, (uint32_t)p.channels.size());
+    put<uint32_t>(b, (uint32_t)p.unshuffle);
+    put<uint32_t>(b, (uint32_t)p.depth_to_space);
+    put<uint32_t>(b, (uint32_t)p.name.size());
+    b.insert(b.end(), p.name.begin(), p.name.end());
+    for (int c : p.channels) put<int32_t>(b, c);
+    for (const PlanStep &s : p.steps) {
+        for (int v : {(int)s.kind, s.in, s.act, s.gate, s.out, s.cin, s.cout, s.src, s.resid, s.dst, s.c, s.nsrc}) put<int32_t>(b, v);
+        for (int x : s.srcs) put<int32_t>(b, x);
+        put<int32_t>(b, s.in_norm ? 1 : 0);
+        for (float x : s.in_mean) put<float>(b, x);
+        for (float x : s.in_scale) put<float>(b, x);
+        put<int32_t>(b, s.out_clamp ? 1 : 0);
+        put_weights(b, s.w);
+        if (s.kind == PlanStep::CONV && s.gate == 2) put_weights(b, s.att);
+    }
+    return b;
+}
+
+bool load_model_bytes(const void *data, size_t size, Plan *out, std::string *why)
+{
+    if (size >= 4 && std::memcmp(data, "AJNM", 4) == 0) return parse_model(data, size, out, why);
+    // otherwise an ONNX model: decoded and lowered to a plan
+    OnnxModel m;
+    std::string w;
+    if (!parse_onnx(data, size, &m, &w)) return fail(why, "neither a native model file (magic AJNM) nor ONNX (" + w + ")");
+    return lower_onnx(m, out, why);
+}
+
 bool load_model_file(const std::string &path, Plan *out, std::string *why)
 {
     std::ifstream f(path, std::ios::binary);
     if (!f) return fail(why, "cannot read the model file " + path);
     std::vector<char> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
-    return parse_model(bytes.data(), bytes.size(), out, why);
+    if (!load_model_bytes(bytes.data(), bytes.size(), out, why)) {
+        if (why) *why = path + ": " + *why;
+        return false;
+    }
+    return true;
 }
 
 // Structural checks: tensor ids in range and written before read, the model output written once

@@ -63,7 +63,13 @@ struct Plan {
 
 // Parse this engine's model file (layout documented in model.cpp). *why on failure.
 bool parse_model(const void *data, size_t size, Plan *out, std::string *why);
+// A native model file, or an ONNX model file lowered to a plan (lower.cpp).
 bool load_model_file(const std::string &path, Plan *out, std::string *why);
+bool load_model_bytes(const void *data, size_t size, Plan *out, std::string *why);
+// The native model file of a plan.
+std::vector<uint8_t> serialize_model(const Plan &p);
+struct OnnxModel;
+bool lower_onnx(const OnnxModel &m, Plan *plan, std::string *why);
 bool validate_plan(const Plan &p, std::string *why);
 std::string describe(const Plan &p);
 // FLOPs per input pixel (algorithmic: 2 * taps * cin * cout per conv output pixel).

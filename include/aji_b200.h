@@ -223,6 +223,12 @@ typedef struct ajib_exec ajib_exec;
 
 AJIB_EXPORT int ajib_model_load(const char *path, ajib_model **out, char *err, size_t err_size);
 AJIB_EXPORT int ajib_model_from_memory(const void *data, size_t size, ajib_model **out, char *err, size_t err_size);
+/* ajib_model_load / ajib_model_from_memory take this engine's model file or an ONNX model, which
+ * is lowered to a plan (reference src/native/lower.h:80-100, lower(); src/native/onnx_graph.h,
+ * parse_onnx): the SRVGG Compact / SuperUltraCompact and SPAN families; anything the kernels
+ * cannot run refuses the model with the reason. ajib_model_save writes the model (lowered or not)
+ * as this engine's model file: *size gets its length; buf is filled when cap is large enough. */
+AJIB_EXPORT int ajib_model_save(const ajib_model *m, void *buf, size_t cap, size_t *size);
 AJIB_EXPORT void ajib_model_release(ajib_model **m);
 /* scale (depth-to-space), steps, algorithmic FLOPs per input pixel; description into desc */
 AJIB_EXPORT int ajib_model_info(const ajib_model *m, int *scale, int *steps, double *flops_per_px, char *desc,

@@ -18,6 +18,10 @@ $CXX -O3 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/sanity" -I"$REF/include" 
 # CPU tiler (src/core/tiling.cpp)
 $CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/src/core" -I"$REF/include" \
     "$HERE/reftiling_shim.cpp" "$REF/src/core/tiling.cpp" -o "$OUT/libref_tiling.so" -lpthread
+# ONNX lowering (src/native/onnx_graph.cpp + lower.cpp + pack.cpp)
+$CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/include" \
+    "$HERE/reflower_shim.cpp" "$REF/src/native/onnx_graph.cpp" "$REF/src/native/lower.cpp" "$REF/src/native/pack.cpp" \
+    -o "$OUT/libref_lower.so"
 # host resampling tables and colour constants (src/resample.h)
 $CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/include" \
     "$HERE/refresample_shim.cpp" -o "$OUT/libref_resample.so"

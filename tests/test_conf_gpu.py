@@ -5,6 +5,7 @@ Spline36 resize before it when the chain asks for one) at the size the previous 
 the post-pass at the chain's output size (src/aji_trt.cpp:1407-1455 for the chain's sizes). The
 oracle runs the same steps on the CPU: oracle pre-pass, oracle resize, the plan oracle per model,
 oracle post-pass; the nets' fp16 tolerance can move a quantised sample by a level or two."""
+import ctypes as C
 import os
 import tempfile
 
@@ -145,3 +146,39 @@ def test_resize_frame(w, h, ow, oh):
     assert np.array_equal(oy.cpu().numpy().view(np.uint16), wy)
     assert np.array_equal(ouv.cpu().numpy().view(np.uint16), wuv)
     vid.close()
+
+
+def test_onnx_models_run_like_their_native_files():
+    """An ONNX model (lowered when loaded) gives the same bytes as the native file of the same plan:
+    video conf mode looking up <name>.onnx, and the image ABI loading the .onnx path."""
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    from onnx_writer import export
+    import ajib
+    m1 = ajib.compact_plan(36, body=2)
+    d_native = model_dir({"m1": m1, "m2": ajib.compact_plan(37, body=1)})
+    d_onnx = tempfile.mkdtemp()
+    with open(os.path.join(d_onnx, "m1.onnx"), "wb") as f:
+        f.write(export(m1))
+    conf = CONF.replace("chain_1_model_2_name=m2\n", "")
+    outs = []
+    for d in (d_native, d_onnx):
+        vid = ajib.Video.from_conf(write_conf(d, conf), slot=1)
+        w, h = 80, 48
+        ow, oh = vid.configure(w, h)
+        assert (ow, oh) == (2 * w, 2 * h), vid.log()
+        outs.append(run_frame(vid, w, h, ow, oh, 3)[2:])
+        vid.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+    # the image ABI on the .onnx file
+    img = np.random.default_rng(9).integers(0, 256, size=(70, 90, 3)).astype(np.uint8)
+    res = []
+    for path in (os.path.join(d_native, "m1.ajnm"), os.path.join(d_onnx, "m1.onnx")):
+        ctx = ajib.Image()
+        m = ctx.load(path, tile=48, overlap=8)
+        rc, out = ctx.upscale(m, img, 2)
+        assert rc == 0, ctx.error()
+        ajib.lib.aji_img_release(C.byref(m))
+        ctx.close()
+        res.append(out)
+    assert np.array_equal(res[0], res[1])
