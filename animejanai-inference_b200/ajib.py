@@ -21,7 +21,7 @@ AJIB_OK, AJIB_ERR, AJIB_ERR_ARGS, AJIB_ERR_UNSUPPORTED, AJIB_ERR_CUDA, AJIB_ERR_
     0, -1, -2, -3, -4, -5, -6)
 
 # op vocabulary (reference src/native/ops.h:13-21)
-IN_NHWC, IN_NCHW3 = 0, 1
+IN_NHWC, IN_NCHW3, IN_NCHW3_UNSHUFFLE2 = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_PRELU, ACT_SILU = 0, 1, 2, 3
 GATE_NONE, GATE_RESIDUAL, GATE_TANH1X1, GATE_SIGMOID_HALF = 0, 1, 2, 3
 OUT_NHWC, OUT_D2S2, OUT_D2S4, OUT_D2S1, OUT_D2S3 = 0, 1, 2, 3, 4
@@ -99,12 +99,14 @@ class Weights:
             pass
 
 
-def conv_op(w, in_=IN_NHWC, act=ACT_NONE, gate=GATE_NONE, out=OUT_NHWC, in_norm=None, out_clamp=False):
+def conv_op(w, in_=IN_NHWC, act=ACT_NONE, gate=GATE_NONE, out=OUT_NHWC, in_norm=None, out_clamp=False, att=None):
+    """att: the tanh gate's 1x1 attention Weights (taps 1, cout -> cout)."""
     op = ConvOp()
     op.in_, op.act, op.gate, op.out = in_, act, gate, out
     op.cin, op.cout = w.cin, w.cout
     op.w = w.handle
-    op.att = None
+    op.att = None if att is None else att.handle
+    op._att = att
     if in_norm is not None:
         op.in_norm = 1
         mean, scale = in_norm
@@ -183,7 +185,8 @@ def model_bytes(plan):
     import numpy as np
     out = [b"AJNM", struct.pack("<I", 1)]
     name = plan.get("name", "").encode()
-    out.append(struct.pack("<IIIII", len(plan["steps"]), len(plan["channels"]), 1, plan["depth_to_space"], len(name)))
+    out.append(struct.pack("<IIIII", len(plan["steps"]), len(plan["channels"]), plan.get("unshuffle", 1),
+                           plan["depth_to_space"], len(name)))
     out.append(name)
     out.append(np.asarray(plan["channels"], np.int32).tobytes())
 
@@ -204,6 +207,9 @@ def model_bytes(plan):
                                s.get("c", 0), s.get("nsrc", 0), *srcs))
         out.append(struct.pack("<i3f3fi", 1 if norm is not None else 0, *mean, *scale, 1 if s.get("out_clamp") else 0))
         out.append(weights(s["w"], s["bias"], s.get("slope")))
+        if s["kind"] == 0 and s.get("gate", 0) == GATE_TANH1X1:
+            aw = np.asarray(s["att"][0], np.float32)
+            out.append(weights(aw.reshape(1, aw.shape[-2], aw.shape[-1]), s["att"][1], None))
     return b"".join(out)
 
 
@@ -214,7 +220,7 @@ def parse_model_bytes(b):
     import numpy as np
     assert b[:4] == b"AJNM"
     at = 8
-    nsteps, nfeat, _unshuffle, d2s, name_len = struct.unpack_from("<IIIII", b, at)
+    nsteps, nfeat, unshuffle, d2s, name_len = struct.unpack_from("<IIIII", b, at)
     at += 20
     name = b[at:at + name_len].decode()
     at += name_len
@@ -255,7 +261,7 @@ def parse_model_bytes(b):
         if f[0] == 0 and f[3] == 2:
             s["att"] = weights()
         steps.append(s)
-    return dict(name=name, steps=steps, channels=channels, depth_to_space=d2s)
+    return dict(name=name, steps=steps, channels=channels, depth_to_space=d2s, unshuffle=unshuffle)
 
 
 def model_from_bytes(b):
@@ -343,6 +349,52 @@ def span_plan(seed, c=48, blocks=6, scale=2, name=None):
     steps.append(_conv_step(_he(rng, c, 3 * scale * scale), bias(3 * scale * scale), out=out_mode, src=cat,
                             dst=MODEL_OUTPUT))
     return dict(name=name or f"span-{c}x{blocks}-{scale}x", steps=steps, channels=channels, depth_to_space=scale)
+
+
+def spanf3_plan(seed, c=48, blocks=5, name=None, gain=1.0):
+    """SPANF3 2x with the 2x pixel-unshuffled input (the shipping AnimeJaNai V3.1 HD Performance /
+    Balanced structure, b5f48 / b8f64): conv_first 12->c at half resolution; `blocks` blocks of
+    c1+ReLU, c2+ReLU, c3 with the tanh gate (c3 + x) * tanh(att(c3)), att a 1x1 c->c conv; concat
+    [feat, last block, first block, the last block's ReLU(c1)] -> 1x1 4c->c; c->48 3x3;
+    depth-to-space 4 (2x overall). The plan the reference's lowering gives such a graph
+    (sanity/native_lower_test.cpp spanf3: 3 * blocks + 3 steps). gain scales every He-init weight
+    (below 1 the random net stays well-conditioned at depth: 8 blocks of 64 at gain 1 amplify a
+    one-ulp input change a hundredfold)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    steps, channels = [], []
+
+    def _he(rng_, cin, cout, taps=9):
+        w = rng_.normal(0.0, gain * np.sqrt(2.0 / (taps * cin)), size=(taps, cin, cout))
+        return w.astype(np.float16).astype(np.float32)
+
+    def bias(n):
+        return rng.normal(0.0, 0.01, size=n).astype(np.float32)
+
+    def new_feat():
+        channels.append(c)
+        return len(channels) - 1
+
+    feat = new_feat()
+    steps.append(_conv_step(_he(rng, 12, c), bias(c), in_=IN_NCHW3_UNSHUFFLE2, src=MODEL_INPUT, dst=feat))
+    x, out_b1, mid = feat, None, None
+    for b in range(blocks):
+        a1 = new_feat()
+        steps.append(_conv_step(_he(rng, c, c), bias(c), act=ACT_RELU, src=x, dst=a1))
+        a2 = new_feat()
+        steps.append(_conv_step(_he(rng, c, c), bias(c), act=ACT_RELU, src=a1, dst=a2))
+        o = new_feat()
+        st = _conv_step(_he(rng, c, c), bias(c), gate=GATE_TANH1X1, src=a2, resid=x, dst=o)
+        st["att"] = (_he(rng, c, c, taps=1), bias(c))
+        steps.append(st)
+        x, mid = o, a1
+        if b == 0:
+            out_b1 = o
+    cat = new_feat()
+    steps.append(_concat_step(_he(rng, 4 * c, c, taps=1), bias(c), [feat, x, out_b1, mid], c, cat))
+    steps.append(_conv_step(_he(rng, c, 48), bias(48), out=OUT_D2S4, src=cat, dst=MODEL_OUTPUT))
+    return dict(name=name or f"spanf3-{c}x{blocks}-unshuffle", steps=steps, channels=channels, depth_to_space=4,
+                unshuffle=2)
 
 
 lib.ajib_model_load.argtypes = [C.c_char_p, C.POINTER(_vp), C.c_char_p, C.c_size_t]

@@ -96,7 +96,7 @@ extern "C" int ajib_model_info(const ajib_model *m, int *scale, int *steps, doub
                                size_t desc_size)
 {
     if (!m) return AJIB_ERR_ARGS;
-    if (scale) *scale = m->plan.depth_to_space;
+    if (scale) *scale = ajib::model_scale(m->plan);
     if (steps) *steps = (int)m->plan.steps.size();
     if (flops_per_px) *flops_per_px = ajib::flops_per_pixel(m->plan);
     put(desc, desc_size, ajib::describe(m->plan));

@@ -123,10 +123,10 @@ cudaError_t launch_pdl(void (*kernel)(Arg), int grid, int threads, int smem, cud
     return cudaLaunchKernelEx(&cfg, kernel, arg);
 }
 
-template <int KPAD, int NPAD, int EK, bool IN3>
+template <int KPAD, int NPAD, int EK, int IN>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
-    using Cf = ConvCfg<KPAD, NPAD>;
+    using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt>;
     static_assert(Cf::SMEM <= kMaxSmem, "shared memory budget");
     // the shared-memory opt-in is per device: set it once on each
     static std::atomic<uint64_t> done{0};
@@ -135,22 +135,24 @@ cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done.load() & bit)) {
         const cudaError_t attr =
-            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD, EK, IN3>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD, EK, IN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    return launch_pdl(k_conv3x3_tc<KPAD, NPAD, EK, IN3>, grid, kConvThreads, Cf::SMEM, s, p);
+    return launch_pdl(k_conv3x3_tc<KPAD, NPAD, EK, IN>, grid, kConvThreads, Cf::SMEM, s, p);
 }
 
 // The kernel instantiation for padded channel counts, epilogue kind and input mode. Built: every
-// K x N with the activation and depth-to-space epilogues; SPAN gates (cin == cout) at the four
-// K x N pairs that cin == cout gives; the NCHW RGB model input (K 16) with activation or
-// depth-to-space.
-ConvFn find_fn(int kpad, int npad, int ek, bool in3)
+// K x N with the activation and depth-to-space epilogues; the SPAN gates and the SPANF3 tanh gate
+// (cin == cout) at the four K x N pairs that cin == cout gives; the NCHW RGB model input, plain
+// or pixel-unshuffled by 2 (K 16 both), with activation or depth-to-space.
+ConvFn find_fn(int kpad, int npad, int ek, int in)
 {
-#define AJIB_K(KP, NP, EK, IN3) \
-    if (kpad == KP && npad == NP && ek == EK && in3 == IN3) return &run_conv<KP, NP, EK, IN3>;
-#define AJIB_KN(KP, EK) AJIB_K(KP, 32, EK, false) AJIB_K(KP, 64, EK, false)
+#define AJIB_K(KP, NP, EK, IN) \
+    if (kpad == KP && npad == NP && ek == EK && in == IN) return &run_conv<KP, NP, EK, IN>;
+#define AJIB_KN(KP, EK) AJIB_K(KP, 32, EK, kInRows) AJIB_K(KP, 64, EK, kInRows)
+#define AJIB_SQ(EK) AJIB_K(16, 32, EK, kInRows) AJIB_K(32, 32, EK, kInRows) AJIB_K(48, 64, EK, kInRows) AJIB_K(64, 64, EK, kInRows)
+#define AJIB_RGB(IN) AJIB_K(16, 32, kEpiAct, IN) AJIB_K(16, 64, kEpiAct, IN) AJIB_K(16, 32, kEpiD2S, IN) AJIB_K(16, 64, kEpiD2S, IN)
     AJIB_KN(16, kEpiAct)
     AJIB_KN(32, kEpiAct)
     AJIB_KN(48, kEpiAct)
@@ -159,14 +161,12 @@ ConvFn find_fn(int kpad, int npad, int ek, bool in3)
     AJIB_KN(32, kEpiD2S)
     AJIB_KN(48, kEpiD2S)
     AJIB_KN(64, kEpiD2S)
-    AJIB_K(16, 32, kEpiGate, false)
-    AJIB_K(32, 32, kEpiGate, false)
-    AJIB_K(48, 64, kEpiGate, false)
-    AJIB_K(64, 64, kEpiGate, false)
-    AJIB_K(16, 32, kEpiAct, true)
-    AJIB_K(16, 64, kEpiAct, true)
-    AJIB_K(16, 32, kEpiD2S, true)
-    AJIB_K(16, 64, kEpiD2S, true)
+    AJIB_SQ(kEpiGate)
+    AJIB_SQ(kEpiAtt)
+    AJIB_RGB(kInRgb)
+    AJIB_RGB(kInRgbUnshuffle2)
+#undef AJIB_RGB
+#undef AJIB_SQ
 #undef AJIB_KN
 #undef AJIB_K
     return nullptr;
@@ -175,10 +175,16 @@ ConvFn find_fn(int kpad, int npad, int ek, bool in3)
 int epi_kind(const ajib_conv *op)
 {
     if (op->out != AJIB_OUT_NHWC) return kEpiD2S;
+    if (op->gate == AJIB_GATE_TANH1X1) return kEpiAtt;
     return op->gate != AJIB_GATE_NONE ? kEpiGate : kEpiAct;
 }
 
-ConvFn op_fn(const ajib_conv *op) { return find_fn(op->w->kpad, op->w->npad, epi_kind(op), op->in == AJIB_IN_NCHW3); }
+int in_kind(const ajib_conv *op)
+{
+    return op->in == AJIB_IN_NCHW3 ? kInRgb : op->in == AJIB_IN_NCHW3_UNSHUFFLE2 ? kInRgbUnshuffle2 : kInRows;
+}
+
+ConvFn op_fn(const ajib_conv *op) { return find_fn(op->w->kpad, op->w->npad, epi_kind(op), in_kind(op)); }
 
 int d2s_factor(int out) { return out == 1 ? 2 : out == 2 ? 4 : out == 3 ? 1 : out == 4 ? 3 : 0; }
 
@@ -202,8 +208,11 @@ bool check(const ajib_conv *op, char *why, size_t n)
     case AJIB_IN_NCHW3:
         if (op->cin != 3) return fail(why, n, "NCHW3 input has 3 channels");
         break;
+    case AJIB_IN_NCHW3_UNSHUFFLE2:
+        if (op->cin != 12) return fail(why, n, "a pixel-unshuffled NCHW3 input has 12 channels");
+        break;
     default:
-        return fail(why, n, "pixel-unshuffled inputs are not supported by this engine");
+        return fail(why, n, "unknown input mode");
     }
     switch (op->out) {
     case AJIB_OUT_NHWC:
@@ -230,7 +239,12 @@ bool check(const ajib_conv *op, char *why, size_t n)
         if (op->act != AJIB_ACT_NONE) return fail(why, n, "gates take no activation");
         if (op->in != AJIB_IN_NHWC || op->out != AJIB_OUT_NHWC || op->cin != op->cout)
             return fail(why, n, "gates need NHWC input and output with cin == cout");
-        if (op->gate == AJIB_GATE_TANH1X1) return fail(why, n, "the tanh 1x1 gate is not supported by this engine");
+        if (op->gate == AJIB_GATE_TANH1X1) {
+            const ajib_weights *t = op->att;
+            if (!t || t->taps != 1 || t->cin != op->cout || t->cout != op->cout)
+                return fail(why, n, "the tanh 1x1 gate needs 1x1 cout -> cout attention weights");
+            if (t->kpad > op->w->npad || t->npad > op->w->npad) return fail(why, n, "attention weights wider than the conv");
+        }
     }
     if (op->act == AJIB_ACT_PRELU && !op->w->slope) return fail(why, n, "PReLU without slopes");
     if (!op_fn(op)) return fail(why, n, "no kernel for these channel counts");
@@ -307,6 +321,8 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     const int H = nimg * img_h;
     if (!src || !dst || H < 1 || W < 1) return AJIB_ERR_ARGS;
     if (op->gate != AJIB_GATE_NONE && !resid) return AJIB_ERR_ARGS;
+    // no model-input skip from a pixel-unshuffled input (its resolution is not the conv's)
+    if (op->in == AJIB_IN_NCHW3_UNSHUFFLE2 && op->out != AJIB_OUT_NHWC && resid) return AJIB_ERR_ARGS;
     if (row_end <= 0 || row_end > H) row_end = H;
     if (row_begin < 0 || row_begin >= row_end) return row_begin == row_end ? AJIB_OK : AJIB_ERR_ARGS;
     // row-chunked maps are read by bulk copies and written by 16-byte stores
@@ -340,6 +356,12 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     p.row_end = row_end;
     p.pitch = feature_pitch(W);
     p.img_h = img_h;
+    if (op->gate == AJIB_GATE_TANH1X1) {
+        p.att_img = (const unsigned char *)op->att->img;
+        p.att_bias = op->att->bias;
+        p.att_kpad = op->att->kpad;
+        p.att_npad = op->att->npad;
+    }
     const long strips = (W + kTileM - 1) / kTileM;
     const long tiles = strips * (row_end - row_begin);
     const int grid = (int)std::min<long>(sm_count(), tiles);

@@ -61,12 +61,17 @@ constexpr int kMaxSmem = 227 * 1024;
 
 // Epilogue kinds, one kernel instantiation each (so each layer runs only the code it needs):
 // row-chunked output with an activation; row-chunked output through a SPAN gate; depth-to-space
-// into NCHW (with the model-input skip).
-enum { kEpiAct = 0, kEpiGate = 1, kEpiD2S = 2 };
+// into NCHW (with the model-input skip); row-chunked output through the SPANF3 tanh gate, whose
+// 1x1 attention conv is a second tensor-core GEMM in the epilogue.
+enum { kEpiAct = 0, kEpiGate = 1, kEpiD2S = 2, kEpiAtt = 3 };
+
+// Input modes: row-chunked feature map (bulk copies); the NCHW RGB model input; the NCHW RGB
+// model input pixel-unshuffled by 2 (12 channels at half resolution).
+enum { kInRows = 0, kInRgb = 1, kInRgbUnshuffle2 = 2 };
 
 // error codes written to the status word (which wait timed out)
 enum { kErrProdEmpty = 101, kErrMmaFull = 102, kErrProdAccEmpty = 103, kErrEpiAccFull = 104, kErrWeights = 105,
-       kErrDrain = 106 };
+       kErrDrain = 106, kErrAttFull = 107 };
 
 struct ConvDev {
     const __half *src;    // row-chunked map [H][cin] or NCHW [3][H][W]
@@ -83,6 +88,11 @@ struct ConvDev {
     int row_begin, row_end;
     int pitch;            // Wp: padded pixels per chunk row of the row-chunked maps
     int img_h;            // rows per image: H = n * img_h images stacked along H, convolved apart
+    // tanh gate: the 1x1 attention conv's packed B image ([K/8][N/8][8][8] fp16, K = att_kpad,
+    // N = att_npad) and bias (att_npad floats)
+    const unsigned char *att_img;
+    const float *att_bias;
+    int att_kpad, att_npad;
 };
 
 // The input rows a segment of output rows [ya, yb) reads: one-row halos that stay inside the
@@ -96,13 +106,15 @@ __device__ __forceinline__ void segment_rows(int ya, int yb, int img_h, int &r0,
 // Padded pixels per chunk row of a row-chunked feature map of width W.
 __host__ __device__ constexpr int feature_pitch(int W) { return (W + kTileM - 1) / kTileM * kTileM + 2; }
 
-template <int KPAD, int NPAD>
+template <int KPAD, int NPAD, bool ATT = false>
 struct ConvCfg {
     static_assert(KPAD % 16 == 0 && NPAD % 16 == 0 && KPAD <= 64 && NPAD <= 64, "padded channel counts");
     static constexpr int KC = KPAD / 8;       // 8-channel chunks per pixel
     static constexpr int KS = KPAD / 16;      // MMA K steps per tap
     static constexpr int NG = NPAD / 8;       // 8-row core-matrix groups of one tap's B
-    static constexpr int S = kTmemCols / NPAD;  // accumulator ring slots
+    // the tanh gate's two attention accumulators (one per epilogue group) take their columns from
+    // the ring
+    static constexpr int S = (kTmemCols - (ATT ? 2 * NPAD : 0)) / NPAD;  // accumulator ring slots
     static constexpr int LBO_A = kHalo * 16;  // bytes between K chunks of a staged row
     static constexpr int LBO_B = 3 * NG * 128;  // bytes between K chunks of a stacked-tap B
     static constexpr int SLOT = (KC * LBO_A + 1023) / 1024 * 1024;
@@ -110,15 +122,22 @@ struct ConvCfg {
     static constexpr int AOFF = (WBYTES + 1023) / 1024 * 1024;
     static constexpr int RP = 2;                     // staged rows per pipeline stage
     static constexpr int STAGE = RP * SLOT;
-    static constexpr int FIXED = AOFF + 2 * 64 * 4 + 1024 + 1024;
+    // tanh gate: the attention conv's B (at most NPAD x NPAD) and one A tile per epilogue group
+    // (the gate's fp16 input o, [NPAD/8][128 pixels][8])
+    static constexpr int ATT_B = ATT ? NPAD * NPAD * 2 : 0;
+    static constexpr int ATT_A = NPAD / 8 * kTileM * 16;
+    static constexpr int ATT_BYTES = ATT ? ATT_B + 2 * ATT_A : 0;
+    static constexpr int FIXED = AOFF + ATT_BYTES + 3 * 64 * 4 + 1024 + 1024;
     static constexpr int NS_FIT = (kMaxSmem - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;
     static_assert(NS >= 2 && S >= 4, "pipeline depth");
-    static constexpr int POFF = AOFF + NS * STAGE;  // bias[64], slope[64] floats
-    static constexpr int BOFF = POFF + 2 * 64 * 4;  // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar
+    static constexpr int ATOFF = AOFF + NS * STAGE;  // attention B, then A tiles 0 and 1
+    static constexpr int POFF = ATOFF + ATT_BYTES;   // bias[64], slope[64], attention bias[64] floats
+    static constexpr int BOFF = POFF + 3 * 64 * 4;  // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2]
     static constexpr int PLOFF = BOFF + 512;        // RowPlan per staged row
     static constexpr int SMEM = BOFF + 1024 + 1024;  // + alignment slack for the base
-    static_assert((2 * NS + 2 * S + 2) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
+    static_assert((2 * NS + 2 * S + 4) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
+    static_assert(SMEM <= kMaxSmem, "shared memory budget");
 };
 
 // The run of tiles a CTA owns, split into per-strip segments. All roles walk the same sequence.
@@ -437,10 +456,11 @@ __device__ __forceinline__ void issue_plan(uint64_t adesc0, uint64_t bdesc0, con
         issue_taps<2, DX0, DX1, KS, KC, NG, LBO_A>(adesc0, bdesc0, p);
 }
 
-template <int KPAD, int NPAD, int EK, bool IN3>
+template <int KPAD, int NPAD, int EK, int IN>
 __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ ConvDev a)
 {
-    using C = ConvCfg<KPAD, NPAD>;
+    constexpr bool ATT = EK == kEpiAtt;
+    using C = ConvCfg<KPAD, NPAD, ATT>;
     constexpr int S = C::S;
     constexpr int HW = NPAD / 2;  // accumulator columns per epilogue warp (half a slot)
     extern __shared__ unsigned char smraw[];
@@ -448,15 +468,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     unsigned char *sm = smraw + ((1024 - (dev::smem_u32(smraw) & 1023)) & 1023);
     const uint32_t sbase = dev::smem_u32(sm);
     const uint32_t wbase = sbase, abase = sbase + C::AOFF;
-    float *sbias = reinterpret_cast<float *>(sm + C::POFF), *sslope = sbias + 64;
+    float *sbias = reinterpret_cast<float *>(sm + C::POFF), *sslope = sbias + 64, *satt = sbias + 128;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::BOFF);
     const uint32_t full0 = dev::smem_u32(bars), empty0 = full0 + 8 * C::NS, accf0 = empty0 + 8 * C::NS,
-                   acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * S + 2);
+                   acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8, attf0 = dbar + 8;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * S + 4);
     RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr bool bulk_in = !IN3;  // row-chunked input by bulk copies, else the NCHW RGB model input
+    constexpr bool bulk_in = IN == kInRows;  // row-chunked input by bulk copies, else the NCHW RGB model input
     const int H = a.H, W = a.W;
 
     // ---- set-up
@@ -467,19 +487,24 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         }
         for (int s = 0; s < S; s++) {
             dev::mbar_init(accf0 + 8 * s, 1);
-            dev::mbar_init(acce0 + 8 * s, kEpiWarps);
+            // the tanh gate's epilogue groups take alternate rows: four warps free each slot
+            dev::mbar_init(acce0 + 8 * s, ATT ? kEpiWarps / 2 : kEpiWarps);
         }
         dev::mbar_init(wbar, 1);
         dev::mbar_init(dbar, 1);
+        dev::mbar_init(attf0, 1);
+        dev::mbar_init(attf0 + 8, 1);
         dev::fence_mbar_init();
         // the weights were uploaded long before any kernel ran: fetch them before the wait below
-        dev::mbar_arrive_expect_tx(wbar, C::WBYTES);
+        const uint32_t att_bytes = ATT ? (uint32_t)(a.att_kpad * a.att_npad * 2) : 0u;
+        dev::mbar_arrive_expect_tx(wbar, C::WBYTES + att_bytes);
         dev::bulk_load(wbase, a.wimg, C::WBYTES, wbar);
+        if (ATT) dev::bulk_load(sbase + C::ATOFF, a.att_img, att_bytes, wbar);
     }
     if (warp == kMmaWarp) dev::tmem_alloc(dev::smem_u32(tslot), kTmemCols);
     // K chunks the producer never writes (channel padding) are zero for the kernel's lifetime
     {
-        const int written = bulk_in ? a.cin / 8 : 1;
+        const int written = bulk_in ? a.cin / 8 : IN == kInRgb ? 1 : 2;
         const int nz = (C::KC - written) * kHalo;
         for (int s = 0; s < C::NS * C::RP; s++)
             for (int i = tid; i < nz; i += kConvThreads)
@@ -488,6 +513,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     for (int n = tid; n < 64; n += kConvThreads) {
         sbias[n] = n < NPAD ? a.bias[n] : 0.f;
         sslope[n] = (n < NPAD && a.slope) ? a.slope[n] : 0.f;
+        satt[n] = (ATT && n < a.att_npad) ? a.att_bias[n] : 0.f;
     }
     dev::fence_proxy_async();
     dev::tc_fence_before();
@@ -545,14 +571,20 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 }
             }
         } else {
-            // NCHW RGB model input -> chunk 0 of the staged row: {r, g, b, 0, 0, 0, 0, 0} per pixel.
-            // Each thread holds pixels tid and tid + 128 of a row. Two stages' pixels are kept in
-            // registers, loaded one stage ahead of their use, so the load latency overlaps a
-            // whole stage of work.
+            // NCHW RGB model input -> the staged row. Plain: chunk 0 = {r, g, b, 0, 0, 0, 0, 0} per
+            // pixel. Pixel-unshuffled by 2 (the input is [3][2H][2W]): channel c * 4 + ry * 2 + rx
+            // is input pixel (2y + ry, 2x + rx) of plane c (PyTorch's pixel_unshuffle order), so the
+            // pair (rx 0, 1) is one 4-byte load and chunks 0 and 1 hold pairs (c, ry) = (0, 0) ..
+            // (2, 1), then zeros. Each thread holds pixels tid and tid + 128 of a row. Two stages'
+            // pixels are kept in registers, loaded one stage ahead of their use, so the load latency
+            // overlaps a whole stage of work.
+            constexpr bool U2 = IN == kInRgbUnshuffle2;
+            constexpr int NV = U2 ? 6 : 3;  // loads per pixel: fp16 values, or fp16 pairs (c, ry)
             RowWalk wl(W, a.row_begin, a.row_end, a.img_h), wp(W, a.row_begin, a.row_end, a.img_h);
-            const size_t plane = (size_t)H * W;
-            typedef __half StagePix[C::RP][2][3];
-            // the next stage's pixels (walk wl), as raw fp16; returns its row count
+            const int IW = U2 ? 2 * W : W;                 // input row length
+            const size_t plane = (size_t)(U2 ? 2 * H : H) * IW;
+            typedef uint32_t StagePix[C::RP][2][NV];
+            // the next stage's pixels (walk wl), as raw fp16 bits; returns its row count
             auto prefetch = [&](StagePix &pv) -> int {
                 int n = 0;
 #pragma unroll
@@ -563,9 +595,17 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     for (int k = 0; k < 2; k++) {
                         const int p = tid + k * kProdWarps * 32, x = x0 - 1 + p;
                         const bool in = p < kHalo && x >= 0 && x < W;
-                        const __half *px = a.src + (size_t)r * W + (in ? x : 0);
 #pragma unroll
-                        for (int c = 0; c < 3; c++) pv[h][k][c] = in ? __ldg(px + c * plane) : __float2half_rn(0.f);
+                        for (int j = 0; j < NV; j++) {
+                            if constexpr (U2) {
+                                const int c = j >> 1, ry = j & 1;
+                                const __half *px = a.src + c * plane + (size_t)(2 * r + ry) * IW + 2 * (in ? x : 0);
+                                pv[h][k][j] = in ? __ldg(reinterpret_cast<const unsigned int *>(px)) : 0u;
+                            } else {
+                                const __half *px = a.src + j * plane + (size_t)r * IW + (in ? x : 0);
+                                pv[h][k][j] = in ? (uint32_t)__half_as_ushort(__ldg(px)) : 0u;
+                            }
+                        }
                     }
                     n = h + 1;
                 }
@@ -596,19 +636,34 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         if (p >= kHalo) continue;
                         // normalisation applies to image pixels; the zero padding stays zero
                         const int x = wp.strip * kTileM - 1 + p;
-                        float v[3];
+                        const bool norm = a.in_norm && x >= 0 && x < W;
+                        if constexpr (U2) {
+                            uint32_t q[6];
 #pragma unroll
-                        for (int c = 0; c < 3; c++) {
-                            v[c] = __half2float(pv[h][k][c]);
-                            if (a.in_norm && x >= 0 && x < W)
-                                v[c] = __half2float(__float2half_rn((v[c] - a.in_mean[c]) * a.in_scale[c]));
+                            for (int j = 0; j < 6; j++) {
+                                q[j] = pv[h][k][j];
+                                if (norm) {
+                                    const int c = j >> 1;
+                                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&q[j]));
+                                    q[j] = pack_h2((f.x - a.in_mean[c]) * a.in_scale[c], (f.y - a.in_mean[c]) * a.in_scale[c]);
+                                }
+                            }
+                            reinterpret_cast<uint4 *>(dst)[p] = make_uint4(q[0], q[1], q[2], q[3]);
+                            reinterpret_cast<uint4 *>(dst + C::LBO_A)[p] = make_uint4(q[4], q[5], 0u, 0u);
+                        } else {
+                            float v[3];
+#pragma unroll
+                            for (int c = 0; c < 3; c++) {
+                                v[c] = __half2float(__ushort_as_half((unsigned short)pv[h][k][c]));
+                                if (norm) v[c] = __half2float(__float2half_rn((v[c] - a.in_mean[c]) * a.in_scale[c]));
+                            }
+                            uint4 q;
+                            q.x = pack_h2(v[0], v[1]);
+                            q.y = pack_h2(v[2], 0.f);
+                            q.z = 0u;
+                            q.w = 0u;
+                            reinterpret_cast<uint4 *>(dst)[p] = q;
                         }
-                        uint4 q;
-                        q.x = pack_h2(v[0], v[1]);
-                        q.y = pack_h2(v[2], 0.f);
-                        q.z = 0u;
-                        q.w = 0u;
-                        reinterpret_cast<uint4 *>(dst)[p] = q;
                     }
                 }
                 if (tid == 0)
@@ -628,7 +683,127 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 nb = prefetch(pb);
             }
         }
+    } else if (ATT && warp < kMmaWarp) {
+      if constexpr (ATT) {
+        // ================= epilogue of the tanh gate (x + o) * tanh(att_bias + W_att^T o), o the conv
+        // output in fp16 (the reference's semantics). Group g (warps 4 + 4g .. 7 + 4g) takes the
+        // output rows of parity g, its warp q TMEM lanes 32q.. (pixels) and whole slots. Per row the
+        // group writes o into its A tile, one thread issues the attention GEMM (M 128 pixels, N and
+        // K the channels) into the group's own TMEM accumulator, and the group finishes the row when
+        // it completes, while the other group works on its own row.
+        const int q = warp & 3, g = (warp - kProdWarps) >> 2;
+        const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        for (int sl = 0; sl < S; sl++)
+#pragma unroll
+            for (int c = 0; c < HW; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + g * HW + c));
+        dev::tmem_wait_st();
+        dev::tc_fence_before();
+        dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
+
+        const int px = q * 32 + lane;  // the tile pixel (TMEM lane) of this thread
+        unsigned char *atile = sm + C::ATOFF + C::ATT_B + g * C::ATT_A;
+        const bool issuer = q == 0 && lane == 0;
+        // A: the group's tile, K-major without swizzle: K chunks 128 x 16 bytes apart, 8-pixel groups
+        // 128 bytes apart. B: the packed 1x1 weights, K chunks (att_npad / 8) x 128 bytes apart.
+        const uint32_t att_lbo_b = (uint32_t)(a.att_npad / 8 * 128);
+        const uint64_t att_adesc = dev::sdesc(sbase + C::ATOFF + C::ATT_B + g * C::ATT_A, kTileM * 16, 128);
+        const uint64_t att_bdesc = dev::sdesc(sbase + C::ATOFF, att_lbo_b, 128);
+        const uint32_t att_idesc = dev::idesc_f16_f32(kTileM, a.att_npad);
+        const int att_ks = a.att_kpad / 16;
+        const uint32_t att_d = tmem + (uint32_t)((S + g) * NPAD);
+        const int ccout = a.cout / 8;
+        const size_t chunk_row = (size_t)a.pitch * 8;
+        SegIter seg(W, a.row_begin, a.row_end);
+        uint32_t ot = 0, na = 0;  // outputs so far (both groups); this group's rows so far
+        int strip, ya, yb;
+        bool alive = true;  // the group's verdict: every warp of it had every wait pass
+        bool good = true;   // this warp's last attention wait passed
+        while (alive && seg.next(strip, ya, yb)) {
+            const int x = strip * kTileM + px;
+            for (int o = ya; o < yb; o++, ot++) {
+                if ((int)(ot & 1u) != g) continue;
+                const int slot = ring_slot<S>(ot);
+                bool ok = good && dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull);
+                if (ok) {
+                    uint32_t oh[NPAD / 2];  // fp16(o + bias), channel pairs
+                    __syncwarp();
+                    dev::tc_fence_after();
+                    const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
+                    // 16 columns at a time, straight to fp16 (few registers live beside the block input)
+#pragma unroll
+                    for (int c = 0; c < NPAD; c += 16) {
+                        float t[16];
+                        dev::tmem_ld16(taddr + c, t);
+                        dev::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; j += 2) oh[(c + j) / 2] = pack_h2(t[j] + sbias[c + j], t[j + 1] + sbias[c + j + 1]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(taddr + c);
+                    dev::tmem_wait_st();
+                    dev::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+#pragma unroll
+                    for (int c = 0; c < NPAD / 8; c++)
+                        *reinterpret_cast<uint4 *>(atile + c * (kTileM * 16) + px * 16) =
+                            make_uint4(oh[4 * c], oh[4 * c + 1], oh[4 * c + 2], oh[4 * c + 3]);
+                }
+                // the block input x: its loads overlap the attention GEMM
+                EpiIn<NPAD> in;
+                epi_prefetch<kEpiGate, NPAD, 0>(in, a, o, x);
+                // the tile is read by the tensor core (the async proxy) once the whole group wrote it
+                dev::fence_proxy_async();
+                dev::tc_fence_before();
+                alive = dev::named_bar_red_and(2 + g, kEpiWarps / 2 * 32, ok);
+                if (!alive) break;
+                if (issuer) {
+                    dev::tc_fence_after();
+                    for (int kk = 0; kk < att_ks; kk++)
+                        dev::mma_f16(att_d, att_adesc + (uint64_t)((kk * 2 * kTileM * 16) >> 4),
+                                     att_bdesc + (uint64_t)((kk * 2 * att_lbo_b) >> 4), att_idesc, kk > 0 ? 1u : 0u, 0);
+                    dev::mma_commit(attf0 + 8 * g);
+                }
+                // a failed wait ends the group at its next barrier (never splits it before one)
+                good = dev::mbar_wait_warp(attf0 + 8 * g, na & 1u, a.err, kErrAttFull);
+                na++;
+                if (!good) continue;
+                __syncwarp();
+                dev::tc_fence_after();
+                __half *drow = a.dst + (size_t)o * ccout * chunk_row + (size_t)(x + 1) * 8;
+#pragma unroll
+                for (int c16 = 0; c16 < NPAD / 16; c16++) {
+                    if (c16 * 16 >= a.cout) break;
+                    float ga[16];
+                    dev::tmem_ld16(tmem + lanes + (uint32_t)((S + g) * NPAD + c16 * 16), ga);
+                    dev::tmem_wait_ld();
+#pragma unroll
+                    for (int c8 = 0; c8 < 2; c8++) {
+                        const int c = c16 * 2 + c8;
+                        if (c >= ccout || x >= W) continue;
+                        const __half2 *xh = reinterpret_cast<const __half2 *>(&in.gate[c]);
+                        uint32_t w4[4];
+                        // fp16(o) back from the tile (the tensor core only read it)
+                        const uint4 o4 = *reinterpret_cast<const uint4 *>(atile + c * (kTileM * 16) + px * 16);
+                        const __half2 *oh2 = reinterpret_cast<const __half2 *>(&o4);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int n = c * 8 + 2 * j;
+                            const float2 xf = __half22float2(xh[j]);
+                            const float2 of = __half22float2(oh2[j]);
+                            const float t0 = dev::tanh_fast(ga[c8 * 8 + 2 * j] + satt[n]);
+                            const float t1 = dev::tanh_fast(ga[c8 * 8 + 2 * j + 1] + satt[n + 1]);
+                            w4[j] = pack_h2((xf.x + of.x) * t0, (xf.y + of.y) * t1);
+                        }
+                        *reinterpret_cast<uint4 *>(drow + c * chunk_row) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+                dev::tc_fence_before();
+            }
+        }
+      }
     } else if (warp < kMmaWarp) {
+      if constexpr (!ATT) {
         // ================= epilogue: warp (q, h) takes TMEM lanes 32q.. (pixels) and half h of
         // each slot's columns; depth-to-space by 3 (groups of 3 channels across the halves) has
         // half 0 take the whole slot
@@ -715,6 +890,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 }
             }
         }
+      }
     } else {
         // ================= MMA issuer (one thread). It takes a stage of RP rows per wait and
         // commit, and waits for the next stage between the rows' MMAs.

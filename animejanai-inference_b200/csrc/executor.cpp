@@ -39,10 +39,16 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
     std::string reason;
     if (!validate_plan(plan, &reason)) return fail(reason);
     if (in_w < 1 || in_h < 1) return fail("bad input size");
+    const int u = plan.unshuffle;
+    // the reference's layout check (src/native/layout.cpp:18)
+    if (in_w % u || in_h % u) return fail("this model needs even video dimensions");
     std::unique_ptr<Executor> e(new Executor());
-    e->W_ = in_w;
-    e->H_ = in_h;
+    e->U_ = u;
+    e->W_ = in_w / u;
+    e->H_ = in_h / u;
     e->R_ = plan.depth_to_space;
+    in_w = e->W_;
+    in_h = e->H_;
 
     for (size_t i = 0; i < plan.steps.size(); i++) {
         const PlanStep &ps = plan.steps[i];
@@ -71,6 +77,15 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
         op.cin = ps.cin;
         op.cout = ps.cout;
         op.w = st.w;
+        if (ps.gate == AJIB_GATE_TANH1X1) {
+            const PlanWeights &pa = ps.att;
+            if (ajib_weights_upload(&st.att, pa.w.data(), pa.bias.data(), nullptr, pa.taps, pa.cin, pa.cout) != AJIB_OK) {
+                ajib_weights_release(&st.w);
+                return fail("weight upload failed (step " + std::to_string(i) + ", attention)");
+            }
+            e->weight_bytes_ += ajib_weights_bytes(st.att);
+            op.att = st.att;
+        }
         op.in_norm = ps.in_norm;
         op.out_clamp = ps.out_clamp;
         for (int c = 0; c < 3; c++) {
@@ -187,8 +202,12 @@ int Executor::launch(const Step &st, const void *in, void *out, int nimg, int im
 
 int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const
 {
+    if (w < 1 || img_h < 1 || nimg < 1 || w % U_ || img_h % U_ || !in || !out) return AJIB_ERR_ARGS;
+    // the conv resolution
+    w /= U_;
+    img_h /= U_;
     const int h = img_h * nimg;
-    if (w < 1 || img_h < 1 || nimg < 1 || w > W_ || h > H_ || !in || !out) return AJIB_ERR_ARGS;
+    if (w > W_ || h > H_) return AJIB_ERR_ARGS;
     const int ns = (int)steps_.size();
     // profiling brackets whole steps (all of a step's bands), so it runs unbanded
     const bool prof = prof_on_ && !prof_ev_.empty();

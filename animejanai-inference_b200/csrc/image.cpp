@@ -296,7 +296,7 @@ extern "C" aji_img_model *aji_img_load(aji_img_ctx *c, const aji_img_model_param
         m->tile_h = p->tile_h > 0 ? p->tile_h : 512;
         m->overlap = p->overlap > 0 ? p->overlap : 128;
         m->flags = p->flags;
-        m->scale = m->plan.depth_to_space;
+        m->scale = ajib::model_scale(m->plan);
         m->execs.resize(c->devs.size());
         for (size_t i = 0; i < c->devs.size(); i++) {
             cudaSetDevice(c->devs[i].device);

@@ -15,8 +15,14 @@
  *   - Conv1x1(Concat(f1..fn)), n = 2..4 -> a concat step;
  *   - the model input scaled and shifted by per-channel constants (Sub / Add / Mul / Div, e.g.
  *     SPAN's (x - mean) * 255) -> the normalisation the first conv applies where it loads;
- *   - Identity, Dropout and casts between float types pass through; nodes off the data path
- *     (shape plumbing) are ignored; anything else on the data path refuses the model, with why.
+ *   - the model input pixel-unshuffled by 2 (PyTorch's Reshape -> Transpose(0,1,3,5,2,4) ->
+ *     Reshape, or SpaceToDepth 2 with its channels reordered) -> the first conv's unshuffled
+ *     input (SPANF3: the conv runs at half resolution, 12 input channels);
+ *   - Identity, Dropout and casts between float types pass through, and so do Pad and Slice
+ *     whose amounts are computed from the input's shape or are zero / open-ended (an exporter's
+ *     alignment to the unshuffle factor, which the even sizes the engine requires make a no-op);
+ *     nodes off the data path (shape plumbing) are ignored; anything else on the data path
+ *     refuses the model, with why.
  */
 #include <algorithm>
 #include <cmath>
@@ -101,6 +107,11 @@ struct Lowering {
     bool norm = false;
     float mean[3] = {0.f, 0.f, 0.f}, scale[3] = {1.f, 1.f, 1.f};
     std::string Xn;                                    // canonical normalised model input
+    struct Unshuffled {
+        bool dcr = false;     // SpaceToDepth order: channel (ry * 2 + rx) * 3 + c
+        bool normed = false;  // of the normalised model input
+    };
+    std::map<std::string, Unshuffled> unshuffled;      // canonical tensor -> the unshuffled input
 
     Lowering(const OnnxModel &m_, Plan &p) : m(m_), plan(p), done(m_.nodes.size(), false) {}
 
@@ -156,6 +167,87 @@ struct Lowering {
         }
         const OnnxTensor *t = constant(name);
         return t && t->to_floats(v);
+    }
+
+    bool ints(const std::string &name, std::vector<int64_t> *v) const
+    {
+        const OnnxTensor *t = constant(name);
+        return t && t->to_ints(v);
+    }
+
+    // Pad / Slice on the data path pass through when they only align the input to the unshuffle
+    // factor: amounts computed at run time (from Shape), zero pads, slices from 0 to an open end
+    // (reference src/native/lower.cpp pass_through_ok).
+    bool pass_through_ok(const OnnxNode &n)
+    {
+        if (n.op == "Pad") {
+            if (n.in.size() < 2 || n.in[1].empty()) {
+                for (int64_t p : n.attr_ints("pads"))
+                    if (p != 0) return fail("Pad by a fixed amount");
+                return true;
+            }
+            std::vector<int64_t> v;
+            if (!constant(n.in[1])) return true;  // computed from the input's shape
+            if (!ints(n.in[1], &v)) return fail("Pad by a fixed amount");
+            for (int64_t p : v)
+                if (p != 0) return fail("Pad by a fixed amount");
+            return true;
+        }
+        // Slice
+        if (n.in.size() < 3) return fail("Slice without starts/ends");
+        std::vector<int64_t> st, en, sp;
+        if (constant(n.in[1])) {
+            if (!ints(n.in[1], &st)) return fail("Slice that crops the start");
+            for (int64_t x : st)
+                if (x != 0) return fail("Slice that crops the start");
+        }
+        if (n.in.size() > 4 && !n.in[4].empty()) {
+            if (!ints(n.in[4], &sp)) return fail("strided Slice");
+            for (int64_t x : sp)
+                if (x != 1) return fail("strided Slice");
+        }
+        if (constant(n.in[2])) {
+            if (!ints(n.in[2], &en)) return fail("Slice by a fixed size");
+            for (int64_t x : en)
+                if (x < (int64_t(1) << 30)) return fail("Slice by a fixed size");
+        }
+        return true;
+    }
+
+    // the sole data node reading t, if it is an op, else -1
+    int sole(const std::string &t, const char *op) const
+    {
+        const std::vector<int> u = uses(t);
+        return u.size() == 1 && node(u[0]).op == op ? u[0] : -1;
+    }
+
+    // Reshape -> Transpose(0,1,3,5,2,4) -> Reshape of the model input: PyTorch's pixel_unshuffle(2)
+    bool lower_unshuffle_reshape(int ri)
+    {
+        const OnnxNode &r1 = node(ri);
+        const int t = sole(r1.out[0], "Transpose");
+        if (t < 0) return fail("a Reshape of the model input that is not a pixel-unshuffle");
+        if (node(t).attr_ints("perm") != std::vector<int64_t>{0, 1, 3, 5, 2, 4})
+            return fail("a Reshape / Transpose of the model input that is not a pixel-unshuffle");
+        const int r2 = sole(node(t).out[0], "Reshape");
+        if (r2 < 0) return fail("a Reshape / Transpose of the model input that is not a pixel-unshuffle");
+        done[(size_t)ri] = done[(size_t)t] = done[(size_t)r2] = true;
+        Unshuffled u;
+        u.normed = !Xn.empty() && canon(r1.in[0]) == Xn;
+        unshuffled[canon(node(r2).out[0])] = u;
+        return true;
+    }
+
+    bool lower_space_to_depth(int si)
+    {
+        const OnnxNode &n = node(si);
+        if (n.attr_i("blocksize", 0) != 2) return fail("SpaceToDepth other than 2x on the model input");
+        done[(size_t)si] = true;
+        Unshuffled u;
+        u.dcr = true;
+        u.normed = !Xn.empty() && canon(n.in[0]) == Xn;
+        unshuffled[canon(n.out[0])] = u;
+        return true;
     }
 
     int new_feature(const std::string &t, int c)
@@ -221,6 +313,30 @@ struct Lowering {
             st.in = AJIB_IN_NCHW3;
             st.src = kModelInput;
             if (src == Xn && norm) {
+                st.in_norm = true;
+                for (int c = 0; c < 3; c++) {
+                    st.in_mean[c] = mean[c];
+                    st.in_scale[c] = scale[c];
+                }
+            }
+        } else if (unshuffled.count(src)) {
+            const Unshuffled u = unshuffled[src];
+            if (st.cin != 12) return fail("the first conv of an unshuffled input reads " + std::to_string(st.cin) + " channels, not 12");
+            st.in = AJIB_IN_NCHW3_UNSHUFFLE2;
+            st.src = kModelInput;
+            plan.unshuffle = 2;
+            if (u.dcr) {
+                // SpaceToDepth's channel (ry * 2 + rx) * 3 + c is the kernel's c * 4 + ry * 2 + rx
+                PlanWeights w2 = st.w;
+                for (int k = 0; k < 12; k++) {
+                    const int from = ((k % 4) / 2 * 2 + k % 2) * 3 + k / 4;
+                    for (int t = 0; t < 9; t++)
+                        for (int o = 0; o < st.cout; o++)
+                            w2.w[((size_t)t * 12 + k) * st.cout + o] = st.w.w[((size_t)t * 12 + from) * st.cout + o];
+                }
+                st.w = w2;
+            }
+            if (u.normed && norm) {
                 st.in_norm = true;
                 for (int c = 0; c < 3; c++) {
                     st.in_mean[c] = mean[c];
@@ -472,7 +588,8 @@ struct Lowering {
             for (const std::string &o : m.nodes[i].out) producer[o] = (int)i;
         // pass-through ops alias their output to their input
         for (const OnnxNode &n : m.nodes)
-            if ((n.op == "Identity" || n.op == "Dropout" || float_cast(n)) && !n.in.empty() && !n.out.empty())
+            if ((n.op == "Identity" || n.op == "Dropout" || float_cast(n) || n.op == "Pad" || n.op == "Slice") &&
+                !n.in.empty() && !n.out.empty())
                 alias[n.out[0]] = n.in[0];
         X = canon(m.inputs[0]);
         Y = canon(m.outputs[0]);
@@ -489,7 +606,7 @@ struct Lowering {
             }
             if (!reads) continue;
             // a pass-through node is its input under another name: not a consumer
-            const bool through = n.op == "Identity" || n.op == "Dropout" || float_cast(n);
+            const bool through = n.op == "Identity" || n.op == "Dropout" || float_cast(n) || n.op == "Pad" || n.op == "Slice";
             for (size_t k = 0; k < n.in.size() && !through; k++)
                 if (!n.in[k].empty() && data.count(canon(n.in[k])) && !(k > 0 && data_input0_only(n.op)))
                     consumers[canon(n.in[k])].push_back((int)i);
@@ -499,6 +616,10 @@ struct Lowering {
             const OnnxNode &n = m.nodes[i];
             if (done[i] || n.out.empty() || !data.count(canon(n.out[0]))) continue;
             if (n.op == "Identity" || n.op == "Dropout" || float_cast(n)) continue;
+            if (n.op == "Pad" || n.op == "Slice") {
+                if (!pass_through_ok(n)) return false;
+                continue;
+            }
             bool ok;
             const std::string in0 = n.in.empty() ? "" : canon(n.in[0]), in1 = n.in.size() > 1 ? canon(n.in[1]) : "";
             const std::string cur_in = Xn.empty() ? X : Xn;
@@ -511,6 +632,10 @@ struct Lowering {
                 ok = lower_norm((int)i);
             } else if (n.op == "Resize" && in0 == X) {
                 continue;  // the skip, taken by the output step
+            } else if (n.op == "Reshape" && in0 == cur_in && plan.steps.empty()) {
+                ok = lower_unshuffle_reshape((int)i);
+            } else if (n.op == "SpaceToDepth" && in0 == cur_in && plan.steps.empty()) {
+                ok = lower_space_to_depth((int)i);
             } else {
                 return fail("op " + n.op + " on the data path is not supported by the native kernels");
             }

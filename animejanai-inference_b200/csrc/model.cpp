@@ -203,8 +203,9 @@ bool validate_plan(const Plan &p, std::string *why)
     const int nf = (int)p.channels.size();
     std::vector<bool> written(nf, false);
     auto readable = [&](int t) { return t == kModelInput || (t >= 0 && t < nf && written[t]); };
-    if (p.depth_to_space < 1 || p.depth_to_space > 4 || p.unshuffle != 1)
-        return fail(why, "unsupported scale (depth-to-space 1..4, no pixel-unshuffle)");
+    if (p.depth_to_space < 1 || p.depth_to_space > 4 || (p.unshuffle != 1 && p.unshuffle != 2) ||
+        p.depth_to_space % p.unshuffle)
+        return fail(why, "unsupported scale (depth-to-space 1..4, pixel-unshuffle 1 or 2, a whole scale)");
     for (size_t i = 0; i < p.steps.size(); i++) {
         const PlanStep &s = p.steps[i];
         const std::string at = "step " + std::to_string(i) + ": ";
@@ -216,11 +217,19 @@ bool validate_plan(const Plan &p, std::string *why)
             if (s.w.taps != 1 || s.w.cin != s.nsrc * s.c || s.w.cout != s.c) return fail(why, at + "concat weights do not match");
         } else if (s.kind == PlanStep::CONV) {
             if (s.w.taps != 9 || s.w.cin != s.cin || s.w.cout != s.cout) return fail(why, at + "conv weights do not match");
-            if (s.in == 1 ? s.src != kModelInput : (!readable(s.src) || s.src < 0 || p.channels[s.src] != s.cin))
+            if (s.in == 1 || s.in == 2) {
+                if (s.src != kModelInput || s.cin != (s.in == 1 ? 3 : 12)) return fail(why, at + "bad conv source");
+                if (p.unshuffle != s.in) return fail(why, at + "the model input's unshuffle does not match the plan's");
+            } else if (s.in != 0 || !readable(s.src) || s.src < 0 || p.channels[s.src] != s.cin) {
                 return fail(why, at + "bad conv source");
+            }
             if (s.gate != 0 && (!readable(s.resid) || s.resid < 0 || p.channels[s.resid] != s.cout))
                 return fail(why, at + "bad gate input");
             if (s.out != 0 && s.resid != -1 && s.resid != kModelInput) return fail(why, at + "bad skip input");
+            if (s.out != 0 && s.resid == kModelInput && p.unshuffle != 1)
+                return fail(why, at + "a model-input skip with a pixel-unshuffled input");
+            if (s.gate == 2 && (s.att.taps != 1 || s.att.cin != s.cout || s.att.cout != s.cout))
+                return fail(why, at + "the tanh gate's 1x1 weights do not match");
             if (s.act == 2 && s.w.slope.size() != (size_t)s.cout) return fail(why, at + "PReLU without slopes");
         } else {
             return fail(why, at + "unknown step kind");
@@ -250,15 +259,19 @@ std::string describe(const Plan &p)
         if (s.kind == PlanStep::CONV && s.out == 0) width = std::max(width, s.cout);
     }
     char b[256];
-    std::snprintf(b, sizeof(b), "%s%s%d kernels (%d conv, %d concat), %d ch, depth-to-space %d", p.name.c_str(),
-                  p.name.empty() ? "" : ": ", convs + cats, convs, cats, width, p.depth_to_space);
+    std::snprintf(b, sizeof(b), "%s%s%d kernels (%d conv, %d concat), %d ch, %sdepth-to-space %d", p.name.c_str(),
+                  p.name.empty() ? "" : ": ", convs + cats, convs, cats, width,
+                  p.unshuffle > 1 ? "pixel-unshuffle 2, " : "", p.depth_to_space);
     return b;
 }
 
 double flops_per_pixel(const Plan &p)
 {
     double f = 0;
-    for (const PlanStep &s : p.steps) f += 2.0 * s.w.taps * s.w.cin * s.w.cout;
+    for (const PlanStep &s : p.steps) {
+        f += 2.0 * s.w.taps * s.w.cin * s.w.cout;
+        if (s.kind == PlanStep::CONV && s.gate == 2) f += 2.0 * s.att.cin * s.att.cout;
+    }
     return f;
 }
 

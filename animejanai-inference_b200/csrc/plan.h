@@ -72,8 +72,11 @@ struct OnnxModel;
 bool lower_onnx(const OnnxModel &m, Plan *plan, std::string *why);
 bool validate_plan(const Plan &p, std::string *why);
 std::string describe(const Plan &p);
-// FLOPs per input pixel (algorithmic: 2 * taps * cin * cout per conv output pixel).
+// FLOPs per conv-resolution pixel (algorithmic: 2 * taps * cin * cout per conv output pixel,
+// plus 2 * cout * cout for a tanh gate's 1x1 attention).
 double flops_per_pixel(const Plan &p);
+// The model's scale: output / input size (depth-to-space over pixel-unshuffle).
+inline int model_scale(const Plan &p) { return p.depth_to_space / (p.unshuffle > 0 ? p.unshuffle : 1); }
 
 class Executor {
 public:
@@ -82,22 +85,24 @@ public:
     Executor(const Executor &) = delete;
     Executor &operator=(const Executor &) = delete;
 
-    int in_w() const { return W_; }
-    int in_h() const { return H_; }
+    // the model input size (U times the conv resolution for a pixel-unshuffled input)
+    int in_w() const { return W_ * U_; }
+    int in_h() const { return H_ * U_; }
     int out_w() const { return W_ * R_; }
     int out_h() const { return H_ * R_; }
-    int scale() const { return R_; }
+    int scale() const { return R_ / U_; }
     size_t device_bytes() const { return bytes_; }
     size_t weight_bytes() const { return weight_bytes_; }
     int launches_per_run() const;
     // bands <= 1: one launch per step over the whole frame; else the banded schedule.
     void set_bands(int bands) { bands_ = bands < 1 ? 1 : bands; }
     int bands() const { return bands_; }
-    // in: NCHW fp16 [3][h][w], out: NCHW fp16 [3][R*h][R*w]; w <= in_w(), h <= in_h().
+    // in: NCHW fp16 [3][h][w], out: NCHW fp16 [3][scale*h][scale*w]; w <= in_w(), h <= in_h(), both
+    // multiples of the plan's unshuffle factor.
     int run(const void *in, void *out, int w, int h, cudaStream_t s) const;
-    int run(const void *in, void *out, cudaStream_t s) const { return run(in, out, W_, H_, s); }
+    int run(const void *in, void *out, cudaStream_t s) const { return run(in, out, in_w(), in_h(), s); }
     // nimg images of img_h rows each, stacked along H (nimg * img_h <= in_h()), each convolved on
-    // its own: in [3][nimg * img_h][w], out [3][R * nimg * img_h][R * w].
+    // its own: in [3][nimg * img_h][w], out [3][scale * nimg * img_h][scale * w].
     int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const;
     // Step timing: while enabled, every launch is bracketed by CUDA events on its stream (a ring of
     // kProfRuns runs); profile_read synchronises and returns per-step summed milliseconds and
@@ -124,7 +129,7 @@ private:
     std::vector<Step> steps_;
     std::vector<void *> buffers_;
     std::vector<void *> tensor_;
-    int W_ = 0, H_ = 0, R_ = 1, bands_ = 1;
+    int W_ = 0, H_ = 0, R_ = 1, U_ = 1, bands_ = 1;  // conv resolution, depth-to-space, unshuffle
     size_t bytes_ = 0, weight_bytes_ = 0;
 };
 

@@ -240,5 +240,17 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over the nthreads threads: every thread gets the same
+// verdict (so a group leaves a loop together).
+__device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool pred)
+{
+    uint32_t r;
+    asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbar.red.and.pred p, %2, %3, q;\nselp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(r)
+                 : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+                 : "memory");
+    return r != 0;
+}
+
 }  // namespace dev
 }  // namespace ajib

@@ -285,7 +285,7 @@ extern "C" aji_ctx *aji_create(const aji_create_params *params)
             c->model_path = params->engine_path;
             c->max_w = params->max_width;
             c->max_h = params->max_height;
-            c->scale = c->plan.depth_to_space;
+            c->scale = model_scale(c->plan);
         }
         if (const char *b = std::getenv("AJIB_BANDS")) c->bands = std::max(1, std::atoi(b));
         return c.release();

@@ -15,6 +15,11 @@ only carries the barrier and the max of the per-rank times.
 net sanity/native_ref.h:run_plan, compiled from the reference sources into oracle/_ref) on the
 host cores, on a bounded sample of the same frame (a band of rows through all 18 steps); where
 that build is absent, the oracle's restatement of it.
+
+--model spanf3 runs the same video path with the shipping AnimeJaNai V3.1 HD "Performance"
+structure instead (SPANF3, 48 features x 5 blocks, 2x pixel-unshuffled input, tanh 1x1 gates,
+depth-to-space 4): not a BASELINE config, but the reference publishes a number for it
+(2.02-2.06 ms per 1080p chain on an RTX 5090).
 """
 import argparse
 import ctypes as C
@@ -33,6 +38,15 @@ sys.path.insert(0, os.path.join(ROOT, "animejanai-inference_b200"))
 W_IN, H_IN, SCALE = 1920, 1080, 2
 MODEL_SEED = 1
 METRIC = "frames/s 1080p->4K 2x Compact fp16 at 1/2/4/8 B200; % tensor-core peak"
+METRIC_SPANF3 = "frames/s 1080p->4K 2x SPANF3 b5f48 unshuffle fp16 (video chain)"
+SPANF3_PUBLISHED_MS = 2.02  # the reference on an RTX 5090, Linux (BENCHMARKS.md:257)
+
+
+def bench_plan(model):
+    import ajib
+    if model == "spanf3":
+        return ajib.spanf3_plan(MODEL_SEED, c=48, blocks=5, gain=0.7)
+    return ajib.compact_plan(MODEL_SEED)
 # DRAM bytes (read + write) of one body-conv launch at 1920x1080, from the ncu capture summarised
 # in profiles/conv3x3_body_64x64_1080p.txt (the roofline's "traffic")
 BODY_TRAFFIC_BYTES = 498.3e6
@@ -123,13 +137,12 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline_sample(rows=16, nthreads=0):
-    """The reference CPU path on a bounded sample: a W_IN x rows band of the Compact net (all 18
-    steps), timed on the host cores. Uses oracle/_ref (the reference's run_plan compiled from its
-    own sources) when built, else the oracle's restatement. Returns (frames/s, cores, kind, sample)."""
-    import ajib
+def cpu_baseline_sample(rows=16, nthreads=0, model="compact"):
+    """The reference CPU path on a bounded sample: a W_IN x rows band of the net (all its steps),
+    timed on the host cores. Uses oracle/_ref (the reference's run_plan compiled from its own
+    sources) when built, else the oracle's restatement. Returns (frames/s, cores, kind, sample)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
-    plan = ajib.compact_plan(MODEL_SEED)
+    plan = bench_plan(model)
     rng = np.random.default_rng(7)
     x = rng.uniform(0, 1, size=(3, rows, W_IN)).astype(np.float16).astype(np.float32)
     ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_net.so")
@@ -149,7 +162,8 @@ def cpu_baseline_sample(rows=16, nthreads=0):
         cores = nthreads if nthreads > 0 else os.cpu_count()
         kind = "port"
     fps = (rows * W_IN) / (H_IN * W_IN) / dt
-    return fps, cores, kind, f"{W_IN}x{rows} band of the 1080p frame through all 18 steps ({dt:.2f} s)"
+    return fps, cores, kind, (f"{W_IN}x{rows} band of the 1080p frame through all {len(plan['steps'])} steps "
+                              f"({dt:.2f} s)")
 
 
 def run_reference(args, rank, world):
@@ -158,16 +172,20 @@ def run_reference(args, rank, world):
     vals = []
     info = None
     for i in range(args.warmup + args.steps):
-        fps, cores, kind, sample = cpu_baseline_sample(rows=16)
+        fps, cores, kind, sample = cpu_baseline_sample(rows=16, model=args.model)
         if i >= args.warmup:
             vals.append(fps)
         info = (cores, kind, sample)
     v = float(np.mean(vals))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+    spanf3 = args.model == "spanf3"
+    line = {"impl": "reference", "metric": METRIC_SPANF3 if spanf3 else METRIC, "value": v, "unit": "frames/s",
+            "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "BASELINE config 1 (Compact 2x 1080p P010 -> 4K), CPU reference net on a band sample",
-                       "model": "SRVGGNetCompact 64x16 2x random-init"},
+            "config": {"workload": ("SPANF3 b5f48 unshuffle 2x 1080p P010 -> 4K" if spanf3 else
+                                    "BASELINE config 1 (Compact 2x 1080p P010 -> 4K)") +
+                       ", CPU reference net on a band sample",
+                       "model": "SPANF3 48x5 unshuffle random-init" if spanf3 else "SRVGGNetCompact 64x16 2x random-init"},
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": info[0], "kind": info[1], "sample": info[2]},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -191,10 +209,11 @@ def run_ours(args, rank, world, local_rank, dist):
     dev = torch.device("cuda", local_rank)
     hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
 
-    # model file (seeded random init, the config-1 architecture)
-    plan = ajib.compact_plan(MODEL_SEED)
+    # model file (seeded random init, the config-1 architecture or SPANF3)
+    plan = bench_plan(args.model)
+    spanf3 = args.model == "spanf3"
     mdir = tempfile.mkdtemp(prefix="ajib_bench_")
-    mpath = os.path.join(mdir, "compact_2x.ajnm")
+    mpath = os.path.join(mdir, f"{args.model}_2x.ajnm")
     with open(mpath, "wb") as f:
         f.write(ajib.model_bytes(plan))
     torch.zeros(1, device=dev)
@@ -312,35 +331,55 @@ def run_ours(args, rank, world, local_rank, dist):
     value = frames_total / (t_ms / 1000.0)
     e2e_value = frames_total / (e2e_ms / 1000.0)
 
-    # roofline of the dominant kernel: the 16 body convs (64 -> 64 + PReLU, steps 1..16)
-    flops_body = 2.0 * 9 * 64 * 64 * W_IN * H_IN
+    # roofline of the dominant kernel: the body convs (Compact: 16 x 64 -> 64 + PReLU; SPANF3:
+    # 15 x 48 -> 48, ReLU or the tanh gate with its 1x1 attention GEMM), FLOPs at conv resolution
+    u = plan.get("unshuffle", 1)
+    cpx = (W_IN // u) * (H_IN // u)
+    body = [k for k, st in enumerate(plan["steps"])
+            if st["kind"] == 0 and st.get("in_", 0) == 0 and st.get("out", 0) == 0]
+    flops_steps = [2.0 * 9 * plan["steps"][k]["cin"] * plan["steps"][k]["cout"] * cpx +
+                   (2.0 * plan["steps"][k]["cout"] ** 2 * cpx if plan["steps"][k].get("gate", 0) == 2 else 0.0)
+                   for k in body]
     body_ms = None
-    if prof and step_n[1] > 0:
-        body_ms = float(np.sum(step_ms[1:17]) / np.sum(step_n[1:17]))
+    if prof and all(step_n[k] > 0 for k in body):
+        body_ms = float(sum(step_ms[k] / step_n[k] for k in body) / len(body))
     roof = None
     if body_ms:
+        flops_body = float(np.mean(flops_steps))
         achieved = flops_body / (body_ms / 1000.0) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_sus, "unit": "TFLOP/s",
-                "frac": achieved / tflops_sus, "traffic": BODY_TRAFFIC_BYTES,
-                "kernel": "k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)",
+                "frac": achieved / tflops_sus, "traffic": None if spanf3 else BODY_TRAFFIC_BYTES,
+                "kernel": ("k_conv3x3_tc<48,64> (SPANF3 body convs 48->48, ReLU / tanh gate, 960x540)" if spanf3 else
+                           "k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)"),
                 "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json)",
                 "flops_per_launch": flops_body,
                 "frame_tflops": plan_flops(plan) / (t_ms / args.steps / 1000.0) / 1e12}
 
-    line = {"metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+    nsteps = len(plan["steps"])
+    if spanf3:
+        workload = "SPANF3 b5f48 2x video (2x pixel-unshuffle, tanh gates), 1920x1080 P010 BT.709 limited -> 3840x2160 P010"
+        model = "SPANF3 48 feat x 5 blocks, unshuffle 2, depth-to-space 4, random-init (seed 1, 0.7 He)"
+    else:
+        workload = "BASELINE config 1: Compact 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010"
+        model = "SRVGGNetCompact 64 feat x 16 body, PReLU, pixel_shuffle 2, random-init (seed 1)"
+    line = {"metric": METRIC_SPANF3 if spanf3 else METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 1: Compact 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010",
-                       "model": "SRVGGNetCompact 64 feat x 16 body, PReLU, pixel_shuffle 2, random-init (seed 1)",
+            "vs_baseline": (value / world) / (1000.0 / SPANF3_PUBLISHED_MS) if spanf3 else None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": workload, "model": model,
                        "global_batch": world, "parallelism": f"frame-parallel x{world} (replicas, no collectives)",
-                       "l2": "inputs larger than L2 (two 265 MB activation buffers per frame)",
+                       "l2": "inputs larger than L2 (activation buffers of 66-265 MB per frame)",
                        "bands": args.bands},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * (2 + 18 * max(1, args.bands)),
+            "gpu_launches": args.steps * (2 + nsteps * max(1, args.bands)),
             "clocks": clk}
+    if spanf3:
+        line["config"]["published"] = (f"reference {SPANF3_PUBLISHED_MS} ms per 1080p chain on an RTX 5090 "
+                                       "(BENCHMARKS.md:257); vs_baseline is per GPU")
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, kind, sample = cpu_baseline_sample(rows=16)
+        fps, cores, kind, sample = cpu_baseline_sample(rows=16, model=args.model)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": kind, "sample": sample}
     vid.close()
     print(json.dumps(line), flush=True)
@@ -435,7 +474,15 @@ def run_kernel(args):
 
 
 def plan_flops(plan):
-    return sum(2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2] for s in plan["steps"]) * W_IN * H_IN
+    """Algorithmic FLOPs of one 1080p frame: every step's 2 * taps * cin * cout (plus a tanh gate's
+    2 * cout^2) per conv-resolution pixel."""
+    u = plan.get("unshuffle", 1)
+    per_px = 0.0
+    for s in plan["steps"]:
+        per_px += 2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2]
+        if s["kind"] == 0 and s.get("gate", 0) == 2:
+            per_px += 2.0 * s["cout"] ** 2
+    return per_px * (W_IN // u) * (H_IN // u)
 
 
 def main():
@@ -449,6 +496,8 @@ def main():
     ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", default="compact", choices=["compact", "spanf3"],
+                    help="compact: BASELINE config 1 (the headline); spanf3: the shipping SPANF3 structure")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -54,7 +54,10 @@ AJIB_EXPORT void ajib_weights_release(ajib_weights **w);
 AJIB_EXPORT size_t ajib_weights_bytes(const ajib_weights *w);
 
 /* ---- one fused 3x3 conv (reference src/native/conv.h:53-66, struct Conv3x3) ----
- * Logical channel counts: an NCHW3 input has cin 3; a D2S1/2/3/4 output has cout 3/12/27/48. */
+ * Logical channel counts: an NCHW3 input has cin 3, a pixel-unshuffled one (NCHW3_UNSHUFFLE2,
+ * channel c * 4 + ry * 2 + rx of the input [3][2H][2W]) 12; a D2S1/2/3/4 output has cout
+ * 3/12/27/48. AJIB_GATE_TANH1X1 computes (x + fp16(o)) * tanh(att(fp16(o))), att the 1x1 conv in
+ * `att` (uploaded with taps 1, cin = cout = the op's cout). */
 typedef struct ajib_conv {
     int in, act, gate, out; /* enum ajib_input / ajib_act / ajib_gate / ajib_output */
     int cin, cout;
@@ -87,10 +90,11 @@ AJIB_EXPORT size_t ajib_feature_bytes(int H, int W, int C);
 
 /* Launch op at conv resolution H x W on output rows [row_begin, row_end) (row_end <= 0: all
  * rows) (reference src/native/conv.h:91, launch). src: a row-chunked map [H][cin] or the NCHW
- * fp16 model input [3][H][W]. resid: gates read the block input x as a row-chunked map
- * [H][cout]; depth-to-space outputs add the NCHW model input [3][H][W] (nearest upsampled) when
- * resid is not NULL. dst: a row-chunked map [H][cout] or NCHW [3][R*H][R*W]. Rows outside the
- * range are neither read beyond the one-row halo nor written, so a frame can be run as bands. */
+ * fp16 model input [3][H][W] ([3][2H][2W] pixel-unshuffled). resid: gates read the block input x
+ * as a row-chunked map [H][cout]; depth-to-space outputs add the NCHW model input [3][H][W]
+ * (nearest upsampled) when resid is not NULL (not with a pixel-unshuffled input: AJIB_ERR_ARGS).
+ * dst: a row-chunked map [H][cout] or NCHW [3][R*H][R*W]. Rows outside the range are neither
+ * read beyond the one-row halo nor written, so a frame can be run as bands. */
 AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                     int row_begin, int row_end, void *stream);
 

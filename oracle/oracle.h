@@ -28,13 +28,19 @@ void orc_f2h_array(const float *x, uint16_t *out, size_t n);
 void orc_h2f_array(const uint16_t *h, float *out, size_t n);
 
 /* One fused 3x3 conv step of a lowered plan (sanity/native_ref.h:53-118), at conv resolution
- * H x W. in_mode 0: src NHWC [H][W][cin]; 1: src NCHW [3][H][W] (the model input, cin 3).
+ * H x W. in_mode 0: src NHWC [H][W][cin]; 1: src NCHW [3][H][W] (the model input, cin 3);
+ * 2: src NCHW [3][2H][2W] pixel-unshuffled by 2 (cin 12, channel c * 4 + ry * 2 + rx).
  * w: [9][cin][cout] (fp16-valued floats), bias [cout], slope [cout] (act 2) or NULL.
- * act 0 none, 1 ReLU, 2 PReLU, 3 SiLU; gate 0 none, 1 residual, 2 (not supported here),
- * 3 sigmoid-half with resid NHWC [H][W][cout]. R == 0: dst NHWC [H][W][cout], each value
+ * act 0 none, 1 ReLU, 2 PReLU, 3 SiLU; gate 0 none, 1 residual, 2 tanh 1x1
+ * ((x + fp16(o)) * tanh(att_bias + att_w^T fp16(o)), att_w [cout][cout] fp16-valued), 3
+ * sigmoid-half, with resid NHWC [H][W][cout]. R == 0: dst NHWC [H][W][cout], each value
  * rounded to fp16. R in 1..4: depth-to-space (CRD) into dst NCHW [3][R*H][R*W] plus model_in
- * NCHW [3][H][W] (nearest upsampled) when not NULL, clamped to [0,1] if out_clamp, rounded to
- * fp16. Accumulates in double. nthreads <= 0: all cores. Returns 0, or -1 on bad arguments. */
+ * NCHW [3][H][W] (nearest upsampled) when not NULL (in_mode 0 and 1 only), clamped to [0,1] if
+ * out_clamp, rounded to fp16. Accumulates in double. nthreads <= 0: all cores. Returns 0, or -1
+ * on bad arguments. orc_conv3x3 is the same without the attention weights (gate 2 refused). */
+int orc_conv3x3_ex(int in_mode, const float *src, int H, int W, int cin, const float *w, const float *bias,
+                   const float *slope, int cout, int act, int gate, const float *resid, const float *att_w,
+                   const float *att_bias, int R, const float *model_in, int out_clamp, float *dst, int nthreads);
 int orc_conv3x3(int in_mode, const float *src, int H, int W, int cin, const float *w, const float *bias,
                 const float *slope, int cout, int act, int gate, const float *resid, int R, const float *model_in,
                 int out_clamp, float *dst, int nthreads);

@@ -75,12 +75,16 @@ static inline float input_at(int in_mode, const float *src, int H, int W, int ci
 {
     if (y < 0 || y >= H || x < 0 || x >= W) return 0.f;  /* pad 1 with zeros */
     if (in_mode == 0) return src[((size_t)y * W + x) * cin + c];
-    return src[((size_t)c * H + y) * W + x];  /* NCHW model input */
+    if (in_mode == 1) return src[((size_t)c * H + y) * W + x];  /* NCHW model input */
+    /* the model input [3][2H][2W] pixel-unshuffled by 2: channel c = cc * 4 + ry * 2 + rx
+     * (sanity/native_ref.h:66-67) */
+    const int cc = c / 4, ry = (c / 2) % 2, rx = c % 2;
+    return src[((size_t)cc * 2 * H + 2 * y + ry) * 2 * W + 2 * x + rx];
 }
 
 struct conv_job {
     int in_mode, H, W, cin, cout, act, gate, R, out_clamp;
-    const float *src, *w, *bias, *slope, *resid, *model_in;
+    const float *src, *w, *bias, *slope, *resid, *att_w, *att_bias, *model_in;
     float *dst;
 };
 
@@ -100,39 +104,64 @@ static void conv_row(void *ctx, int y)
                 for (int n = 0; n < cout; n++) acc[n] += (double)v * wr[n];
             }
         const size_t p = (size_t)y * W + x;
+        float o[256];
         for (int n = 0; n < cout; n++) {
             float v = (float)acc[n];
             if (j->act == 1) v = fmaxf(v, 0.f);
             if (j->act == 2) v = v >= 0.f ? v : v * j->slope[n];
             if (j->act == 3) v = v / (1.f + expf(-v));
+            o[n] = v;
+        }
+        /* the tanh 1x1 gate's attention: att_bias + att_w^T fp16(o), in double (native_ref.h:93-99) */
+        float ga[256];
+        if (j->gate == 2)
+            for (int n = 0; n < cout; n++) {
+                double a = j->att_bias[n];
+                for (int k = 0; k < cout; k++) a += (double)f16r(o[k]) * j->att_w[(size_t)k * cout + n];
+                ga[n] = (float)a;
+            }
+        for (int n = 0; n < cout; n++) {
+            float v = o[n];
             if (j->gate == 1) v = j->resid[p * cout + n] + v;
+            if (j->gate == 2) v = (j->resid[p * cout + n] + f16r(v)) * tanhf(ga[n]);
             if (j->gate == 3) v = (j->resid[p * cout + n] + v) * (1.f / (1.f + expf(-v)) - 0.5f);
             if (R == 0) {
                 j->dst[p * cout + n] = f16r(v);
             } else if (n < 3 * R * R) {
                 const int c3 = n / (R * R), ry = (n / R) % R, rx = n % R;
                 const float add = j->model_in ? j->model_in[((size_t)c3 * H + y) * W + x] : 0.f;
-                float o = v + add;
-                if (j->out_clamp) o = fminf(fmaxf(o, 0.f), 1.f);
-                j->dst[((size_t)c3 * OH + (size_t)R * y + ry) * OW + (size_t)R * x + rx] = f16r(o);
+                float out = v + add;
+                if (j->out_clamp) out = fminf(fmaxf(out, 0.f), 1.f);
+                j->dst[((size_t)c3 * OH + (size_t)R * y + ry) * OW + (size_t)R * x + rx] = f16r(out);
             }
         }
     }
+}
+
+int orc_conv3x3_ex(int in_mode, const float *src, int H, int W, int cin, const float *w, const float *bias,
+                   const float *slope, int cout, int act, int gate, const float *resid, const float *att_w,
+                   const float *att_bias, int R, const float *model_in, int out_clamp, float *dst, int nthreads)
+{
+    if (!src || !w || !bias || !dst || H < 1 || W < 1 || cin < 1 || cout < 1 || cout > 256) return -1;
+    if (in_mode < 0 || in_mode > 2 || (in_mode == 1 && cin != 3) || (in_mode == 2 && cin != 12)) return -1;
+    if (gate && !resid) return -1;
+    if (gate == 2 && (!att_w || !att_bias)) return -1;
+    if (act == 2 && !slope) return -1;
+    if (R < 0 || R > 4 || (R > 0 && cout < 3 * R * R)) return -1;
+    if (in_mode == 2 && model_in) return -1; /* no skip from an unshuffled input */
+    struct conv_job j = {in_mode, H,     W,        cin,      cout,     act, gate,  R, out_clamp, src, w, bias, slope,
+                         resid,   att_w, att_bias, model_in, dst};
+    orc_par_for(H, nthreads, conv_row, &j);
+    return 0;
 }
 
 int orc_conv3x3(int in_mode, const float *src, int H, int W, int cin, const float *w, const float *bias,
                 const float *slope, int cout, int act, int gate, const float *resid, int R, const float *model_in,
                 int out_clamp, float *dst, int nthreads)
 {
-    if (!src || !w || !bias || !dst || H < 1 || W < 1 || cin < 1 || cout < 1 || cout > 256) return -1;
-    if (in_mode == 1 && cin != 3) return -1;
-    if ((gate == 1 || gate == 3) && !resid) return -1;
     if (gate == 2) return -1;
-    if (act == 2 && !slope) return -1;
-    if (R < 0 || R > 4 || (R > 0 && cout < 3 * R * R)) return -1;
-    struct conv_job j = {in_mode, H, W, cin, cout, act, gate, R, out_clamp, src, w, bias, slope, resid, model_in, dst};
-    orc_par_for(H, nthreads, conv_row, &j);
-    return 0;
+    return orc_conv3x3_ex(in_mode, src, H, W, cin, w, bias, slope, cout, act, gate, resid, NULL, NULL, R, model_in,
+                          out_clamp, dst, nthreads);
 }
 
 struct cat_job {

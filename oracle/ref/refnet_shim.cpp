@@ -13,13 +13,16 @@ struct ref_step {
     const uint16_t *w;  // [taps][cin][cout]
     const float *bias;  // [cout]
     const float *slope; // [cout] or null
+    const uint16_t *att_w;   // gate 2: the 1x1 attention conv [cout][cout], else null
+    const float *att_bias;   // gate 2: [cout]
 };
 
+// in: NCHW [3][h][w]; out: NCHW [3][h * depth_to_space / unshuffle][w * depth_to_space / unshuffle]
 extern "C" int ref_run_plan(const ref_step *steps, int nsteps, const int *channels, int nfeat, int depth_to_space,
-                            const float *in, int w, int h, float *out)
+                            int unshuffle, const float *in, int w, int h, float *out)
 {
     ajinative::Plan p;
-    p.unshuffle = 1;
+    p.unshuffle = unshuffle;
     p.depth_to_space = depth_to_space;
     p.channels.assign(channels, channels + nfeat);
     for (int i = 0; i < nsteps; i++) {
@@ -45,6 +48,12 @@ extern "C" int ref_run_plan(const ref_step *steps, int nsteps, const int *channe
         s.w.w.assign(r.w, r.w + (size_t)r.taps * cin * cout);
         s.w.bias.assign(r.bias, r.bias + cout);
         if (r.slope) s.w.slope.assign(r.slope, r.slope + cout);
+        if (r.att_w) {
+            s.att.taps = 1;
+            s.att.cin = s.att.cout = cout;
+            s.att.w.assign(r.att_w, r.att_w + (size_t)cout * cout);
+            s.att.bias.assign(r.att_bias, r.att_bias + cout);
+        }
         p.steps.push_back(std::move(s));
     }
     std::vector<float> x(in, in + (size_t)3 * w * h);

@@ -4,7 +4,8 @@ present; the vectors are committed and the CPU tests need only them):
 
   conv_plans.npz   outputs of the reference's CPU reference net (sanity/native_ref.h:run_plan)
                    for small seeded plans of each family: Compact 2x, SuperUltraCompact 4x, SPAN 2x
-                   (gates, SiLU, concat). Inputs and weights are regenerated from the seeds.
+                   (gates, SiLU, concat), SPANF3 2x (pixel-unshuffled input, tanh 1x1 gates,
+                   ReLU, depth-to-space 4). Inputs and weights are regenerated from the seeds.
   resample.npz     the reference's zimg filter tables (src/resample.h:compute) for the chroma
                    passes of the BASELINE sizes and every siting, and aji_csp constants
                    (src/resample.h:make_csp) for every format / matrix / range.
@@ -31,6 +32,7 @@ PLANS = [
     ("compact", dict(kind="compact", c=64, body=3, scale=2), 101, 12, 20),
     ("suc", dict(kind="compact", c=24, body=2, scale=4), 102, 9, 14),
     ("span", dict(kind="span", c=48, blocks=2, scale=2), 103, 10, 16),
+    ("spanf3", dict(kind="spanf3", c=48, blocks=2), 104, 12, 20),
 ]
 RESAMPLE = [  # (src, dst, siting, up)
     (960, 1920, 1, 1), (540, 1080, 1, 1), (960, 1920, 2, 1), (540, 1080, 3, 1), (31, 62, 1, 1),
@@ -46,6 +48,8 @@ def plan_for(spec, seed):
     import ajib
     if spec["kind"] == "compact":
         return ajib.compact_plan(seed, c=spec["c"], body=spec["body"], scale=spec["scale"])
+    if spec["kind"] == "spanf3":
+        return ajib.spanf3_plan(seed, c=spec["c"], blocks=spec["blocks"])
     return ajib.span_plan(seed, c=spec["c"], blocks=spec["blocks"], scale=spec["scale"])
 
 

@@ -216,3 +216,48 @@ def export_span(plan, **kw):
             o = g.node("Mul", [add, sub])
         t[s["dst"]] = o
     return g.model()
+
+
+def export_spanf3(plan, space_to_depth=False, wdtype=1):
+    """A SPANF3 plan (animejanai-inference_b200/ajib.py spanf3_plan) as PyTorch exports the
+    network: the input padded to the unshuffle factor and the output cropped back (both by
+    amounts computed from the input's Shape), the 2x pixel-unshuffle as Reshape -> Transpose ->
+    Reshape (or SpaceToDepth, whose DCR channel order the head conv's weights follow), each block's
+    gate as Add(x, c3) * Tanh(Conv1x1(c3)), and the last step's DepthToSpace 4."""
+    g = Graph(wdtype)
+    steps = plan["steps"]
+    shp = g.node("Shape", ["input"])
+    hdim = g.node("Gather", [shp, g.init(np.array([2]), "i", dtype=7)], axis=0)
+    padded = g.node("Pad", ["input", hdim], mode="reflect")
+    head = steps[0]
+    w0 = np.asarray(head["w"], np.float32)
+    if space_to_depth:
+        u = g.node("SpaceToDepth", [padded], blocksize=2)
+        # ONNX channel j = (ry * 2 + rx) * 3 + c holds the plan's channel k = c * 4 + ry * 2 + rx
+        perm = np.zeros(12, np.int64)
+        for k in range(12):
+            perm[((k % 4) // 2 * 2 + k % 2) * 3 + k // 4] = k
+        w0 = w0[:, perm, :]
+    else:
+        r1 = g.node("Reshape", [padded, shp])
+        tr = g.node("Transpose", [r1], perm=[0, 1, 3, 5, 2, 4])
+        u = g.node("Reshape", [tr, shp])
+    t = {head["dst"]: g.conv(u, w0, head["bias"], 3)}
+    for s in steps[1:]:
+        if s["kind"] == 1:
+            cat = g.node("Concat", [t[f] for f in s["srcs"]], axis=1)
+            t[s["dst"]] = g.conv(cat, np.asarray(s["w"], np.float32), s["bias"], 1)
+            continue
+        o = g.conv(t[s["src"]], s["w"], s["bias"], 3)
+        if s.get("out", 0):
+            d = g.node("DepthToSpace", [o], blocksize=4, mode="CRD")
+            g.node("Slice", [d, g.init(np.array([0]), "z", dtype=7), hdim], ["output"])
+            continue
+        if s.get("act", 0) == 1:
+            o = g.node("Relu", [o])
+        if s.get("gate", 0) == 2:
+            add = g.node("Add", [t[s["resid"]], o])
+            att = g.node("Tanh", [g.conv(o, s["att"][0], s["att"][1], 1)])
+            o = g.node("Mul", [add, att])
+        t[s["dst"]] = o
+    return g.model()

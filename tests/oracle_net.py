@@ -8,9 +8,18 @@ MODEL_INPUT, MODEL_OUTPUT = -2, -3
 D2S = {0: 0, 1: 2, 2: 4, 3: 1, 4: 3}
 
 
+def _att(s):
+    """The tanh gate's 1x1 weights as [cout][cout] fp16-valued floats and the bias."""
+    w, b = s["att"][0], s["att"][1]
+    return np.asarray(w, np.float32).astype(np.float16).astype(np.float32).reshape(s["cout"], s["cout"]), b
+
+
 def run_plan(plan, x, nthreads=0):
-    """x: NCHW float32 [3][h][w] (fp16-valued). Returns NCHW [3][R*h][R*w] float32 (fp16-valued)."""
+    """x: NCHW float32 [3][h][w] (fp16-valued). Returns NCHW [3][R*h/u][R*w/u] float32 (fp16-valued),
+    u the plan's pixel-unshuffle factor (the conv resolution is h/u x w/u)."""
+    u = plan.get("unshuffle", 1)
     _, h, w = x.shape
+    h, w = h // u, w // u
     feats = {}
     out = None
     for s in plan["steps"]:
@@ -21,7 +30,7 @@ def run_plan(plan, x, nthreads=0):
             feats[s["dst"]] = y.reshape(h, w, s["c"])
             continue
         src = x if s["src"] == MODEL_INPUT else feats[s["src"]]
-        in_mode = 1 if s["src"] == MODEL_INPUT else 0
+        in_mode = (2 if s.get("in_", 1) == 2 else 1) if s["src"] == MODEL_INPUT else 0
         R = D2S[s.get("out", 0)]
         resid = None
         model_in = None
@@ -31,7 +40,8 @@ def run_plan(plan, x, nthreads=0):
             model_in = x
         y = oracle_conv(src, in_mode, h, w, s["cin"], wq, s["bias"], s.get("slope"), s["cout"], act=s.get("act", 0),
                         gate=s.get("gate", 0), resid=resid, R=R, model_in=model_in,
-                        out_clamp=bool(s.get("out_clamp")), nthreads=nthreads)
+                        out_clamp=bool(s.get("out_clamp")), nthreads=nthreads,
+                        att=_att(s) if s.get("gate", 0) == 2 else None)
         if s["dst"] == MODEL_OUTPUT:
             out = y
         else:

@@ -13,14 +13,15 @@ class RefStep(C.Structure):
     _fields_ = [("kind", C.c_int), ("in_", C.c_int), ("act", C.c_int), ("gate", C.c_int), ("out", C.c_int),
                 ("cin", C.c_int), ("cout", C.c_int), ("src", C.c_int), ("resid", C.c_int), ("dst", C.c_int),
                 ("c", C.c_int), ("nsrc", C.c_int), ("srcs", C.c_int * 4), ("taps", C.c_int),
-                ("w", C.c_void_p), ("bias", C.c_void_p), ("slope", C.c_void_p)]
+                ("w", C.c_void_p), ("bias", C.c_void_p), ("slope", C.c_void_p), ("att_w", C.c_void_p),
+                ("att_bias", C.c_void_p)]
 
 
 def _lib(path):
     if path not in _libs:
         lib = C.CDLL(path)
-        lib.ref_run_plan.argtypes = [C.POINTER(RefStep), C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int, C.c_void_p,
-                                     C.c_int, C.c_int, C.c_void_p]
+        lib.ref_run_plan.argtypes = [C.POINTER(RefStep), C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int, C.c_int,
+                                     C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         lib.ref_run_plan.restype = C.c_int
         lib.ref_threads.restype = C.c_int
         _libs[path] = lib
@@ -32,7 +33,7 @@ def threads(path, nthreads=0):
 
 
 def run_plan(path, plan, x, nthreads=0):
-    """x: NCHW float32 [3][h][w]. Returns the reference's NCHW output [3][R*h][R*w]."""
+    """x: NCHW float32 [3][h][w]. Returns the reference's NCHW output [3][R*h/u][R*w/u]."""
     lib = _lib(path)
     keep = []
     steps = (RefStep * len(plan["steps"]))()
@@ -53,12 +54,18 @@ def run_plan(path, plan, x, nthreads=0):
         r.taps = w.shape[0]
         r.w, r.bias = w.ctypes.data, b.ctypes.data
         r.slope = None if sl is None else sl.ctypes.data
+        r.att_w = r.att_bias = None
+        if s.get("gate", 0) == 2:
+            aw = np.ascontiguousarray(np.asarray(s["att"][0], np.float32).astype(np.float16).view(np.uint16))
+            ab = np.ascontiguousarray(s["att"][1], np.float32)
+            keep += [aw, ab]
+            r.att_w, r.att_bias = aw.ctypes.data, ab.ctypes.data
     ch = (C.c_int * len(plan["channels"]))(*plan["channels"])
     x = np.ascontiguousarray(x, np.float32)
     _, h, wd = x.shape
-    R = plan["depth_to_space"]
-    out = np.zeros((3, R * h, R * wd), np.float32)
-    rc = lib.ref_run_plan(steps, len(plan["steps"]), ch, len(plan["channels"]), R, x.ctypes.data, wd, h,
+    R, u = plan["depth_to_space"], plan.get("unshuffle", 1)
+    out = np.zeros((3, R * h // u, R * wd // u), np.float32)
+    rc = lib.ref_run_plan(steps, len(plan["steps"]), ch, len(plan["channels"]), R, u, x.ctypes.data, wd, h,
                           out.ctypes.data)
     assert rc == 0
     return out

@@ -21,7 +21,7 @@ def _plans():
     return mg
 
 
-@pytest.mark.parametrize("idx", [0, 1, 2])
+@pytest.mark.parametrize("idx", [0, 1, 2, 3])
 def test_oracle_net_matches_reference_golden(idx):
     from oracle_net import run_plan
     mg = _plans()
@@ -40,8 +40,10 @@ def test_oracle_net_matches_reference_live(seed):
     import refnet
     from oracle_net import run_plan
     for plan in (ajib.compact_plan(seed, body=2), ajib.span_plan(seed, c=16, blocks=2),
-                 ajib.compact_plan(seed, c=24, body=1, scale=4)):
-        x = np.random.default_rng(seed).uniform(0, 1, size=(3, 11, 17)).astype(np.float16).astype(np.float32)
+                 ajib.compact_plan(seed, c=24, body=1, scale=4), ajib.spanf3_plan(seed, c=16, blocks=2)):
+        # an unshuffled model takes even sizes
+        h, w = (12, 18) if plan.get("unshuffle", 1) == 2 else (11, 17)
+        x = np.random.default_rng(seed).uniform(0, 1, size=(3, h, w)).astype(np.float16).astype(np.float32)
         assert np.array_equal(run_plan(plan, x), refnet.run_plan(REF_NET, plan, x))
 
 

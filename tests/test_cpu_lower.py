@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from onnx_writer import Graph, export, export_span
+from onnx_writer import Graph, export, export_span, export_spanf3
 from util import ROOT
 
 REF_LOWER = os.path.join(ROOT, "oracle", "_ref", "libref_lower.so")
@@ -53,6 +53,12 @@ def same_plan(got, want, norm=None, clamp=False, f16_params=False):
         assert np.array_equal(g["bias"], rnd(w["bias"])), i
         if w.get("slope") is not None:
             assert np.array_equal(g["slope"], rnd(w["slope"])), i
+        if w.get("gate", 0) == 2:
+            aw = np.asarray(w["att"][0], np.float32)
+            assert np.array_equal(g["att"][0].astype(np.float16).view(np.uint16),
+                                  aw.reshape(g["att"][0].shape).astype(np.float16).view(np.uint16)), i
+            assert np.array_equal(g["att"][1], rnd(w["att"][1])), i
+    assert got.get("unshuffle", 1) == want.get("unshuffle", 1)
     first = got["steps"][0]
     if norm is not None:
         mean, scale = norm
@@ -97,6 +103,34 @@ def test_span(merged):
     same_plan(lowered(onnx), plan)
 
 
+@pytest.mark.parametrize("s2d", [False, True])
+@pytest.mark.parametrize("c,blocks", [(48, 5), (64, 8), (16, 2)])
+def test_spanf3(s2d, c, blocks):
+    """SPANF3 with the 2x pixel-unshuffle (Reshape/Transpose or SpaceToDepth), the input Pad and
+    output Slice computed from the input's shape, tanh gates, ReLU convs, depth-to-space 4."""
+    import ajib
+    plan = ajib.spanf3_plan(60 + c, c=c, blocks=blocks)
+    got = lowered(export_spanf3(plan, space_to_depth=s2d))
+    same_plan(got, plan)
+    assert len(got["steps"]) == 3 * blocks + 3 and got["depth_to_space"] == 4 and got["unshuffle"] == 2
+    assert got["steps"][0]["in_"] == 2 and got["steps"][0]["cin"] == 12
+
+
+def test_fixed_pad_and_crop_refused():
+    import ajib
+    plan = ajib.spanf3_plan(61, c=16, blocks=1)
+    onnx = export_spanf3(plan)
+    # the same graph with a Pad by a constant amount
+    g = Graph()
+    rng = np.random.default_rng(1)
+    w = rng.normal(0, 0.1, size=(9, 3, 12)).astype(np.float32)
+    p = g.node("Pad", ["input", g.init(np.array([0, 0, 1, 1, 0, 0, 1, 1]), "p", dtype=7)])
+    o = g.conv(p, w, np.zeros(12, np.float32), 3)
+    g.node("DepthToSpace", [o], ["output"], blocksize=2, mode="CRD")
+    _refused(g.model(), "Pad by a fixed amount")
+    assert lowered(onnx)["unshuffle"] == 2
+
+
 def test_input_normalisation():
     import ajib
     plan = ajib.span_plan(45, c=16, blocks=2)
@@ -106,7 +140,8 @@ def test_input_normalisation():
 
 
 @pytest.mark.skipif(not os.path.exists(REF_LOWER), reason="reference lowering not built (oracle/_ref)")
-@pytest.mark.parametrize("which", ["compact", "suc", "span", "span_merged", "compact_dcr_clip"])
+@pytest.mark.parametrize("which", ["compact", "suc", "span", "span_merged", "compact_dcr_clip", "spanf3",
+                                   "spanf3_s2d"])
 def test_against_reference_lowering(which):
     """The same ONNX bytes through the reference's lowering: the same plan, byte for byte (the
     name aside)."""
@@ -119,6 +154,10 @@ def test_against_reference_lowering(which):
         onnx = export(ajib.span_plan(48, c=48, blocks=2))
     elif which == "span_merged":
         onnx = export_span(ajib.span_plan(49, c=48, blocks=2))
+    elif which == "spanf3":
+        onnx = export_spanf3(ajib.spanf3_plan(51, c=48, blocks=2))
+    elif which == "spanf3_s2d":
+        onnx = export_spanf3(ajib.spanf3_plan(52, c=64, blocks=2), space_to_depth=True)
     else:
         onnx = export(ajib.compact_plan(50, body=2), d2s_mode="DCR", clip=True)
     ours = ajib.parse_model_bytes(ajib.model_from_bytes(onnx))
@@ -133,6 +172,10 @@ def test_against_reference_lowering(which):
         assert (a.get("slope") is None) == (b.get("slope") is None)
         if a.get("slope") is not None:
             assert np.array_equal(a["slope"], b["slope"])
+        assert ("att" in a) == ("att" in b)
+        if "att" in a:
+            assert all(np.array_equal(u, v) for u, v in zip(a["att"][:2], b["att"][:2]))
+    assert ours["unshuffle"] == ref["unshuffle"]
 
 
 def _refused(onnx, what):

@@ -21,6 +21,9 @@ def oracle():
         o.orc_conv3x3.argtypes = [C.c_int, fp, C.c_int, C.c_int, C.c_int, fp, fp, fp, C.c_int, C.c_int, C.c_int,
                                   fp, C.c_int, fp, C.c_int, fp, C.c_int]
         o.orc_conv3x3.restype = C.c_int
+        o.orc_conv3x3_ex.argtypes = [C.c_int, fp, C.c_int, C.c_int, C.c_int, fp, fp, fp, C.c_int, C.c_int, C.c_int,
+                                     fp, fp, fp, C.c_int, fp, C.c_int, fp, C.c_int]
+        o.orc_conv3x3_ex.restype = C.c_int
         o.orc_concat1x1.argtypes = [C.POINTER(fp), C.c_int, C.c_int, C.c_int, fp, fp, fp, C.c_int]
         o.orc_concat1x1.restype = C.c_int
         o.orc_f2h.argtypes = [C.c_float]
@@ -41,21 +44,27 @@ def f16r(x):
 
 
 def oracle_conv(src, in_mode, H, W, cin, w, bias, slope, cout, act=0, gate=0, resid=None, R=0, model_in=None,
-                out_clamp=False, nthreads=0):
+                out_clamp=False, nthreads=0, att=None):
     """One fused conv step on the CPU (oracle/oracle_conv.c, sanity/native_ref.h semantics).
-    w: [9][cin][cout] fp16-valued float32."""
+    w: [9][cin][cout] fp16-valued float32. in_mode 2: src is the model input [3][2H][2W],
+    pixel-unshuffled by 2. att: (w [cout][cout], bias [cout]) of the tanh 1x1 gate (gate 2)."""
     src = np.ascontiguousarray(src, dtype=np.float32)
     w = np.ascontiguousarray(w, dtype=np.float32)
     bias = np.ascontiguousarray(bias, dtype=np.float32)
     slope = None if slope is None else np.ascontiguousarray(slope, dtype=np.float32)
     resid = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
     model_in = None if model_in is None else np.ascontiguousarray(model_in, dtype=np.float32)
+    aw = ab = None
+    if att is not None:
+        aw = np.ascontiguousarray(np.asarray(att[0], np.float32).reshape(cout, cout))
+        ab = np.ascontiguousarray(att[1], dtype=np.float32)
     if R == 0:
         dst = np.zeros((H, W, cout), np.float32)
     else:
         dst = np.zeros((3, R * H, R * W), np.float32)
-    rc = oracle().orc_conv3x3(in_mode, _fp(src), H, W, cin, _fp(w), _fp(bias), _fp(slope), cout, act, gate,
-                              _fp(resid), R, _fp(model_in), 1 if out_clamp else 0, _fp(dst), nthreads)
+    rc = oracle().orc_conv3x3_ex(in_mode, _fp(src), H, W, cin, _fp(w), _fp(bias), _fp(slope), cout, act, gate,
+                                 _fp(resid), _fp(aw), _fp(ab), R, _fp(model_in), 1 if out_clamp else 0, _fp(dst),
+                                 nthreads)
     assert rc == 0, "oracle rejected the arguments"
     return dst
 
