@@ -158,20 +158,33 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
 }
 
 // ---------------- post: fp16 NCHW RGB -> NV12/P010 ----------------
-constexpr int kPostTW = 32, kPostTH = 8;          // chroma samples per tile
-constexpr int kPostRows = 40, kPostCols = 96;      // staged luma halo capacity
+// A tile is 64 x 16 chroma samples (128 x 32 luma pixels). Staging: each staged (mirrored) luma
+// pixel of the tile's filter halo is read once, its colour differences (b - Y) / db and
+// (r - Y) / dr go to shared memory split by column parity (so the horizontal taps of 32
+// consecutive outputs, two source columns apart, are 32 consecutive words), and where the pixel
+// is one of the tile's own, its quantised luma is stored. Then the horizontal pass (each thread
+// keeps one output column's weights in registers and walks rows), then the vertical pass.
+constexpr int kPostTW = 64, kPostTH = 16;          // chroma samples per tile
+constexpr int kPostRows = 44, kPostCols = 140;     // staged luma halo capacity
+constexpr int kPostHalf = kPostCols / 2;           // words per staged row of one parity
+constexpr int kPostPar = kPostRows * kPostHalf + 16;  // one parity plane (+16: the other parity on other banks)
+constexpr int kPostMaxTaps = 16;
+constexpr size_t kPostSmem = (size_t)(4 * kPostPar + 2 * kPostRows * kPostTW + kPostTH * kPostMaxTaps) * sizeof(float);
 
 template <typename T>
 __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, DevPass ph, DevPass pv, aji_csp csp,
                                               float qdiv, float qmax, uint8_t *yp, ptrdiff_t ys, uint8_t *uvp,
                                               ptrdiff_t uvs)
 {
-    extern __shared__ float2 post_sm[];
-    float2 *cuv = post_sm;                              // [kPostRows][kPostCols] (U, V) of staged luma pixels
-    float2 *huv = post_sm + kPostRows * kPostCols;      // [kPostRows][kPostTW] after the horizontal pass
+    extern __shared__ float post_sm[];
+    float *su = post_sm;                            // [2 parities][kPostRows][kPostHalf] (b - Y) / db
+    float *sv = su + 2 * kPostPar;                  // the same for (r - Y) / dr
+    float *hu = sv + 2 * kPostPar;                  // [kPostRows][kPostTW] after the horizontal pass
+    float *hv = hu + kPostRows * kPostTW;
+    float *swv = hv + kPostRows * kPostTW;          // [kPostTH][kPostMaxTaps] vertical weights of the tile
     const int cx0 = blockIdx.x * kPostTW, cy0 = blockIdx.y * kPostTH;
     const int cw = ph.dst, chh = pv.dst;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int cxl = min(cx0 + kPostTW, cw) - 1, cyl = min(cy0 + kPostTH, chh) - 1;
     const int xlo = ph.start[cx0], xhi = ph.start[cxl] + ph.taps - 1;
     const int ylo = pv.start[cy0], yhi = pv.start[cyl] + pv.taps - 1;
@@ -180,55 +193,85 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
     const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
     const float db = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
     const float dr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));
+    // the tile's own luma pixels, and whether the staged halo holds all of them
+    const int lx0 = 2 * cx0, lx1 = min(2 * (cx0 + kPostTW), w), ly0 = 2 * cy0, ly1 = min(2 * (cy0 + kPostTH), h);
+    const bool covered = xlo <= lx0 && xhi >= lx1 - 1 && ylo <= ly0 && yhi >= ly1 - 1;
 
-    // luma of the tile's own pixels, quantised
-    for (int i = tid; i < 4 * kPostTW * kPostTH; i += 256) {
-        const int ly = 2 * cy0 + i / (2 * kPostTW), lx = 2 * cx0 + i % (2 * kPostTW);
-        if (lx >= w || ly >= h) continue;
-        const size_t idx = (size_t)ly * w + lx;
-        const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
-        const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
-        reinterpret_cast<T *>(yp + (size_t)ly * ys)[lx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+    for (int i = tid; i < kPostTH * pv.taps; i += 256) {
+        const int ty = i / pv.taps, j = i % pv.taps;
+        swv[ty * kPostMaxTaps + j] = cy0 + ty < chh ? pv.wt[(size_t)(cy0 + ty) * pv.taps + j] : 0.0f;
     }
-    // chroma difference planes of the staged (mirrored) luma pixels
-    for (int i = tid; i < nrows * ncols; i += 256) {
-        const int rr = i / ncols, cc = i % ncols;
-        const size_t idx = (size_t)mirror_index(ylo + rr, h) * w + mirror_index(xlo + cc, w);
-        const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
-        const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
-        cuv[rr * kPostCols + cc] = make_float2(__fdiv_rn(__fsub_rn(b, Y), db), __fdiv_rn(__fsub_rn(r, Y), dr));
+    // staging: one warp per staged row, lanes along it
+    for (int rr = warp; rr < nrows; rr += 8) {
+        const int gy = ylo + rr, my = mirror_index(gy, h);
+        const bool own_row = covered && gy == my && gy >= ly0 && gy < ly1;
+        for (int cc = lane; cc < ncols; cc += 32) {
+            const int gx = xlo + cc, mx = mirror_index(gx, w);
+            const size_t idx = (size_t)my * w + mx;
+            const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+            const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
+            const int at = (cc & 1) * kPostPar + rr * kPostHalf + (cc >> 1);
+            su[at] = __fdiv_rn(__fsub_rn(b, Y), db);
+            sv[at] = __fdiv_rn(__fsub_rn(r, Y), dr);
+            if (own_row && gx == mx && gx >= lx0 && gx < lx1)
+                reinterpret_cast<T *>(yp + (size_t)gy * ys)[gx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+        }
+    }
+    if (!covered) {
+        // (no filter table of this engine gets here: a 2:1 table's halo always covers the tile)
+        for (int i = tid; i < (lx1 - lx0) * (ly1 - ly0); i += 256) {
+            const int ly = ly0 + i / (lx1 - lx0), lx = lx0 + i % (lx1 - lx0);
+            const size_t idx = (size_t)ly * w + lx;
+            const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+            const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
+            reinterpret_cast<T *>(yp + (size_t)ly * ys)[lx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+        }
     }
     __syncthreads();
-    // horizontal pass
-    for (int i = tid; i < nrows * kPostTW; i += 256) {
-        const int rr = i / kPostTW, tx = i % kPostTW, cx = cx0 + tx;
-        if (cx >= cw) continue;
-        const float *wt = ph.wt + (size_t)cx * ph.taps;
+    // horizontal pass: thread (row group, column) keeps its column's weights in registers
+    const int tx = tid & (kPostTW - 1), grp = tid / kPostTW, cx = cx0 + tx;
+    if (cx < cw) {
+        float wt[kPostMaxTaps];
+        const int taps = ph.taps;
+#pragma unroll
+        for (int j = 0; j < kPostMaxTaps; j++) wt[j] = j < taps ? ph.wt[(size_t)cx * taps + j] : 0.0f;
         const int s0 = ph.start[cx] - xlo;
-        float u = 0.0f, v = 0.0f;
-        for (int j = 0; j < ph.taps; j++) {
-            const float2 q = cuv[rr * kPostCols + s0 + j];
-            u = __fmaf_rn(wt[j], q.x, u);
-            v = __fmaf_rn(wt[j], q.y, v);
+        for (int rr = grp; rr < nrows; rr += 256 / kPostTW) {
+            float u = 0.0f, v = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kPostMaxTaps; j++) {
+                if (j < taps) {
+                    const int c = s0 + j;
+                    const int at = (c & 1) * kPostPar + rr * kPostHalf + (c >> 1);
+                    u = __fmaf_rn(wt[j], su[at], u);
+                    v = __fmaf_rn(wt[j], sv[at], v);
+                }
+            }
+            hu[rr * kPostTW + tx] = u;
+            hv[rr * kPostTW + tx] = v;
         }
-        huv[rr * kPostTW + tx] = make_float2(u, v);
     }
     __syncthreads();
     // vertical pass, quantise, interleave
-    for (int i = tid; i < kPostTW * kPostTH; i += 256) {
-        const int ty = i / kPostTW, tx = i % kPostTW, cx = cx0 + tx, cy = cy0 + ty;
-        if (cx >= cw || cy >= chh) continue;
-        const float *wt = pv.wt + (size_t)cy * pv.taps;
-        const int s0 = pv.start[cy] - ylo;
-        float u = 0.0f, v = 0.0f;
-        for (int j = 0; j < pv.taps; j++) {
-            const float2 q = huv[(s0 + j) * kPostTW + tx];
-            u = __fmaf_rn(wt[j], q.x, u);
-            v = __fmaf_rn(wt[j], q.y, v);
+    if (cx < cw) {
+        const int taps = pv.taps;
+        for (int ty = grp; ty < kPostTH; ty += 256 / kPostTW) {
+            const int cy = cy0 + ty;
+            if (cy >= chh) break;
+            const float *wv = swv + ty * kPostMaxTaps;
+            const int s0 = pv.start[cy] - ylo;
+            float u = 0.0f, v = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kPostMaxTaps; j++) {
+                if (j < taps) {
+                    u = __fmaf_rn(wv[j], hu[(s0 + j) * kPostTW + tx], u);
+                    v = __fmaf_rn(wv[j], hv[(s0 + j) * kPostTW + tx], v);
+                }
+            }
+            T *row = reinterpret_cast<T *>(uvp + (size_t)cy * uvs);
+            row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qmax);
+            row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qmax);
         }
-        T *row = reinterpret_cast<T *>(uvp + (size_t)cy * uvs);
-        row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qmax);
-        row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qmax);
     }
 }
 
@@ -364,7 +407,7 @@ aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting,
         p->tv = make_filter(h, ch, sy, filter);
         p->max_rows = span_of(p->tv, kPostTH);
         p->max_cols = span_of(p->th, kPostTW);
-        if (p->max_rows > kPostRows || p->max_cols > kPostCols) {
+        if (p->max_rows > kPostRows || p->max_cols > kPostCols || p->th.taps > kPostMaxTaps || p->tv.taps > kPostMaxTaps) {
             delete p;
             return nullptr;
         }
@@ -474,7 +517,7 @@ extern "C" int aji_run_post(aji_plan *p, const void *src_f16, const aji_csp *csp
     if (!p || p->kind != aji_plan::POST || !src_f16 || !csp || !y_plane || !uv_plane) return (int)cudaErrorInvalidValue;
     const int cw = p->w / 2, ch = p->h / 2;
     const dim3 grid((cw + kPostTW - 1) / kPostTW, (ch + kPostTH - 1) / kPostTH);
-    const size_t smem = (size_t)(kPostRows * kPostCols + kPostRows * kPostTW) * sizeof(float2);
+    const size_t smem = kPostSmem;
     cudaStream_t s = (cudaStream_t)stream;
     const bool p010 = p->format == AJI_FMT_P010;
     const float qdiv = p010 ? 64.0f : 1.0f, qmax = p010 ? 1023.0f : 255.0f;

@@ -452,3 +452,63 @@ extern "C" int ajib_kernel_status(int clear)
     if (clear && v && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return AJIB_ERR_CUDA;
     return v;
 }
+
+// ---- the model input packed into a row-chunked map (the executor's head path) ----
+namespace ajib {
+namespace {
+
+// One conv pixel per thread: the NCHW fp16 model input [3][H][W] -> chunk 0 {r, g, b, 0 x 5} of
+// an 8-channel row-chunked map; pixel-unshuffled by 2 ([3][2H][2W] -> channels c*4 + ry*2 + rx,
+// then 4 zeros) -> chunks 0 and 1 of a 16-channel map. Normalised as the conv's own NCHW input
+// path does it ((x - mean) * scale, rounded to fp16). Pad columns are never written.
+__global__ void __launch_bounds__(128) k_pack_input(const __half *src, int H, int W, int unshuffle, int in_norm,
+                                                     float m0, float m1, float m2, float s0, float s1, float s2,
+                                                     int pitch, int row_begin, __half *dst)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = row_begin + blockIdx.y;
+    if (x >= W) return;
+    const float mean[3] = {m0, m1, m2}, scale[3] = {s0, s1, s2};
+    const size_t chunk_row = (size_t)pitch * 8;
+    if (!unshuffle) {
+        const size_t plane = (size_t)H * W, at = (size_t)y * W + x;
+        float v[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            v[c] = __half2float(__ldg(src + c * plane + at));
+            if (in_norm) v[c] = (v[c] - mean[c]) * scale[c];
+        }
+        *reinterpret_cast<uint4 *>(dst + (size_t)y * chunk_row + (size_t)(x + 1) * 8) =
+            make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u);
+        return;
+    }
+    const int IW = 2 * W;
+    const size_t plane = (size_t)2 * H * IW;
+    uint32_t q[6];
+#pragma unroll
+    for (int j = 0; j < 6; j++) {
+        const int c = j >> 1, ry = j & 1;
+        q[j] = __ldg(reinterpret_cast<const unsigned int *>(src + c * plane + (size_t)(2 * y + ry) * IW + 2 * x));
+        if (in_norm) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&q[j]));
+            q[j] = pack_h2((f.x - mean[c]) * scale[c], (f.y - mean[c]) * scale[c]);
+        }
+    }
+    __half *d = dst + (size_t)y * 2 * chunk_row + (size_t)(x + 1) * 8;
+    *reinterpret_cast<uint4 *>(d) = make_uint4(q[0], q[1], q[2], q[3]);
+    *reinterpret_cast<uint4 *>(d + chunk_row) = make_uint4(q[4], q[5], 0u, 0u);
+}
+
+}  // namespace
+
+int pack_model_input(const void *src, int H, int W, int unshuffle, bool in_norm, const float *mean, const float *scale,
+                     int row_begin, int row_end, void *dst, cudaStream_t s)
+{
+    if (!src || !dst || H < 1 || W < 1 || row_begin < 0 || row_end > H || row_begin >= row_end) return AJIB_ERR_ARGS;
+    if (((uintptr_t)src & 3) || ((uintptr_t)dst & 15)) return AJIB_ERR_ARGS;
+    const dim3 grid((W + 127) / 128, row_end - row_begin);
+    k_pack_input<<<grid, 128, 0, s>>>((const __half *)src, H, W, unshuffle ? 1 : 0, in_norm ? 1 : 0, mean[0], mean[1],
+                                      mean[2], scale[0], scale[1], scale[2], feature_pitch(W), row_begin, (__half *)dst);
+    return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+}  // namespace ajib

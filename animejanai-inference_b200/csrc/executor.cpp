@@ -18,6 +18,7 @@ Executor::~Executor()
     for (Step &s : steps_) {
         ajib_weights_release(&s.w);
         ajib_weights_release(&s.att);
+        cudaFree(s.pack_buf);
     }
 }
 
@@ -28,7 +29,12 @@ const void *Executor::ptr(int t, const void *in, void *out) const
     return t >= 0 ? tensor_[t] : nullptr;
 }
 
-int Executor::launches_per_run() const { return (int)steps_.size() * bands_; }
+int Executor::launches_per_run() const
+{
+    int n = 0;
+    for (const Step &st : steps_) n += st.pack ? 2 : 1;  // the head's input pack is a launch of its own
+    return n * bands_;
+}
 
 std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h, std::string *why)
 {
@@ -57,9 +63,40 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
         st.resid = ps.resid;
         st.dst = ps.dst;
         const PlanWeights &pw = ps.w;
-        int rc = ajib_weights_upload(&st.w, pw.w.data(), pw.bias.data(), pw.slope.empty() ? nullptr : pw.slope.data(),
-                                     pw.taps, pw.cin, pw.cout);
+        // the head reads the model input packed into a row-chunked map of 8 (16 unshuffled)
+        // channels: its weights gain zero input channels to match
+        const bool head = ps.kind == PlanStep::CONV && (ps.in == AJIB_IN_NCHW3 || ps.in == AJIB_IN_NCHW3_UNSHUFFLE2);
+        const int cin = head ? (ps.in == AJIB_IN_NCHW3 ? 8 : 16) : pw.cin;
+        std::vector<uint16_t> wpad;
+        if (head) {
+            wpad.assign((size_t)9 * cin * pw.cout, 0);
+            for (int t = 0; t < 9; t++)
+                for (int k = 0; k < pw.cin; k++)
+                    for (int o = 0; o < pw.cout; o++)
+                        wpad[((size_t)t * cin + k) * pw.cout + o] = pw.w[((size_t)t * pw.cin + k) * pw.cout + o];
+        }
+        int rc = ajib_weights_upload(&st.w, head ? wpad.data() : pw.w.data(), pw.bias.data(),
+                                     pw.slope.empty() ? nullptr : pw.slope.data(), pw.taps, cin, pw.cout);
         if (rc != AJIB_OK) return fail("weight upload failed (step " + std::to_string(i) + ")");
+        if (head) {
+            st.pack = true;
+            st.pack_c = cin;
+            st.unshuffle = ps.in == AJIB_IN_NCHW3_UNSHUFFLE2 ? 1 : 0;
+            st.in_norm = ps.in_norm;
+            for (int c = 0; c < 3; c++) {
+                st.in_mean[c] = ps.in_mean[c];
+                st.in_scale[c] = ps.in_scale[c];
+            }
+            const size_t need = ajib_feature_bytes(in_h, in_w, cin);
+            if (cudaMalloc(&st.pack_buf, need) != cudaSuccess || cudaMemset(st.pack_buf, 0, need) != cudaSuccess) {
+                cudaFree(st.pack_buf);
+                cudaGetLastError();
+                ajib_weights_release(&st.w);
+                return fail("input buffer allocation failed");
+            }
+            e->bytes_ += need;
+            e->pack_bytes_ = need;
+        }
         e->weight_bytes_ += ajib_weights_bytes(st.w);
         if (ps.kind == PlanStep::CONCAT) {
             st.concat = true;
@@ -70,11 +107,11 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
             continue;
         }
         ajib_conv &op = st.op;
-        op.in = ps.in;
+        op.in = head ? AJIB_IN_NHWC : ps.in;
         op.act = ps.act;
         op.gate = ps.gate;
         op.out = ps.out;
-        op.cin = ps.cin;
+        op.cin = head ? cin : ps.cin;
         op.cout = ps.cout;
         op.w = st.w;
         if (ps.gate == AJIB_GATE_TANH1X1) {
@@ -86,7 +123,7 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
             e->weight_bytes_ += ajib_weights_bytes(st.att);
             op.att = st.att;
         }
-        op.in_norm = ps.in_norm;
+        op.in_norm = head ? 0 : ps.in_norm;
         op.out_clamp = ps.out_clamp;
         for (int c = 0; c < 3; c++) {
             op.in_mean[c] = ps.in_mean[c];
@@ -135,7 +172,9 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
             if (buffer[t] >= 0 && (last[t] == i || (last[t] < 0 && born[t] == i)))
                 free_list.push_back({ajib_feature_bytes(in_h, in_w, plan.channels[t]), buffer[t]});
     }
+    e->last_w_ = in_w;
     for (size_t need : sizes) {
+        e->buffer_bytes_.push_back(need);
         void *b = nullptr;
         // the pad columns of row-chunked maps must read as zero: clear once, kernels never write them
         if (cudaMalloc(&b, need) != cudaSuccess || cudaMemset(b, 0, need) != cudaSuccess) {
@@ -190,6 +229,15 @@ int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
 int Executor::launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1,
                      cudaStream_t s) const
 {
+    if (st.pack) {
+        // the input rows the head's rows [r0, r1) read: one-row halos
+        const int H = nimg * img_h;
+        const int rc = pack_model_input(in, H, w, st.unshuffle, st.in_norm, st.in_mean, st.in_scale, std::max(0, r0 - 1),
+                                        std::min(H, r1 + 1), st.pack_buf, s);
+        if (rc != AJIB_OK) return rc;
+        return ajib_conv3x3_launch_images(&st.op, st.pack_buf, nullptr, const_cast<void *>(ptr(st.dst, in, out)), nimg,
+                                          img_h, w, r0, r1, s);
+    }
     if (st.concat) {
         const void *srcs[4] = {nullptr, nullptr, nullptr, nullptr};
         for (int k = 0; k < st.nsrc; k++) srcs[k] = ptr(st.srcs[k], in, out);
@@ -208,6 +256,15 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
     img_h /= U_;
     const int h = img_h * nimg;
     if (w > W_ || h > H_) return AJIB_ERR_ARGS;
+    // a row-chunked map's pitch follows its width: at another width, columns that held pixels
+    // become pad columns, which must read as zero again
+    if (w != last_w_) {
+        for (size_t k = 0; k < buffers_.size(); k++)
+            if (cudaMemsetAsync(buffers_[k], 0, buffer_bytes_[k], s) != cudaSuccess) return AJIB_ERR_CUDA;
+        for (const Step &st : steps_)
+            if (st.pack_buf && cudaMemsetAsync(st.pack_buf, 0, pack_bytes_, s) != cudaSuccess) return AJIB_ERR_CUDA;
+        last_w_ = w;
+    }
     const int ns = (int)steps_.size();
     // profiling brackets whole steps (all of a step's bands), so it runs unbanded
     const bool prof = prof_on_ && !prof_ev_.empty();

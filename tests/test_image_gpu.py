@@ -147,6 +147,26 @@ def test_upscale_suc_against_oracle(W, H, ci, tile, ov, even):
     ctx.close()
 
 
+def test_even_tiles_of_changing_width():
+    """Even tiles narrower than the model's tile, then at another width, with one model: the
+    executor's maps change pitch between the runs and their pad columns must read as zero again."""
+    import ajib
+    plan = ajib.compact_plan(23, c=24, body=3, scale=4)
+    path = _model_file(plan)
+    ctx = ajib.Image()
+    m = ctx.load(path, tile=64, overlap=8, flags=ajib.IMG_LOAD_EVEN_TILES)
+    # even tile widths 48 (65 and 45 wide), 64 (100 wide), then 48 again
+    for W, H in [(65, 77), (100, 90), (45, 50)]:
+        img = np.random.default_rng(W * H).integers(0, 256, size=(H, W, 3)).astype(np.uint8)
+        rc, got = ctx.upscale(m, img, 4)
+        assert rc == 0, ctx.error()
+        want = oracle_upscale_tiled(lambda x: run_plan(plan, x.astype(np.float16).astype(np.float32)), 64, 64, 4, 8,
+                                    img, even=True)
+        assert np.abs(got.astype(int) - want.astype(int)).max() <= 3, (W, H)
+    ajib.lib.aji_img_release(C.byref(m))
+    ctx.close()
+
+
 def test_image_api_errors_and_progress():
     import ajib
     plan = ajib.compact_plan(22, c=24, body=2, scale=4)
