@@ -126,7 +126,7 @@ cudaError_t launch_pdl(void (*kernel)(Arg), int grid, int threads, int smem, cud
 template <int KPAD, int NPAD, int EK, int IN>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
-    using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt>;
+    using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt, EK == kEpiD2S>;
     static_assert(Cf::SMEM <= kMaxSmem, "shared memory budget");
     // the shared-memory opt-in is per device: set it once on each
     static std::atomic<uint64_t> done{0};
@@ -356,6 +356,8 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     p.row_end = row_end;
     p.pitch = feature_pitch(W);
     p.img_h = img_h;
+    p.skip_smem = op->out != AJIB_OUT_NHWC && resid && op->in == AJIB_IN_NHWC && W % 8 == 0 &&
+                  ((uintptr_t)resid & 15) == 0;
     if (op->gate == AJIB_GATE_TANH1X1) {
         p.att_img = (const unsigned char *)op->att->img;
         p.att_bias = op->att->bias;

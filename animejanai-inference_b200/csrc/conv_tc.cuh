@@ -26,16 +26,18 @@
  *
  * A CTA is persistent on one SM and walks a contiguous run of (strip, row) tiles down a
  * 128-pixel-wide vertical strip, so each input row is fetched once. Roles:
- *   warps 0-3   producer: one thread issues the bulk copies of each input row (row-chunked
- *               inputs), or all 128 threads convert the NCHW RGB model input into the same layout;
- *               it also waits for the accumulators a row starts to be free and writes the row's
- *               MMA plan beside the staged row;
+ *   warps 0-3   producer: warp 0 issues the bulk copies of each input row, one lane per 8-channel
+ *               chunk (row-chunked inputs), or all 128 threads convert the NCHW RGB model input
+ *               into the same layout; lane 0 also waits for the accumulators a row starts to be
+ *               free and writes the row's MMA plan beside the staged row, and after the last row
+ *               fills one terminator stage;
  *   warps 4-11  epilogue: TMEM -> registers (one pixel per thread, half a slot's channels per
  *               warp), bias, activation, SPAN gate or depth-to-space with the model-input skip,
  *               fp16 store; then zero the half slot;
  *   warp 12     MMA issuer (one thread) and TMEM owner. The tensor pipe queues only a few MMAs
  *               and a lone thread's bookkeeping is slow, so this thread only waits for a staged
- *               row, reads its plan and issues; the next row's wait sits between this row's MMAs.
+ *               row, reads its plan and issues, straight-line per stage of two rows; the next
+ *               stage's wait sits between the two rows' MMAs.
  * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime.
  *
  * The semantics are those of the reference kernel k_conv3x3 (src/native/conv_kernels.cuh:100-350)
@@ -93,6 +95,9 @@ struct ConvDev {
     const unsigned char *att_img;
     const float *att_bias;
     int att_kpad, att_npad;
+    // depth-to-space with the skip: its rows reach shared memory by bulk copies (row-chunked
+    // input and W a multiple of 8, so every copy is 16-byte aligned), else the epilogue loads them
+    int skip_smem;
 };
 
 // The input rows a segment of output rows [ya, yb) reads: one-row halos that stay inside the
@@ -106,7 +111,7 @@ __device__ __forceinline__ void segment_rows(int ya, int yb, int img_h, int &r0,
 // Padded pixels per chunk row of a row-chunked feature map of width W.
 __host__ __device__ constexpr int feature_pitch(int W) { return (W + kTileM - 1) / kTileM * kTileM + 2; }
 
-template <int KPAD, int NPAD, bool ATT = false>
+template <int KPAD, int NPAD, bool ATT = false, bool SKIP = false>
 struct ConvCfg {
     static_assert(KPAD % 16 == 0 && NPAD % 16 == 0 && KPAD <= 64 && NPAD <= 64, "padded channel counts");
     static constexpr int KC = KPAD / 8;       // 8-channel chunks per pixel
@@ -127,16 +132,22 @@ struct ConvCfg {
     static constexpr int ATT_B = ATT ? NPAD * NPAD * 2 : 0;
     static constexpr int ATT_A = NPAD / 8 * kTileM * 16;
     static constexpr int ATT_BYTES = ATT ? ATT_B + 2 * ATT_A : 0;
-    static constexpr int FIXED = AOFF + ATT_BYTES + 3 * 64 * 4 + 1024 + 1024;
+    // depth-to-space: per ring slot the model-input row its output adds (3 planes x 128 pixels),
+    // copied in by the producer's bulk copies
+    static constexpr int SKIP_ROW = 3 * kTileM * 2;
+    static constexpr int SKIP_BYTES = SKIP ? S * SKIP_ROW : 0;
+    static constexpr int FIXED = AOFF + ATT_BYTES + SKIP_BYTES + 3 * 64 * 4 + 1024 + 1024;
     static constexpr int NS_FIT = (kMaxSmem - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;
     static_assert(NS >= 2 && S >= 4, "pipeline depth");
     static constexpr int ATOFF = AOFF + NS * STAGE;  // attention B, then A tiles 0 and 1
-    static constexpr int POFF = ATOFF + ATT_BYTES;   // bias[64], slope[64], attention bias[64] floats
-    static constexpr int BOFF = POFF + 3 * 64 * 4;  // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2]
+    static constexpr int SKOFF = ATOFF + ATT_BYTES;  // skip rows [S][3][128] fp16
+    static constexpr int POFF = SKOFF + SKIP_BYTES;  // bias[64], slope[64], attention bias[64] floats
+    // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S]
+    static constexpr int BOFF = POFF + 3 * 64 * 4;
     static constexpr int PLOFF = BOFF + 512;        // RowPlan per staged row
     static constexpr int SMEM = BOFF + 1024 + 1024;  // + alignment slack for the base
-    static_assert((2 * NS + 2 * S + 4) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
+    static_assert((2 * NS + 3 * S + 4) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
     static_assert(SMEM <= kMaxSmem, "shared memory budget");
 };
 
@@ -220,6 +231,19 @@ template <int CW>
 struct EpiIn {
     float skip[3];       // depth-to-space: the model-input pixel (nearest-upsampled skip), or zeros
     uint4 gate[CW / 8];  // SPAN gate: the block input's chunks of this half
+};
+
+// The epilogue's inputs of the next rows, loaded PF rows ahead (a register ring: e[0] is the row
+// being finished).
+template <int PF, typename T>
+struct EpiRing {
+    T e[PF];
+    __device__ __forceinline__ void push(const T &next)
+    {
+#pragma unroll
+        for (int i = 0; i + 1 < PF; i++) e[i] = e[i + 1];
+        e[PF - 1] = next;
+    }
 };
 
 template <int EK, int CW, int C0>
@@ -362,10 +386,11 @@ struct RowWalk {
 // writes it into shared memory beside the staged row, so the MMA thread only reads it.
 struct RowPlan {
     uint32_t pd[3], pb[3], pi[3];
-    uint32_t np;
+    uint32_t np;                  // pieces (0: no row); kPlanEnd in a stage's first plan: the walk is over
     uint32_t commit_a, commit_b;  // accumulator-full mbarrier addresses to commit after the row, or 0
 };
 static_assert(sizeof(RowPlan) == 48, "row plan layout");
+constexpr uint32_t kPlanEnd = 0xFFFFFFFFu;
 
 // The accumulator-free waits a row's plan depends on: up to two (mbarrier, parity) pairs.
 struct RowWaits {
@@ -460,7 +485,7 @@ template <int KPAD, int NPAD, int EK, int IN>
 __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ ConvDev a)
 {
     constexpr bool ATT = EK == kEpiAtt;
-    using C = ConvCfg<KPAD, NPAD, ATT>;
+    using C = ConvCfg<KPAD, NPAD, ATT, EK == kEpiD2S>;
     constexpr int S = C::S;
     constexpr int HW = NPAD / 2;  // accumulator columns per epilogue warp (half a slot)
     extern __shared__ unsigned char smraw[];
@@ -471,8 +496,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     float *sbias = reinterpret_cast<float *>(sm + C::POFF), *sslope = sbias + 64, *satt = sbias + 128;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::BOFF);
     const uint32_t full0 = dev::smem_u32(bars), empty0 = full0 + 8 * C::NS, accf0 = empty0 + 8 * C::NS,
-                   acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8, attf0 = dbar + 8;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 2 * S + 4);
+                   acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8, attf0 = dbar + 8,
+                   skipf0 = attf0 + 16;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 3 * S + 4);
     RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -487,6 +513,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         }
         for (int s = 0; s < S; s++) {
             dev::mbar_init(accf0 + 8 * s, 1);
+            dev::mbar_init(skipf0 + 8 * s, 1);
             // the tanh gate's epilogue groups take alternate rows: four warps free each slot
             dev::mbar_init(acce0 + 8 * s, ATT ? kEpiWarps / 2 : kEpiWarps);
         }
@@ -529,7 +556,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         // ================= producer: stages each input row and writes its MMA plan beside it,
         // after waiting for the accumulators the row starts to be free
         if constexpr (bulk_in) {
-            if (tid == 0) {
+            if (warp == 0) {
+                // warp 0: every lane walks the same rows (warp-uniform control flow); lane 0 waits for
+                // the accumulators, writes the plan and arrives, lane k issues the bulk copy of K
+                // chunk k (one lane issuing them all measured ~700 cycles per 64-channel row)
                 const int kcin = a.cin / 8;
                 const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
                 const size_t chunk_row = (size_t)a.pitch * 8;  // halves per chunk row
@@ -538,7 +568,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 bool ok = true;
                 while (ok && walk.next()) {
                     const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
-                    if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
+                    if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
                     // each row's copies go out once the accumulators it starts are free (issuing them
                     // earlier, as soon as the stage is free, measured slower: more reads in flight
                     // against the epilogue's writes)
@@ -548,24 +578,57 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         RowWaits wt;
                         RowPlan p;
                         plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, p, wt);
-                        if (!(ok = wt.wait(a.err))) break;
-                        plans[s * C::RP + h] = p;
-                        dev::mbar_expect_tx(full0 + 8 * s, bytes);
+                        bool good = true;
+                        if (lane == 0) good = wt.wait(a.err);
+                        if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
+                        if (lane == 0) {
+                            plans[s * C::RP + h] = p;
+                            dev::mbar_expect_tx(full0 + 8 * s, bytes);
+                        }
+                        if constexpr (EK == kEpiD2S) {
+                            // the skip rows of the outputs this row starts (r + 1; r at an image's
+                            // first row), into their slots: lanes 8-10 and 11-13, one plane each
+                            if (a.skip_smem) {
+                                const int x0 = walk.strip * kTileM;
+                                const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
+                                const int k = lane - 8, which = k / 3, c3 = k % 3;
+                                const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
+                                const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
+                                const int orow = which == 0 ? walk.r + 1 : walk.r;
+                                if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
+                                __syncwarp();
+                                if (mine)
+                                    dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + c3 * (kTileM * 2),
+                                                   a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
+                            }
+                        }
                         const uint32_t dst = abase + s * C::STAGE + h * C::SLOT;
                         // padded column x0 is pixel x0 - 1: the left halo
                         const __half *row = a.src + (size_t)walk.r * kcin * chunk_row + (size_t)walk.strip * kTileM * 8;
-                        for (int kc = 0; kc < kcin; kc++)
-                            dev::bulk_load(dst + kc * C::LBO_A, row + kc * chunk_row, kHalo * 16, full0 + 8 * s);
+                        if (lane < kcin)
+                            dev::bulk_load(dst + lane * C::LBO_A, row + lane * chunk_row, kHalo * 16, full0 + 8 * s);
+                        __syncwarp();
                     }
                     // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
-                    // empty: the MMA thread skips rows whose plan has no pieces
-                    for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
-                    // one arrival per stage; it completes once the copies above have landed
-                    dev::mbar_arrive(full0 + 8 * s);
+                    // empty: the MMA thread skips rows whose plan has no pieces. One arrival per
+                    // stage; it completes once the copies above have landed.
+                    if (lane == 0) {
+                        for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
+                        dev::mbar_arrive(full0 + 8 * s);
+                    }
                     pi++;
                 }
+                if (ok) {
+                    // the terminator: one more stage whose first plan says the walk is over, so the
+                    // MMA thread never walks the rows itself
+                    const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                    if ((ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) && lane == 0) {
+                        plans[s * C::RP].np = kPlanEnd;
+                        dev::mbar_arrive(full0 + 8 * s);
+                    }
+                }
                 // on an error exit, let the last copies land before the CTA can leave
-                if (!ok && pi > 0) {
+                if (!ok && pi > 0 && lane == 0) {
                     const uint32_t s = (pi - 1) % C::NS, ph = ((pi - 1) / C::NS) & 1;
                     dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
                 }
@@ -681,6 +744,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 fill(pb, nb);
                 if (!ok) break;
                 nb = prefetch(pb);
+            }
+            if (ok) {
+                // the terminator stage (every producer thread arrives, as for a filled stage)
+                const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                if (dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) {
+                    if (tid == 0) plans[s * C::RP].np = kPlanEnd;
+                    dev::mbar_arrive(full0 + 8 * s);
+                }
             }
         }
     } else if (ATT && warp < kMmaWarp) {
@@ -822,22 +893,50 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         uint32_t ot = 0;
         int strip, ya, yb;
         bool ok = true;
+        // a row's global inputs (skip pixel, gate's block input) are loaded ahead (three rows for
+        // the skip pixel, whose DRAM latency is several rows of this epilogue; one for the gate's
+        // larger input), so their latency overlaps earlier rows' epilogues
+        auto prefetch = [&](EpiIn<HW> &in, EpiIn<NPAD> &inw, int o, int x) {
+            if (!whole) {
+                if (h == 0)
+                    epi_prefetch<EK, HW, 0>(in, a, o, x);
+                else
+                    epi_prefetch<EK, HW, HW>(in, a, o, x);
+            } else if (h == 0) {
+                epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
+            }
+        };
+        constexpr int PF = EK == kEpiD2S ? 3 : 1;
+        const bool pf_on = !(EK == kEpiD2S && a.skip_smem);  // a skip in shared memory needs no prefetch
         while (ok && seg.next(strip, ya, yb)) {
             const int x0 = strip * kTileM;
             const int x = x0 + q * 32 + lane;
+            EpiRing<PF, EpiIn<HW>> rin;
+            EpiRing<PF, EpiIn<NPAD>> rinw;
+#pragma unroll
+            for (int k = 0; k < PF; k++)
+                if (pf_on && ya + k < yb) prefetch(rin.e[k], rinw.e[k], ya + k, x);
             for (int o = ya; o < yb; o++, ot++) {
                 const int slot = ring_slot<S>(ot);
-                EpiIn<HW> in;
-                EpiIn<NPAD> inw;
-                if (!whole) {
-                    if (h == 0)
-                        epi_prefetch<EK, HW, 0>(in, a, o, x);
-                    else
-                        epi_prefetch<EK, HW, HW>(in, a, o, x);
-                } else if (h == 0) {
-                    epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
-                }
+                EpiIn<HW> in = rin.e[0];
+                EpiIn<NPAD> inw = rinw.e[0];
+                EpiIn<HW> nin;
+                EpiIn<NPAD> ninw;
+                if (pf_on && o + PF < yb) prefetch(nin, ninw, o + PF, x);
                 if (!(ok = dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                if constexpr (EK == kEpiD2S) {
+                    if (!pf_on) {
+                        // the skip row landed in this output's slot (its own barrier, one phase per use)
+                        if (!(ok = dev::mbar_wait_warp(skipf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                        const __half *sk = reinterpret_cast<const __half *>(sm + C::SKOFF + slot * C::SKIP_ROW);
+#pragma unroll
+                        for (int c3 = 0; c3 < 3; c3++) {
+                            const float v = x < W ? __half2float(sk[c3 * kTileM + (x - x0)]) : 0.f;
+                            in.skip[c3] = v;
+                            inw.skip[c3] = v;
+                        }
+                    }
+                }
                 __syncwarp();
                 dev::tc_fence_after();
                 const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
@@ -888,6 +987,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                     }
                 }
+                rin.push(nin);
+                rinw.push(ninw);
             }
         }
       }
@@ -902,13 +1003,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             // offset d is added as d >> 4
             const uint64_t bdesc0 = dev::sdesc(wbase, C::LBO_B, 128);
             const uint64_t adesc_base = dev::sdesc(abase, C::LBO_A, 128);
-            RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
-            // the rows of the next stage fill: up to RP rows of the walk
-            auto count = [&]() -> int {
-                int n = 0;
-                while (n < C::RP && walk.next()) n++;
-                return n;
-            };
             // the pi-th stage fill: wait until it is full, then take its rows' plans
             static_assert(C::RP == 2, "the loop below takes stages of two rows");
             auto fetch = [&](uint32_t pi, RowPlan &p0, RowPlan &p1) -> bool {
@@ -919,32 +1013,24 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 dev::tc_fence_after();
                 return good;
             };
+            // straight-line per stage: row 0's MMAs, the wait for the next stage, row 1's MMAs, the
+            // commits; the producer's terminator stage ends the loop (so no row bookkeeping here,
+            // which measured ~100 cycles a row with the tensor pipe idle)
             RowPlan c0, c1, n0, n1;
             uint32_t pi = 0;
-            int n = ok ? count() : 0;
-            if (n) ok = fetch(pi, c0, c1);
-            while (n && ok) {
+            ok = ok && fetch(0, c0, c1);
+            while (ok && c0.np != kPlanEnd) {
                 const uint32_t s = pi % C::NS;
                 const uint64_t adesc0 = adesc_base + (uint64_t)((s * C::STAGE) >> 4);
-                int nn = 0;
-                bool okn = true;
-                // one copy of the row's MMA code for both rows; the next stage is fetched between them
-#pragma unroll 1
-                for (int h = 0; h < n; h++) {
-                    const RowPlan &p = h ? c1 : c0;
-                    if (p.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)((h * C::SLOT) >> 4), bdesc0, p);
-                    if (h == 0) {
-                        nn = count();
-                        if (nn) okn = fetch(pi + 1, n0, n1);
-                    }
-                }
+                if (c0.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, c0);
+                const bool okn = fetch(pi + 1, n0, n1);
+                if (c1.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)(C::SLOT >> 4), bdesc0, c1);
                 dev::mma_commit(empty0 + 8 * s);
                 if (c0.np && c0.commit_a) dev::mma_commit(c0.commit_a);
                 if (c0.np && c0.commit_b) dev::mma_commit(c0.commit_b);
-                if (n > 1 && c1.np && c1.commit_a) dev::mma_commit(c1.commit_a);
-                if (n > 1 && c1.np && c1.commit_b) dev::mma_commit(c1.commit_b);
+                if (c1.np && c1.commit_a) dev::mma_commit(c1.commit_a);
+                if (c1.np && c1.commit_b) dev::mma_commit(c1.commit_b);
                 pi++;
-                n = nn;
                 ok = okn;
                 c0 = n0;
                 c1 = n1;
