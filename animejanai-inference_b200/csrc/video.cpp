@@ -509,18 +509,31 @@ extern "C" int aji_wait(aji_ctx *c, uint64_t ticket)
     return AJI_OK;
 }
 
+// The model step profiled: the chain's last model (in a chain, the largest and costliest).
+namespace {
+Executor *profiled_exec(aji_ctx *c)
+{
+    for (auto it = c->steps.rbegin(); it != c->steps.rend(); ++it)
+        if (it->exec) return it->exec.get();
+    return c->exec;
+}
+}  // namespace
+
 extern "C" int ajib_video_profile(aji_ctx *c, int on)
 {
-    if (!c || !c->exec) return AJIB_ERR_ARGS;
-    return c->exec->profile(on != 0);
+    if (!c) return AJIB_ERR_ARGS;
+    Executor *e = profiled_exec(c);
+    return e ? e->profile(on != 0) : AJIB_ERR_ARGS;
 }
 
 extern "C" int ajib_video_profile_read(aji_ctx *c, double *ms, int *counts, int nsteps)
 {
-    if (!c || !c->exec || !ms || !counts) return AJIB_ERR_ARGS;
+    if (!c || !ms || !counts) return AJIB_ERR_ARGS;
+    Executor *e = profiled_exec(c);
+    if (!e) return AJIB_ERR_ARGS;
     CtxGuard g(c->cu);
     if (!g.ok) return AJIB_ERR_CUDA;
-    return c->exec->profile_read(ms, counts, nsteps);
+    return e->profile_read(ms, counts, nsteps);
 }
 
 extern "C" const char *aji_current_log(aji_ctx *c) { return c ? c->current_log.c_str() : ""; }

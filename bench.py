@@ -38,15 +38,47 @@ sys.path.insert(0, os.path.join(ROOT, "animejanai-inference_b200"))
 W_IN, H_IN, SCALE = 1920, 1080, 2
 MODEL_SEED = 1
 METRIC = "frames/s 1080p->4K 2x Compact fp16 at 1/2/4/8 B200; % tensor-core peak"
-METRIC_SPANF3 = "frames/s 1080p->4K 2x SPANF3 b5f48 unshuffle fp16 (video chain)"
 SPANF3_PUBLISHED_MS = 2.02  # the reference on an RTX 5090, Linux (BENCHMARKS.md:257)
 
+# The workloads: BASELINE config 1 (the headline, default), config 3 (SPAN), config 4 (a chain of
+# two Compact nets, 960x540 -> 1920x1080 -> 3840x2160, through animejanai.conf), and the shipping
+# SPANF3 structure. Each runs through the video ABI on P010 frames.
+MODELS = {
+    "compact": dict(metric=METRIC, w=1920, h=1080,
+                    workload="BASELINE config 1: Compact 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010",
+                    model="SRVGGNetCompact 64 feat x 16 body, PReLU, pixel_shuffle 2, random-init (seed 1)",
+                    kernel="k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)"),
+    "span": dict(metric="frames/s 1080p->4K 2x SPAN-S 48x6 fp16 (BASELINE config 3)", w=1920, h=1080,
+                 workload="BASELINE config 3: SPAN 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010",
+                 model="SPAN 48 feat x 6 blocks (SiLU, sigmoid gates, concat 1x1), pixel_shuffle 2, random-init (seed 1)",
+                 kernel="k_conv3x3_tc<48,64> (SPAN body convs 48->48, SiLU / sigmoid gate, 1920x1080)"),
+    "chain": dict(metric="frames/s 960x540->1080p->4K two-model Compact chain fp16 (BASELINE config 4)", w=960, h=540,
+                  workload="BASELINE config 4: two Compact 2x nets chained by animejanai.conf, 960x540 P010 -> "
+                           "3840x2160 P010 (a stream of frames, frame-parallel over ranks)",
+                  model="2 x SRVGGNetCompact 64x16 2x, random-init (seeds 1, 2)",
+                  kernel="k_conv3x3_tc<64,64> (second net's body conv 64->64 + PReLU, 1920x1080)"),
+    "spanf3": dict(metric="frames/s 1080p->4K 2x SPANF3 b5f48 unshuffle fp16 (video chain)", w=1920, h=1080,
+                   workload="SPANF3 b5f48 2x video (2x pixel-unshuffle, tanh gates), 1920x1080 P010 BT.709 limited -> "
+                            "3840x2160 P010",
+                   model="SPANF3 48 feat x 5 blocks, unshuffle 2, depth-to-space 4, random-init (seed 1, 0.7 He)",
+                   kernel="k_conv3x3_tc<48,64> (SPANF3 body convs 48->48, ReLU / tanh gate, 960x540)"),
+}
 
-def bench_plan(model):
+
+def bench_plans(model):
+    """The model's plans, in chain order."""
     import ajib
     if model == "spanf3":
-        return ajib.spanf3_plan(MODEL_SEED, c=48, blocks=5, gain=0.7)
-    return ajib.compact_plan(MODEL_SEED)
+        return [ajib.spanf3_plan(MODEL_SEED, c=48, blocks=5, gain=0.7)]
+    if model == "span":
+        return [ajib.span_plan(MODEL_SEED, c=48, blocks=6)]
+    if model == "chain":
+        return [ajib.compact_plan(MODEL_SEED), ajib.compact_plan(MODEL_SEED + 1)]
+    return [ajib.compact_plan(MODEL_SEED)]
+
+
+def plan_scale(plan):
+    return plan["depth_to_space"] // plan.get("unshuffle", 1)
 # DRAM bytes (read + write) of one body-conv launch at 1920x1080, from the ncu capture summarised
 # in profiles/conv3x3_body_64x64_1080p.txt (the roofline's "traffic")
 BODY_TRAFFIC_BYTES = 498.3e6
@@ -138,32 +170,37 @@ class ClockSampler:
 
 
 def cpu_baseline_sample(rows=16, nthreads=0, model="compact"):
-    """The reference CPU path on a bounded sample: a W_IN x rows band of the net (all its steps),
-    timed on the host cores. Uses oracle/_ref (the reference's run_plan compiled from its own
-    sources) when built, else the oracle's restatement. Returns (frames/s, cores, kind, sample)."""
+    """The reference CPU path on a bounded sample: a band of `rows` input rows through the net(s)
+    (every step; a chain's second net on the first's output band), timed on the host cores. Uses
+    oracle/_ref (the reference's run_plan compiled from its own sources) when built, else the
+    oracle's restatement. Returns (frames/s, cores, kind, sample)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
-    plan = bench_plan(model)
+    spec = MODELS[model]
+    plans = bench_plans(model)
     rng = np.random.default_rng(7)
-    x = rng.uniform(0, 1, size=(3, rows, W_IN)).astype(np.float16).astype(np.float32)
+    x = rng.uniform(0, 1, size=(3, rows, spec["w"])).astype(np.float16).astype(np.float32)
     ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_net.so")
+    dt = 0.0
     if os.path.exists(ref_lib):
         import refnet
-        t0 = time.perf_counter()
-        refnet.run_plan(ref_lib, plan, x, nthreads)
-        dt = time.perf_counter() - t0
+        for plan in plans:
+            t0 = time.perf_counter()
+            x = refnet.run_plan(ref_lib, plan, x, nthreads)
+            dt += time.perf_counter() - t0
         cores = refnet.threads(ref_lib, nthreads)
         kind = "reference"
     else:
-        from util import oracle_conv
         import oracle_net
-        t0 = time.perf_counter()
-        oracle_net.run_plan(plan, x, nthreads)
-        dt = time.perf_counter() - t0
+        for plan in plans:
+            t0 = time.perf_counter()
+            x = oracle_net.run_plan(plan, x, nthreads)
+            dt += time.perf_counter() - t0
         cores = nthreads if nthreads > 0 else os.cpu_count()
         kind = "port"
-    fps = (rows * W_IN) / (H_IN * W_IN) / dt
-    return fps, cores, kind, (f"{W_IN}x{rows} band of the 1080p frame through all {len(plan['steps'])} steps "
-                              f"({dt:.2f} s)")
+    fps = rows / spec["h"] / dt
+    nsteps = sum(len(p["steps"]) for p in plans)
+    return fps, cores, kind, (f"{spec['w']}x{rows} band of the {spec['w']}x{spec['h']} input through all {nsteps} "
+                              f"steps ({dt:.2f} s)")
 
 
 def run_reference(args, rank, world):
@@ -177,15 +214,12 @@ def run_reference(args, rank, world):
             vals.append(fps)
         info = (cores, kind, sample)
     v = float(np.mean(vals))
-    spanf3 = args.model == "spanf3"
-    line = {"impl": "reference", "metric": METRIC_SPANF3 if spanf3 else METRIC, "value": v, "unit": "frames/s",
+    spec = MODELS[args.model]
+    line = {"impl": "reference", "metric": spec["metric"], "value": v, "unit": "frames/s",
             "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": ("SPANF3 b5f48 unshuffle 2x 1080p P010 -> 4K" if spanf3 else
-                                    "BASELINE config 1 (Compact 2x 1080p P010 -> 4K)") +
-                       ", CPU reference net on a band sample",
-                       "model": "SPANF3 48x5 unshuffle random-init" if spanf3 else "SRVGGNetCompact 64x16 2x random-init"},
+            "config": {"workload": spec["workload"] + ", CPU reference net on a band sample", "model": spec["model"]},
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": info[0], "kind": info[1], "sample": info[2]},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -209,23 +243,33 @@ def run_ours(args, rank, world, local_rank, dist):
     dev = torch.device("cuda", local_rank)
     hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
 
-    # model file (seeded random init, the config-1 architecture or SPANF3)
-    plan = bench_plan(args.model)
+    # model files (seeded random init); a chain through animejanai.conf
+    spec = MODELS[args.model]
+    W_IN, H_IN = spec["w"], spec["h"]
+    plans = bench_plans(args.model)
+    plan = plans[-1]  # the profiled (last) model
     spanf3 = args.model == "spanf3"
     mdir = tempfile.mkdtemp(prefix="ajib_bench_")
-    mpath = os.path.join(mdir, f"{args.model}_2x.ajnm")
-    with open(mpath, "wb") as f:
-        f.write(ajib.model_bytes(plan))
+    for k, pl in enumerate(plans):
+        with open(os.path.join(mdir, f"m{k + 1}.ajnm"), "wb") as f:
+            f.write(ajib.model_bytes(pl))
     torch.zeros(1, device=dev)
     if args.bands > 1:
         os.environ["AJIB_BANDS"] = str(args.bands)  # read by aji_create
-    vid = ajib.Video(mpath, W_IN, H_IN, cuda_context=current_context())
+    if len(plans) == 1:
+        vid = ajib.Video(os.path.join(mdir, "m1.ajnm"), W_IN, H_IN, cuda_context=current_context())
+    else:
+        conf = os.path.join(mdir, "animejanai.conf")
+        with open(conf, "w") as f:
+            f.write("[global]\nlogging=no\n\n[slot_1]\nprofile_name=bench\n" +
+                    "".join(f"chain_1_model_{k + 1}_name=m{k + 1}\n" for k in range(len(plans))))
+        vid = ajib.Video.from_conf(conf, mdir, slot=1, cuda_context=current_context())
     ow, oh = vid.configure(W_IN, H_IN)
 
     nfr = 4
     frames_in = []
     for i in range(nfr):
-        y, uv = p010_frame(1000 * rank + i)
+        y, uv = p010_frame(1000 * rank + i, W_IN, H_IN)
         frames_in.append((torch.from_numpy(y.view(np.int16)).to(dev), torch.from_numpy(uv.view(np.int16)).to(dev)))
     outs = [(torch.empty((oh, ow), dtype=torch.int16, device=dev), torch.empty((oh // 2, ow), dtype=torch.int16, device=dev))
             for _ in range(2)]
@@ -289,8 +333,9 @@ def run_ours(args, rank, world, local_rank, dist):
         ajib.lib.ajib_video_profile(vid.handle, 0)
 
     # ---- e2e: pinned host frame in, result read back, every step
-    hy = [torch.from_numpy(p010_frame(5000 + rank * 10 + i)[0].view(np.int16)).pin_memory() for i in range(2)]
-    huv = [torch.from_numpy(p010_frame(5000 + rank * 10 + i)[1].view(np.int16)).pin_memory() for i in range(2)]
+    hy = [torch.from_numpy(p010_frame(5000 + rank * 10 + i, W_IN, H_IN)[0].view(np.int16)).pin_memory() for i in range(2)]
+    huv = [torch.from_numpy(p010_frame(5000 + rank * 10 + i, W_IN, H_IN)[1].view(np.int16)).pin_memory()
+           for i in range(2)]
     hoy = torch.empty((oh, ow), dtype=torch.int16).pin_memory()
     houv = torch.empty((oh // 2, ow), dtype=torch.int16).pin_memory()
     din_y, din_uv = frames_in[0]
@@ -339,7 +384,10 @@ def run_ours(args, rank, world, local_rank, dist):
     # roofline of the dominant kernel: the body convs (Compact: 16 x 64 -> 64 + PReLU; SPANF3:
     # 15 x 48 -> 48, ReLU or the tanh gate with its 1x1 attention GEMM), FLOPs at conv resolution
     u = plan.get("unshuffle", 1)
-    cpx = (W_IN // u) * (H_IN // u)
+    pw, ph = W_IN, H_IN  # the profiled model's input size
+    for pl in plans[:-1]:
+        pw, ph = pw * plan_scale(pl), ph * plan_scale(pl)
+    cpx = (pw // u) * (ph // u)
     body = [k for k, st in enumerate(plan["steps"])
             if st["kind"] == 0 and st.get("in_", 0) == 0 and st.get("out", 0) == 0]
     flops_steps = [2.0 * 9 * plan["steps"][k]["cin"] * plan["steps"][k]["cout"] * cpx +
@@ -353,21 +401,15 @@ def run_ours(args, rank, world, local_rank, dist):
         flops_body = float(np.mean(flops_steps))
         achieved = flops_body / (body_ms / 1000.0) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_sus, "unit": "TFLOP/s",
-                "frac": achieved / tflops_sus, "traffic": None if spanf3 else BODY_TRAFFIC_BYTES,
-                "kernel": ("k_conv3x3_tc<48,64> (SPANF3 body convs 48->48, ReLU / tanh gate, 960x540)" if spanf3 else
-                           "k_conv3x3_tc<64,64> (body conv 64->64 + PReLU, 1920x1080)"),
+                "frac": achieved / tflops_sus, "traffic": BODY_TRAFFIC_BYTES if args.model in ("compact", "chain") else None,
+                "kernel": spec["kernel"],
                 "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json)",
                 "flops_per_launch": flops_body,
-                "frame_tflops": plan_flops(plan) / (t_ms / args.steps / 1000.0) / 1e12}
+                "frame_tflops": chain_flops(plans, W_IN, H_IN) / (t_ms / args.steps / 1000.0) / 1e12}
 
-    nsteps = len(plan["steps"])
-    if spanf3:
-        workload = "SPANF3 b5f48 2x video (2x pixel-unshuffle, tanh gates), 1920x1080 P010 BT.709 limited -> 3840x2160 P010"
-        model = "SPANF3 48 feat x 5 blocks, unshuffle 2, depth-to-space 4, random-init (seed 1, 0.7 He)"
-    else:
-        workload = "BASELINE config 1: Compact 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010"
-        model = "SRVGGNetCompact 64 feat x 16 body, PReLU, pixel_shuffle 2, random-init (seed 1)"
-    line = {"metric": METRIC_SPANF3 if spanf3 else METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+    nsteps = sum(len(pl["steps"]) for pl in plans)
+    workload, model = spec["workload"], spec["model"]
+    line = {"metric": spec["metric"], "value": value, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / world) / (1000.0 / SPANF3_PUBLISHED_MS) if spanf3 else None,
@@ -378,8 +420,8 @@ def run_ours(args, rank, world, local_rank, dist):
                        "bands": args.bands},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            # in the timed region: pre, the input pack, the net's steps, post
-            "gpu_launches": args.steps * (2 + (nsteps + 1) * max(1, args.bands)),
+            # in the timed region: pre, per net its input pack and steps, post
+            "gpu_launches": args.steps * (2 + (nsteps + len(plans)) * max(1, args.bands)),
             "clocks": clk}
     if spanf3:
         line["config"]["published"] = (f"reference {SPANF3_PUBLISHED_MS} ms per 1080p chain on an RTX 5090 "
@@ -479,16 +521,20 @@ def run_kernel(args):
                       "frac_of_hbm_peak": nbytes / (ms / 1000.0) / 1e9 / hbm_peak}), flush=True)
 
 
-def plan_flops(plan):
-    """Algorithmic FLOPs of one 1080p frame: every step's 2 * taps * cin * cout (plus a tanh gate's
-    2 * cout^2) per conv-resolution pixel."""
-    u = plan.get("unshuffle", 1)
-    per_px = 0.0
-    for s in plan["steps"]:
-        per_px += 2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2]
-        if s["kind"] == 0 and s.get("gate", 0) == 2:
-            per_px += 2.0 * s["cout"] ** 2
-    return per_px * (W_IN // u) * (H_IN // u)
+def chain_flops(plans, w, h):
+    """Algorithmic FLOPs of one frame of w x h through the chain: every step's 2 * taps * cin * cout
+    (plus a tanh gate's 2 * cout^2) per conv-resolution pixel."""
+    total = 0.0
+    for plan in plans:
+        u = plan.get("unshuffle", 1)
+        per_px = 0.0
+        for s in plan["steps"]:
+            per_px += 2.0 * s["w"].shape[0] * s["w"].shape[1] * s["w"].shape[2]
+            if s["kind"] == 0 and s.get("gate", 0) == 2:
+                per_px += 2.0 * s["cout"] ** 2
+        total += per_px * (w // u) * (h // u)
+        w, h = w * plan_scale(plan), h * plan_scale(plan)
+    return total
 
 
 def main():
@@ -502,8 +548,9 @@ def main():
     ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--model", default="compact", choices=["compact", "spanf3"],
-                    help="compact: BASELINE config 1 (the headline); spanf3: the shipping SPANF3 structure")
+    ap.add_argument("--model", default="compact", choices=list(MODELS),
+                    help="compact: BASELINE config 1 (the headline); span: config 3; chain: config 4; "
+                         "spanf3: the shipping SPANF3 structure")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

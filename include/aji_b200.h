@@ -249,7 +249,7 @@ AJIB_EXPORT int ajib_exec_set_bands(ajib_exec *e, int bands);
  * stream; profile_read synchronises and fills per-step summed milliseconds and run counts. */
 AJIB_EXPORT int ajib_exec_profile(ajib_exec *e, int on);
 AJIB_EXPORT int ajib_exec_profile_read(ajib_exec *e, double *ms, int *counts, int nsteps);
-/* The same for the executor inside a configured video context (aji.h). */
+/* The same for the executor inside a configured video context (aji.h): the chain's last model. */
 AJIB_EXPORT int ajib_video_profile(aji_ctx *c, int on);
 AJIB_EXPORT int ajib_video_profile_read(aji_ctx *c, double *ms, int *counts, int nsteps);
 /* device bytes held, launches per run */
