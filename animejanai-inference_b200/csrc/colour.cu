@@ -17,6 +17,7 @@
 #include <cstring>
 #include <new>
 
+#include "colour_math.cuh"
 #include "resample.h"
 #include "../../include/aji_b200.h"
 
@@ -86,9 +87,11 @@ __device__ __forceinline__ int mirror_index(int i, int n)
     return min(max(i, 0), n - 1);
 }
 
-__device__ __forceinline__ float quantize(float v, float qdiv, float qmax)
+// rintf(v / qdiv) clamped and scaled back. qdiv is 1, 16 or 64 (a power of two), so v / qdiv is
+// exactly v * qinv with qinv = 1 / qdiv.
+__device__ __forceinline__ float quantize(float v, float qdiv, float qinv, float qmax)
 {
-    return __fmul_rn(fminf(fmaxf(rintf(__fdiv_rn(v, qdiv)), 0.0f), qmax), qdiv);
+    return __fmul_rn(fminf(fmaxf(rintf(__fmul_rn(v, qinv)), 0.0f), qmax), qdiv);
 }
 
 // ---------------- pre: NV12/P010 -> fp16 NCHW RGB ----------------
@@ -193,6 +196,8 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
     const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
     const float db = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
     const float dr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));
+    const float rdb = __frcp_rn(db), rdr = __frcp_rn(dr);  // (x / db and x / dr by dev::div_by)
+    const float qinv = __frcp_rn(qdiv);
     // the tile's own luma pixels, and whether the staged halo holds all of them
     const int lx0 = 2 * cx0, lx1 = min(2 * (cx0 + kPostTW), w), ly0 = 2 * cy0, ly1 = min(2 * (cy0 + kPostTH), h);
     const bool covered = xlo <= lx0 && xhi >= lx1 - 1 && ylo <= ly0 && yhi >= ly1 - 1;
@@ -211,10 +216,10 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
             const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
             const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
             const int at = (cc & 1) * kPostPar + rr * kPostHalf + (cc >> 1);
-            su[at] = __fdiv_rn(__fsub_rn(b, Y), db);
-            sv[at] = __fdiv_rn(__fsub_rn(r, Y), dr);
+            su[at] = dev::div_by(__fsub_rn(b, Y), db, rdb);
+            sv[at] = dev::div_by(__fsub_rn(r, Y), dr, rdr);
             if (own_row && gx == mx && gx >= lx0 && gx < lx1)
-                reinterpret_cast<T *>(yp + (size_t)gy * ys)[gx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+                reinterpret_cast<T *>(yp + (size_t)gy * ys)[gx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qinv, qmax);
         }
     }
     if (!covered) {
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
             const size_t idx = (size_t)ly * w + lx;
             const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
             const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
-            reinterpret_cast<T *>(yp + (size_t)ly * ys)[lx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
+            reinterpret_cast<T *>(yp + (size_t)ly * ys)[lx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qinv, qmax);
         }
     }
     __syncthreads();
@@ -269,8 +274,8 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
                 }
             }
             T *row = reinterpret_cast<T *>(uvp + (size_t)cy * uvs);
-            row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qmax);
-            row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qmax);
+            row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qinv, qmax);
+            row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qinv, qmax);
         }
     }
 }
@@ -319,15 +324,16 @@ __global__ void k_post444(const __half *src, int w, int h, aji_csp csp, float qd
 {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (x >= w || y >= h) return;
+    const float qinv = __frcp_rn(qdiv);
     const size_t plane = (size_t)w * h, idx = (size_t)y * w + x;
     const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
     const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
     const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
     const float U = __fdiv_rn(__fsub_rn(b, Y), __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb)));
     const float V = __fdiv_rn(__fsub_rn(r, Y), __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr)));
-    reinterpret_cast<uint16_t *>(yp + (size_t)y * ys)[x] = (uint16_t)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qmax);
-    reinterpret_cast<uint16_t *>(cbp + (size_t)y * cbs)[x] = (uint16_t)quantize(__fmaf_rn(U, csp.cscale, csp.coff), qdiv, qmax);
-    reinterpret_cast<uint16_t *>(crp + (size_t)y * crs)[x] = (uint16_t)quantize(__fmaf_rn(V, csp.cscale, csp.coff), qdiv, qmax);
+    reinterpret_cast<uint16_t *>(yp + (size_t)y * ys)[x] = (uint16_t)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qinv, qmax);
+    reinterpret_cast<uint16_t *>(cbp + (size_t)y * cbs)[x] = (uint16_t)quantize(__fmaf_rn(U, csp.cscale, csp.coff), qdiv, qinv, qmax);
+    reinterpret_cast<uint16_t *>(crp + (size_t)y * crs)[x] = (uint16_t)quantize(__fmaf_rn(V, csp.cscale, csp.coff), qdiv, qinv, qmax);
 }
 
 __global__ void k_pre444(const uint8_t *yp, ptrdiff_t ys, const uint8_t *cbp, ptrdiff_t cbs, const uint8_t *crp,

@@ -97,3 +97,65 @@ extern "C" int ajib_selftest_umma(const void *a, const void *b, float *out, int 
                                                             err);
     return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
 }
+
+// ---- the colour kernels' division by a constant (colour_math.cuh) against the IEEE division ----
+#include "colour_math.cuh"
+
+namespace ajib {
+namespace {
+
+// Every float with 2^-80 <= |a| < 2^18 (exponent field 47..144, both signs) divided by 2 (1 - k)
+// for each given k, the divisors of the post pass's colour differences: dev::div_by against
+// __fdiv_rn. Counts the quotients that differ and records the first such a. Tinier dividends are
+// outside the correction's range (below ~2^-100 its remainder underflows) and outside the
+// pass's: its dividends b - Y are differences of an fp16 colour (a multiple of 2^-24) and a
+// weighted sum of fp16 colours by fp32 coefficients (a multiple of 2^-52), so zero or at least
+// 2^-52 in magnitude, and below 2^18 (fp16 colours are below 2^16).
+__global__ void k_div_check(const float *ks, int nk, unsigned long long *bad, unsigned int *first)
+{
+    float d[8], r[8];
+    for (int j = 0; j < nk; j++) {
+        d[j] = __fmul_rn(2.0f, __fsub_rn(1.0f, ks[j]));
+        r[j] = __frcp_rn(d[j]);
+    }
+    const uint64_t half = (145ull - 47ull) << 23, n = 2 * half;
+    unsigned long long mine = 0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t bits = ((uint32_t)(i % half) + (47u << 23)) | (i >= half ? 0x80000000u : 0u);
+        const float a = __uint_as_float(bits);
+        for (int j = 0; j < nk; j++) {
+            if (dev::div_by(a, d[j], r[j]) != __fdiv_rn(a, d[j])) {
+                mine++;
+                atomicCAS(first, 0xFFFFFFFFu, bits);
+            }
+        }
+    }
+    if (mine) atomicAdd(bad, mine);
+}
+
+}  // namespace
+}  // namespace ajib
+
+extern "C" int ajib_selftest_division(const float *k, int nk, unsigned long long *mismatches, unsigned int *first_bits)
+{
+    if (!k || nk < 1 || nk > 8 || !mismatches || !first_bits) return AJIB_ERR_ARGS;
+    float *dk = nullptr;
+    unsigned long long *dbad = nullptr;
+    unsigned int *dfirst = nullptr;
+    cudaError_t e = cudaMalloc(&dk, 8 * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&dbad, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&dfirst, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpy(dk, k, nk * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(dbad, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(dfirst, 0xFF, sizeof(unsigned int));
+    if (e == cudaSuccess) {
+        ajib::k_div_check<<<148 * 8, 256>>>(dk, nk, dbad, dfirst);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, dbad, sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(first_bits, dfirst, sizeof(unsigned int), cudaMemcpyDeviceToHost);
+    cudaFree(dk);
+    cudaFree(dbad);
+    cudaFree(dfirst);
+    return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}

@@ -263,6 +263,12 @@ AJIB_EXPORT int ajib_kernel_status(int clear);
  * b: [2n][32] fp16, out: [2][128][n] fp32 = A[shift:shift+128] x B-halves^T). For tests. */
 AJIB_EXPORT int ajib_selftest_umma(const void *a, const void *b, float *out, int n, int shift, int collector, int *err,
                                    void *stream);
+/* Self-test of the colour post pass's division by a constant (a reciprocal and one FMA correction
+ * in place of a division per sample): every float of magnitude in [2^-80, 2^18) (the pass's
+ * dividends are zero or in [2^-52, 2^18)) divided by 2 (1 - k[i]),
+ * i < nk <= 8, against the IEEE division; *mismatches counts differing quotients, *first_bits the
+ * first dividend's bits (0xFFFFFFFF: none). No reference counterpart (the reference divides). */
+AJIB_EXPORT int ajib_selftest_division(const float *k, int nk, unsigned long long *mismatches, unsigned int *first_bits);
 
 #ifdef __cplusplus
 }

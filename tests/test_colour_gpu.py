@@ -207,3 +207,21 @@ def test_resize_against_reference_kernels(sw, sh, dw, dh):
     torch.cuda.synchronize()
     ref.aji_plan_destroy(p)
     assert np.array_equal(_resize_ours(src, sw, sh, dw, dh), out.cpu().numpy().view(np.uint16))
+
+
+def test_post_division_matches_ieee():
+    """The post pass divides the colour differences by 2 (1 - kb) and 2 (1 - kr) with a reciprocal
+    and one FMA correction (Markstein): bit-identical to the IEEE division for every float the pass
+    can divide (2^-80 <= |a| < 2^18; its dividends are zero or in [2^-52, 2^18)), for the BT.601,
+    BT.709 and BT.2020 coefficients."""
+    import ctypes as C
+
+    import ajib
+    ks = []
+    for matrix in (1, 2, 3):
+        c = ajib.lib.aji_make_csp(2, matrix, 1)
+        ks += [c.kb, c.kr]
+    k = (C.c_float * 8)(*ks)
+    bad, first = C.c_ulonglong(), C.c_uint()
+    assert ajib.lib.ajib_selftest_division(k, len(ks), C.byref(bad), C.byref(first)) == 0
+    assert bad.value == 0, f"{bad.value} quotients differ, first dividend bits {first.value:#x}"
