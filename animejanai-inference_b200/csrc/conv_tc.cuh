@@ -454,7 +454,10 @@ __device__ __forceinline__ void plan_row(const RowWalk &w, uint32_t tmem, uint32
     p.commit_b = (v1 && r == last) ? accf0 + 8 * sl1 : 0u;
 }
 
-// One staged row's MMAs for tap columns [DX0, DX1): for each K step, one MMA per piece.
+// One staged row's MMAs for tap columns [DX0, DX1): for each K step, one MMA per piece. Two
+// pieces share their A operand (the same staged row and K step): the first fills the A collector
+// buffer, the second reads it from there (an MMA's cost is bound by fetching A, so a split row
+// costs little more than a whole one).
 template <int NP, int DX0, int DX1, int KS, int KC, int NG, int LBO_A>
 __device__ __forceinline__ void issue_taps(uint64_t adesc0, uint64_t bdesc0, const RowPlan &p)
 {
@@ -464,8 +467,12 @@ __device__ __forceinline__ void issue_taps(uint64_t adesc0, uint64_t bdesc0, con
         for (int kk = 0; kk < KS; kk++) {
             const uint64_t ad = adesc0 + (uint64_t)((kk * 2 * LBO_A + dx * 16) >> 4);
             const uint64_t bd = bdesc0 + (uint64_t)(((dx * KC + 2 * kk) * 3 * NG * 128) >> 4);
-#pragma unroll
-            for (int q = 0; q < NP; q++) dev::mma_f16(p.pd[q], ad, bd + p.pb[q], p.pi[q], 1u, 0);
+            if constexpr (NP == 1) {
+                dev::mma_f16(p.pd[0], ad, bd + p.pb[0], p.pi[0], 1u, 0);
+            } else {
+                dev::mma_f16(p.pd[0], ad, bd + p.pb[0], p.pi[0], 1u, 1);  // collector::a::fill
+                dev::mma_f16(p.pd[1], ad, bd + p.pb[1], p.pi[1], 1u, 3);  // collector::a::lastuse
+            }
         }
     }
 }
