@@ -127,6 +127,9 @@ template <int KPAD, int NPAD, int EK, int IN>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
     using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt, EK == kEpiD2S>;
+    // at least half the SM's shared memory, so one CTA holds an SM and its whole TMEM (a second
+    // CTA on the SM would only wait in its TMEM allocation)
+    constexpr int smem = Cf::SMEM > 117 * 1024 ? Cf::SMEM : 117 * 1024;
     static_assert(Cf::SMEM <= kMaxSmem, "shared memory budget");
     // the shared-memory opt-in is per device: set it once on each
     static std::atomic<uint64_t> done{0};
@@ -135,11 +138,11 @@ cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done.load() & bit)) {
         const cudaError_t attr =
-            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD, EK, IN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            cudaFuncSetAttribute(k_conv3x3_tc<KPAD, NPAD, EK, IN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (attr != cudaSuccess) return attr;
         done.fetch_or(bit);
     }
-    return launch_pdl(k_conv3x3_tc<KPAD, NPAD, EK, IN>, grid, kConvThreads, Cf::SMEM, s, p);
+    return launch_pdl(k_conv3x3_tc<KPAD, NPAD, EK, IN>, grid, kConvThreads, smem, s, p);
 }
 
 // The kernel instantiation for padded channel counts, epilogue kind and input mode. Built: every

@@ -136,18 +136,18 @@ struct ConvCfg {
     // copied in by the producer's bulk copies
     static constexpr int SKIP_ROW = 3 * kTileM * 2;
     static constexpr int SKIP_BYTES = SKIP ? S * SKIP_ROW : 0;
-    static constexpr int FIXED = AOFF + ATT_BYTES + SKIP_BYTES + 3 * 64 * 4 + 1024 + 1024;
+    static constexpr int FIXED = AOFF + ATT_BYTES + SKIP_BYTES + 3 * 64 * 4 + 1024 + 1024 + 1024;
     static constexpr int NS_FIT = (kMaxSmem - FIXED) / STAGE;
-    static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;
+    static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;  // stages of RP rows: as many as fit, up to 6
     static_assert(NS >= 2 && S >= 4, "pipeline depth");
     static constexpr int ATOFF = AOFF + NS * STAGE;  // attention B, then A tiles 0 and 1
     static constexpr int SKOFF = ATOFF + ATT_BYTES;  // skip rows [S][3][128] fp16
     static constexpr int POFF = SKOFF + SKIP_BYTES;  // bias[64], slope[64], attention bias[64] floats
     // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S]
     static constexpr int BOFF = POFF + 3 * 64 * 4;
-    static constexpr int PLOFF = BOFF + 512;        // RowPlan per staged row
-    static constexpr int SMEM = BOFF + 1024 + 1024;  // + alignment slack for the base
-    static_assert((2 * NS + 3 * S + 4) * 8 + 8 <= 512 && NS * RP * 48 <= 512, "barrier and plan area");
+    static constexpr int PLOFF = BOFF + 1024;       // RowPlan per staged row
+    static constexpr int SMEM = BOFF + 1024 + 1024 + 1024;  // + alignment slack for the base
+    static_assert((2 * NS + 3 * S + 4) * 8 + 8 <= 1024 && NS * RP * 48 <= 1024, "barrier and plan area");
     static_assert(SMEM <= kMaxSmem, "shared memory budget");
 };
 
@@ -576,32 +576,48 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 while (ok && walk.next()) {
                     const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
                     if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
-                    // each row's copies go out once the accumulators it starts are free (issuing them
-                    // earlier, as soon as the stage is free, measured slower: more reads in flight
-                    // against the epilogue's writes)
+                    // the stage's copies go out as soon as its buffer is free (waiting first for the
+                    // accumulators the rows start, as the plans need, left the MMA thread waiting
+                    // ~800 cycles a stage for data: the TMEM ring, not the stages, bounded how far
+                    // ahead rows were fetched); then the accumulator waits, the plans and, for
+                    // depth-to-space, the skip rows, whose buffers belong to the accumulator slots
+                    RowPlan pl[C::RP];
+                    RowWaits wts[C::RP];
+                    int rows_r[C::RP], rows_strip[C::RP];
+                    int n = 0;
+#pragma unroll
+                    for (int h = 0; h < C::RP; h++) {
+                        if (h > 0 && (n < h || !walk.next())) break;
+                        plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, pl[h], wts[h]);
+                        rows_r[h] = walk.r;
+                        rows_strip[h] = walk.strip;
+                        if (lane == 0) dev::mbar_expect_tx(full0 + 8 * s, bytes);
+                        const uint32_t dst = abase + s * C::STAGE + h * C::SLOT;
+                        // padded column x0 is pixel x0 - 1: the left halo
+                        const __half *row = a.src + (size_t)walk.r * kcin * chunk_row + (size_t)walk.strip * kTileM * 8;
+                        if (lane < kcin)
+                            dev::bulk_load(dst + lane * C::LBO_A, row + lane * chunk_row, kHalo * 16, full0 + 8 * s);
+                        n = h + 1;
+                    }
                     int h = 0;
+#pragma unroll
                     for (; h < C::RP; h++) {
-                        if (h > 0 && !walk.next()) break;
-                        RowWaits wt;
-                        RowPlan p;
-                        plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, p, wt);
+                        if (h >= n) break;
+                        const RowWaits &wt = wts[h];
                         bool good = true;
                         if (lane == 0) good = wt.wait(a.err);
                         if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
-                        if (lane == 0) {
-                            plans[s * C::RP + h] = p;
-                            dev::mbar_expect_tx(full0 + 8 * s, bytes);
-                        }
+                        if (lane == 0) plans[s * C::RP + h] = pl[h];
                         if constexpr (EK == kEpiD2S) {
                             // the skip rows of the outputs this row starts (r + 1; r at an image's
                             // first row), into their slots: lanes 8-10 and 11-13, one plane each
                             if (a.skip_smem) {
-                                const int x0 = walk.strip * kTileM;
+                                const int x0 = rows_strip[h] * kTileM;
                                 const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
                                 const int k = lane - 8, which = k / 3, c3 = k % 3;
                                 const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
                                 const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
-                                const int orow = which == 0 ? walk.r + 1 : walk.r;
+                                const int orow = which == 0 ? rows_r[h] + 1 : rows_r[h];
                                 if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
                                 __syncwarp();
                                 if (mine)
@@ -609,11 +625,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                                                    a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
                             }
                         }
-                        const uint32_t dst = abase + s * C::STAGE + h * C::SLOT;
-                        // padded column x0 is pixel x0 - 1: the left halo
-                        const __half *row = a.src + (size_t)walk.r * kcin * chunk_row + (size_t)walk.strip * kTileM * 8;
-                        if (lane < kcin)
-                            dev::bulk_load(dst + lane * C::LBO_A, row + lane * chunk_row, kHalo * 16, full0 + 8 * s);
                         __syncwarp();
                     }
                     // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
