@@ -812,20 +812,28 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             for (int o = ya; o < yb; o++, ot++) {
                 if ((int)(ot & 1u) != g) continue;
                 const int slot = ring_slot<S>(ot);
+                // the block input x: loaded before the waits, so its latency overlaps them
+                EpiIn<NPAD> in;
+                epi_prefetch<kEpiGate, NPAD, 0>(in, a, o, x);
                 bool ok = good && dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull);
                 if (ok) {
-                    uint32_t oh[NPAD / 2];  // fp16(o + bias), channel pairs
                     __syncwarp();
                     dev::tc_fence_after();
                     const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
-                    // 16 columns at a time, straight to fp16 (few registers live beside the block input)
+                    // 16 columns at a time, straight to fp16 into the A tile (few registers live
+                    // beside the block input)
 #pragma unroll
                     for (int c = 0; c < NPAD; c += 16) {
                         float t[16];
                         dev::tmem_ld16(taddr + c, t);
                         dev::tmem_wait_ld();
+                        uint32_t oh[8];  // fp16(o + bias), channel pairs c .. c + 15
 #pragma unroll
-                        for (int j = 0; j < 16; j += 2) oh[(c + j) / 2] = pack_h2(t[j] + sbias[c + j], t[j + 1] + sbias[c + j + 1]);
+                        for (int j = 0; j < 16; j += 2) oh[j / 2] = pack_h2(t[j] + sbias[c + j], t[j + 1] + sbias[c + j + 1]);
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++)
+                            *reinterpret_cast<uint4 *>(atile + (c / 8 + h2) * (kTileM * 16) + px * 16) =
+                                make_uint4(oh[4 * h2], oh[4 * h2 + 1], oh[4 * h2 + 2], oh[4 * h2 + 3]);
                     }
 #pragma unroll
                     for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(taddr + c);
@@ -833,14 +841,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     dev::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
-#pragma unroll
-                    for (int c = 0; c < NPAD / 8; c++)
-                        *reinterpret_cast<uint4 *>(atile + c * (kTileM * 16) + px * 16) =
-                            make_uint4(oh[4 * c], oh[4 * c + 1], oh[4 * c + 2], oh[4 * c + 3]);
                 }
-                // the block input x: its loads overlap the attention GEMM
-                EpiIn<NPAD> in;
-                epi_prefetch<kEpiGate, NPAD, 0>(in, a, o, x);
                 // the tile is read by the tensor core (the async proxy) once the whole group wrote it
                 dev::fence_proxy_async();
                 dev::tc_fence_before();
