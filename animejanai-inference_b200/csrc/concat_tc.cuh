@@ -10,7 +10,8 @@
  * (source, 8-channel chunk) row segment of a tile is one 2048-byte bulk copy of the row-chunked
  * map (the tile's 128 pixels are contiguous in it), staged K-major as [K/8][128][8] — the MMA's A
  * layout without any reshuffle. Persistent CTAs walk contiguous runs of (strip, row) tiles.
- * Roles: warp 0 producer (one thread), warp 1 MMA issuer (one thread) and TMEM owner, warps 2-5
+ * Roles: warp 0 producer (lane 0 arms the barriers, every lane issues copies), warp 1 MMA issuer
+ * (one thread) and TMEM owner, warps 2-5
  * epilogue (TMEM lane quarter = warp % 4, one pixel per thread).
  */
 #pragma once
@@ -103,30 +104,34 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
     const int H = a.H, W = a.W;
     (void)H;
     if (warp == 0) {
-        // ================= producer
-        if (lane == 0) {
-            SegIter seg(W, a.row_begin, a.row_end);
-            uint32_t it = 0;
-            int strip, ya, yb;
-            bool ok = true;
-            const size_t chunk_row = (size_t)a.pitch * 8;  // halves
-            while (ok && seg.next(strip, ya, yb)) {
-                for (int y = ya; y < yb; y++, it++) {
-                    const uint32_t s = it % NS, ph = (it / NS) & 1;
-                    if (!(ok = dev::mbar_wait(empty0 + 8 * s, ph ^ 1, a.err, kErrCatEmpty))) break;
-                    dev::mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)(kc_real * kCatChunkBytes));
-                    const uint32_t dst = abase + s * L.stage;
-                    for (int k = 0; k < a.nsrc; k++)
-                        for (int j = 0; j < cc; j++)
-                            dev::bulk_load(dst + (k * cc + j) * kCatChunkBytes,
-                                           a.src[k] + ((size_t)y * cc + j) * chunk_row + (size_t)(strip * kTileM + 1) * 8,
-                                           kCatChunkBytes, full0 + 8 * s);
+        // ================= producer: the whole warp walks the tiles (uniform control flow); lane 0
+        // arms the stage's barrier, and the tile's (source, chunk) copies go out one per lane
+        // (one thread issuing a tile's 24 copies was the kernel's bottleneck)
+        SegIter seg(W, a.row_begin, a.row_end);
+        uint32_t it = 0;
+        int strip, ya, yb;
+        bool ok = true;
+        const size_t chunk_row = (size_t)a.pitch * 8;  // halves
+        const int ncopy = a.nsrc * cc;
+        while (ok && seg.next(strip, ya, yb)) {
+            for (int y = ya; y < yb; y++, it++) {
+                const uint32_t s = it % NS, ph = (it / NS) & 1;
+                if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrCatEmpty))) break;
+                if (lane == 0) dev::mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)(kc_real * kCatChunkBytes));
+                __syncwarp();
+                const uint32_t dst = abase + s * L.stage;
+                for (int q = lane; q < ncopy; q += 32) {
+                    const int k = q / cc, j = q % cc;
+                    dev::bulk_load(dst + q * kCatChunkBytes,
+                                   a.src[k] + ((size_t)y * cc + j) * chunk_row + (size_t)(strip * kTileM + 1) * 8,
+                                   kCatChunkBytes, full0 + 8 * s);
                 }
+                __syncwarp();
             }
-            if (!ok && it > 0) {
-                const uint32_t s = (it - 1) % NS, ph = ((it - 1) / NS) & 1;
-                dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
-            }
+        }
+        if (!ok && it > 0 && lane == 0) {
+            const uint32_t s = (it - 1) % NS, ph = ((it - 1) / NS) & 1;
+            dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
         }
     } else if (warp == 1) {
         // ================= MMA issuer
