@@ -53,8 +53,8 @@ lib.ajib_conv3x3_launch.restype = C.c_int
 lib.ajib_conv3x3_launch_images.argtypes = [C.POINTER(ConvOp), _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                            _vp]
 lib.ajib_conv3x3_launch_images.restype = C.c_int
-lib.ajib_feature_pitch.argtypes = [C.c_int]
-lib.ajib_feature_pitch.restype = C.c_int
+lib.ajib_feature_strips.argtypes = [C.c_int]
+lib.ajib_feature_strips.restype = C.c_int
 lib.ajib_feature_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
 lib.ajib_feature_bytes.restype = C.c_size_t
 lib.ajib_kernel_status.argtypes = [C.c_int]
@@ -143,7 +143,7 @@ lib.ajib_concat1x1_launch.restype = C.c_int
 
 
 def concat1x1(w, srcs, c, dst, H, W, row_begin=0, row_end=0, stream=0):
-    """SPAN's concat + 1x1 conv on row-chunked maps (ajib_concat1x1_launch); w: Weights(taps=1)."""
+    """SPAN's concat + 1x1 conv on strip-chunked maps (ajib_concat1x1_launch); w: Weights(taps=1)."""
     arr = (_vp * len(srcs))(*srcs)
     return lib.ajib_concat1x1_launch(w.handle, len(srcs), arr, c, dst, H, W, row_begin, row_end, stream)
 

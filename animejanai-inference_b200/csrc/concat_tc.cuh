@@ -6,10 +6,10 @@
  *
  * GEMM with M = 128 consecutive pixels of one row, K = nsrc * c (the concatenation, padded to a
  * multiple of 16), N = c. The work is bound by HBM (for SPAN's 4 x 48 channels a 128-pixel tile
- * reads 48 KB and writes 12 KB for 2.4 MFLOP), so the design keeps many tiles in flight: every
- * (source, 8-channel chunk) row segment of a tile is one 2048-byte bulk copy of the row-chunked
- * map (the tile's 128 pixels are contiguous in it), staged K-major as [K/8][128][8] — the MMA's A
- * layout without any reshuffle. Persistent CTAs walk contiguous runs of (strip, row) tiles.
+ * reads 48 KB and writes 12 KB for 2.4 MFLOP), so the design keeps many tiles in flight: each
+ * source's (row, strip) block of the strip-chunked map (conv_tc.cuh) is one bulk copy, staged
+ * K-major as [K/8][130][8] — the MMA's A layout, its descriptor starting past the halo column.
+ * Persistent CTAs walk contiguous runs of (strip, row) tiles.
  * Roles: warp 0 producer (lane 0 arms the barriers, every lane issues copies), warp 1 MMA issuer
  * (one thread) and TMEM owner, warps 2-5
  * epilogue (TMEM lane quarter = warp % 4, one pixel per thread).
@@ -26,7 +26,7 @@ namespace ajib {
 constexpr int kCatThreads = 6 * 32;
 constexpr int kCatMaxStages = 4;
 constexpr int kCatSlots = 8;        // TMEM accumulator slots of 64 columns
-constexpr int kCatChunkBytes = kTileM * 16;  // one 8-channel chunk of a 128-pixel tile
+constexpr int kCatChunkBytes = kStripW * 16;  // one 8-channel chunk of a strip, halo columns included
 
 enum { kErrCatEmpty = 201, kErrCatFull = 202, kErrCatAccEmpty = 203, kErrCatAccFull = 204, kErrCatWeights = 205,
        kErrCatDrain = 206 };
@@ -37,7 +37,7 @@ struct CatDev {
     const unsigned char *wimg;  // B image [kpad / 8][npad / 8][8 n][8 k]
     const float *bias;     // npad floats
     int *err;
-    int nsrc, c, H, W, pitch, kpad, row_begin, row_end;
+    int nsrc, c, H, W, nstrips, kpad, row_begin, row_end;
     int ns;                // pipeline stages
 };
 
@@ -47,7 +47,7 @@ struct CatSmem {
     __host__ __device__ CatSmem(int kpad, int npad, int ns)
     {
         b_bytes = (kpad * npad * 2 + 1023) / 1024 * 1024;
-        stage = kpad / 8 * kCatChunkBytes;
+        stage = (kpad / 8 * kCatChunkBytes + 127) / 128 * 128;
         a_off = b_bytes;
         bias_off = a_off + ns * stage;
         bar_off = bias_off + 64 * 4;
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
     if (warp == 1) dev::tmem_alloc(dev::smem_u32(tslot), 512);
     // K chunks past the concatenation (padding to a multiple of 16) stay zero
     for (int s = 0; s < NS; s++)
-        for (int i = tid; i < (KC - kc_real) * kTileM; i += kCatThreads)
+        for (int i = tid; i < (KC - kc_real) * kStripW; i += kCatThreads)
             reinterpret_cast<uint4 *>(sm + L.a_off + s * L.stage + kc_real * kCatChunkBytes)[i] = make_uint4(0, 0, 0, 0);
     for (int n = tid; n < 64; n += kCatThreads) sbias[n] = n < NPAD ? a.bias[n] : 0.f;
     dev::fence_proxy_async();
@@ -111,8 +111,7 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
         uint32_t it = 0;
         int strip, ya, yb;
         bool ok = true;
-        const size_t chunk_row = (size_t)a.pitch * 8;  // halves
-        const int ncopy = a.nsrc * cc;
+        const int ncopy = a.nsrc;
         while (ok && seg.next(strip, ya, yb)) {
             for (int y = ya; y < yb; y++, it++) {
                 const uint32_t s = it % NS, ph = (it / NS) & 1;
@@ -120,12 +119,10 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
                 if (lane == 0) dev::mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)(kc_real * kCatChunkBytes));
                 __syncwarp();
                 const uint32_t dst = abase + s * L.stage;
-                for (int q = lane; q < ncopy; q += 32) {
-                    const int k = q / cc, j = q % cc;
-                    dev::bulk_load(dst + q * kCatChunkBytes,
-                                   a.src[k] + ((size_t)y * cc + j) * chunk_row + (size_t)(strip * kTileM + 1) * 8,
-                                   kCatChunkBytes, full0 + 8 * s);
-                }
+                // source k's (row, strip) block: its cc chunks, K chunks k * cc ..
+                for (int k = lane; k < ncopy; k += 32)
+                    dev::bulk_load(dst + k * cc * kCatChunkBytes, a.src[k] + map_at(y, strip, 0, 0, a.nstrips, cc),
+                                   (uint32_t)(cc * kCatChunkBytes), full0 + 8 * s);
                 __syncwarp();
             }
         }
@@ -138,7 +135,8 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
         if (lane == 0) {
             bool ok = dev::mbar_wait(wbar, 0, a.err, kErrCatWeights);
             const uint64_t bdesc0 = dev::sdesc(wbase, (NPAD / 8) * 128, 128);
-            const uint64_t adesc_base = dev::sdesc(abase, kCatChunkBytes, 128);
+            // A starts at column 1 of each staged chunk (column 0 is the halo)
+            const uint64_t adesc_base = dev::sdesc(abase + 16, kCatChunkBytes, 128);
             const uint32_t idesc = dev::idesc_f16_f32(kTileM, NPAD);
             SegIter seg(W, a.row_begin, a.row_end);
             uint32_t it = 0;
@@ -170,7 +168,6 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
         uint32_t it = 0;
         int strip, ya, yb;
         bool ok = true;
-        const size_t chunk_row = (size_t)a.pitch * 8;
         while (ok && seg.next(strip, ya, yb)) {
             const int x = strip * kTileM + q * 32 + lane;
             for (int y = ya; y < yb; y++, it++) {
@@ -191,7 +188,6 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
                 __syncwarp();
                 if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                 if (x < W) {
-                    __half *drow = a.dst + (size_t)y * cc * chunk_row + (size_t)(x + 1) * 8;
 #pragma unroll
                     for (int j = 0; j < NPAD / 8; j++) {
                         if (j < cc) {
@@ -200,7 +196,7 @@ __global__ void __launch_bounds__(kCatThreads, 1) k_concat1x1(const __grid_const
                             w4.y = pack_h2(v[j * 8 + 2] + sbias[j * 8 + 2], v[j * 8 + 3] + sbias[j * 8 + 3]);
                             w4.z = pack_h2(v[j * 8 + 4] + sbias[j * 8 + 4], v[j * 8 + 5] + sbias[j * 8 + 5]);
                             w4.w = pack_h2(v[j * 8 + 6] + sbias[j * 8 + 6], v[j * 8 + 7] + sbias[j * 8 + 7]);
-                            *reinterpret_cast<uint4 *>(drow + j * chunk_row) = w4;
+                            store_px(a.dst, y, x, j, a.nstrips, cc, w4);
                         }
                     }
                 }

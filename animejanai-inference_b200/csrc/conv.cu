@@ -357,7 +357,7 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     }
     p.row_begin = row_begin;
     p.row_end = row_end;
-    p.pitch = feature_pitch(W);
+    p.nstrips = feature_strips(W);
     p.img_h = img_h;
     p.skip_smem = op->out != AJIB_OUT_NHWC && resid && op->in == AJIB_IN_NHWC && W % 8 == 0 &&
                   ((uintptr_t)resid & 15) == 0;
@@ -417,7 +417,7 @@ extern "C" int ajib_concat1x1_launch(const ajib_weights *w, int nsrc, const void
     p.c = c;
     p.H = H;
     p.W = W;
-    p.pitch = feature_pitch(W);
+    p.nstrips = feature_strips(W);
     p.kpad = w->kpad;
     p.row_begin = row_begin;
     p.row_end = row_end;
@@ -440,12 +440,12 @@ extern "C" int ajib_concat1x1_launch(const ajib_weights *w, int nsrc, const void
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
 }
 
-extern "C" int ajib_feature_pitch(int W) { return W > 0 ? feature_pitch(W) : 0; }
+extern "C" int ajib_feature_strips(int W) { return W > 0 ? feature_strips(W) : 0; }
 
 extern "C" size_t ajib_feature_bytes(int H, int W, int C)
 {
     if (H < 1 || W < 1 || C < 8 || C % 8) return 0;
-    return (size_t)H * (C / 8) * feature_pitch(W) * 16;
+    return (size_t)H * feature_strips(W) * (C / 8) * kStripW * 16;
 }
 
 extern "C" int ajib_kernel_status(int clear)
@@ -463,17 +463,17 @@ namespace ajib {
 namespace {
 
 // One conv pixel per thread: the NCHW fp16 model input [3][H][W] -> chunk 0 {r, g, b, 0 x 5} of
-// an 8-channel row-chunked map; pixel-unshuffled by 2 ([3][2H][2W] -> channels c*4 + ry*2 + rx,
+// an 8-channel strip-chunked map; pixel-unshuffled by 2 ([3][2H][2W] -> channels c*4 + ry*2 + rx,
 // then 4 zeros) -> chunks 0 and 1 of a 16-channel map. Normalised as the conv's own NCHW input
-// path does it ((x - mean) * scale, rounded to fp16). Pad columns are never written.
+// path does it ((x - mean) * scale, rounded to fp16). Strip edge pixels also go to the
+// neighbouring strips' halo columns; the image's edge columns are never written.
 __global__ void __launch_bounds__(128) k_pack_input(const __half *src, int H, int W, int unshuffle, int in_norm,
                                                      float m0, float m1, float m2, float s0, float s1, float s2,
-                                                     int pitch, int row_begin, __half *dst)
+                                                     int nstrips, int row_begin, __half *dst)
 {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = row_begin + blockIdx.y;
     if (x >= W) return;
     const float mean[3] = {m0, m1, m2}, scale[3] = {s0, s1, s2};
-    const size_t chunk_row = (size_t)pitch * 8;
     if (!unshuffle) {
         const size_t plane = (size_t)H * W, at = (size_t)y * W + x;
         float v[3];
@@ -482,8 +482,7 @@ __global__ void __launch_bounds__(128) k_pack_input(const __half *src, int H, in
             v[c] = __half2float(__ldg(src + c * plane + at));
             if (in_norm) v[c] = (v[c] - mean[c]) * scale[c];
         }
-        *reinterpret_cast<uint4 *>(dst + (size_t)y * chunk_row + (size_t)(x + 1) * 8) =
-            make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u);
+        store_px(dst, y, x, 0, nstrips, 1, make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u));
         return;
     }
     const int IW = 2 * W;
@@ -498,9 +497,8 @@ __global__ void __launch_bounds__(128) k_pack_input(const __half *src, int H, in
             q[j] = pack_h2((f.x - mean[c]) * scale[c], (f.y - mean[c]) * scale[c]);
         }
     }
-    __half *d = dst + (size_t)y * 2 * chunk_row + (size_t)(x + 1) * 8;
-    *reinterpret_cast<uint4 *>(d) = make_uint4(q[0], q[1], q[2], q[3]);
-    *reinterpret_cast<uint4 *>(d + chunk_row) = make_uint4(q[4], q[5], 0u, 0u);
+    store_px(dst, y, x, 0, nstrips, 2, make_uint4(q[0], q[1], q[2], q[3]));
+    store_px(dst, y, x, 1, nstrips, 2, make_uint4(q[4], q[5], 0u, 0u));
 }
 
 }  // namespace
@@ -512,7 +510,7 @@ int pack_model_input(const void *src, int H, int W, int unshuffle, bool in_norm,
     if (((uintptr_t)src & 3) || ((uintptr_t)dst & 15)) return AJIB_ERR_ARGS;
     const dim3 grid((W + 127) / 128, row_end - row_begin);
     k_pack_input<<<grid, 128, 0, s>>>((const __half *)src, H, W, unshuffle ? 1 : 0, in_norm ? 1 : 0, mean[0], mean[1],
-                                      mean[2], scale[0], scale[1], scale[2], feature_pitch(W), row_begin, (__half *)dst);
+                                      mean[2], scale[0], scale[1], scale[2], feature_strips(W), row_begin, (__half *)dst);
     return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
 }
 

@@ -72,28 +72,32 @@ typedef struct ajib_conv {
  * receives the reason for a refusal. Returns 1 or 0. */
 AJIB_EXPORT int ajib_conv_supported(const ajib_conv *op, char *why, size_t why_size);
 
-/* Feature maps (the NHWC tensors between steps) are stored row-chunked and padded: element
- * (y, x, c) of a C-channel map (C a multiple of 8) is the fp16 at index
- *   ((y * C/8 + c/8) * pitch + x + 1) * 8 + c % 8,   pitch = ajib_feature_pitch(W),
- * and the pad columns (x = -1 and x >= W) must hold zeros (clear the buffer once; the kernels never
- * write them). Each 8-channel chunk of a row is then one contiguous run the kernels copy in one
- * piece. ajib_feature_bytes gives the buffer size. */
-/* The 1x1 convolution over the concatenation of nsrc (2..4) row-chunked maps of c channels (c a
- * multiple of 8, 8..64) into a row-chunked map of c channels, plus bias (SPAN's concat + conv;
+/* Feature maps (the NHWC tensors between steps) are stored strip-chunked: each row of a C-channel
+ * map (C a multiple of 8) is cut into S = ajib_feature_strips(W) strips of 128 pixels, and each
+ * (row, strip) is one contiguous block of C/8 chunks of 130 columns of 8 fp16 channels — the
+ * strip's pixels and a halo column on each side. Element (y, x, c), x in strip s = x / 128, is the
+ * fp16 at index
+ *   ((((y * S + s) * C/8 + c/8) * 130 + x - 128 s + 1) * 8 + c % 8,
+ * and a strip's halo columns (0 and 129) hold copies of the neighbouring strips' edge pixels; the
+ * columns at the image's edges (column 0 of strip 0, and every column past W) must hold zeros
+ * (clear the buffer once; the kernels never write them). A staged input row is then one
+ * contiguous block the kernels copy in one piece. ajib_feature_bytes gives the buffer size. */
+/* The 1x1 convolution over the concatenation of nsrc (2..4) strip-chunked maps of c channels (c a
+ * multiple of 8, 8..64) into a strip-chunked map of c channels, plus bias (SPAN's concat + conv;
  * replaces the reference's ConcatConv1x1 / k_concat1x1, src/native/conv.h:38-102 and
  * conv_kernels.cuh:351-407). w: 1x1 weights uploaded with taps 1, cin nsrc * c, cout c (K index
  * k * c + i is channel i of source k). Rows [row_begin, row_end) (row_end <= 0: all). */
 AJIB_EXPORT int ajib_concat1x1_launch(const ajib_weights *w, int nsrc, const void *const *srcs, int c, void *dst,
                                       int H, int W, int row_begin, int row_end, void *stream);
-AJIB_EXPORT int ajib_feature_pitch(int W);
+AJIB_EXPORT int ajib_feature_strips(int W);
 AJIB_EXPORT size_t ajib_feature_bytes(int H, int W, int C);
 
 /* Launch op at conv resolution H x W on output rows [row_begin, row_end) (row_end <= 0: all
- * rows) (reference src/native/conv.h:91, launch). src: a row-chunked map [H][cin] or the NCHW
+ * rows) (reference src/native/conv.h:91, launch). src: a strip-chunked map [H][cin] or the NCHW
  * fp16 model input [3][H][W] ([3][2H][2W] pixel-unshuffled). resid: gates read the block input x
- * as a row-chunked map [H][cout]; depth-to-space outputs add the NCHW model input [3][H][W]
+ * as a strip-chunked map [H][cout]; depth-to-space outputs add the NCHW model input [3][H][W]
  * (nearest upsampled) when resid is not NULL (not with a pixel-unshuffled input: AJIB_ERR_ARGS).
- * dst: a row-chunked map [H][cout] or NCHW [3][R*H][R*W]. Rows outside the range are neither
+ * dst: a strip-chunked map [H][cout] or NCHW [3][R*H][R*W]. Rows outside the range are neither
  * read beyond the one-row halo nor written, so a frame can be run as bands. */
 AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const void *resid, void *dst, int H, int W,
                                     int row_begin, int row_end, void *stream);

@@ -7,7 +7,8 @@ bounds (the reference's DevBuf pattern, native_conv_test.cu:49-76)."""
 import numpy as np
 import pytest
 
-from util import conv_weights, f16r, from_rows, oracle_concat, oracle_conv, rows_pad_mask, to_f16_bits, to_rows
+from util import (conv_weights, f16r, from_rows, oracle_concat, oracle_conv, rows_halo_consistent, rows_pad_mask,
+                  to_f16_bits, to_rows)
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -22,13 +23,13 @@ def dev_f16(x):
 
 
 def dev_rows(x):
-    """An NHWC map in the engine's row-chunked layout (zero pad columns)."""
+    """An NHWC map in the engine's strip-chunked layout (zero image-edge columns)."""
     return torch.from_numpy(to_rows(x).astype(np.float16)).cuda()
 
 
 class Guarded:
     """A device fp16 buffer with GUARD elements of a fixed pattern on each side. An NHWC shape
-    (H, W, C) is allocated row-chunked, its pad columns also holding the pattern: the kernels must
+    (H, W, C) is allocated strip-chunked, its image-edge columns also holding the pattern: the kernels must
     never write them."""
 
     def __init__(self, shape, nhwc=False):
@@ -36,7 +37,7 @@ class Guarded:
         self.shape = shape
         if nhwc:
             H, W, Cc = shape
-            n = H * (Cc // 8) * ((W + 127) // 128 * 128 + 2) * 8
+            n = H * ((W + 127) // 128) * (Cc // 8) * 130 * 8
         else:
             n = int(np.prod(shape))
         self.n = n
@@ -52,7 +53,8 @@ class Guarded:
         if not self.nhwc:
             return body.view(np.float16).astype(np.float32).reshape(self.shape)
         H, W, Cc = self.shape
-        assert (body[rows_pad_mask(H, W, Cc).ravel()] == GUARD_BITS).all(), "write into a pad column"
+        assert (body[rows_pad_mask(H, W, Cc).ravel()] == GUARD_BITS).all(), "write into an image-edge column"
+        assert rows_halo_consistent(body, H, W, Cc), "a strip halo column differs from its neighbour's edge pixel"
         return from_rows(body.view(np.float16).astype(np.float32), H, W, Cc)
 
 

@@ -182,31 +182,58 @@ def yuv420_frame(rng, w, h, fmt, lo=None, hi=None):
     return y, uv
 
 
-# ---- row-chunked padded feature maps (the engine's layout for maps between steps) ----
-def feature_pitch(W):
-    return (W + 127) // 128 * 128 + 2
+# ---- strip-chunked feature maps (the engine's layout for maps between steps) ----
+STRIP_W = 130  # a strip's 128 pixels and a halo column on each side
+
+
+def feature_strips(W):
+    return (W + 127) // 128
 
 
 def to_rows(x, pad_value=0.0):
-    """NHWC [H][W][C] -> row-chunked [H][C/8][pitch][8] with pad columns = pad_value."""
+    """NHWC [H][W][C] -> strip-chunked [H][S][C/8][130][8]: each strip's halo columns hold the
+    neighbouring strips' edge pixels; the image's edge columns (column 0 of strip 0, everything
+    past W) hold pad_value."""
     H, W, Cc = x.shape
-    KC, P = Cc // 8, feature_pitch(W)
-    out = np.full((H, KC, P, 8), pad_value, dtype=np.float32)
-    out[:, :, 1:W + 1, :] = np.asarray(x, np.float32).reshape(H, W, KC, 8).transpose(0, 2, 1, 3)
+    KC, S = Cc // 8, feature_strips(W)
+    padded = np.full((H, S * 128 + 2, KC, 8), pad_value, dtype=np.float32)
+    padded[:, 1:W + 1] = np.asarray(x, np.float32).reshape(H, W, KC, 8)
+    out = np.empty((H, S, KC, STRIP_W, 8), np.float32)
+    for s in range(S):
+        out[:, s] = padded[:, 128 * s:128 * s + STRIP_W].transpose(0, 2, 1, 3)
     return out
 
 
 def from_rows(buf, H, W, Cc):
-    KC, P = Cc // 8, feature_pitch(W)
-    return np.asarray(buf).reshape(H, KC, P, 8)[:, :, 1:W + 1, :].transpose(0, 2, 1, 3).reshape(H, W, Cc)
+    """The pixels of a strip-chunked map, NHWC [H][W][C]."""
+    KC, S = Cc // 8, feature_strips(W)
+    b = np.asarray(buf).reshape(H, S, KC, STRIP_W, 8)
+    full = b[:, :, :, 1:129, :].transpose(0, 1, 3, 2, 4).reshape(H, S * 128, Cc)
+    return full[:, :W]
 
 
 def rows_pad_mask(H, W, Cc):
-    """True at the pad columns of a row-chunked map."""
-    KC, P = Cc // 8, feature_pitch(W)
-    m = np.ones((H, KC, P, 8), bool)
-    m[:, :, 1:W + 1, :] = False
+    """True at the image-edge columns of a strip-chunked map (the kernels never write them)."""
+    KC, S = Cc // 8, feature_strips(W)
+    m = np.zeros((H, S, KC, STRIP_W, 8), bool)
+    m[:, 0, :, 0, :] = True
+    for s in range(S):
+        for u in range(STRIP_W):
+            if 128 * s + u - 1 >= W:
+                m[:, s, :, u, :] = True
     return m
+
+
+def rows_halo_consistent(buf, H, W, Cc):
+    """Whether every interior halo column of a strip-chunked map equals the neighbour's edge pixel."""
+    KC, S = Cc // 8, feature_strips(W)
+    b = np.asarray(buf).reshape(H, S, KC, STRIP_W, 8)
+    for s in range(S - 1):
+        if 128 * (s + 1) >= W:
+            break
+        if not (np.array_equal(b[:, s, :, 129], b[:, s + 1, :, 1]) and np.array_equal(b[:, s + 1, :, 0], b[:, s, :, 128])):
+            return False
+    return True
 
 
 # ---- tiler oracle (oracle/oracle_tiling.c) ----
