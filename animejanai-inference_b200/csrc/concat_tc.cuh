@@ -32,8 +32,8 @@ enum { kErrCatEmpty = 201, kErrCatFull = 202, kErrCatAccEmpty = 203, kErrCatAccF
        kErrCatDrain = 206 };
 
 struct CatDev {
-    const __half *src[4];  // row-chunked maps of c channels
-    __half *dst;           // row-chunked map of c channels
+    const __half *src[4];  // strip-chunked maps of c channels
+    __half *dst;           // strip-chunked map of c channels
     const unsigned char *wimg;  // B image [kpad / 8][npad / 8][8 n][8 k]
     const float *bias;     // npad floats
     int *err;

@@ -328,7 +328,7 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     if (op->in == AJIB_IN_NCHW3_UNSHUFFLE2 && op->out != AJIB_OUT_NHWC && resid) return AJIB_ERR_ARGS;
     if (row_end <= 0 || row_end > H) row_end = H;
     if (row_begin < 0 || row_begin >= row_end) return row_begin == row_end ? AJIB_OK : AJIB_ERR_ARGS;
-    // row-chunked maps are read by bulk copies and written by 16-byte stores
+    // strip-chunked maps are read by bulk copies and written by 16-byte stores
     if (((uintptr_t)src & 15) || ((uintptr_t)dst & 15) || (resid && op->gate && ((uintptr_t)resid & 15)))
         return AJIB_ERR_ARGS;
 
@@ -458,7 +458,7 @@ extern "C" int ajib_kernel_status(int clear)
     return v;
 }
 
-// ---- the model input packed into a row-chunked map (the executor's head path) ----
+// ---- the model input packed into a strip-chunked map (the executor's head path) ----
 namespace ajib {
 namespace {
 

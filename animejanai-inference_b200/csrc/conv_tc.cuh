@@ -29,8 +29,8 @@
  *
  * A CTA is persistent on one SM and walks a contiguous run of (strip, row) tiles down a
  * 128-pixel-wide vertical strip, so each input row is fetched once. Roles:
- *   warps 0-3   producer: warp 0 issues the bulk copies of each input row, one lane per 8-channel
- *               chunk (row-chunked inputs), or all 128 threads convert the NCHW RGB model input
+ *   warps 0-3   producer: warp 0 issues the bulk copy of each input row (strip-chunked inputs),
+ *               or all 128 threads convert the NCHW RGB model input
  *               into the same layout; lane 0 also waits for the accumulators a row starts to be
  *               free and writes the row's MMA plan beside the staged row, and after the last row
  *               fills one terminator stage;
@@ -65,12 +65,12 @@ constexpr int kConvThreads = (kMmaWarp + 1) * 32;
 constexpr int kMaxSmem = 227 * 1024;
 
 // Epilogue kinds, one kernel instantiation each (so each layer runs only the code it needs):
-// row-chunked output with an activation; row-chunked output through a SPAN gate; depth-to-space
-// into NCHW (with the model-input skip); row-chunked output through the SPANF3 tanh gate, whose
+// strip-chunked output with an activation; strip-chunked output through a SPAN gate; depth-to-space
+// into NCHW (with the model-input skip); strip-chunked output through the SPANF3 tanh gate, whose
 // 1x1 attention conv is a second tensor-core GEMM in the epilogue.
 enum { kEpiAct = 0, kEpiGate = 1, kEpiD2S = 2, kEpiAtt = 3 };
 
-// Input modes: row-chunked feature map (bulk copies); the NCHW RGB model input; the NCHW RGB
+// Input modes: strip-chunked feature map (bulk copies); the NCHW RGB model input; the NCHW RGB
 // model input pixel-unshuffled by 2 (12 channels at half resolution).
 enum { kInRows = 0, kInRgb = 1, kInRgbUnshuffle2 = 2 };
 
@@ -79,15 +79,15 @@ enum { kErrProdEmpty = 101, kErrMmaFull = 102, kErrProdAccEmpty = 103, kErrEpiAc
        kErrDrain = 106, kErrAttFull = 107 };
 
 struct ConvDev {
-    const __half *src;    // row-chunked map [H][cin] or NCHW [3][H][W]
-    const __half *resid;  // gate: row-chunked [H][cout]; depth-to-space: NCHW model input [3][H][W] or null
-    __half *dst;          // row-chunked [H][cout] or NCHW [3][R*H][R*W]
+    const __half *src;    // strip-chunked map [H][cin] or NCHW [3][H][W]
+    const __half *resid;  // gate: strip-chunked [H][cout]; depth-to-space: NCHW model input [3][H][W] or null
+    __half *dst;          // strip-chunked [H][cout] or NCHW [3][R*H][R*W]
     const unsigned char *wimg;  // packed B operand image, all taps
     const float *bias;    // NPAD floats
     const float *slope;   // NPAD floats or null
     int *err;             // status word
     int H, W, cin, cout;
-    int in_mode, act, gate, R;  // R = 0: row-chunked output, else depth-to-space factor
+    int in_mode, act, gate, R;  // R = 0: strip-chunked output, else depth-to-space factor
     int in_norm, out_clamp;
     float in_mean[3], in_scale[3];
     int row_begin, row_end;
@@ -98,7 +98,7 @@ struct ConvDev {
     const unsigned char *att_img;
     const float *att_bias;
     int att_kpad, att_npad;
-    // depth-to-space with the skip: its rows reach shared memory by bulk copies (row-chunked
+    // depth-to-space with the skip: its rows reach shared memory by bulk copies (strip-chunked
     // input and W a multiple of 8, so every copy is 16-byte aligned), else the epilogue loads them
     int skip_smem;
 };
@@ -289,7 +289,7 @@ __device__ __forceinline__ void epi_prefetch(EpiIn<CW> &in, const ConvDev &a, in
 }
 
 // The epilogue of one output row for pixel x and channels [C0, C0 + CW): bias, then activation
-// and SPAN gate into the row-chunked map, or depth-to-space into NCHW. (Staging the row in shared
+// and SPAN gate into the strip-chunked map, or depth-to-space into NCHW. (Staging the row in shared
 // memory for bulk stores measured slower than these coalesced 512-byte warp stores.)
 template <int EK, int CW, int C0>
 __device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, const float *sbias, const float *sslope,
@@ -530,7 +530,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr bool bulk_in = IN == kInRows;  // row-chunked input by bulk copies, else the NCHW RGB model input
+    constexpr bool bulk_in = IN == kInRows;  // strip-chunked input by bulk copies, else the NCHW RGB model input
     const int H = a.H, W = a.W;
 
     // ---- set-up

@@ -63,7 +63,7 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
         st.resid = ps.resid;
         st.dst = ps.dst;
         const PlanWeights &pw = ps.w;
-        // the head reads the model input packed into a row-chunked map of 8 (16 unshuffled)
+        // the head reads the model input packed into a strip-chunked map of 8 (16 unshuffled)
         // channels: its weights gain zero input channels to match
         const bool head = ps.kind == PlanStep::CONV && (ps.in == AJIB_IN_NCHW3 || ps.in == AJIB_IN_NCHW3_UNSHUFFLE2);
         const int cin = head ? (ps.in == AJIB_IN_NCHW3 ? 8 : 16) : pw.cin;
@@ -176,7 +176,8 @@ std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h,
     for (size_t need : sizes) {
         e->buffer_bytes_.push_back(need);
         void *b = nullptr;
-        // the pad columns of row-chunked maps must read as zero: clear once, kernels never write them
+        // the image-edge columns of strip-chunked maps must read as zero: clear once, kernels never
+        // write them
         if (cudaMalloc(&b, need) != cudaSuccess || cudaMemset(b, 0, need) != cudaSuccess) {
             cudaFree(b);
             cudaGetLastError();
@@ -256,8 +257,8 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
     img_h /= U_;
     const int h = img_h * nimg;
     if (w > W_ || h > H_) return AJIB_ERR_ARGS;
-    // a row-chunked map's pitch follows its width: at another width, columns that held pixels
-    // become pad columns, which must read as zero again
+    // at another width, columns of a strip-chunked map that held pixels may become columns past
+    // the image's edge, which must read as zero again
     if (w != last_w_) {
         for (size_t k = 0; k < buffers_.size(); k++)
             if (cudaMemsetAsync(buffers_[k], 0, buffer_bytes_[k], s) != cudaSuccess) return AJIB_ERR_CUDA;

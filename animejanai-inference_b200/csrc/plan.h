@@ -79,7 +79,7 @@ double flops_per_pixel(const Plan &p);
 inline int model_scale(const Plan &p) { return p.depth_to_space / (p.unshuffle > 0 ? p.unshuffle : 1); }
 
 // The NCHW fp16 model input [3][H][W] (pixel-unshuffled by 2: [3][2H][2W]) of conv rows
-// [row_begin, row_end) as a row-chunked map at H x W of 8 channels {r, g, b, 0...} (16: the 12
+// [row_begin, row_end) as a strip-chunked map at H x W of 8 channels {r, g, b, 0...} (16: the 12
 // unshuffled channels, then zeros), normalised if in_norm; pad columns untouched (conv.cu).
 int pack_model_input(const void *src, int H, int W, int unshuffle, bool in_norm, const float *mean, const float *scale,
                      int row_begin, int row_end, void *dst, cudaStream_t s);
@@ -120,7 +120,7 @@ private:
     Executor() = default;
     struct Step {
         bool concat = false;
-        // the head: the model input is first packed into pack (a row-chunked map of pack_c
+        // the head: the model input is first packed into pack (a strip-chunked map of pack_c
         // channels), which the conv reads by bulk copies like any feature map
         bool pack = false;
         int pack_c = 0, unshuffle = 1;
@@ -144,7 +144,7 @@ private:
     std::vector<size_t> buffer_bytes_;
     std::vector<void *> tensor_;
     size_t pack_bytes_ = 0;
-    mutable int last_w_ = 0;  // the conv width of the last run (the maps' pitch)
+    mutable int last_w_ = 0;  // the conv width of the last run (which columns are past the edge)
     int W_ = 0, H_ = 0, R_ = 1, U_ = 1, bands_ = 1;  // conv resolution, depth-to-space, unshuffle
     size_t bytes_ = 0, weight_bytes_ = 0;
 };
