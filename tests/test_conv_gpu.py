@@ -171,6 +171,56 @@ def test_tail_clamp():
     check_close(got, want)
 
 
+# kind, channels in/out, rows per CTA (enough for two turns of the kernel's accumulator ring:
+# 8 slots at 64 padded output channels, 6 with the tanh gate, 16 at 32)
+LONG = [("body", 64, 64, 20), ("body", 16, 16, 36), ("silu", 48, 48, 20), ("gate", 48, 48, 20), ("att", 48, 48, 16),
+        ("head", 3, 64, 20), ("tail", 64, 12, 36), ("tail4", 24, 48, 20)]
+
+
+@pytest.mark.parametrize("kind,cin,cout,rpc", LONG)
+def test_long_segments(kind, cin, cout, rpc):
+    """Each CTA walks rpc rows down its strip, so every CTA's accumulator ring turns at least twice
+    (frames of 1080p and up give each CTA ~110 rows; the small cases above give it one or two):
+    every row position in the ring, its wrap included, against the oracle on windows of output rows
+    at the top of the frame and in its middle."""
+    import ajib
+    rng = np.random.default_rng(600 + cin + cout + rpc)
+    H, W = 148 * rpc, 128
+    nchw = kind == "head"
+    x = f16r(rng.uniform(0 if nchw else -1, 1, size=(3, H, W) if nchw else (H, W, cin)))
+    R = {"tail": 2, "tail4": 4}.get(kind, 0)
+    act = {"body": 2, "silu": 3, "head": 2}.get(kind, 0)
+    gate = {"gate": 3, "att": 2}.get(kind, 0)
+    w, b, sl = conv_weights(rng, cin, cout, prelu=act == 2)
+    r = f16r(rng.uniform(-1, 1, size=(H, W, cout))) if gate else None
+    mi = f16r(rng.uniform(0, 1, size=(3, H, W))) if kind == "tail" else None
+    att = None
+    kw = {}
+    if gate == 2:
+        aw = f16r(rng.normal(0.0, np.sqrt(2.0 / cout), size=(1, cout, cout)))
+        att = (aw, rng.normal(0.0, 0.01, size=cout).astype(np.float32))
+        kw["att"] = ajib.Weights(to_f16_bits(aw), att[1], taps=1)
+    out = {2: ajib.OUT_D2S2, 4: ajib.OUT_D2S4}.get(R, ajib.OUT_NHWC)
+    op = ajib.conv_op(ajib.Weights(to_f16_bits(w), b, sl if act == 2 else None), in_=ajib.IN_NCHW3 if nchw else ajib.IN_NHWC,
+                      act=act, gate={3: ajib.GATE_SIGMOID_HALF, 2: ajib.GATE_TANH1X1}.get(gate, 0), out=out, **kw)
+    src = dev_f16(x) if nchw else dev_rows(x)
+    resid = dev_rows(r) if gate else (dev_f16(mi) if mi is not None else None)
+    got = run_conv(op, src, resid, (3, R * H, R * W) if R else (H, W, cout), H, W)
+    for y0, y1 in [(0, 2 * rpc + 6), (H // 2 - 3, H // 2 + rpc + 3)]:
+        a0 = max(0, y0 - 1)
+        xs = x[:, a0:y1 + 1] if nchw else x[a0:y1 + 1]
+        n = (y1 + 1) - a0
+        want = oracle_conv(xs, 1 if nchw else 0, n, W, 3 if nchw else cin, w, b, sl if act == 2 else None, cout, act=act,
+                           gate=gate, resid=None if r is None else r[a0:y1 + 1], R=R,
+                           model_in=None if mi is None else mi[:, a0:y1 + 1], att=att)
+        # the window's own edge rows see zero padding in the oracle: compare [y0, y1) only
+        k0 = y0 - a0
+        if R:
+            check_close(got[:, R * y0:R * y1], want[:, R * k0:R * (k0 + y1 - y0)])
+        else:
+            check_close(got[y0:y1], want[k0:k0 + y1 - y0])
+
+
 def test_bands_match_whole_frame():
     """Launching a frame as row bands gives exactly the whole-frame result (the band schedule)."""
     import ajib
