@@ -37,10 +37,13 @@
  *   warps 4-11  epilogue: TMEM -> registers (one pixel per thread, half a slot's channels per
  *               warp), bias, activation, SPAN gate or depth-to-space with the model-input skip,
  *               fp16 store; then zero the half slot;
- *   warp 12     MMA issuer (one thread) and TMEM owner. The tensor pipe queues only a few MMAs
- *               and a lone thread's bookkeeping is slow, so this thread only waits for a staged
- *               row, reads its plan and issues, straight-line per stage of two rows; the next
- *               stage's wait sits between the two rows' MMAs.
+ *   warp 12     idle, so that
+ *   warp 13     the MMA issuer (one thread) and TMEM owner sits on the second sub-partition (warp
+ *               % 4), away from the producer thread: sharing the first one's issue slots cost
+ *               2-4 % on every conv. The tensor pipe queues only a few MMAs and a lone thread's
+ *               bookkeeping is slow, so this thread only waits for a staged row, reads its plan
+ *               and issues, straight-line per stage of two rows; the next stage's wait sits
+ *               between the two rows' MMAs.
  * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime.
  *
  * The semantics are those of the reference kernel k_conv3x3 (src/native/conv_kernels.cuh:100-350)
@@ -60,7 +63,8 @@ constexpr int kHalo = kTileM + 2;  // staged input pixels per row
 constexpr int kTmemCols = 512;     // the whole TMEM: the accumulator ring
 constexpr int kProdWarps = 4;      // producer warps (all of them convert an NCHW model input)
 constexpr int kEpiWarps = 8;       // epilogue warps: two per TMEM lane quarter, one per half slot
-constexpr int kMmaWarp = kProdWarps + kEpiWarps;
+constexpr int kIdleWarp = kProdWarps + kEpiWarps;  // keeps the MMA warp off the producer's sub-partition
+constexpr int kMmaWarp = kIdleWarp + 1;
 constexpr int kConvThreads = (kMmaWarp + 1) * 32;
 constexpr int kMaxSmem = 227 * 1024;
 
@@ -793,6 +797,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 }
             }
         }
+    } else if (warp == kIdleWarp) {
+        // no work: see kIdleWarp
     } else if (ATT && warp < kMmaWarp) {
       if constexpr (ATT) {
         // ================= epilogue of the tanh gate (x + o) * tanh(att_bias + W_att^T o), o the conv
