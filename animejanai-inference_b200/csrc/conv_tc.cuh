@@ -292,21 +292,48 @@ __device__ __forceinline__ void epi_prefetch(EpiIn<CW> &in, const ConvDev &a, in
     }
 }
 
-// The epilogue of one output row for pixel x and channels [C0, C0 + CW): bias, then activation
-// and SPAN gate into the strip-chunked map, or depth-to-space into NCHW. (Staging the row in shared
-// memory for bulk stores measured slower than these coalesced 512-byte warp stores.)
+// The epilogue of one output row for pixel x and channels [C0, C0 + CW) (v already holds the bias:
+// every accumulator starts from it): activation or SPAN gate into the strip-chunked map, or
+// depth-to-space into NCHW. (Staging the row in shared memory for bulk stores measured slower
+// than these coalesced 512-byte warp stores.)
 template <int EK, int CW, int C0>
-__device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, const float *sbias, const float *sslope,
-                                          int o, int x, const EpiIn<CW> &in)
+__device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, const float *sslope_m1, int o, int x,
+                                          const EpiIn<CW> &in)
 {
     if (x >= a.W) return;
+    const int ccout = a.cout / 8;  // 16-byte chunks per pixel
+    if constexpr (EK == kEpiAct) {
+        // ReLU in the rounding to fp16 (exact: max(round(v), 0) = round(max(v, 0))); PReLU as
+        // v + min(v, 0) * (slope - 1), one FMA a channel
+        uint32_t w[CW / 2];
+        if (a.act == 1) {
 #pragma unroll
-    for (int n = 0; n < CW; n += 4) {
-        const float4 b4 = *reinterpret_cast<const float4 *>(sbias + C0 + n);
-        v[n] += b4.x;
-        v[n + 1] += b4.y;
-        v[n + 2] += b4.z;
-        v[n + 3] += b4.w;
+            for (int j = 0; j < CW / 2; j++) w[j] = dev::pack_relu_h2(v[2 * j], v[2 * j + 1]);
+        } else if (a.act == 2) {
+#pragma unroll
+            for (int n = 0; n < CW; n += 4) {
+                const float4 s4 = *reinterpret_cast<const float4 *>(sslope_m1 + C0 + n);
+                v[n] = fmaf(fminf(v[n], 0.f), s4.x, v[n]);
+                v[n + 1] = fmaf(fminf(v[n + 1], 0.f), s4.y, v[n + 1]);
+                v[n + 2] = fmaf(fminf(v[n + 2], 0.f), s4.z, v[n + 2]);
+                v[n + 3] = fmaf(fminf(v[n + 3], 0.f), s4.w, v[n + 3]);
+            }
+#pragma unroll
+            for (int j = 0; j < CW / 2; j++) w[j] = pack_h2(v[2 * j], v[2 * j + 1]);
+        } else {
+            if (a.act == 3) {
+#pragma unroll
+                for (int n = 0; n < CW; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
+            }
+#pragma unroll
+            for (int j = 0; j < CW / 2; j++) w[j] = pack_h2(v[2 * j], v[2 * j + 1]);
+        }
+        // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
+#pragma unroll
+        for (int c = 0; c < CW / 8; c++)
+            if (C0 / 8 + c < ccout)
+                store_px(a.dst, o, x, C0 / 8 + c, a.nstrips, ccout, make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]));
+        return;
     }
     if constexpr (EK == kEpiD2S) {
         switch (a.R) {
@@ -317,25 +344,6 @@ __device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, cons
         }
         return;
     }
-    if constexpr (EK == kEpiAct) {
-    if (a.act == 1) {
-#pragma unroll
-        for (int n = 0; n < CW; n++) v[n] = fmaxf(v[n], 0.f);
-    } else if (a.act == 2) {
-#pragma unroll
-        for (int n = 0; n < CW; n += 4) {
-            const float4 s4 = *reinterpret_cast<const float4 *>(sslope + C0 + n);
-            v[n] = v[n] >= 0.f ? v[n] : v[n] * s4.x;
-            v[n + 1] = v[n + 1] >= 0.f ? v[n + 1] : v[n + 1] * s4.y;
-            v[n + 2] = v[n + 2] >= 0.f ? v[n + 2] : v[n + 2] * s4.z;
-            v[n + 3] = v[n + 3] >= 0.f ? v[n + 3] : v[n + 3] * s4.w;
-        }
-    } else if (a.act == 3) {
-#pragma unroll
-        for (int n = 0; n < CW; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
-    }
-    }
-    const int ccout = a.cout / 8;  // 16-byte chunks per pixel
     if constexpr (EK == kEpiGate) {
 #pragma unroll
         for (int c = 0; c < CW / 8; c++) {
@@ -355,17 +363,17 @@ __device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, cons
                 }
             }
         }
-    }
-    // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
+        // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes
 #pragma unroll
-    for (int c = 0; c < CW / 8; c++) {
-        if (C0 / 8 + c < ccout) {
-            uint4 w4;
-            w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
-            w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
-            w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
-            w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
-            store_px(a.dst, o, x, C0 / 8 + c, a.nstrips, ccout, w4);
+        for (int c = 0; c < CW / 8; c++) {
+            if (C0 / 8 + c < ccout) {
+                uint4 w4;
+                w4.x = pack_h2(v[c * 8 + 0], v[c * 8 + 1]);
+                w4.y = pack_h2(v[c * 8 + 2], v[c * 8 + 3]);
+                w4.z = pack_h2(v[c * 8 + 4], v[c * 8 + 5]);
+                w4.w = pack_h2(v[c * 8 + 6], v[c * 8 + 7]);
+                store_px(a.dst, o, x, C0 / 8 + c, a.nstrips, ccout, w4);
+            }
         }
     }
 }
@@ -574,7 +582,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     }
     for (int n = tid; n < 64; n += kConvThreads) {
         sbias[n] = n < NPAD ? a.bias[n] : 0.f;
-        sslope[n] = (n < NPAD && a.slope) ? a.slope[n] : 0.f;
+        // PReLU slopes less one (the epilogue's v + min(v, 0) * (slope - 1))
+        sslope[n] = ((n < NPAD && a.slope) ? a.slope[n] : 0.f) - 1.f;
         satt[n] = (ATT && n < a.att_npad) ? a.att_bias[n] : 0.f;
     }
     dev::fence_proxy_async();
@@ -925,10 +934,22 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         const int q = warp & 3, h = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const bool whole = EK == kEpiD2S && a.R == 3;
-        // every ring slot starts at zero; the MMA warp waits on named barrier 1 for this
-        for (int sl = 0; sl < S; sl++)
+        // every accumulator starts from its channel's bias, so the epilogue adds none: this warp's
+        // half of the bias as TMEM words, written into each slot it hands back (the MMA warp waits
+        // on named barrier 1 for the first fill)
+        uint32_t bz[HW];
 #pragma unroll
-            for (int c = 0; c < HW; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + h * HW + c));
+        for (int c = 0; c < HW; c++) bz[c] = __float_as_uint(sbias[h * HW + c]);
+        auto fill_bias = [&](uint32_t taddr) {
+#pragma unroll
+            for (int c = 0; c < HW; c += 16) {
+                uint32_t b16[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) b16[j] = bz[c + j];
+                dev::tmem_st16(taddr + c, b16);
+            }
+        };
+        for (int sl = 0; sl < S; sl++) fill_bias(tmem + lanes + (uint32_t)(sl * NPAD + h * HW));
         dev::tmem_wait_st();
         dev::tc_fence_before();
         dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
@@ -994,17 +1015,16 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         for (int j = 0; j < 16; j++) v[c + j] = t[j];
                     }
                     dev::tmem_wait_ld();
-                    // hand the half slot back zeroed: the MMAs accumulate into it from scratch
-#pragma unroll
-                    for (int c = 0; c < HW; c += 16) dev::tmem_zero16(taddr + h * HW + c);
+                    // hand the half slot back holding the bias: the MMAs accumulate onto it
+                    fill_bias(taddr + h * HW);
                     dev::tmem_wait_st();
                     dev::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                     if (h == 0)
-                        epi_store<EK, HW, 0>(v, a, sbias, sslope, o, x, in);
+                        epi_store<EK, HW, 0>(v, a, sslope, o, x, in);
                     else
-                        epi_store<EK, HW, HW>(v, a, sbias, sslope, o, x, in);
+                        epi_store<EK, HW, HW>(v, a, sslope, o, x, in);
                 } else {
                     // depth-to-space by 3 only comes with 27 output channels (NPAD 32)
                     if constexpr (NPAD == 32 && EK == kEpiD2S) {
@@ -1018,14 +1038,20 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                                 for (int j = 0; j < 16; j++) v[c + j] = t[j];
                             }
                             dev::tmem_wait_ld();
+                            // both halves back to the bias (the other half's from shared memory)
+                            fill_bias(taddr);
+                            {
+                                uint32_t b16[16];
 #pragma unroll
-                            for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(taddr + c);
+                                for (int j = 0; j < 16; j++) b16[j] = __float_as_uint(sbias[HW + j]);
+                                dev::tmem_st16(taddr + HW, b16);
+                            }
                             dev::tmem_wait_st();
                         }
                         dev::tc_fence_before();
                         __syncwarp();
                         if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
-                        if (h == 0) epi_store<EK, NPAD, 0>(v, a, sbias, sslope, o, x, inw);
+                        if (h == 0) epi_store<EK, NPAD, 0>(v, a, sslope, o, x, inw);
                     } else {
                         __syncwarp();
                         if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);

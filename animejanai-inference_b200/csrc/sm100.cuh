@@ -226,6 +226,24 @@ __device__ __forceinline__ void tmem_zero16(uint32_t taddr)
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Store 16 consecutive 32-bit TMEM columns of this warp's 32 lanes from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// fp16x2 of (lo, hi) rounded to nearest, negative values to zero (ReLU on the rounded values)
+__device__ __forceinline__ uint32_t pack_relu_h2(float lo, float hi)
+{
+    uint32_t d;
+    asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 // ---- misc ------------------------------------------------------------------------------------
 
 __device__ __forceinline__ float tanh_fast(float x)
