@@ -43,7 +43,7 @@
  *               2-4 % on every conv. The tensor pipe queues only a few MMAs and a lone thread's
  *               bookkeeping is slow, so this thread only waits for a staged row, reads its plan
  *               and issues, straight-line per stage of two rows; the next stage's wait sits
- *               between the two rows' MMAs.
+ *               inside the second row's MMAs.
  * Weights for all 9 taps stay resident in shared memory for the CTA's lifetime.
  *
  * The semantics are those of the reference kernel k_conv3x3 (src/native/conv_kernels.cuh:100-350)
@@ -1083,21 +1083,25 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                 dev::tc_fence_after();
                 return good;
             };
-            // straight-line per stage: row 0's MMAs, the wait for the next stage, row 1's MMAs, the
-            // commits; the producer's terminator stage ends the loop (so no row bookkeeping here,
-            // which measured ~100 cycles a row with the tensor pipe idle)
+            // straight-line per stage; the producer's terminator stage ends the loop (so no row
+            // bookkeeping here, which measured ~100 cycles a row with the tensor pipe idle)
             RowPlan c0, c1, n0, n1;
             uint32_t pi = 0;
             ok = ok && fetch(0, c0, c1);
             while (ok && c0.np != kPlanEnd) {
                 const uint32_t s = pi % C::NS;
                 const uint64_t adesc0 = adesc_base + (uint64_t)((s * C::STAGE) >> 4);
+                // row 0, its completed outputs' commits at once (the epilogue starts on them a row
+                // earlier); row 1's first tap column, then the next stage's wait and plans while
+                // those MMAs run (the pipe queues only a few, so bookkeeping between two rows
+                // leaves it idle), the rest of row 1 and the stage's commits
                 if (c0.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0, bdesc0, c0);
-                const bool okn = fetch(pi + 1, n0, n1);
-                if (c1.np) issue_plan<0, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)(C::SLOT >> 4), bdesc0, c1);
-                dev::mma_commit(empty0 + 8 * s);
                 if (c0.np && c0.commit_a) dev::mma_commit(c0.commit_a);
                 if (c0.np && c0.commit_b) dev::mma_commit(c0.commit_b);
+                if (c1.np) issue_plan<0, 1, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)(C::SLOT >> 4), bdesc0, c1);
+                const bool okn = fetch(pi + 1, n0, n1);
+                if (c1.np) issue_plan<1, 3, C::KS, C::KC, C::NG, C::LBO_A>(adesc0 + (uint64_t)(C::SLOT >> 4), bdesc0, c1);
+                dev::mma_commit(empty0 + 8 * s);
                 if (c1.np && c1.commit_a) dev::mma_commit(c1.commit_a);
                 if (c1.np && c1.commit_b) dev::mma_commit(c1.commit_b);
                 pi++;
