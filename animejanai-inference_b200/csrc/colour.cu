@@ -96,6 +96,7 @@ __device__ __forceinline__ float quantize(float v, float qdiv, float qinv, float
 
 // ---------------- pre: NV12/P010 -> fp16 NCHW RGB ----------------
 constexpr int kPreTW = 64, kPreTH = 16, kPreRows = 24;
+constexpr int kPreMaxTaps = 8;  // taps per pass the kernel holds (plans with more are refused)
 
 template <typename T>
 __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
@@ -109,20 +110,43 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
     const int nrows = hi - lo + 1;  // <= kPreRows (checked at plan creation)
     const int ch = pv.src;
 
-    // pass 1: horizontal resample of the staged chroma rows (interleaved CbCr)
-    for (int i = tid; i < nrows * kPreTW; i += 256) {
-        const int rr = i / kPreTW, tx = i % kPreTW, x = x0 + tx;
-        if (x >= w) continue;
-        const T *row = reinterpret_cast<const T *>(uvp + (size_t)mirror_index(lo + rr, ch) * uvs);
-        const float *wt = ph.wt + (size_t)x * ph.taps;
-        const int s0 = ph.start[x];
-        float u = 0.0f, v = 0.0f;
-        for (int j = 0; j < ph.taps; j++) {
-            const int sx = mirror_index(s0 + j, ph.src);
-            u = __fmaf_rn(wt[j], (float)row[2 * sx], u);
-            v = __fmaf_rn(wt[j], (float)row[2 * sx + 1], v);
+    // pass 1: horizontal resample of the staged chroma rows (interleaved CbCr). A thread keeps its
+    // column's taps and weights in registers and walks the rows, each row's samples loaded before
+    // its FMA chain.
+    {
+        const int tx = tid % kPreTW, x = x0 + tx;
+        if (x < w) {
+            const int taps = ph.taps;
+            const float *wtp = ph.wt + (size_t)x * taps;
+            const int s0 = ph.start[x];
+            float wt[kPreMaxTaps];
+            int sx[kPreMaxTaps];
+#pragma unroll
+            for (int j = 0; j < kPreMaxTaps; j++) {
+                wt[j] = j < taps ? wtp[j] : 0.0f;
+                sx[j] = mirror_index(s0 + min(j, taps - 1), ph.src);
+            }
+            for (int rr = tid / kPreTW; rr < nrows; rr += 256 / kPreTW) {
+                const T *row = reinterpret_cast<const T *>(uvp + (size_t)mirror_index(lo + rr, ch) * uvs);
+                float cu[kPreMaxTaps], cv[kPreMaxTaps];
+#pragma unroll
+                for (int j = 0; j < kPreMaxTaps; j++) {
+                    if (j < taps) {
+                        cu[j] = (float)row[2 * sx[j]];
+                        cv[j] = (float)row[2 * sx[j] + 1];
+                    }
+                }
+                float u = 0.0f, v = 0.0f;
+#pragma unroll
+                for (int j = 0; j < kPreMaxTaps; j++) {
+                    if (j < taps) {
+                        u = __fmaf_rn(wt[j], cu[j], u);
+                        v = __fmaf_rn(wt[j], cv[j], v);
+                    }
+                }
+                uvh[rr][tx] = make_float2(u, v);
+            }
         }
-        uvh[rr][tx] = make_float2(u, v);
     }
     __syncthreads();
 
@@ -135,18 +159,40 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
     const float cb = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));   // 2 (1 - kb)
     const float gb = __fmul_rn(__fmul_rn(2.0f, csp.kb), __fsub_rn(1.0f, csp.kb));  // 2 kb (1 - kb)
     const float gr = __fmul_rn(__fmul_rn(2.0f, csp.kr), __fsub_rn(1.0f, csp.kr));  // 2 kr (1 - kr)
-    for (int ty = tid / kPreTW; ty < kPreTH; ty += 256 / kPreTW) {
+    // the thread's four rows: luma loads first, then independent FMA chains
+    constexpr int kG = 256 / kPreTW, kN = kPreTH / kG;
+    const int taps = pv.taps;
+    float lraw[kN];
+#pragma unroll
+    for (int k = 0; k < kN; k++) {
+        const int y = min(y0 + tid / kPreTW + k * kG, h - 1);
+        lraw[k] = (float)reinterpret_cast<const T *>(yp + (size_t)y * ys)[x];
+    }
+    float uu[kN], vv[kN];
+#pragma unroll
+    for (int k = 0; k < kN; k++) {
+        const int y = min(y0 + tid / kPreTW + k * kG, h - 1);
+        const float *wt = pv.wt + (size_t)y * taps;
+        const int s0 = pv.start[y] - lo;
+        float u = 0.0f, v = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kPreMaxTaps; j++) {
+            if (j < taps) {
+                const float2 q = uvh[s0 + j][tx];
+                u = __fmaf_rn(wt[j], q.x, u);
+                v = __fmaf_rn(wt[j], q.y, v);
+            }
+        }
+        uu[k] = u;
+        vv[k] = v;
+    }
+#pragma unroll
+    for (int k = 0; k < kN; k++) {
+        const int ty = tid / kPreTW + k * kG;
         const int y = y0 + ty;
         if (y >= h) break;
-        const float *wt = pv.wt + (size_t)y * pv.taps;
-        const int s0 = pv.start[y];
-        float u = 0.0f, v = 0.0f;
-        for (int j = 0; j < pv.taps; j++) {
-            const float2 q = uvh[s0 + j - lo][tx];
-            u = __fmaf_rn(wt[j], q.x, u);
-            v = __fmaf_rn(wt[j], q.y, v);
-        }
-        const float raw = (float)reinterpret_cast<const T *>(yp + (size_t)y * ys)[x];
+        const float u = uu[k], v = vv[k];
+        const float raw = lraw[k];
         const float Y = __fdiv_rn(__fsub_rn(raw, csp.yoff), csp.yscale);
         const float U = __fdiv_rn(__fsub_rn(u, csp.coff), csp.cscale);
         const float V = __fdiv_rn(__fsub_rn(v, csp.coff), csp.cscale);
@@ -206,19 +252,35 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
         const int ty = i / pv.taps, j = i % pv.taps;
         swv[ty * kPostMaxTaps + j] = cy0 + ty < chh ? pv.wt[(size_t)(cy0 + ty) * pv.taps + j] : 0.0f;
     }
-    // staging: one warp per staged row, lanes along it
+    // staging: one warp per staged row, lanes along it; a row's pixels are all loaded before any
+    // is converted, so their global loads are in flight together
+    constexpr int kPostIt = (kPostCols + 31) / 32;
     for (int rr = warp; rr < nrows; rr += 8) {
         const int gy = ylo + rr, my = mirror_index(gy, h);
         const bool own_row = covered && gy == my && gy >= ly0 && gy < ly1;
-        for (int cc = lane; cc < ncols; cc += 32) {
-            const int gx = xlo + cc, mx = mirror_index(gx, w);
-            const size_t idx = (size_t)my * w + mx;
-            const float r = __half2float(src[idx]), g = __half2float(src[plane + idx]), b = __half2float(src[2 * plane + idx]);
+        const __half *srow = src + (size_t)my * w;
+        __half pr[kPostIt], pg[kPostIt], pb[kPostIt];
+#pragma unroll
+        for (int k = 0; k < kPostIt; k++) {
+            const int cc = lane + 32 * k;
+            if (cc < ncols) {
+                const int mx = mirror_index(xlo + cc, w);
+                pr[k] = srow[mx];
+                pg[k] = srow[plane + mx];
+                pb[k] = srow[2 * plane + mx];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kPostIt; k++) {
+            const int cc = lane + 32 * k;
+            if (cc >= ncols) continue;
+            const int gx = xlo + cc;
+            const float r = __half2float(pr[k]), g = __half2float(pg[k]), b = __half2float(pb[k]);
             const float Y = __fmaf_rn(csp.kb, b, __fmaf_rn(csp.kr, r, __fmul_rn(kg, g)));
             const int at = (cc & 1) * kPostPar + rr * kPostHalf + (cc >> 1);
             su[at] = dev::div_by(__fsub_rn(b, Y), db, rdb);
             sv[at] = dev::div_by(__fsub_rn(r, Y), dr, rdr);
-            if (own_row && gx == mx && gx >= lx0 && gx < lx1)
+            if (own_row && gx == mirror_index(gx, w) && gx >= lx0 && gx < lx1)
                 reinterpret_cast<T *>(yp + (size_t)gy * ys)[gx] = (T)quantize(__fmaf_rn(Y, csp.yscale, csp.yoff), qdiv, qinv, qmax);
         }
     }
@@ -241,41 +303,63 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
 #pragma unroll
         for (int j = 0; j < kPostMaxTaps; j++) wt[j] = j < taps ? ph.wt[(size_t)cx * taps + j] : 0.0f;
         const int s0 = ph.start[cx] - xlo;
-        for (int rr = grp; rr < nrows; rr += 256 / kPostTW) {
-            float u = 0.0f, v = 0.0f;
+        // two staged rows at a time (rr and rr + 4): four independent FMA chains per thread
+        constexpr int kG = 256 / kPostTW;
+        for (int rr = grp; rr < nrows; rr += 2 * kG) {
+            const int r1 = rr + kG < nrows ? rr + kG : rr;
+            float u0 = 0.0f, v0 = 0.0f, u1 = 0.0f, v1 = 0.0f;
 #pragma unroll
             for (int j = 0; j < kPostMaxTaps; j++) {
                 if (j < taps) {
                     const int c = s0 + j;
-                    const int at = (c & 1) * kPostPar + rr * kPostHalf + (c >> 1);
-                    u = __fmaf_rn(wt[j], su[at], u);
-                    v = __fmaf_rn(wt[j], sv[at], v);
+                    const int at = (c & 1) * kPostPar + (c >> 1);
+                    u0 = __fmaf_rn(wt[j], su[at + rr * kPostHalf], u0);
+                    v0 = __fmaf_rn(wt[j], sv[at + rr * kPostHalf], v0);
+                    u1 = __fmaf_rn(wt[j], su[at + r1 * kPostHalf], u1);
+                    v1 = __fmaf_rn(wt[j], sv[at + r1 * kPostHalf], v1);
                 }
             }
-            hu[rr * kPostTW + tx] = u;
-            hv[rr * kPostTW + tx] = v;
+            hu[rr * kPostTW + tx] = u0;
+            hv[rr * kPostTW + tx] = v0;
+            if (r1 != rr) {
+                hu[r1 * kPostTW + tx] = u1;
+                hv[r1 * kPostTW + tx] = v1;
+            }
         }
     }
     __syncthreads();
     // vertical pass, quantise, interleave
     if (cx < cw) {
         const int taps = pv.taps;
-        for (int ty = grp; ty < kPostTH; ty += 256 / kPostTW) {
-            const int cy = cy0 + ty;
-            if (cy >= chh) break;
-            const float *wv = swv + ty * kPostMaxTaps;
-            const int s0 = pv.start[cy] - ylo;
-            float u = 0.0f, v = 0.0f;
+        // the thread's four output rows at once (independent FMA chains)
+        constexpr int kG = 256 / kPostTW, kN = kPostTH / kG;
+        float u[kN], v[kN];
+        int s0[kN];
 #pragma unroll
-            for (int j = 0; j < kPostMaxTaps; j++) {
-                if (j < taps) {
-                    u = __fmaf_rn(wv[j], hu[(s0 + j) * kPostTW + tx], u);
-                    v = __fmaf_rn(wv[j], hv[(s0 + j) * kPostTW + tx], v);
+        for (int k = 0; k < kN; k++) {
+            const int cy = min(cy0 + grp + k * kG, chh - 1);
+            s0[k] = pv.start[cy] - ylo;
+            u[k] = 0.0f;
+            v[k] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kPostMaxTaps; j++) {
+            if (j < taps) {
+#pragma unroll
+                for (int k = 0; k < kN; k++) {
+                    const float wj = swv[(grp + k * kG) * kPostMaxTaps + j];
+                    u[k] = __fmaf_rn(wj, hu[(s0[k] + j) * kPostTW + tx], u[k]);
+                    v[k] = __fmaf_rn(wj, hv[(s0[k] + j) * kPostTW + tx], v[k]);
                 }
             }
+        }
+#pragma unroll
+        for (int k = 0; k < kN; k++) {
+            const int cy = cy0 + grp + k * kG;
+            if (cy >= chh) break;
             T *row = reinterpret_cast<T *>(uvp + (size_t)cy * uvs);
-            row[2 * cx] = (T)quantize(__fmaf_rn(u, csp.cscale, csp.coff), qdiv, qinv, qmax);
-            row[2 * cx + 1] = (T)quantize(__fmaf_rn(v, csp.cscale, csp.coff), qdiv, qinv, qmax);
+            row[2 * cx] = (T)quantize(__fmaf_rn(u[k], csp.cscale, csp.coff), qdiv, qinv, qmax);
+            row[2 * cx + 1] = (T)quantize(__fmaf_rn(v[k], csp.cscale, csp.coff), qdiv, qinv, qmax);
         }
     }
 }
@@ -404,7 +488,7 @@ aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting,
         p->th = make_filter(cw, w, sx, filter);
         p->tv = make_filter(ch, h, sy, filter);
         p->max_rows = span_of(p->tv, kPreTH);
-        if (p->max_rows > kPreRows) {
+        if (p->max_rows > kPreRows || p->th.taps > kPreMaxTaps || p->tv.taps > kPreMaxTaps) {
             delete p;
             return nullptr;
         }
