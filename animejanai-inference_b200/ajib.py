@@ -63,6 +63,8 @@ lib.ajib_selftest_umma.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp
 lib.ajib_selftest_umma.restype = C.c_int
 lib.ajib_selftest_division.argtypes = [_vp, C.c_int, _vp, _vp]
 lib.ajib_selftest_division.restype = C.c_int
+lib.ajib_selftest_division_by.argtypes = [_vp, C.c_int, _vp, _vp]
+lib.ajib_selftest_division_by.restype = C.c_int
 
 
 class AjibError(RuntimeError):

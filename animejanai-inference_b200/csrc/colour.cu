@@ -159,6 +159,9 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
     const float cb = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));   // 2 (1 - kb)
     const float gb = __fmul_rn(__fmul_rn(2.0f, csp.kb), __fsub_rn(1.0f, csp.kb));  // 2 kb (1 - kb)
     const float gr = __fmul_rn(__fmul_rn(2.0f, csp.kr), __fsub_rn(1.0f, csp.kr));  // 2 kr (1 - kr)
+    // (x / yscale and x / cscale by dev::div_by: bit-identical to the IEEE division over these
+    // dividends, ajib_selftest_division_by)
+    const float ry = __frcp_rn(csp.yscale), rc = __frcp_rn(csp.cscale);
     // the thread's four rows: luma loads first, then independent FMA chains
     constexpr int kG = 256 / kPreTW, kN = kPreTH / kG;
     const int taps = pv.taps;
@@ -193,9 +196,9 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
         if (y >= h) break;
         const float u = uu[k], v = vv[k];
         const float raw = lraw[k];
-        const float Y = __fdiv_rn(__fsub_rn(raw, csp.yoff), csp.yscale);
-        const float U = __fdiv_rn(__fsub_rn(u, csp.coff), csp.cscale);
-        const float V = __fdiv_rn(__fsub_rn(v, csp.coff), csp.cscale);
+        const float Y = dev::div_by(__fsub_rn(raw, csp.yoff), csp.yscale, ry);
+        const float U = dev::div_by(__fsub_rn(u, csp.coff), csp.cscale, rc);
+        const float V = dev::div_by(__fsub_rn(v, csp.coff), csp.cscale, rc);
         const float r = __fmaf_rn(cr, V, Y);
         const float b = __fmaf_rn(cb, U, Y);
         const float g = __fsub_rn(Y, __fdiv_rn(__fmaf_rn(gb, U, __fmul_rn(gr, V)), kg));

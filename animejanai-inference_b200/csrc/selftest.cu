@@ -104,18 +104,20 @@ extern "C" int ajib_selftest_umma(const void *a, const void *b, float *out, int 
 namespace ajib {
 namespace {
 
-// Every float with 2^-80 <= |a| < 2^18 (exponent field 47..144, both signs) divided by 2 (1 - k)
-// for each given k, the divisors of the post pass's colour differences: dev::div_by against
-// __fdiv_rn. Counts the quotients that differ and records the first such a. Tinier dividends are
-// outside the correction's range (below ~2^-100 its remainder underflows) and outside the
-// pass's: its dividends b - Y are differences of an fp16 colour (a multiple of 2^-24) and a
-// weighted sum of fp16 colours by fp32 coefficients (a multiple of 2^-52), so zero or at least
-// 2^-52 in magnitude, and below 2^18 (fp16 colours are below 2^16).
-__global__ void k_div_check(const float *ks, int nk, unsigned long long *bad, unsigned int *first)
+// Every float with 2^-80 <= |a| < 2^18 (exponent field 47..144, both signs) divided by each
+// given divisor (direct), or by 2 (1 - k) for each given k (the post pass's divisors of its colour
+// differences): dev::div_by against __fdiv_rn. Counts the quotients that differ and records the
+// first such a. Tinier dividends are outside the correction's range (below ~2^-100 its remainder
+// underflows) and outside the passes': the post pass's dividends b - Y are differences of an fp16
+// colour (a multiple of 2^-24) and a weighted sum of fp16 colours by fp32 coefficients (a multiple
+// of 2^-52), so zero or at least 2^-52 in magnitude, and below 2^18 (fp16 colours are below
+// 2^16); the pre pass's are raw - yoff (integers below 2^17) and u - coff, u an FMA chain of fp32
+// filter weights (zero or above 2^-40) times integer samples below 2^16, so zero or at least 2^-63.
+__global__ void k_div_check(const float *ks, int nk, int direct, unsigned long long *bad, unsigned int *first)
 {
     float d[8], r[8];
     for (int j = 0; j < nk; j++) {
-        d[j] = __fmul_rn(2.0f, __fsub_rn(1.0f, ks[j]));
+        d[j] = direct ? ks[j] : __fmul_rn(2.0f, __fsub_rn(1.0f, ks[j]));
         r[j] = __frcp_rn(d[j]);
     }
     const uint64_t half = (145ull - 47ull) << 23, n = 2 * half;
@@ -136,7 +138,8 @@ __global__ void k_div_check(const float *ks, int nk, unsigned long long *bad, un
 }  // namespace
 }  // namespace ajib
 
-extern "C" int ajib_selftest_division(const float *k, int nk, unsigned long long *mismatches, unsigned int *first_bits)
+static int selftest_division(const float *k, int nk, int direct, unsigned long long *mismatches,
+                             unsigned int *first_bits)
 {
     if (!k || nk < 1 || nk > 8 || !mismatches || !first_bits) return AJIB_ERR_ARGS;
     float *dk = nullptr;
@@ -149,7 +152,7 @@ extern "C" int ajib_selftest_division(const float *k, int nk, unsigned long long
     if (e == cudaSuccess) e = cudaMemset(dbad, 0, sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMemset(dfirst, 0xFF, sizeof(unsigned int));
     if (e == cudaSuccess) {
-        ajib::k_div_check<<<148 * 8, 256>>>(dk, nk, dbad, dfirst);
+        ajib::k_div_check<<<148 * 8, 256>>>(dk, nk, direct, dbad, dfirst);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaMemcpy(mismatches, dbad, sizeof(unsigned long long), cudaMemcpyDeviceToHost);
@@ -158,4 +161,14 @@ extern "C" int ajib_selftest_division(const float *k, int nk, unsigned long long
     cudaFree(dbad);
     cudaFree(dfirst);
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+extern "C" int ajib_selftest_division(const float *k, int nk, unsigned long long *mismatches, unsigned int *first_bits)
+{
+    return selftest_division(k, nk, 0, mismatches, first_bits);
+}
+
+extern "C" int ajib_selftest_division_by(const float *d, int nd, unsigned long long *mismatches, unsigned int *first_bits)
+{
+    return selftest_division(d, nd, 1, mismatches, first_bits);
 }

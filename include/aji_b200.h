@@ -273,6 +273,10 @@ AJIB_EXPORT int ajib_selftest_umma(const void *a, const void *b, float *out, int
  * i < nk <= 8, against the IEEE division; *mismatches counts differing quotients, *first_bits the
  * first dividend's bits (0xFFFFFFFF: none). No reference counterpart (the reference divides). */
 AJIB_EXPORT int ajib_selftest_division(const float *k, int nk, unsigned long long *mismatches, unsigned int *first_bits);
+/* The same check for the given divisors d[i], i < nd <= 8 (the pre pass divides by the colour
+ * space's luma and chroma scales). */
+AJIB_EXPORT int ajib_selftest_division_by(const float *d, int nd, unsigned long long *mismatches,
+                                          unsigned int *first_bits);
 
 #ifdef __cplusplus
 }

@@ -209,6 +209,22 @@ def test_resize_against_reference_kernels(sw, sh, dw, dh):
     assert np.array_equal(_resize_ours(src, sw, sh, dw, dh), out.cpu().numpy().view(np.uint16))
 
 
+def test_pre_division_matches_ieee():
+    """The pre pass divides by the colour space's luma and chroma scales with a reciprocal and one
+    FMA correction: bit-identical to the IEEE division for every float of magnitude in
+    [2^-80, 2^18) (its dividends are zero or in [2^-63, 2^17)), for NV12 and P010 at both ranges."""
+    import ctypes as C
+
+    import ajib
+    ds = sorted({v for fmt in (1, 2) for rng in (1, 2) for v in
+                 (ajib.lib.aji_make_csp(fmt, 2, rng).yscale, ajib.lib.aji_make_csp(fmt, 2, rng).cscale)})
+    assert 2 <= len(ds) <= 8
+    d = (C.c_float * 8)(*ds)
+    bad, first = C.c_ulonglong(), C.c_uint()
+    assert ajib.lib.ajib_selftest_division_by(d, len(ds), C.byref(bad), C.byref(first)) == 0
+    assert bad.value == 0, f"{bad.value} quotients differ, first dividend bits {first.value:#x}"
+
+
 def test_post_division_matches_ieee():
     """The post pass divides the colour differences by 2 (1 - kb) and 2 (1 - kr) with a reciprocal
     and one FMA correction (Markstein): bit-identical to the IEEE division for every float the pass
