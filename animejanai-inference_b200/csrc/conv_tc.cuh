@@ -169,11 +169,11 @@ struct ConvCfg {
     static constexpr int ATOFF = AOFF + NS * STAGE;  // attention B, then A tiles 0 and 1
     static constexpr int SKOFF = ATOFF + ATT_BYTES;  // skip rows [S][3][128] fp16
     static constexpr int POFF = SKOFF + SKIP_BYTES;  // bias[64], slope[64], attention bias[64] floats
-    // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S]
+    // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S], landed[NS]
     static constexpr int BOFF = POFF + 3 * 64 * 4;
     static constexpr int PLOFF = BOFF + 1024;       // RowPlan per staged row
     static constexpr int SMEM = BOFF + 1024 + 1024 + 1024;  // + alignment slack for the base
-    static_assert((2 * NS + 3 * S + 4) * 8 + 8 <= 1024 && NS * RP * 48 <= 1024, "barrier and plan area");
+    static_assert((3 * NS + 3 * S + 4) * 8 + 8 <= 1024 && NS * RP * 48 <= 1024, "barrier and plan area");
     static_assert(SMEM <= kMaxSmem, "shared memory budget");
 };
 
@@ -540,12 +540,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + C::BOFF);
     const uint32_t full0 = dev::smem_u32(bars), empty0 = full0 + 8 * C::NS, accf0 = empty0 + 8 * C::NS,
                    acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8, attf0 = dbar + 8,
-                   skipf0 = attf0 + 16;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * C::NS + 3 * S + 4);
+                   skipf0 = attf0 + 16, landed0 = skipf0 + 8 * S;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 3 * C::NS + 3 * S + 4);
     RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr bool bulk_in = IN == kInRows;  // strip-chunked input by bulk copies, else the NCHW RGB model input
+    // strip-chunked input copied by its own warp (see the producer)
+    constexpr bool split_in = bulk_in && (EK == kEpiD2S || KPAD == 16);
     const int H = a.H, W = a.W;
 
     // ---- set-up
@@ -553,6 +555,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         for (int s = 0; s < C::NS; s++) {
             dev::mbar_init(full0 + 8 * s, bulk_in ? 1 : kProdWarps * 32);
             dev::mbar_init(empty0 + 8 * s, 1);
+            dev::mbar_init(landed0 + 8 * s, 1);
         }
         for (int s = 0; s < S; s++) {
             dev::mbar_init(accf0 + 8 * s, 1);
@@ -600,89 +603,201 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         // ================= producer: stages each input row and writes its MMA plan beside it,
         // after waiting for the accumulators the row starts to be free
         if constexpr (bulk_in) {
-            if (warp == 0) {
-                // warp 0: every lane walks the same rows (warp-uniform control flow); lane 0 issues
-                // each row's bulk copy, waits for the accumulators, writes the plan and arrives
-                const int kcin = a.cin / 8;
-                const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
-                RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
-                uint32_t pi = 0;  // stage fills so far (pairs of rows)
-                bool ok = true;
-                while (ok && walk.next()) {
-                    const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
-                    if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
-                    // the stage's copies go out as soon as its buffer is free (waiting first for the
-                    // accumulators the rows start, as the plans need, left the MMA thread waiting
-                    // ~800 cycles a stage for data: the TMEM ring, not the stages, bounded how far
-                    // ahead rows were fetched); then the accumulator waits, the plans and, for
-                    // depth-to-space, the skip rows, whose buffers belong to the accumulator slots
-                    RowPlan pl[C::RP];
-                    RowWaits wts[C::RP];
-                    int rows_r[C::RP], rows_strip[C::RP];
-                    int n = 0;
-#pragma unroll
-                    for (int h = 0; h < C::RP; h++) {
-                        if (h > 0 && (n < h || !walk.next())) break;
-                        plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, pl[h], wts[h]);
-                        rows_r[h] = walk.r;
-                        rows_strip[h] = walk.strip;
-                        if (lane == 0) dev::mbar_expect_tx(full0 + 8 * s, bytes);
-                        // the (row, strip) block, halo columns included: the staged row as it is
-                        if (lane == 0)
-                            dev::bulk_load(abase + s * C::STAGE + h * C::SLOT,
-                                           a.src + map_at(walk.r, walk.strip, 0, 0, a.nstrips, kcin), bytes, full0 + 8 * s);
-                        n = h + 1;
-                    }
-                    int h = 0;
-#pragma unroll
-                    for (; h < C::RP; h++) {
-                        if (h >= n) break;
-                        const RowWaits &wt = wts[h];
-                        bool good = true;
-                        if (lane == 0) good = wt.wait(a.err);
-                        if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
-                        if (lane == 0) plans[s * C::RP + h] = pl[h];
-                        if constexpr (EK == kEpiD2S) {
-                            // the skip rows of the outputs this row starts (r + 1; r at an image's
-                            // first row), into their slots: lanes 8-10 and 11-13, one plane each
-                            if (a.skip_smem) {
-                                const int x0 = rows_strip[h] * kTileM;
-                                const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
-                                const int k = lane - 8, which = k / 3, c3 = k % 3;
-                                const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
-                                const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
-                                const int orow = which == 0 ? rows_r[h] + 1 : rows_r[h];
-                                if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
-                                __syncwarp();
-                                if (mine)
-                                    dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + c3 * (kTileM * 2),
-                                                   a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
-                            }
+            // Depth-to-space convs (skip rows to copy) and the head's narrow rows (a staged row's
+            // copy is 2 KB) split the producer in two warps on different SM sub-partitions,
+            // walking the same rows in the same stages: warp 0 copies, warp 2 plans. One warp doing
+            // both spends ~2000 cycles of its own a stage there, more than the stage's MMAs (tail
+            // 108 -> 96 us, head 86 -> 81 us); the body convs measured ~1 % slower split.
+            if constexpr (split_in) {
+                if (warp == 0) {
+                    // the copier: once a stage's buffer is free, one bulk copy per staged row, all
+                    // completing landed[s]; it waits for nothing else
+                    const int kcin = a.cin / 8;
+                    const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
+                    RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
+                    uint32_t pi = 0;  // stage fills so far (pairs of rows)
+                    bool ok = true;
+                    while (ok && walk.next()) {
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
+                        int rr[C::RP], rs[C::RP];
+                        int n = 0;
+    #pragma unroll
+                        for (int h = 0; h < C::RP; h++) {
+                            if (h > 0 && (n < h || !walk.next())) break;
+                            rr[h] = walk.r;
+                            rs[h] = walk.strip;
+                            n = h + 1;
+                        }
+                        if (lane == 0) {
+                            dev::mbar_arrive_expect_tx(landed0 + 8 * s, (uint32_t)n * bytes);
+    #pragma unroll
+                            for (int h = 0; h < C::RP; h++)
+                                if (h < n)
+                                    // the (row, strip) block, halo columns included: the staged row as it is
+                                    dev::bulk_load(abase + s * C::STAGE + h * C::SLOT,
+                                                   a.src + map_at(rr[h], rs[h], 0, 0, a.nstrips, kcin), bytes, landed0 + 8 * s);
                         }
                         __syncwarp();
+                        pi++;
                     }
-                    // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
-                    // empty: the MMA thread skips rows whose plan has no pieces. One arrival per
-                    // stage; it completes once the copies above have landed.
-                    if (lane == 0) {
-                        for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
-                        dev::mbar_arrive(full0 + 8 * s);
+                    if (ok) {
+                        // the terminator stage lands at once (no bytes)
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        if ((ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) && lane == 0)
+                            dev::mbar_arrive(landed0 + 8 * s);
                     }
-                    pi++;
+                    // on an error exit, let the last copies land before the CTA can leave
+                    if (!ok && pi > 0 && lane == 0) {
+                        const uint32_t s = (pi - 1) % C::NS, ph = ((pi - 1) / C::NS) & 1;
+                        dev::mbar_wait(landed0 + 8 * s, ph, nullptr, 0);
+                    }
+                } else if (warp == 2) {
+                    // the planner: per staged row, waits for the accumulators the row starts to be free,
+                    // writes the row's MMA plan beside it and, for depth-to-space, bulk-copies the skip
+                    // rows into those accumulators' slots; one arrival on full[s] a stage, and after the
+                    // last row one terminator stage. Every lane walks the same rows (warp-uniform control
+                    // flow); lane 0 waits and writes.
+                    RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
+                    uint32_t pi = 0;
+                    bool ok = true;
+                    while (ok && walk.next()) {
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        // the stage's plans are free once its MMAs are done
+                        if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
+                        int h = 0;
+    #pragma unroll
+                        for (; h < C::RP; h++) {
+                            if (h > 0 && !walk.next()) break;
+                            RowPlan pl;
+                            RowWaits wt;
+                            plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, pl, wt);
+                            bool good = true;
+                            if (lane == 0) good = wt.wait(a.err);
+                            if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
+                            if (lane == 0) plans[s * C::RP + h] = pl;
+                            if constexpr (EK == kEpiD2S) {
+                                // the skip rows of the outputs this row starts (r + 1; r at an image's
+                                // first row), into their slots: lanes 8-10 and 11-13, one plane each
+                                if (a.skip_smem) {
+                                    const int x0 = walk.strip * kTileM;
+                                    const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
+                                    const int k = lane - 8, which = k / 3, c3 = k % 3;
+                                    const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
+                                    const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
+                                    const int orow = which == 0 ? walk.r + 1 : walk.r;
+                                    if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
+                                    __syncwarp();
+                                    if (mine)
+                                        dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + c3 * (kTileM * 2),
+                                                       a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
+                                }
+                            }
+                            __syncwarp();
+                        }
+                        // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
+                        // empty: the MMA thread skips rows whose plan has no pieces
+                        if (lane == 0) {
+                            for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
+                            dev::mbar_arrive(full0 + 8 * s);
+                        }
+                        pi++;
+                    }
+                    if (ok) {
+                        // the terminator: one more stage whose first plan says the walk is over, so the
+                        // MMA thread never walks the rows itself
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        if ((ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) && lane == 0) {
+                            plans[s * C::RP].np = kPlanEnd;
+                            dev::mbar_arrive(full0 + 8 * s);
+                        }
+                    }
                 }
-                if (ok) {
-                    // the terminator: one more stage whose first plan says the walk is over, so the
-                    // MMA thread never walks the rows itself
-                    const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
-                    if ((ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) && lane == 0) {
-                        plans[s * C::RP].np = kPlanEnd;
-                        dev::mbar_arrive(full0 + 8 * s);
+            } else {
+                if (warp == 0) {
+                    // warp 0: every lane walks the same rows (warp-uniform control flow); lane 0 issues
+                    // each row's bulk copy, waits for the accumulators, writes the plan and arrives
+                    const int kcin = a.cin / 8;
+                    const uint32_t bytes = (uint32_t)kcin * kHalo * 16;
+                    RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
+                    uint32_t pi = 0;  // stage fills so far (pairs of rows)
+                    bool ok = true;
+                    while (ok && walk.next()) {
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        if (!(ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty))) break;
+                        // the stage's copies go out as soon as its buffer is free (waiting first for the
+                        // accumulators the rows start, as the plans need, left the MMA thread waiting
+                        // ~800 cycles a stage for data: the TMEM ring, not the stages, bounded how far
+                        // ahead rows were fetched); then the accumulator waits, the plans and, for
+                        // depth-to-space, the skip rows, whose buffers belong to the accumulator slots
+                        RowPlan pl[C::RP];
+                        RowWaits wts[C::RP];
+                        int rows_r[C::RP], rows_strip[C::RP];
+                        int n = 0;
+    #pragma unroll
+                        for (int h = 0; h < C::RP; h++) {
+                            if (h > 0 && (n < h || !walk.next())) break;
+                            plan_row<S, NPAD, C::NG>(walk, tmem, accf0, acce0, pl[h], wts[h]);
+                            rows_r[h] = walk.r;
+                            rows_strip[h] = walk.strip;
+                            if (lane == 0) dev::mbar_expect_tx(full0 + 8 * s, bytes);
+                            // the (row, strip) block, halo columns included: the staged row as it is
+                            if (lane == 0)
+                                dev::bulk_load(abase + s * C::STAGE + h * C::SLOT,
+                                               a.src + map_at(walk.r, walk.strip, 0, 0, a.nstrips, kcin), bytes, full0 + 8 * s);
+                            n = h + 1;
+                        }
+                        int h = 0;
+    #pragma unroll
+                        for (; h < C::RP; h++) {
+                            if (h >= n) break;
+                            const RowWaits &wt = wts[h];
+                            bool good = true;
+                            if (lane == 0) good = wt.wait(a.err);
+                            if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
+                            if (lane == 0) plans[s * C::RP + h] = pl[h];
+                            if constexpr (EK == kEpiD2S) {
+                                // the skip rows of the outputs this row starts (r + 1; r at an image's
+                                // first row), into their slots: lanes 8-10 and 11-13, one plane each
+                                if (a.skip_smem) {
+                                    const int x0 = rows_strip[h] * kTileM;
+                                    const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
+                                    const int k = lane - 8, which = k / 3, c3 = k % 3;
+                                    const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
+                                    const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
+                                    const int orow = which == 0 ? rows_r[h] + 1 : rows_r[h];
+                                    if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
+                                    __syncwarp();
+                                    if (mine)
+                                        dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + c3 * (kTileM * 2),
+                                                       a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
+                                }
+                            }
+                            __syncwarp();
+                        }
+                        // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
+                        // empty: the MMA thread skips rows whose plan has no pieces. One arrival per
+                        // stage; it completes once the copies above have landed.
+                        if (lane == 0) {
+                            for (int e = h; e < C::RP; e++) plans[s * C::RP + e].np = 0;
+                            dev::mbar_arrive(full0 + 8 * s);
+                        }
+                        pi++;
                     }
-                }
-                // on an error exit, let the last copies land before the CTA can leave
-                if (!ok && pi > 0 && lane == 0) {
-                    const uint32_t s = (pi - 1) % C::NS, ph = ((pi - 1) / C::NS) & 1;
-                    dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
+                    if (ok) {
+                        // the terminator: one more stage whose first plan says the walk is over, so the
+                        // MMA thread never walks the rows itself
+                        const uint32_t s = pi % C::NS, ph = (pi / C::NS) & 1;
+                        if ((ok = dev::mbar_wait_warp(empty0 + 8 * s, ph ^ 1, a.err, kErrProdEmpty)) && lane == 0) {
+                            plans[s * C::RP].np = kPlanEnd;
+                            dev::mbar_arrive(full0 + 8 * s);
+                        }
+                    }
+                    // on an error exit, let the last copies land before the CTA can leave
+                    if (!ok && pi > 0 && lane == 0) {
+                        const uint32_t s = (pi - 1) % C::NS, ph = ((pi - 1) / C::NS) & 1;
+                        dev::mbar_wait(full0 + 8 * s, ph, nullptr, 0);
+                    }
                 }
             }
         } else {
@@ -1077,7 +1192,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             static_assert(C::RP == 2, "the loop below takes stages of two rows");
             auto fetch = [&](uint32_t pi, RowPlan &p0, RowPlan &p1) -> bool {
                 const uint32_t s = pi % C::NS;
-                const bool good = dev::mbar_wait(full0 + 8 * s, (pi / C::NS) & 1, a.err, kErrMmaFull);
+                // the stage's plans (full), and where a separate warp copies the rows, the rows (landed)
+                bool good = dev::mbar_wait(full0 + 8 * s, (pi / C::NS) & 1, a.err, kErrMmaFull);
+                if (split_in && good) good = dev::mbar_wait(landed0 + 8 * s, (pi / C::NS) & 1, a.err, kErrMmaFull);
                 p0 = plans[s * C::RP];
                 p1 = plans[s * C::RP + 1];
                 dev::tc_fence_after();
