@@ -27,6 +27,7 @@ struct DevPass {
     int taps, src, dst;
     const int *start;
     const float *wt;
+    int step2;  // start[i] = start[0] + 2 i for every output i (a 2:1 table)
 };
 
 struct aji_plan {
@@ -298,9 +299,56 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
         }
     }
     __syncthreads();
-    // horizontal pass: thread (row group, column) keeps its column's weights in registers
+    // horizontal pass. For a 2:1 table (every output's taps start two staged columns after the
+    // previous one's) a thread takes two adjacent outputs, whose twelve taps overlap in ten: the
+    // union is seven words of each parity, loaded as float2 pairs (consecutive threads read
+    // consecutive pairs, no bank conflicts), a third of the shared-memory loads of one output a
+    // thread. Each output's FMAs run in tap order as below.
     const int tx = tid & (kPostTW - 1), grp = tid / kPostTW, cx = cx0 + tx;
-    if (cx < cw) {
+    if (ph.step2) {
+        const int t = tid & 31, rg = tid >> 5;  // output pair (2t, 2t + 1), row group
+        const int ca = cx0 + 2 * t, cb = ca + 1;
+        const int taps = ph.taps;
+        float wa[kPostMaxTaps], wb[kPostMaxTaps];
+#pragma unroll
+        for (int j = 0; j < kPostMaxTaps; j++) {
+            wa[j] = (j < taps && ca < cw) ? ph.wt[(size_t)ca * taps + j] : 0.0f;
+            wb[j] = (j < taps && cb < cw) ? ph.wt[(size_t)cb * taps + j] : 0.0f;
+        }
+        // output a's taps start at staged column 4t (s0 = start[ca] - xlo), b's at 4t + 2: words
+        // 2t .. 2t + taps / 2 of each parity plane (kPostHalf leaves room for the widest table)
+        constexpr int kW = kPostMaxTaps / 2 + 2;  // words loaded per plane (float2 pairs)
+        if (ca < cw) {
+            for (int rr = rg; rr < nrows; rr += 256 / 32) {
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const float *pl = q == 0 ? su : sv;
+                    float e[kW], o[kW];
+#pragma unroll
+                    for (int k = 0; k < kW; k += 2) {
+                        const float2 pe = *reinterpret_cast<const float2 *>(pl + rr * kPostHalf + 2 * t + k);
+                        const float2 po = *reinterpret_cast<const float2 *>(pl + kPostPar + rr * kPostHalf + 2 * t + k);
+                        e[k] = pe.x;
+                        e[k + 1] = pe.y;
+                        o[k] = po.x;
+                        o[k + 1] = po.y;
+                    }
+                    float xa = 0.0f, xb = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kPostMaxTaps; j++) {
+                        if (j < taps) {
+                            const float ta = (j & 1) ? o[j >> 1] : e[j >> 1];
+                            const float tb = (j & 1) ? o[(j >> 1) + 1] : e[(j >> 1) + 1];
+                            xa = __fmaf_rn(wa[j], ta, xa);
+                            xb = __fmaf_rn(wb[j], tb, xb);
+                        }
+                    }
+                    float *hq = q == 0 ? hu : hv;
+                    *reinterpret_cast<float2 *>(hq + rr * kPostTW + 2 * t) = make_float2(xa, xb);
+                }
+            }
+        }
+    } else if (cx < cw) {
         float wt[kPostMaxTaps];
         const int taps = ph.taps;
 #pragma unroll
@@ -461,6 +509,9 @@ bool upload_pass(DevPass *d, const FilterTable &t)
     d->dst = t.dst;
     d->start = s;
     d->wt = w;
+    d->step2 = 1;
+    for (size_t i = 1; i < t.start.size(); i++)
+        if (t.start[i] != t.start[0] + 2 * (int)i) d->step2 = 0;
     return true;
 }
 
