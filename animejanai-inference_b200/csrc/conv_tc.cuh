@@ -975,6 +975,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     // beside the block input)
 #pragma unroll
                     for (int c = 0; c < NPAD; c += 16) {
+                        // the attention GEMM's K columns only (the output channels padded to 16; the
+                        // slot's other columns accumulate zero products and are never read)
+                        if (c >= a.att_kpad) break;
                         float t[16];
                         dev::tmem_ld16(taddr + c, t);
                         dev::tmem_wait_ld();
@@ -987,7 +990,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                                 make_uint4(oh[4 * h2], oh[4 * h2 + 1], oh[4 * h2 + 2], oh[4 * h2 + 3]);
                     }
 #pragma unroll
-                    for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(taddr + c);
+                    for (int c = 0; c < NPAD; c += 16)
+                        if (c < a.att_kpad) dev::tmem_zero16(taddr + c);
                     dev::tmem_wait_st();
                     dev::tc_fence_before();
                     __syncwarp();
