@@ -22,7 +22,9 @@ depth-to-space 4): not a BASELINE config, but the reference publishes a number f
 (2.02-2.06 ms per 1080p chain on an RTX 5090).
 """
 import argparse
+import atexit
 import ctypes as C
+import datetime
 import json
 import os
 import subprocess
@@ -120,7 +122,11 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms, started before the warm-up
+    steps so that it is sampling when the timed region begins. stop(t0, t1) keeps the samples
+    taken inside the timed region [t0, t1] (host wall clock); a region shorter than the sampling
+    period may hold none, and then the last sample taken before it ended (under the warm-up
+    steps' load) stands in, marked by "window"."""
 
     def __init__(self, index):
         self.index = index
@@ -133,14 +139,27 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "--query-gpu=timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            atexit.register(self._end)  # an exception before stop() must not leave it sampling
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def _end(self):
+        if self.proc and self.proc.poll() is None:
+            self.proc.kill()
+
+    def wait_first(self, timeout=5.0):
+        """Wait (at most `timeout` seconds) until the first sample has been written."""
+        t_end = time.time() + timeout
+        while self.proc and time.time() < t_end:
+            if os.path.getsize(self.path) > 0:
+                return
+            time.sleep(0.02)
+
+    def stop(self, t0=None, t1=None):
         if not self.proc:
             return None
         self.proc.terminate()
@@ -148,25 +167,35 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []  # (time, sm MHz, max MHz, reasons)
         with open(self.path) as f:
             for line in f:
                 parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 7:
+                if len(parts) < 8:
                     continue
                 try:
-                    sm.append(float(parts[0]))
-                    mx = max(mx, float(parts[1]))
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                except ValueError:
+                    ts = None  # an unexpected timestamp format: the sample counts as inside
+                try:
+                    row = (ts, float(parts[1]), float(parts[2]),
+                           {n for n, v in zip(names, parts[4:8]) if v.lower() == "active"})
                 except ValueError:
                     continue
-                for n, v in zip(names, parts[3:7]):
-                    if v.lower() == "active":
-                        reasons.add(n)
+                rows.append(row)
         os.unlink(self.path)
-        if not sm:
+        window = "timed region"
+        if t0 is not None and t1 is not None:
+            inside = [r for r in rows if r[0] is None or t0 <= r[0] <= t1]
+            if not inside:
+                inside, window = [r for r in rows if r[0] <= t1][-1:], "last sample before the timed region ended"
+            rows = inside
+        if not rows:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set().union(*(r[3] for r in rows))
+        return {"sm_mhz": float(np.median([r[1] for r in rows])), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "window": window}
 
 
 def cpu_baseline_sample(rows=16, nthreads=0, model="compact"):
@@ -296,6 +325,9 @@ def run_ours(args, rank, world, local_rank, dist):
         if dist is not None:
             dist.barrier()
 
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    clocks.wait_first()
     for i in range(args.warmup):
         step(i)
     stream.synchronize()
@@ -304,10 +336,9 @@ def run_ours(args, rank, world, local_rank, dist):
     # ---- device-timed region (frames resident in HBM); no per-step events inside it (they would
     # split the programmatic overlap of consecutive kernels)
     prof = args.bands <= 1
-    clocks = ClockSampler(local_rank)
     barrier()
     torch.cuda.synchronize()
-    clocks.start()
+    t0 = datetime.datetime.now()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
@@ -315,7 +346,8 @@ def run_ours(args, rank, world, local_rank, dist):
     e1.record(stream)
     e1.synchronize()
     torch.cuda.synchronize()
-    clk = clocks.stop()
+    t1 = datetime.datetime.now()
+    clk = clocks.stop(t0, t1)
     barrier()
     t_ms = e0.elapsed_time(e1)
     assert ajib.kernel_status() == 0, "a kernel pipeline wait timed out"
@@ -563,7 +595,7 @@ def chain_flops(plans, w, h):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "refgpu"])
     ap.add_argument("--kernel", default=None, choices=[None, "conv64", "head", "head8", "tail"],
