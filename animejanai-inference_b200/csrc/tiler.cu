@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "cuctx.h"
 #include "tiler.h"
 #include "../../include/aji_b200.h"
 
@@ -155,21 +156,32 @@ namespace {
 
 constexpr size_t kStaticTableBytes = 1u << 20;  // 1 MiB: outputs up to about 24K x 24K pixels
 static __device__ __align__(256) unsigned char g_tiler_tables[kStaticTableBytes];
+// The host image of the tables a call uploads: file-scope, so the copy's source lives as long as
+// the process whatever the copy's timing; written and copied under g_static_mu.
+static unsigned char g_host_tables[kStaticTableBytes];
+std::mutex g_static_mu;
 
-// The area's device address on the current device. In host code g_tiler_tables names a host-side
-// stand-in, not the device memory, so the address comes from cudaGetSymbolAddress: once per
-// device, on the first call made with that device current.
+// The area's device address for the current device and context. In host code g_tiler_tables names
+// a host-side stand-in, not the device memory, so the address comes from cudaGetSymbolAddress:
+// once per device, on the first call made with that device current, and again if that device's
+// current context has changed since (a reset or a recreated primary context maps the module
+// anew). The caller holds g_static_mu.
 void *static_tables()
 {
-    static std::mutex mu;
     static void *addr[64] = {};
+    static CUcontext ctx_of[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    CUcontext cur = nullptr;
+    const Driver &d = driver();
+    if (!d.ok || d.ctx_get_current(&cur) != CUDA_SUCCESS) return nullptr;
+    if (!addr[dev] || ctx_of[dev] != cur) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_tiler_tables) != cudaSuccess) return nullptr;
+        // the lookup may have made the device's primary context current: key the cache on that
+        if (d.ctx_get_current(&cur) != CUDA_SUCCESS) return nullptr;
         addr[dev] = p;
+        ctx_of[dev] = cur;
     }
     return addr[dev];
 }
@@ -204,11 +216,18 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
         const size_t o_wx = put(img, axis_weights(g.ox, g.W, g.tw, s)), o_wy = put(img, axis_weights(g.oy, g.H, g.th, s));
         const size_t o_cx = put(img, cover(g.ox, spw, s, g.W)), o_cy = put(img, cover(g.oy, sph, s, g.H));
         if (img.size() > kStaticTableBytes) return AJIB_ERR_UNSUPPORTED;  // tables beyond the fixed area
-        unsigned char *base = static_cast<unsigned char *>(static_tables());
-        if (!base) return AJIB_ERR_CUDA;
         const cudaStream_t st = (cudaStream_t)stream;
-        // from pageable host memory: returns once the bytes are staged, so img may go
-        if (cudaMemcpyAsync(base, img.data(), img.size(), cudaMemcpyHostToDevice, st) != cudaSuccess) return AJIB_ERR_CUDA;
+        unsigned char *base = nullptr;
+        {
+            std::lock_guard<std::mutex> lk(g_static_mu);
+            base = static_cast<unsigned char *>(static_tables());
+            if (!base) return AJIB_ERR_CUDA;
+            // a copy from pageable host memory: it returns once the bytes are staged (and may wait
+            // for earlier work on st first), so the next call may rewrite the host image
+            std::memcpy(g_host_tables, img.data(), img.size());
+            if (cudaMemcpyAsync(base, g_host_tables, img.size(), cudaMemcpyHostToDevice, st) != cudaSuccess)
+                return AJIB_ERR_CUDA;
+        }
         const int OW = g.W * s, OH = g.H * s;
         const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
         k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),

@@ -36,6 +36,9 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "animejanai-inference_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+from synth import p010_frame  # noqa: E402  (seeded synthetic frames, shared with the tests)
 
 W_IN, H_IN, SCALE = 1920, 1080, 2
 MODEL_SEED = 1
@@ -68,15 +71,15 @@ MODELS = {
 
 
 def bench_plans(model):
-    """The model's plans, in chain order."""
-    import ajib
+    """The model's plans, in chain order (pure numpy: ajib_plans loads no library)."""
+    import ajib_plans as P
     if model == "spanf3":
-        return [ajib.spanf3_plan(MODEL_SEED, c=48, blocks=5, gain=0.7)]
+        return [P.spanf3_plan(MODEL_SEED, c=48, blocks=5, gain=0.7)]
     if model == "span":
-        return [ajib.span_plan(MODEL_SEED, c=48, blocks=6)]
+        return [P.span_plan(MODEL_SEED, c=48, blocks=6)]
     if model == "chain":
-        return [ajib.compact_plan(MODEL_SEED), ajib.compact_plan(MODEL_SEED + 1)]
-    return [ajib.compact_plan(MODEL_SEED)]
+        return [P.compact_plan(MODEL_SEED), P.compact_plan(MODEL_SEED + 1)]
+    return [P.compact_plan(MODEL_SEED)]
 
 
 def plan_scale(plan):
@@ -84,32 +87,6 @@ def plan_scale(plan):
 # DRAM bytes (read + write) of one body-conv launch at 1920x1080, from the ncu capture summarised
 # in profiles/conv3x3_body_64x64_1080p.txt (the roofline's "traffic")
 BODY_TRAFFIC_BYTES = 503.5e6
-
-
-def value_noise(rng, h, w, lo, hi, cell=32):
-    """Seeded smooth value noise in [lo, hi]: random values on a coarse grid, bilinear between."""
-    gh, gw = h // cell + 2, w // cell + 2
-    g = rng.uniform(lo, hi, size=(gh, gw))
-    ys = np.arange(h) / cell
-    xs = np.arange(w) / cell
-    y0, x0 = np.floor(ys).astype(int), np.floor(xs).astype(int)
-    fy, fx = (ys - y0)[:, None], (xs - x0)[None, :]
-    a = g[y0][:, x0]
-    b = g[y0][:, x0 + 1]
-    c = g[y0 + 1][:, x0]
-    d = g[y0 + 1][:, x0 + 1]
-    return (a * (1 - fy) * (1 - fx) + b * (1 - fy) * fx + c * fy * (1 - fx) + d * fy * fx)
-
-
-def p010_frame(seed, w=W_IN, h=H_IN):
-    """One P010 frame: Y and interleaved CbCr from smooth value noise spanning 64..940 (10-bit),
-    stored in the high bits of 16."""
-    rng = np.random.default_rng(seed)
-    y = np.rint(value_noise(rng, h, w, 64, 940)).astype(np.uint16) << 6
-    u = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
-    v = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
-    uv = np.stack([u, v], axis=-1).reshape(h // 2, w)
-    return y, uv
 
 
 def load_peaks():
@@ -198,60 +175,212 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows), "window": window}
 
 
-def cpu_baseline_sample(rows=16, nthreads=0, model="compact"):
-    """The reference CPU path on a bounded sample: a band of `rows` input rows through the net(s)
-    (every step; a chain's second net on the first's output band), timed on the host cores. Uses
-    oracle/_ref (the reference's run_plan compiled from its own sources) when built, else the
-    oracle's restatement. Returns (frames/s, cores, kind, sample)."""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
+CPU_BAND_ROWS = 16  # the CPU baseline's sample: a band of this many input rows of the frame
+
+
+def cpu_baseline_sample(rows=CPU_BAND_ROWS, nthreads=0, model="compact"):
+    """The reference CPU path on a bounded sample: a band of `rows` input rows of a P010 frame
+    through the colour pre pass, the net(s) (every step; a chain's second net on the first's
+    output band) and the colour post pass, timed on the host cores. The net is the reference's own
+    run_plan (sanity/native_ref.h) compiled from its sources into oracle/_ref when built, else the
+    oracle's restatement; the colour passes are the oracle's restatement of src/kernels.cu (the
+    reference has no CPU colour code). Loads neither libaji.so nor the GPU.
+    Returns (frames/s extrapolated from the band, band seconds, cores, kind, sample)."""
+    from util import oracle_post, oracle_pre
     spec = MODELS[model]
     plans = bench_plans(model)
-    rng = np.random.default_rng(7)
-    x = rng.uniform(0, 1, size=(3, rows, spec["w"])).astype(np.float16).astype(np.float32)
+    u = plans[0].get("unshuffle", 1)
+    rows = max(rows, 2 * u)
+    y, uv = p010_frame(7, spec["w"], rows)
     ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_net.so")
-    dt = 0.0
     if os.path.exists(ref_lib):
         import refnet
-        for plan in plans:
-            t0 = time.perf_counter()
-            x = refnet.run_plan(ref_lib, plan, x, nthreads)
-            dt += time.perf_counter() - t0
-        cores = refnet.threads(ref_lib, nthreads)
-        kind = "reference"
+
+        def net(plan, x):
+            return refnet.run_plan(ref_lib, plan, x, nthreads)
+        cores, kind = refnet.threads(ref_lib, nthreads), "reference"
     else:
         import oracle_net
-        for plan in plans:
-            t0 = time.perf_counter()
-            x = oracle_net.run_plan(plan, x, nthreads)
-            dt += time.perf_counter() - t0
-        cores = nthreads if nthreads > 0 else os.cpu_count()
-        kind = "port"
+
+        def net(plan, x):
+            return oracle_net.run_plan(plan, x, nthreads)
+        cores, kind = (nthreads if nthreads > 0 else os.cpu_count()), "port"
+    t0 = time.perf_counter()
+    x = oracle_pre(2, y, uv, 2, 1, 1).view(np.float16).astype(np.float32)
+    for plan in plans:
+        x = net(plan, x)
+    oracle_post(2, x.astype(np.float16).view(np.uint16), 2, 1, 1)
+    dt = time.perf_counter() - t0
     fps = rows / spec["h"] / dt
     nsteps = sum(len(p["steps"]) for p in plans)
-    return fps, cores, kind, (f"{spec['w']}x{rows} band of the {spec['w']}x{spec['h']} input through all {nsteps} "
-                              f"steps ({dt:.2f} s)")
+    return fps, dt, cores, kind, (f"a {spec['w']}x{rows} P010 band of the {spec['w']}x{spec['h']} frame: colour pre "
+                                  f"pass, all {nsteps} net steps ({kind} run_plan), colour post pass; "
+                                  f"{dt:.2f} s per band, frames/s = {rows}/{spec['h']} frame / band time")
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path on the host cores, on rank 0 only. A step is
+    one band sample (cpu_baseline_sample); value = frames/s extrapolated from the bands."""
     if rank != 0:
         return
-    vals = []
+    bands = []
     info = None
     for i in range(args.warmup + args.steps):
-        fps, cores, kind, sample = cpu_baseline_sample(rows=16, model=args.model)
+        fps, dt, cores, kind, sample = cpu_baseline_sample(model=args.model)
         if i >= args.warmup:
-            vals.append(fps)
+            bands.append(dt)
         info = (cores, kind, sample)
-    v = float(np.mean(vals))
+    band_s = float(np.mean(bands))
     spec = MODELS[args.model]
+    rows = max(CPU_BAND_ROWS, 2 * bench_plans(args.model)[0].get("unshuffle", 1))
+    v = rows / spec["h"] / band_s
     line = {"impl": "reference", "metric": spec["metric"], "value": v, "unit": "frames/s",
             "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": 1000.0 * band_s, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": spec["workload"] + ", CPU reference net on a band sample", "model": spec["model"]},
+            "config": {"workload": spec["workload"] + ", reference CPU path on band samples", "model": spec["model"],
+                       "step": f"one {spec['w']}x{rows} band of the frame through the whole path (ms_per_step is "
+                               f"the band's time); value = {rows}/{spec['h']} frame per step / ms_per_step, "
+                               "an extrapolation to whole frames"},
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": info[0], "kind": info[1], "sample": info[2]},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+class RefCsp(C.Structure):
+    _fields_ = [("kr", C.c_float), ("kb", C.c_float), ("yoff", C.c_float), ("yscale", C.c_float),
+                ("coff", C.c_float), ("cscale", C.c_float)]
+
+
+def reference_gpu_bar(args, plans, spec, frames_in, stream, dev):
+    """The reference's own native video path on this B200, on the same frames: its colour kernels
+    (src/kernels.cu aji_run_pre / aji_run_post) and its executor (src/native/executor.cpp, one
+    mma.sync k_conv3x3 / k_concat1x1 launch per plan step), all compiled for sm_100a from its
+    sources into oracle/_ref. K frames timed with CUDA events on the launching stream, as this
+    engine's frames are; plus the reference's body conv (64 -> 64 + PReLU at the frame's size)
+    alone. Returns (fields for the JSON line, the P010 output of frame 0)."""
+    import torch
+    import refnet
+    kern = os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so")
+    exe = os.path.join(ROOT, "oracle", "_ref", "libref_exec.so")
+    if not (os.path.exists(kern) and os.path.exists(exe)):
+        return {"unavailable": "the reference's GPU kernels are not built (oracle/_ref)"}, None
+    ref = C.CDLL(kern)
+    ref.aji_pre_plan_create.restype = C.c_void_p
+    ref.aji_post_plan_create.restype = C.c_void_p
+    ref.aji_pre_plan_create.argtypes = [C.c_int] * 5
+    ref.aji_post_plan_create.argtypes = [C.c_int] * 5
+    ref.aji_run_pre.argtypes = [C.c_void_p, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_void_p,
+                                C.c_void_p]
+    ref.aji_run_post.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_ssize_t, C.c_void_p, C.c_ssize_t,
+                                 C.c_void_p]
+    ref.aji_make_csp.restype = RefCsp
+    ref.aji_make_csp.argtypes = [C.c_int] * 3
+    ref.aji_plan_destroy.argtypes = [C.c_void_p]
+    sp = stream.cuda_stream
+    W, H = spec["w"], spec["h"]
+    csp = ref.aji_make_csp(2, 2, 1)
+    sizes, cw, ch = [], W, H
+    for pl in plans:
+        sizes.append((cw, ch))
+        cw, ch = cw * plan_scale(pl), ch * plan_scale(pl)
+    OW, OH = cw, ch
+    execs = [refnet.RefExec(exe, pl, w_, h_, sp) for pl, (w_, h_) in zip(plans, sizes)]
+    bufs = [torch.empty((3, h_, w_), dtype=torch.float16, device=dev) for (w_, h_) in sizes]
+    bufs.append(torch.empty((3, OH, OW), dtype=torch.float16, device=dev))
+    pre = ref.aji_pre_plan_create(2, W, H, 1, 0)
+    post = ref.aji_post_plan_create(2, OW, OH, 1, 0)
+    oy = torch.empty((OH, OW), dtype=torch.int16, device=dev)
+    ouv = torch.empty((OH // 2, OW), dtype=torch.int16, device=dev)
+
+    def frame(i):
+        yi, uvi = frames_in[i % len(frames_in)]
+        assert ref.aji_run_pre(pre, yi.data_ptr(), W * 2, uvi.data_ptr(), W * 2, C.byref(csp), bufs[0].data_ptr(),
+                               sp) == 0
+        for k, e in enumerate(execs):
+            assert e.run(bufs[k].data_ptr(), bufs[k + 1].data_ptr(), sp) == 0
+        assert ref.aji_run_post(post, bufs[-1].data_ptr(), C.byref(csp), oy.data_ptr(), OW * 2, ouv.data_ptr(),
+                                OW * 2, sp) == 0
+
+    n = max(3, min(args.steps, 50))
+    for i in range(3):
+        frame(i)
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        frame(i)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    frame(0)
+    stream.synchronize()
+    out0 = (oy.cpu().numpy().view(np.uint16).copy(), ouv.cpu().numpy().view(np.uint16).copy())
+    for e in execs:
+        e.close()
+    ref.aji_plan_destroy(pre)
+    ref.aji_plan_destroy(post)
+    fields = {"what": "the reference's native video path (aji_run_pre -> Executor::run, one mma.sync k_conv3x3 per "
+                      "step -> aji_run_post) compiled for sm_100a from its own sources, same frames, same GPU",
+              "frames": n, "ms_per_frame": ms, "frames_per_s": 1000.0 / ms}
+    # the reference's body conv alone (the kernel to beat), where the model has one of 64 channels
+    conv_lib = os.path.join(ROOT, "oracle", "_ref", "libref_conv.so")
+    body = [st for st in plans[-1]["steps"] if st["kind"] == 0 and st.get("in_", 0) == 0 and st.get("out", 0) == 0]
+    if os.path.exists(conv_lib) and body and body[0]["cin"] == 64 and body[0]["cout"] == 64:
+        from util import conv_weights, to_f16_bits
+        rc_ = C.CDLL(conv_lib)
+        rc_.ref_conv_upload.restype = C.c_void_p
+        rc_.ref_conv_upload.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]
+        rc_.ref_conv_launch.argtypes = [C.c_void_p] + [C.c_int] * 6 + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p]
+        rc_.ref_conv_release.argtypes = [C.c_void_p]
+        bw, bh = sizes[-1]
+        rng = np.random.default_rng(0)
+        w, b, sl = conv_weights(rng, 64, 64, prelu=True)
+        wb = to_f16_bits(w)
+        hw = rc_.ref_conv_upload(wb.ctypes.data, b.ctypes.data, sl.ctypes.data, 64, 64, 64, 64)
+        src = torch.from_numpy(rng.uniform(-1, 1, size=(bh, bw, 64)).astype(np.float16)).to(dev)
+        dst = torch.empty_like(src)
+
+        def launch():
+            assert rc_.ref_conv_launch(hw, 0, 2, 0, 0, 64, 64, src.data_ptr(), None, dst.data_ptr(), bh, bw, -1, sp) == 0
+        for _ in range(3):
+            launch()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(20):
+            launch()
+        c1.record(stream)
+        c1.synchronize()
+        fields["body_conv_ms"] = c0.elapsed_time(c1) / 20
+        fields["body_conv"] = f"reference k_conv3x3<64,64,PReLU> at {bw}x{bh} alone, its own tile pick"
+        rc_.ref_conv_release(hw)
+    return fields, out0
+
+
+def oracle_window_check(plan, y, uv, gy, guv, W, H):
+    """The frame's P010 output on a window of rows against the oracle's own chain (pre pass, the
+    net on the input rows the window's receptive field reaches, post pass), within the tests'
+    3 codes of 10 bits. Untimed; for single-model workloads."""
+    from oracle_net import run_plan
+    from util import oracle_post, oracle_pre
+    u = plan.get("unshuffle", 1)
+    R = plan_scale(plan)
+    radius = u * sum(1 for st in plan["steps"] if np.asarray(st["w"]).shape[0] == 9)
+    a = (H // 2 - 4) // (2 * u) * (2 * u)
+    b = a + 8
+    # 8 more input rows each side: the post pass's 12-tap vertical chroma filter reaches 6 output rows
+    c0, c1 = max(0, a - radius - 8) // (2 * u) * (2 * u), min(H, b + radius + 8)
+    x = oracle_pre(2, y, uv, 2, 1, 1).view(np.float16).astype(np.float32)
+    t0 = time.perf_counter()
+    net = run_plan(plan, np.ascontiguousarray(x[:, c0:c1]))
+    wy, wuv = oracle_post(2, net.astype(np.float16).view(np.uint16), 2, 1, 1)
+    dt = time.perf_counter() - t0
+    ly = (wy[R * (a - c0):R * (b - c0)] >> 6).astype(int)
+    luv = (wuv[R * (a - c0) // 2:R * (b - c0) // 2] >> 6).astype(int)
+    dy = int(np.abs((gy[R * a:R * b] >> 6).astype(int) - ly).max())
+    duv = int(np.abs((guv[R * a // 2:R * b // 2] >> 6).astype(int) - luv).max())
+    return {"input_rows": [a, b], "oracle_rows": [c0, c1], "max_code_diff_y": dy, "max_code_diff_uv": duv,
+            "ok": dy <= 3 and duv <= 3, "oracle_s": dt}
 
 
 def current_context():
@@ -420,6 +549,27 @@ def run_ours(args, rank, world, local_rank, dist):
     barrier()
     e2e_ms = f0.elapsed_time(f1)
 
+    # ---- untimed: the output of frame 0 (checksum, and a window of rows against the oracle's own
+    # chain), and the reference's own GPU path on the same frames (N = 1 only)
+    check = None
+    ref_gpu = None
+    if world == 1 and not args.no_check:
+        step(0)
+        stream.synchronize()
+        gy = outs[0][0].cpu().numpy().view(np.uint16)
+        guv = outs[0][1].cpu().numpy().view(np.uint16)
+        import hashlib
+        check = {"frame": 0, "p010_sha256": hashlib.sha256(gy.tobytes() + guv.tobytes()).hexdigest()}
+        if len(plans) == 1:
+            y0, uv0 = p010_frame(1000 * rank + 0, W_IN, H_IN)
+            check["oracle_window"] = oracle_window_check(plan, y0, uv0, gy, guv, W_IN, H_IN)
+        ref_gpu, rout = reference_gpu_bar(args, plans, spec, frames_in, stream, dev)
+        if rout is not None:
+            ref_gpu["speedup_frame"] = ref_gpu["ms_per_frame"] / (t_ms / args.steps)
+            ref_gpu["max_code_diff_vs_this_engine"] = int(max(
+                np.abs((rout[0] >> 6).astype(int) - (gy >> 6).astype(int)).max(),
+                np.abs((rout[1] >> 6).astype(int) - (guv >> 6).astype(int)).max()))
+
     # max over ranks
     times = np.array([t_ms, e2e_ms], dtype=np.float64)
     if dist is not None:
@@ -453,14 +603,18 @@ def run_ours(args, rank, world, local_rank, dist):
         body_ms = float(sum(step_ms[k] / step_n[k] for k in body) / len(body))
     roof = None
     if body_ms:
+        # the kernel time comes from a short per-launch event pass (at most 32 frames, well under a
+        # second), so the burst peak is the denominator; the sustained fraction is reported beside it
         flops_body = float(np.mean(flops_steps))
         achieved = flops_body / (body_ms / 1000.0) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_sus, "unit": "TFLOP/s",
-                "frac": achieved / tflops_sus, "traffic": BODY_TRAFFIC_BYTES if args.model in ("compact", "chain") else None,
+        frame_tf = chain_flops(plans, W_IN, H_IN) / (t_ms / args.steps / 1000.0) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_burst, "unit": "TFLOP/s",
+                "frac": achieved / tflops_burst,
+                "traffic": BODY_TRAFFIC_BYTES if args.model in ("compact", "chain") else None,
                 "kernel": spec["kernel"],
-                "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json)",
-                "flops_per_launch": flops_body,
-                "frame_tflops": chain_flops(plans, W_IN, H_IN) / (t_ms / args.steps / 1000.0) / 1e12}
+                "kernel_ms": body_ms, "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
+                "frac_of_sustained": achieved / tflops_sus, "flops_per_launch": flops_body,
+                "frame_tflops": frame_tf, "frame_frac_of_burst": frame_tf / tflops_burst}
 
     nsteps = sum(len(pl["steps"]) for pl in plans)
     workload, model = spec["workload"], spec["model"]
@@ -478,11 +632,17 @@ def run_ours(args, rank, world, local_rank, dist):
             # in the timed region: pre, per net its input pack and steps, post
             "gpu_launches": args.steps * (2 + (nsteps + len(plans)) * max(1, args.bands)),
             "clocks": clk}
+    if check is not None:
+        line["check"] = check
+    if ref_gpu is not None:
+        if body_ms and "body_conv_ms" in ref_gpu and args.model in ("compact", "chain"):
+            ref_gpu["speedup_body_conv"] = ref_gpu["body_conv_ms"] / body_ms
+        line["reference_gpu"] = ref_gpu
     if spanf3:
         line["config"]["published"] = (f"reference {SPANF3_PUBLISHED_MS} ms per 1080p chain on an RTX 5090 "
                                        "(BENCHMARKS.md:257); vs_baseline is per GPU")
     if world == 1 and not args.no_cpu_baseline:
-        fps, cores, kind, sample = cpu_baseline_sample(rows=16, model=args.model)
+        fps, _, cores, kind, sample = cpu_baseline_sample(model=args.model)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": kind, "sample": sample}
     vid.close()
     print(json.dumps(line), flush=True)
@@ -603,6 +763,8 @@ def main():
     ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the untimed output check and the reference GPU bar")
     ap.add_argument("--model", default="compact", choices=list(MODELS),
                     help="compact: BASELINE config 1 (the headline); span: config 3; chain: config 4; "
                          "spanf3: the shipping SPANF3 structure")

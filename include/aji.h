@@ -5,7 +5,8 @@
  * these symbols. The types, enum values, struct layouts and function signatures are those of the
  * reference header (the-database/animejanai-inference include/aji.h:45-501), so a caller built
  * against that header loads this library unchanged. Only the native conv path (SRVGG Compact,
- * SuperUltraCompact, SPAN) is implemented; RIFE, temporal models and frame resizing answer as an
+ * SuperUltraCompact, SPAN, SPANF3) is implemented, with Spline36 resizing (aji_resize_frame and
+ * conf chains' resize-before-upscale steps); RIFE, temporal models and aji_resize answer as an
  * inactive feature does (0, or AJI_ERR with aji_last_error set).
  *
  * Frames: aji_frame.plane[] are CUDA device pointers (CUdeviceptr), stride[] in bytes.
@@ -13,9 +14,12 @@
  * returns a ticket that completes once everything enqueued before it has.
  *
  * Modes:
- *  - direct mode (conf_path NULL): engine_path names a native model file (a conv net this
- *    library runs: see aji_b200.h, ajib_model_load); aji_configure(w, h) sizes it for w x h.
- *  - conf mode is not implemented by this engine: aji_create returns NULL for it.
+ *  - direct mode (conf_path NULL): engine_path names a model file (this engine's native format
+ *    or an ONNX SRVGG / SPAN export, see aji_b200.h, ajib_model_load); aji_configure(w, h) sizes
+ *    it for w x h.
+ *  - conf mode (conf_path set): an animejanai.conf; aji_configure picks the slot's chain for the
+ *    stream's size and fps and builds it from the models in model_dir (the conf's directory when
+ *    NULL): resize steps and models one after another, or passthrough when no chain matches.
  */
 #ifndef AJI_H
 #define AJI_H

@@ -198,7 +198,9 @@ AJIB_EXPORT void ajib_tiler_release(ajib_tiler **t);
  * The first call on a device looks up the area's device address (with that device current);
  * make that first call before any stream capture. Every call on a device uses the same area and
  * leaves its tables there: calls that overlap on the GPU (other streams, or the next call before
- * this one's kernel has run on another stream) race. */
+ * this one's kernel has run on another stream) race; calls on one stream are ordered by it. Each
+ * call uploads its tables by a copy from host memory inside this library, which may wait for
+ * earlier work on `stream` before the call returns. */
 AJIB_EXPORT int ajib_tiler_compose_static(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap,
                                           int even, const void *tiles, uint8_t *out, void *stream);
 
@@ -260,7 +262,9 @@ AJIB_EXPORT int ajib_video_profile_read(aji_ctx *c, double *ms, int *counts, int
 AJIB_EXPORT int ajib_exec_info(const ajib_exec *e, size_t *device_bytes, size_t *weight_bytes, int *launches);
 
 /* Reads and optionally clears the current device's kernel status word: 0, or the code of the
- * first pipeline wait that timed out in a kernel of this library. */
+ * first pipeline wait that timed out in a kernel of this library. There is one word per device,
+ * shared by every context and executor on it: a code may come from another context's kernels,
+ * and a read that clears it clears it for all of them. */
 AJIB_EXPORT int ajib_kernel_status(int clear);
 
 /* A one-CTA check of the tensor-core operand encodings the conv kernels use (a: [130][32] fp16,

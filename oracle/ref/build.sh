@@ -3,9 +3,11 @@
 # oracle/_ref/: the checkers and the CPU baseline. Nothing here is part of the product, and no
 # reference source is copied: each library is built from the files where they lie, plus the thin
 # C shims in this directory. Only the compilers run (no reference build system).
+# The reference tree: the first argument, else $AJIB_REFERENCE, else a `reference` directory beside
+# this repository.
 set -euo pipefail
-REF=${1:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+REF=${1:-${AJIB_REFERENCE:-$HERE/../../../reference}}
 OUT=$HERE/../_ref
 mkdir -p "$OUT"
 CXX=${CXX:-g++}
@@ -14,7 +16,7 @@ ARCH="-gencode arch=compute_100a,code=sm_100a"
 
 # CPU reference net (sanity/native_ref.h + src/native/pack.cpp)
 $CXX -O3 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/sanity" -I"$REF/include" \
-    "$HERE/refnet_shim.cpp" "$REF/src/native/pack.cpp" -o "$OUT/libref_net.so" -lpthread
+    -I"$HERE" "$HERE/refnet_shim.cpp" "$REF/src/native/pack.cpp" -o "$OUT/libref_net.so" -lpthread
 # CPU tiler (src/core/tiling.cpp)
 $CXX -O2 -std=c++17 -fPIC -shared -I"$REF/src" -I"$REF/src/core" -I"$REF/include" \
     "$HERE/reftiling_shim.cpp" "$REF/src/core/tiling.cpp" -o "$OUT/libref_tiling.so" -lpthread
@@ -34,5 +36,9 @@ if command -v "$NVCC" >/dev/null; then
         "$HERE/reftiling_gpu_shim.cu" "$REF/src/core/tiling_gpu.cu" -o "$OUT/libref_tiling_gpu.so"
     $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" \
         "$HERE/refconv_shim.cu" "$REF/src/native/conv.cu" "$REF/src/native/pack.cpp" -o "$OUT/libref_conv.so"
+    # the reference's GPU executor over those kernels (src/native/executor.cpp + layout.cpp)
+    $NVCC $ARCH -O3 -std=c++17 -Xcompiler -fPIC -shared -I"$REF/src" -I"$REF/include" -I"$HERE" \
+        "$HERE/refexec_shim.cu" "$REF/src/native/executor.cpp" "$REF/src/native/layout.cpp" \
+        "$REF/src/native/conv.cu" "$REF/src/native/pack.cpp" -o "$OUT/libref_exec.so"
 fi
 echo "oracle/_ref built from $REF"

@@ -32,9 +32,9 @@ def threads(path, nthreads=0):
     return _lib(path).ref_threads()
 
 
-def run_plan(path, plan, x, nthreads=0):
-    """x: NCHW float32 [3][h][w]. Returns the reference's NCHW output [3][R*h/u][R*w/u]."""
-    lib = _lib(path)
+def plan_struct(plan):
+    """The plan as the shims' ref_step array (oracle/ref/refplan.h) and the channel list; the third
+    element keeps the weight arrays alive while the structures point at them."""
     keep = []
     steps = (RefStep * len(plan["steps"]))()
     for i, s in enumerate(plan["steps"]):
@@ -61,6 +61,13 @@ def run_plan(path, plan, x, nthreads=0):
             keep += [aw, ab]
             r.att_w, r.att_bias = aw.ctypes.data, ab.ctypes.data
     ch = (C.c_int * len(plan["channels"]))(*plan["channels"])
+    return steps, ch, keep
+
+
+def run_plan(path, plan, x, nthreads=0):
+    """x: NCHW float32 [3][h][w]. Returns the reference's NCHW output [3][R*h/u][R*w/u]."""
+    lib = _lib(path)
+    steps, ch, keep = plan_struct(plan)
     x = np.ascontiguousarray(x, np.float32)
     _, h, wd = x.shape
     R, u = plan["depth_to_space"], plan.get("unshuffle", 1)
@@ -69,3 +76,32 @@ def run_plan(path, plan, x, nthreads=0):
                           out.ctypes.data)
     assert rc == 0
     return out
+
+
+class RefExec:
+    """The reference's own GPU executor (src/native/executor.cpp, its k_conv3x3 / k_concat1x1
+    kernels for sm_100a) for a plan at w x h, from oracle/_ref/libref_exec.so."""
+
+    def __init__(self, path, plan, w, h, stream=None):
+        lib = C.CDLL(path)
+        lib.ref_exec_create.restype = C.c_void_p
+        lib.ref_exec_create.argtypes = [C.POINTER(RefStep), C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_void_p, C.c_char_p, C.c_int]
+        lib.ref_exec_run.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        lib.ref_exec_run.restype = C.c_int
+        lib.ref_exec_release.argtypes = [C.c_void_p]
+        self.lib = lib
+        steps, ch, keep = plan_struct(plan)
+        err = C.create_string_buffer(512)
+        self.handle = lib.ref_exec_create(steps, len(plan["steps"]), ch, len(plan["channels"]), plan["depth_to_space"],
+                                          plan.get("unshuffle", 1), w, h, stream, err, 512)
+        if not self.handle:
+            raise RuntimeError("reference executor refused the plan: " + err.value.decode())
+
+    def run(self, src, dst, stream=None):
+        return self.lib.ref_exec_run(self.handle, src, dst, stream)
+
+    def close(self):
+        if self.handle:
+            self.lib.ref_exec_release(self.handle)
+            self.handle = None
