@@ -378,6 +378,106 @@ class Video:
             pass
 
 
+lib.ajib_video_create_multi.argtypes = [C.POINTER(CreateParams), C.POINTER(C.c_int), C.c_int, C.c_int, C.c_char_p,
+                                        C.c_size_t]
+lib.ajib_video_create_multi.restype = C.c_void_p
+lib.ajib_video_multi_configure.argtypes = [_vp, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+lib.ajib_video_multi_configure.restype = C.c_int
+lib.ajib_video_multi_submit.argtypes = [_vp, C.POINTER(Frame), C.POINTER(Frame)]
+lib.ajib_video_multi_submit.restype = C.c_int64
+lib.ajib_video_multi_wait.argtypes = [_vp, C.c_int64]
+lib.ajib_video_multi_wait.restype = C.c_int
+lib.ajib_video_multi_done.argtypes = [_vp, C.c_int64]
+lib.ajib_video_multi_done.restype = C.c_int
+lib.ajib_video_multi_devices.argtypes = [_vp]
+lib.ajib_video_multi_devices.restype = C.c_int
+lib.ajib_video_multi_error.argtypes = [_vp]
+lib.ajib_video_multi_error.restype = C.c_char_p
+lib.ajib_video_multi_destroy.argtypes = [C.POINTER(_vp)]
+lib.ajib_video_multi_destroy.restype = None
+lib.ajib_video_multi_timing.argtypes = [_vp, C.c_int]
+lib.ajib_video_multi_timing.restype = C.c_int
+lib.ajib_video_multi_device_ms.argtypes = [_vp, C.POINTER(C.c_double), C.c_int]
+lib.ajib_video_multi_device_ms.restype = C.c_int
+lib.ajib_selftest_frame_order.argtypes = [C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp]
+lib.ajib_selftest_frame_order.restype = C.c_int
+
+
+class VideoMulti:
+    """One stream over several GPUs (ajib_video_create_multi): host frames in and out, frame k on
+    device k mod n, results in submission order. model_path: direct mode; conf_path: conf mode."""
+
+    def __init__(self, devices, model_path=None, max_w=0, max_h=0, conf_path=None, model_dir=None, slot=1, depth=2):
+        p = CreateParams()
+        p.api_version = AJI_API_VERSION
+        if conf_path is not None:
+            p.conf_path = conf_path.encode()
+            p.model_dir = None if model_dir is None else model_dir.encode()
+            p.slot = slot
+        else:
+            p.engine_path = model_path.encode()
+            p.max_width, p.max_height = max_w, max_h
+        self._p = p
+        ids = (C.c_int * len(devices))(*devices)
+        err = C.create_string_buffer(512)
+        h = lib.ajib_video_create_multi(C.byref(p), ids, len(devices), depth, err, 512)
+        if not h:
+            raise AjibError("ajib_video_create_multi: " + err.value.decode())
+        self.handle = _vp(h)
+
+    def configure(self, w, h, fps=24.0):
+        ow, oh = C.c_int(), C.c_int()
+        rc = lib.ajib_video_multi_configure(self.handle, w, h, fps, C.byref(ow), C.byref(oh))
+        if rc != 0:
+            raise AjibError(f"ajib_video_multi_configure: {rc} {self.error()}")
+        return ow.value, oh.value
+
+    def submit(self, fin, fout):
+        return lib.ajib_video_multi_submit(self.handle, C.byref(fin), C.byref(fout))
+
+    def wait(self, ticket):
+        return lib.ajib_video_multi_wait(self.handle, ticket)
+
+    def done(self, ticket):
+        return lib.ajib_video_multi_done(self.handle, ticket)
+
+    def timing(self, on):
+        return lib.ajib_video_multi_timing(self.handle, 1 if on else 0)
+
+    def device_ms(self):
+        n = lib.ajib_video_multi_devices(self.handle)
+        ms = (C.c_double * n)()
+        check(lib.ajib_video_multi_device_ms(self.handle, ms, n), "ajib_video_multi_device_ms")
+        return list(ms)
+
+    def error(self):
+        return (lib.ajib_video_multi_error(self.handle) or b"").decode()
+
+    def close(self):
+        if self.handle:
+            lib.ajib_video_multi_destroy(C.byref(self.handle))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def frame_order(ndev, depth, finish_order):
+    """ajib_selftest_frame_order: (device_of, slot_of, reuse_of, completed_after)."""
+    import numpy as np
+    n = len(finish_order)
+    fo = np.ascontiguousarray(finish_order, np.int64)
+    dev = np.zeros(n, np.int32)
+    slot = np.zeros(n, np.int32)
+    reuse = np.zeros(n, np.int64)
+    comp = np.zeros(n, np.int64)
+    check(lib.ajib_selftest_frame_order(ndev, depth, n, fo.ctypes.data, dev.ctypes.data, slot.ctypes.data,
+                                        reuse.ctypes.data, comp.ctypes.data), "ajib_selftest_frame_order")
+    return dev, slot, reuse, comp
+
+
 # colour passes (aji_b200.h, named as the reference's src/kernels.h)
 class Csp(C.Structure):
     _fields_ = [("kr", C.c_float), ("kb", C.c_float), ("yoff", C.c_float), ("yscale", C.c_float), ("coff", C.c_float),

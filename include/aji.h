@@ -79,7 +79,7 @@ typedef void (*aji_log_fn)(void *opaque, int level, const char *msg);
 typedef struct aji_create_params {
     uint32_t api_version;  /* AJI_API_VERSION */
     void *cuda_context;    /* CUcontext to run in; NULL = the primary context of device 0 */
-    const char *conf_path; /* NULL = direct mode (the only mode this engine serves) */
+    const char *conf_path; /* an animejanai.conf (conf mode); NULL = direct mode */
     const char *model_dir;
     const char *trtexec;
     const char *trtexec_env;

@@ -222,6 +222,48 @@ AJIB_EXPORT aji_img_ctx *ajib_img_create_multi(const aji_img_create_params *p, c
 AJIB_EXPORT int ajib_img_shares(int W, int H, int ci, int scale, int tile_w, int tile_h, int overlap, int even, int ndev,
                                 int *y0, int *y1, int *j0, int *j1);
 
+/* ---- several GPUs for one video stream ----
+ * One stream upscaled frame-parallel on n devices of this host (CUDA ordinals, no duplicates):
+ * frame k (ticket k + 1) runs on device k mod n, each device with its own video context built
+ * from the same create params (direct or conf mode, see aji.h), its own upload, compute and
+ * download streams and a ring of `depth` (1..16) frame slots; results complete in submission
+ * order, as a one-device player sees them (the reference harness's one-stream loop,
+ * src/harness.c:646-700). The reference's video ABI serves one device per context (aji_create,
+ * include/aji.h:149-160); this additive entry point is what its dispatcher would probe, like the
+ * image ABI's optional 0.24+ additions (aji_image.h:220-222). No data crosses devices.
+ *
+ * Frames here are HOST memory: aji_frame.plane[] are host addresses (page-locked for
+ * asynchronous copies at link speed; pageable memory works, staged by the driver), stride[] in
+ * bytes. submit copies the input into the next device's slot, enqueues aji_infer and the copy of
+ * the result into the caller's output planes, and returns the frame's ticket (> 0) or a negative
+ * AJIB_ERR_*; it blocks only while that device's ring is full. Both buffers must stay untouched
+ * until the ticket finishes: wait(t) blocks until t and every earlier ticket have finished
+ * (their outputs are in host memory), done(t) asks without blocking (1 finished, 0 not yet).
+ * Driven by one host thread, like aji_ctx. configure sizes every device's chain for w x h input
+ * (aji_configure) and waits for frames in flight first. */
+typedef struct ajib_video_multi ajib_video_multi;
+AJIB_EXPORT ajib_video_multi *ajib_video_create_multi(const aji_create_params *p, const int *devices, int n, int depth,
+                                                      char *err, size_t err_size);
+AJIB_EXPORT int ajib_video_multi_configure(ajib_video_multi *m, int w, int h, double fps, int *out_w, int *out_h);
+AJIB_EXPORT int64_t ajib_video_multi_submit(ajib_video_multi *m, const aji_frame *in, const aji_frame *out);
+AJIB_EXPORT int ajib_video_multi_wait(ajib_video_multi *m, int64_t ticket);
+AJIB_EXPORT int ajib_video_multi_done(ajib_video_multi *m, int64_t ticket);
+AJIB_EXPORT int ajib_video_multi_devices(const ajib_video_multi *m);
+AJIB_EXPORT const char *ajib_video_multi_error(const ajib_video_multi *m);
+AJIB_EXPORT void ajib_video_multi_destroy(ajib_video_multi **m);
+/* Device timing for benchmarks: after timing(m, 1) (which waits for frames in flight), each
+ * device records a CUDA event before its first upload and after every download; device_ms waits
+ * for everything in flight and gives, per device in the order given at creation, the device time
+ * from its first upload's start to its last download's end (0 for a device that ran nothing). */
+AJIB_EXPORT int ajib_video_multi_timing(ajib_video_multi *m, int on);
+AJIB_EXPORT int ajib_video_multi_device_ms(ajib_video_multi *m, double *ms, int n);
+/* The frame order alone (host only, for tests): nframes frames over ndev devices with ring depth
+ * depth get device_of / slot_of and the ticket each must wait for before reusing its slot
+ * (reuse_of, 0: none); then the tickets finish in finish_order (a permutation of 1..nframes) and
+ * completed_after[i] is the count of tickets finished in order after the i-th of them. */
+AJIB_EXPORT int ajib_selftest_frame_order(int ndev, int depth, int nframes, const int64_t *finish_order, int *device_of,
+                                          int *slot_of, int64_t *reuse_of, int64_t *completed_after);
+
 /* ---- the native model and its executor ----
  * A model is a plan of fused conv steps (reference src/native/lower.h:38-77, Plan), read from
  * this engine's model file (format: animejanai-inference_b200/csrc/model.cpp). An executor is
