@@ -195,6 +195,12 @@ lib.ajib_exec_release.argtypes = [C.POINTER(_vp)]
 lib.ajib_exec_release.restype = None
 lib.ajib_exec_run.argtypes = [_vp, _vp, _vp, _vp]
 lib.ajib_exec_run.restype = C.c_int
+lib.ajib_exec_profile.argtypes = [_vp, C.c_int]
+lib.ajib_exec_profile.restype = C.c_int
+lib.ajib_exec_profile_read.argtypes = [_vp, C.POINTER(C.c_double), C.POINTER(C.c_int), C.c_int]
+lib.ajib_exec_profile_read.restype = C.c_int
+lib.ajib_exec_run_images.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp]
+lib.ajib_exec_run_images.restype = C.c_int
 lib.ajib_exec_set_bands.argtypes = [_vp, C.c_int]
 lib.ajib_exec_set_bands.restype = C.c_int
 lib.ajib_exec_info.argtypes = [_vp, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.POINTER(C.c_int)]
@@ -239,6 +245,20 @@ class Exec:
 
     def run(self, src, dst, stream=0):
         return lib.ajib_exec_run(self.handle, src, dst, stream)
+
+    def run_images(self, src, dst, w, img_h, nimg, stream=0):
+        return lib.ajib_exec_run_images(self.handle, src, dst, w, img_h, nimg, stream)
+
+    def profile(self, on):
+        return lib.ajib_exec_profile(self.handle, 1 if on else 0)
+
+    def profile_read(self, nsteps):
+        import numpy as np
+        ms = np.zeros(nsteps)
+        n = np.zeros(nsteps, np.int32)
+        check(lib.ajib_exec_profile_read(self.handle, ms.ctypes.data_as(C.POINTER(C.c_double)),
+                                         n.ctypes.data_as(C.POINTER(C.c_int)), nsteps), "ajib_exec_profile_read")
+        return ms, n
 
     def info(self):
         a, b, n = C.c_size_t(), C.c_size_t(), C.c_int()

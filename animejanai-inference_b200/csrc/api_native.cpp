@@ -134,6 +134,12 @@ extern "C" int ajib_exec_run(ajib_exec *e, const void *in, void *out, void *stre
     return e->ex->run(in, out, (cudaStream_t)stream);
 }
 
+extern "C" int ajib_exec_run_images(ajib_exec *e, const void *in, void *out, int w, int img_h, int nimg, void *stream)
+{
+    if (!e || !e->ex) return AJIB_ERR_ARGS;
+    return e->ex->run_images(in, out, w, img_h, nimg, (cudaStream_t)stream);
+}
+
 extern "C" int ajib_exec_set_bands(ajib_exec *e, int bands)
 {
     if (!e || !e->ex || bands < 1) return AJIB_ERR_ARGS;

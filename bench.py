@@ -2,14 +2,16 @@
 fp16 net with random-init seeded weights, through the engine's video C ABI (include/aji.h:
 aji_create / aji_configure / aji_infer).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|refgpu] [--model M]
 
 A step is one frame through pre-pass -> 18 fused convs -> post-pass. `value` is frames/s over all
 ranks with frames already resident in HBM (device-timed with CUDA events on the launching
-stream, max over ranks); `e2e` is the same through aji_infer with the frame copied from pinned
-host memory and the result read back every step. N > 1: one process per GPU (torchrun), each
-rank upscales its own frames, no collectives on the data path ("scaling": "weak"); a gloo group
-only carries the barrier and the max of the per-rank times.
+stream, max over ranks). N > 1: one process per GPU (torchrun), each rank upscales its own
+frames, no collectives on the data path ("scaling": "weak"); a gloo group only carries barriers
+and the max of the per-rank times. `e2e` is the product's own multi-GPU path: rank 0 drives
+ajib_video_create_multi over devices 0..N-1 (frame k on device k mod N, results in submission
+order) with the frames in pinned host memory, each frame's upload and download inside the
+device-timed region (max over the GPUs).
 
 --impl reference times the reference's own CPU implementation of this path (the fp32 reference
 net sanity/native_ref.h:run_plan, compiled from the reference sources into oracle/_ref) on the
@@ -62,6 +64,13 @@ MODELS = {
                            "3840x2160 P010 (a stream of frames, frame-parallel over ranks)",
                   model="2 x SRVGGNetCompact 64x16 2x, random-init (seeds 1, 2)",
                   kernel="k_conv3x3_tc<64,64> (second net's body conv 64->64 + PReLU, 1920x1080)"),
+    "suc-image": dict(metric="images/s 2048x2048->8192x8192 4x SuperUltraCompact 24x8 fp16, tiles 512 overlap 16 "
+                               "(BASELINE config 2)", w=2048, h=2048,
+                      workload="BASELINE config 2: one 2048x2048 8-bit RGB image, SuperUltraCompact 4x, tiled on the "
+                               "device as 25 tiles of 512 with 16 px overlap and linear blending -> 8192x8192 8-bit RGB",
+                      model="SRVGGNetCompact 24 feat x 8 body (SuperUltraCompact), PReLU, pixel_shuffle 4, random-init "
+                            "(seed 1)",
+                      kernel="k_conv3x3_tc<32,32> (SUC body conv 24->24 + PReLU over the 25 stacked 512x512 tiles)"),
     "spanf3": dict(metric="frames/s 1080p->4K 2x SPANF3 b5f48 unshuffle fp16 (video chain)", w=1920, h=1080,
                    workload="SPANF3 b5f48 2x video (2x pixel-unshuffle, tanh gates), 1920x1080 P010 BT.709 limited -> "
                             "3840x2160 P010",
@@ -79,6 +88,8 @@ def bench_plans(model):
         return [P.span_plan(MODEL_SEED, c=48, blocks=6)]
     if model == "chain":
         return [P.compact_plan(MODEL_SEED), P.compact_plan(MODEL_SEED + 1)]
+    if model == "suc-image":
+        return [P.compact_plan(MODEL_SEED, c=24, body=8, scale=4)]
     return [P.compact_plan(MODEL_SEED)]
 
 
@@ -383,6 +394,64 @@ def oracle_window_check(plan, y, uv, gy, guv, W, H):
             "ok": dy <= 3 and duv <= 3, "oracle_s": dt}
 
 
+CHAIN_STREAM_FRAMES = 240  # a stream of 240 frames through the two-model chain
+
+
+def run_e2e_multi(args, world, plans, mdir, W, H, depth=2):
+    """The e2e leg: the workload through ajib_video_create_multi over devices 0..world-1 from this
+    one process, host frames in pinned memory. config 4 (chain) is its 240-frame stream; the other
+    workloads run `steps` frames per GPU. Returns the line's e2e object."""
+    import torch
+    import ajib
+    devices = list(range(world))
+    if len(plans) == 1:
+        vm = ajib.VideoMulti(devices, model_path=os.path.join(mdir, "m1.ajnm"), max_w=W, max_h=H, depth=depth)
+    else:
+        vm = ajib.VideoMulti(devices, conf_path=os.path.join(mdir, "animejanai.conf"), model_dir=mdir, slot=1,
+                             depth=depth)
+    ow, oh = vm.configure(W, H)
+    nin = 2 * world
+    hin = []
+    for i in range(nin):
+        y, uv = p010_frame(5000 + i, W, H)
+        hin.append((torch.from_numpy(y.view(np.int16)).pin_memory(), torch.from_numpy(uv.view(np.int16)).pin_memory()))
+    nout = 2 * depth * world  # output buffers in flight: one is reused once its frame has finished
+    hout = [(torch.empty((oh, ow), dtype=torch.int16).pin_memory(),
+             torch.empty((oh // 2, ow), dtype=torch.int16).pin_memory()) for _ in range(nout)]
+    fin = [ajib.frame(W, H, ajib.FMT_P010, [y.data_ptr(), uv.data_ptr()], [W * 2, W * 2]) for y, uv in hin]
+    fout = [ajib.frame(ow, oh, ajib.FMT_P010, [y.data_ptr(), uv.data_ptr()], [ow * 2, ow * 2]) for y, uv in hout]
+    tickets = []
+
+    def submit(i):
+        if i >= nout:
+            assert vm.wait(tickets[i - nout]) == 0, vm.error()
+        t = vm.submit(fin[i % nin], fout[i % nout])
+        if t <= 0:
+            raise RuntimeError(f"ajib_video_multi_submit failed: {t} {vm.error()}")
+        tickets.append(t)
+
+    for i in range(max(3, args.warmup) * world):
+        submit(i)
+    assert vm.wait(tickets[-1]) == 0, vm.error()
+    nframes = CHAIN_STREAM_FRAMES if args.model == "chain" else args.steps * world
+    tickets.clear()
+    assert vm.timing(True) == 0, vm.error()
+    t0 = time.perf_counter()
+    for i in range(nframes):
+        submit(i)
+    assert vm.wait(tickets[-1]) == 0, vm.error()
+    host_s = time.perf_counter() - t0
+    ms = vm.device_ms()
+    vm.close()
+    t_ms = max(ms)
+    h2d = (hin[0][0].numel() + hin[0][1].numel()) * 2
+    d2h = (hout[0][0].numel() + hout[0][1].numel()) * 2
+    return {"value": nframes / (t_ms / 1000.0), "unit": "frames/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "frames": nframes, "api": f"ajib_video_create_multi over {world} GPU(s) "
+            f"(ring depth {depth}), pinned host frames, submission-order completion",
+            "device_ms_max": t_ms, "device_ms": ms, "host_wall_s": host_s}
+
+
 def current_context():
     """The CUDA driver context torch made current on this rank's device (passed to aji_create)."""
     import torch
@@ -493,61 +562,16 @@ def run_ours(args, rank, world, local_rank, dist):
                                          step_n.ctypes.data_as(C.POINTER(C.c_int)), 64)
         ajib.lib.ajib_video_profile(vid.handle, 0)
 
-    # ---- e2e: pinned host frame in, result read back, every step. Copies run on their own
-    # streams, double-buffered, so frame i+1's upload and frame i-1's download overlap frame i's
-    # compute (as a player feeding aji_infer would); the timed region runs from the first upload's
-    # start to the last download's end.
-    hy = [torch.from_numpy(p010_frame(5000 + rank * 10 + i, W_IN, H_IN)[0].view(np.int16)).pin_memory() for i in range(2)]
-    huv = [torch.from_numpy(p010_frame(5000 + rank * 10 + i, W_IN, H_IN)[1].view(np.int16)).pin_memory()
-           for i in range(2)]
-    hoy = [torch.empty((oh, ow), dtype=torch.int16).pin_memory() for _ in range(2)]
-    houv = [torch.empty((oh // 2, ow), dtype=torch.int16).pin_memory() for _ in range(2)]
-    h2d = (hy[0].numel() + huv[0].numel()) * 2
-    d2h = (hoy[0].numel() + houv[0].numel()) * 2
-    s_up, s_down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_up = [torch.cuda.Event() for _ in range(2)]     # upload of buffer b landed
-    ev_done = [torch.cuda.Event() for _ in range(2)]   # frame in buffer b computed
-    ev_down = [torch.cuda.Event() for _ in range(2)]   # result of buffer b downloaded
-
-    def e2e_step(i):
-        b = i % 2
-        din_y, din_uv = frames_in[b]
-        dout_y, dout_uv = outs[b]
-        if i >= 2:
-            s_up.wait_event(ev_done[b])        # the frame that last read din[b] is computed
-        with torch.cuda.stream(s_up):
-            din_y.copy_(hy[b], non_blocking=True)
-            din_uv.copy_(huv[b], non_blocking=True)
-            ev_up[b].record(s_up)
-        stream.wait_event(ev_up[b])
-        if i >= 2:
-            stream.wait_event(ev_down[b])      # dout[b]'s previous result is downloaded
-        rc = vid.infer(fins[b], fouts[b], sp)
-        if rc != 0:
-            raise RuntimeError(f"aji_infer failed: {rc} {vid.error()}")
-        ev_done[b].record(stream)
-        s_down.wait_event(ev_done[b])
-        with torch.cuda.stream(s_down):
-            hoy[b].copy_(dout_y, non_blocking=True)
-            houv[b].copy_(dout_uv, non_blocking=True)
-            ev_down[b].record(s_down)
-
-    for i in range(4):
-        e2e_step(i)
-    torch.cuda.synchronize()
+    # ---- e2e through the product's multi-device entry point (ajib_video_create_multi), driven by
+    # rank 0 over devices 0..N-1 while the other ranks wait: host frames in pinned memory, frame k
+    # on device k mod N, each device uploading, upscaling and downloading on its own streams, the
+    # results completing in submission order. Device-timed per GPU from its first upload's start
+    # to its last download's end; the max over the GPUs is the time.
     barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(s_up)
-    stream.wait_event(f0)
-    s_down.wait_event(f0)
-    for i in range(args.steps):
-        e2e_step(i)
-    f1.record(s_down)
-    f1.synchronize()
-    torch.cuda.synchronize()
+    e2e_info = None
+    if rank == 0:
+        e2e_info = run_e2e_multi(args, world, plans, mdir, W_IN, H_IN)
     barrier()
-    e2e_ms = f0.elapsed_time(f1)
 
     # ---- untimed: the output of frame 0 (checksum, and a window of rows against the oracle's own
     # chain), and the reference's own GPU path on the same frames (N = 1 only)
@@ -571,20 +595,19 @@ def run_ours(args, rank, world, local_rank, dist):
                 np.abs((rout[1] >> 6).astype(int) - (guv >> 6).astype(int)).max()))
 
     # max over ranks
-    times = np.array([t_ms, e2e_ms], dtype=np.float64)
+    times = np.array([t_ms], dtype=np.float64)
     if dist is not None:
         import torch as _t
         tt = _t.from_numpy(times)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         times = tt.numpy()
-    t_ms, e2e_ms = float(times[0]), float(times[1])
+    t_ms = float(times[0])
 
     if rank != 0:
         vid.close()
         return
     frames_total = args.steps * world
     value = frames_total / (t_ms / 1000.0)
-    e2e_value = frames_total / (e2e_ms / 1000.0)
 
     # roofline of the dominant kernel: the body convs (Compact: 16 x 64 -> 64 + PReLU; SPANF3:
     # 15 x 48 -> 48, ReLU or the tanh gate with its 1x1 attention GEMM), FLOPs at conv resolution
@@ -628,7 +651,7 @@ def run_ours(args, rank, world, local_rank, dist):
                        "l2": "inputs larger than L2 (activation buffers of 66-265 MB per frame)",
                        "bands": args.bands},
             "roofline": roof,
-            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": e2e_info,
             # in the timed region: pre, per net its input pack and steps, post
             "gpu_launches": args.steps * (2 + (nsteps + len(plans)) * max(1, args.bands)),
             "clocks": clk}
@@ -736,6 +759,202 @@ def run_kernel(args):
                       "frac_of_hbm_peak": nbytes / (ms / 1000.0) / 1e9 / hbm_peak}), flush=True)
 
 
+IMG_TILE, IMG_OVERLAP = 512, 16
+
+
+def run_image(args, rank, world, local_rank, dist):
+    """the still-image path. `value`: images/s with the image resident in HBM,
+    a step being the tiler's extract of all 25 tiles, the net over the 25 stacked tiles (one launch
+    per step, ajib_exec_run_images) and the gather composition into the 8-bit output, device-timed
+    with CUDA events, max over ranks (each rank its own images). `e2e`: aji_img_upscale (the image
+    ABI, blocking) from host memory to host memory, on rank 0 over devices 0..N-1
+    (ajib_img_create_multi when N > 1: output-row bands per GPU), host wall clock around each
+    blocking call (its copies included). Roofline: the body conv, bound by HBM at 24 channels."""
+    import torch
+    import ajib
+    from synth import rgb8_image
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
+    spec = MODELS[args.model]
+    plan = bench_plans(args.model)[0]
+    W, H, S = spec["w"], spec["h"], plan["depth_to_space"]
+    torch.zeros(1, device=dev)
+    t = C.c_void_p()
+    ajib.check(ajib.lib.ajib_tiler_create(W, H, 3, S, IMG_TILE, IMG_TILE, IMG_OVERLAP, 0, C.byref(t)), "ajib_tiler_create")
+    nx, ny, tw, th = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    ajib.lib.ajib_tiler_info(t, C.byref(nx), C.byref(ny), C.byref(tw), C.byref(th))
+    n, tw, th = nx.value * ny.value, tw.value, th.value
+    model = ajib.Model(plan)
+    ex = ajib.Exec(model, tw, th * n)
+    img = rgb8_image(31 + rank, W, H)
+    d_img = torch.from_numpy(img.reshape(-1)).to(dev)
+    d_tin = torch.empty((3, n * th, tw), dtype=torch.float16, device=dev)
+    d_tout = torch.empty((3, n * th * S, tw * S), dtype=torch.float16, device=dev)
+    d_out = torch.empty(H * S * W * S * 3, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+
+    def extract():
+        ajib.check(ajib.lib.ajib_tiler_extract(t, C.c_void_p(d_img.data_ptr()), 0, n, C.c_void_p(d_tin.data_ptr()),
+                                               C.c_void_p(sp)), "ajib_tiler_extract")
+
+    def net():
+        ajib.check(ex.run_images(d_tin.data_ptr(), d_tout.data_ptr(), tw, th, n, sp), "ajib_exec_run_images")
+
+    def compose():
+        ajib.check(ajib.lib.ajib_tiler_compose(t, C.c_void_p(d_tout.data_ptr()), C.c_void_p(d_out.data_ptr()),
+                                               C.c_void_p(sp)), "ajib_tiler_compose")
+
+    def step():
+        extract()
+        net()
+        compose()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    clocks.wait_first()
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    assert ajib.kernel_status() == 0
+    barrier()
+    torch.cuda.synchronize()
+    t0 = datetime.datetime.now()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    t1 = datetime.datetime.now()
+    clk = clocks.stop(t0, t1)
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    assert ajib.kernel_status() == 0
+
+    # per-kernel times (a separate pass): extract and compose by events, the net's steps by the
+    # executor's per-step events
+    def timed(fn, reps=10):
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record(stream)
+        for _ in range(reps):
+            fn()
+        b_.record(stream)
+        b_.synchronize()
+        return a_.elapsed_time(b_) / reps
+    extract_ms, compose_ms = timed(extract), timed(compose)
+    ex.profile(True)
+    for _ in range(10):
+        net()
+    stream.synchronize()
+    step_ms, step_n = ex.profile_read(len(plan["steps"]))
+    ex.profile(False)
+    body = [k for k, st in enumerate(plan["steps"]) if st.get("in_", 0) == 0 and st.get("out", 0) == 0]
+    body_ms = float(np.mean([step_ms[k] / max(1, step_n[k]) for k in body]))
+    net_ms = float(np.sum(step_ms / np.maximum(1, step_n)))
+    px = n * th * tw
+    body_bytes = 2.0 * px * 24 * 2   # read and write one 24-channel fp16 map of the stacked tiles
+    body_flops = 2.0 * 9 * 24 * 24 * px
+    extract_bytes = W * H * 3 + n * 3 * th * tw * 2
+    compose_bytes = n * 3 * th * S * tw * S * 2 + W * S * H * S * 3
+
+    # e2e through the image ABI, rank 0 over all the GPUs
+    barrier()
+    e2e = None
+    if rank == 0:
+        mdir = tempfile.mkdtemp(prefix="ajib_bench_")
+        path = os.path.join(mdir, "suc.ajnm")
+        with open(path, "wb") as f:
+            f.write(ajib.model_bytes(plan))
+        ctx = ajib.Image(device_ids=None) if world == 1 else ajib.Image(device_ids=_img_device_ids(world))
+        mh = ctx.load(path, tile=IMG_TILE, overlap=IMG_OVERLAP)
+        hin = torch.from_numpy(img).pin_memory()
+        hout = torch.empty((H * S, W * S, 3), dtype=torch.uint8).pin_memory()
+        bi, bo = ajib.img_buffer(hin.numpy()), ajib.img_buffer(hout.numpy())
+        for _ in range(max(1, args.warmup)):
+            assert ajib.lib.aji_img_upscale(mh, C.byref(bi), C.byref(bo), ajib.PROGRESS_FN(), None) == 0, ctx.error()
+        reps = max(3, min(args.steps, 20))
+        w0 = time.perf_counter()
+        for _ in range(reps):
+            assert ajib.lib.aji_img_upscale(mh, C.byref(bi), C.byref(bo), ajib.PROGRESS_FN(), None) == 0, ctx.error()
+        wall = (time.perf_counter() - w0) / reps
+        ajib.lib.aji_img_release(C.byref(mh))
+        ctx.close()
+        e2e = {"value": 1.0 / wall, "unit": "images/s", "h2d_bytes_per_step": W * H * 3,
+               "d2h_bytes_per_step": W * S * H * S * 3, "api": f"aji_img_upscale over {world} GPU(s)"
+               + (" (ajib_img_create_multi)" if world > 1 else "") + ", pinned host buffers",
+               "timing": f"host wall clock around {reps} blocking calls"}
+    barrier()
+    times = np.array([t_ms], dtype=np.float64)
+    if dist is not None:
+        tt = torch.from_numpy(times)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        times = tt.numpy()
+    t_ms = float(times[0])
+    ajib.lib.ajib_tiler_release(C.byref(t))
+    launches_net = ex.info()["launches"]  # the net's launches per run (the head's input pack included)
+    if rank != 0:
+        return
+    achieved = body_bytes / (body_ms / 1000.0) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "traffic": None, "kernel": spec["kernel"], "kernel_ms": body_ms, "bytes_per_launch": body_bytes,
+            "peak_source": f"{peak_src} HBM copy (MEASURED_PEAKS.json)",
+            "tensor_tflops": body_flops / (body_ms / 1000.0) / 1e12,
+            "tensor_frac_of_burst": body_flops / (body_ms / 1000.0) / 1e12 / tflops_burst,
+            "extract": {"ms": extract_ms, "bytes": extract_bytes,
+                        "frac_of_hbm": extract_bytes / (extract_ms / 1000.0) / 1e9 / hbm_peak},
+            "compose": {"ms": compose_ms, "bytes": compose_bytes,
+                        "frac_of_hbm": compose_bytes / (compose_ms / 1000.0) / 1e9 / hbm_peak},
+            "net_ms": net_ms, "net_tflops": chain_flops([plan], tw, th * n) / (net_ms / 1000.0) / 1e12}
+    value = args.steps * world / (t_ms / 1000.0)
+    line = {"metric": spec["metric"], "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": spec["workload"], "model": spec["model"], "global_batch": world,
+                       "parallelism": f"image-parallel x{world} (replicas) for value; e2e splits one image's output "
+                                      "rows over the GPUs", "tiles_per_net_launch": n,
+                       "l2": "inputs larger than L2 (629 MB of stacked tile outputs per image)"},
+            "roofline": roof, "e2e": e2e,
+            "gpu_launches": args.steps * (2 + launches_net), "clocks": clk}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_image_sample(plan)
+    print(json.dumps(line), flush=True)
+
+
+def _img_device_ids(n):
+    """The image ABI's device ids (aji_img_enum_devices) of CUDA devices 0..n-1."""
+    import ajib
+    devs = (ajib.ImgDevice * 64)()
+    k = ajib.lib.aji_img_enum_devices(ajib.IMG_TENSORRT, devs, 64)
+    return [devs[i].id for i in range(min(n, k))]
+
+
+def cpu_image_sample(plan, nthreads=0):
+    """The reference CPU path for config 2 on a bounded sample: one 512x512 tile of the image
+    through the reference net (run_plan, oracle/_ref) on all host cores, scaled to the 25 tiles
+    of a 2048x2048 image (the tiler's host-side blend is a small part of it)."""
+    from synth import rgb8_image
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libref_net.so")
+    x = (rgb8_image(31, IMG_TILE, IMG_TILE).astype(np.float32) / 255.0).transpose(2, 0, 1).copy()
+    t0 = time.perf_counter()
+    if os.path.exists(ref_lib):
+        import refnet
+        refnet.run_plan(ref_lib, plan, x, nthreads)
+        cores, kind = refnet.threads(ref_lib, nthreads), "reference"
+    else:
+        import oracle_net
+        oracle_net.run_plan(plan, x, nthreads)
+        cores, kind = (nthreads if nthreads > 0 else os.cpu_count()), "port"
+    dt = time.perf_counter() - t0
+    return {"value": 1.0 / (25 * dt), "unit": "images/s", "cores": cores, "kind": kind,
+            "sample": f"one 512x512 tile through the {kind} run_plan ({dt:.2f} s), x 25 tiles per image"}
+
+
 def chain_flops(plans, w, h):
     """Algorithmic FLOPs of one frame of w x h through the chain: every step's 2 * taps * cin * cout
     (plus a tanh gate's 2 * cout^2) per conv-resolution pixel."""
@@ -783,10 +1002,13 @@ def main():
         import datetime
 
         import torch.distributed as td
-        td.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        td.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
         dist = td
     try:
-        run_ours(args, rank, world, local_rank, dist)
+        if args.model == "suc-image":
+            run_image(args, rank, world, local_rank, dist)
+        else:
+            run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()

@@ -290,6 +290,11 @@ AJIB_EXPORT int ajib_exec_create(const ajib_model *m, int w, int h, ajib_exec **
 AJIB_EXPORT void ajib_exec_release(ajib_exec **e);
 /* in: NCHW fp16 [3][h][w]; out: NCHW fp16 [3][R*h][R*w] (device pointers). */
 AJIB_EXPORT int ajib_exec_run(ajib_exec *e, const void *in, void *out, void *stream);
+/* The same on nimg images of img_h rows stacked along H, each convolved on its own: in
+ * [3][nimg * img_h][w], out [3][R * nimg * img_h][R * w], nimg * img_h no more than the executor's
+ * height. One launch per step for a whole batch of tiles (the image tiler's); no reference
+ * counterpart (the reference runs tiles one at a time, src/aji_img_trt.cpp:980-1011). */
+AJIB_EXPORT int ajib_exec_run_images(ajib_exec *e, const void *in, void *out, int w, int img_h, int nimg, void *stream);
 /* Run the net as `bands` horizontal bands (1 = whole frame per step): each band runs every step,
  * its rows shifted down one per step, so a band's activations stay in L2 between steps. */
 AJIB_EXPORT int ajib_exec_set_bands(ajib_exec *e, int bands);
