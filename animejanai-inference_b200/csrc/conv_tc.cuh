@@ -55,6 +55,8 @@
 
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "sm100.cuh"
 
 namespace ajib {
@@ -531,7 +533,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     constexpr bool ATT = EK == kEpiAtt;
     using C = ConvCfg<KPAD, NPAD, ATT, EK == kEpiD2S>;
     constexpr int S = C::S;
-    constexpr int HW = NPAD / 2;  // accumulator columns per epilogue warp (half a slot)
     extern __shared__ unsigned char smraw[];
     // 1024-byte aligned base (bulk-copy destinations and descriptor bases)
     unsigned char *sm = smraw + ((1024 - (dev::smem_u32(smraw) & 1023)) & 1023);
@@ -934,9 +935,11 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         // it completes, while the other group works on its own row.
         const int q = warp & 3, g = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        // each group zeroes its share of every slot's columns, 16 at a 16-column boundary
+        constexpr int ZA = NPAD == 48 ? 32 : NPAD / 2;
+        const int zc0 = g == 0 ? 0 : ZA, zcw = g == 0 ? ZA : NPAD - ZA;
         for (int sl = 0; sl < S; sl++)
-#pragma unroll
-            for (int c = 0; c < HW; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + g * HW + c));
+            for (int c = 0; c < zcw; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + zc0 + c));
         dev::tmem_wait_st();
         dev::tc_fence_before();
         dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
@@ -1049,107 +1052,103 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     } else if (warp < kMmaWarp) {
       if constexpr (!ATT) {
         // ================= epilogue: warp (q, h) takes TMEM lanes 32q.. (pixels) and half h of
-        // each slot's columns; depth-to-space by 3 (groups of 3 channels across the halves) has
-        // half 0 take the whole slot
+        // each slot's columns (NPAD / 2 each; at 48 channels 32 + 16, so that every TMEM access is
+        // 16 columns at a 16-column boundary); depth-to-space by 3 (groups of 3 channels across the
+        // halves) has half 0 take the whole slot
         const int q = warp & 3, h = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const bool whole = EK == kEpiD2S && a.R == 3;
-        // every accumulator starts from its channel's bias, so the epilogue adds none: this warp's
-        // half of the bias as TMEM words, written into each slot it hands back (the MMA warp waits
-        // on named barrier 1 for the first fill)
-        uint32_t bz[HW];
+        constexpr int CWA = NPAD == 48 ? 32 : NPAD / 2, CWB = NPAD - CWA;
+        auto run_half = [&](auto cw_tag, auto c0_tag) {
+            constexpr int CW = decltype(cw_tag)::value, C0 = decltype(c0_tag)::value;
+            // every accumulator starts from its channel's bias, so the epilogue adds none: this warp's
+            // columns of the bias as TMEM words, written into each slot it hands back (the MMA warp
+            // waits on named barrier 1 for the first fill)
+            uint32_t bz[CW];
 #pragma unroll
-        for (int c = 0; c < HW; c++) bz[c] = __float_as_uint(sbias[h * HW + c]);
-        auto fill_bias = [&](uint32_t taddr) {
+            for (int c = 0; c < CW; c++) bz[c] = __float_as_uint(sbias[C0 + c]);
+            auto fill_bias = [&](uint32_t taddr) {
 #pragma unroll
-            for (int c = 0; c < HW; c += 16) {
-                uint32_t b16[16];
+                for (int c = 0; c < CW; c += 16) {
+                    uint32_t b16[16];
 #pragma unroll
-                for (int j = 0; j < 16; j++) b16[j] = bz[c + j];
-                dev::tmem_st16(taddr + c, b16);
-            }
-        };
-        for (int sl = 0; sl < S; sl++) fill_bias(tmem + lanes + (uint32_t)(sl * NPAD + h * HW));
-        dev::tmem_wait_st();
-        dev::tc_fence_before();
-        dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
+                    for (int j = 0; j < 16; j++) b16[j] = bz[c + j];
+                    dev::tmem_st16(taddr + c, b16);
+                }
+            };
+            for (int sl = 0; sl < S; sl++) fill_bias(tmem + lanes + (uint32_t)(sl * NPAD + C0));
+            dev::tmem_wait_st();
+            dev::tc_fence_before();
+            dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
 
-        SegIter seg(W, a.row_begin, a.row_end);
-        uint32_t ot = 0;
-        int strip, ya, yb;
-        bool ok = true;
-        // a row's global inputs (skip pixel, gate's block input) are loaded ahead (three rows for
-        // the skip pixel, whose DRAM latency is several rows of this epilogue; one for the gate's
-        // larger input), so their latency overlaps earlier rows' epilogues
-        auto prefetch = [&](EpiIn<HW> &in, EpiIn<NPAD> &inw, int o, int x) {
-            if (!whole) {
-                if (h == 0)
-                    epi_prefetch<EK, HW, 0>(in, a, o, x);
-                else
-                    epi_prefetch<EK, HW, HW>(in, a, o, x);
-            } else if (h == 0) {
-                epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
-            }
-        };
-        constexpr int PF = EK == kEpiD2S ? 3 : 1;
-        const bool pf_on = !(EK == kEpiD2S && a.skip_smem);  // a skip in shared memory needs no prefetch
-        while (ok && seg.next(strip, ya, yb)) {
-            const int x0 = strip * kTileM;
-            const int x = x0 + q * 32 + lane;
-            EpiRing<PF, EpiIn<HW>> rin;
-            EpiRing<PF, EpiIn<NPAD>> rinw;
+            SegIter seg(W, a.row_begin, a.row_end);
+            uint32_t ot = 0;
+            int strip, ya, yb;
+            bool ok = true;
+            // a row's global inputs (skip pixel, gate's block input) are loaded ahead (three rows for
+            // the skip pixel, whose DRAM latency is several rows of this epilogue; one for the gate's
+            // larger input), so their latency overlaps earlier rows' epilogues
+            auto prefetch = [&](EpiIn<CW> &in, EpiIn<NPAD> &inw, int o, int x) {
+                if (!whole)
+                    epi_prefetch<EK, CW, C0>(in, a, o, x);
+                else if (C0 == 0)
+                    epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
+            };
+            constexpr int PF = EK == kEpiD2S ? 3 : 1;
+            const bool pf_on = !(EK == kEpiD2S && a.skip_smem);  // a skip in shared memory needs no prefetch
+            while (ok && seg.next(strip, ya, yb)) {
+                const int x0 = strip * kTileM;
+                const int x = x0 + q * 32 + lane;
+                EpiRing<PF, EpiIn<CW>> rin;
+                EpiRing<PF, EpiIn<NPAD>> rinw;
 #pragma unroll
-            for (int k = 0; k < PF; k++)
-                if (pf_on && ya + k < yb) prefetch(rin.e[k], rinw.e[k], ya + k, x);
-            for (int o = ya; o < yb; o++, ot++) {
-                const int slot = ring_slot<S>(ot);
-                EpiIn<HW> in = rin.e[0];
-                EpiIn<NPAD> inw = rinw.e[0];
-                EpiIn<HW> nin;
-                EpiIn<NPAD> ninw;
-                if (pf_on && o + PF < yb) prefetch(nin, ninw, o + PF, x);
-                if (!(ok = dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
-                if constexpr (EK == kEpiD2S) {
-                    if (!pf_on) {
-                        // the skip row landed in this output's slot (its own barrier, one phase per use)
-                        if (!(ok = dev::mbar_wait_warp(skipf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
-                        const __half *sk = reinterpret_cast<const __half *>(sm + C::SKOFF + slot * C::SKIP_ROW);
+                for (int k = 0; k < PF; k++)
+                    if (pf_on && ya + k < yb) prefetch(rin.e[k], rinw.e[k], ya + k, x);
+                for (int o = ya; o < yb; o++, ot++) {
+                    const int slot = ring_slot<S>(ot);
+                    EpiIn<CW> in = rin.e[0];
+                    EpiIn<NPAD> inw = rinw.e[0];
+                    EpiIn<CW> nin;
+                    EpiIn<NPAD> ninw;
+                    if (pf_on && o + PF < yb) prefetch(nin, ninw, o + PF, x);
+                    if (!(ok = dev::mbar_wait_warp(accf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                    if constexpr (EK == kEpiD2S) {
+                        if (!pf_on) {
+                            // the skip row landed in this output's slot (its own barrier, one phase per use)
+                            if (!(ok = dev::mbar_wait_warp(skipf0 + 8 * slot, ring_phase<S>(ot), a.err, kErrEpiAccFull))) break;
+                            const __half *sk = reinterpret_cast<const __half *>(sm + C::SKOFF + slot * C::SKIP_ROW);
 #pragma unroll
-                        for (int c3 = 0; c3 < 3; c3++) {
-                            const float v = x < W ? __half2float(sk[c3 * kTileM + (x - x0)]) : 0.f;
-                            in.skip[c3] = v;
-                            inw.skip[c3] = v;
+                            for (int c3 = 0; c3 < 3; c3++) {
+                                const float v = x < W ? __half2float(sk[c3 * kTileM + (x - x0)]) : 0.f;
+                                in.skip[c3] = v;
+                                inw.skip[c3] = v;
+                            }
                         }
                     }
-                }
-                __syncwarp();
-                dev::tc_fence_after();
-                const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
-                if (!whole) {
-                    float v[HW];
-#pragma unroll
-                    for (int c = 0; c < HW; c += 16) {
-                        float t[16];
-                        dev::tmem_ld16(taddr + h * HW + c, t);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) v[c + j] = t[j];
-                    }
-                    dev::tmem_wait_ld();
-                    // hand the half slot back holding the bias: the MMAs accumulate onto it
-                    fill_bias(taddr + h * HW);
-                    dev::tmem_wait_st();
-                    dev::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
-                    if (h == 0)
-                        epi_store<EK, HW, 0>(v, a, sslope, o, x, in);
-                    else
-                        epi_store<EK, HW, HW>(v, a, sslope, o, x, in);
-                } else {
-                    // depth-to-space by 3 only comes with 27 output channels (NPAD 32)
-                    if constexpr (NPAD == 32 && EK == kEpiD2S) {
-                        float v[NPAD];
-                        if (h == 0) {
+                    dev::tc_fence_after();
+                    const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
+                    if (!whole) {
+                        float v[CW];
+#pragma unroll
+                        for (int c = 0; c < CW; c += 16) {
+                            float t[16];
+                            dev::tmem_ld16(taddr + C0 + c, t);
+#pragma unroll
+                            for (int j = 0; j < 16; j++) v[c + j] = t[j];
+                        }
+                        dev::tmem_wait_ld();
+                        // hand the columns back holding the bias: the MMAs accumulate onto it
+                        fill_bias(taddr + C0);
+                        dev::tmem_wait_st();
+                        dev::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+                        epi_store<EK, CW, C0>(v, a, sslope, o, x, in);
+                    } else {
+                        // depth-to-space by 3 only comes with 27 output channels (NPAD 32)
+                        if constexpr (NPAD == 32 && EK == kEpiD2S && C0 == 0) {
+                            float v[NPAD];
 #pragma unroll
                             for (int c = 0; c < NPAD; c += 16) {
                                 float t[16];
@@ -1163,24 +1162,29 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                             {
                                 uint32_t b16[16];
 #pragma unroll
-                                for (int j = 0; j < 16; j++) b16[j] = __float_as_uint(sbias[HW + j]);
-                                dev::tmem_st16(taddr + HW, b16);
+                                for (int j = 0; j < 16; j++) b16[j] = __float_as_uint(sbias[CWA + j]);
+                                dev::tmem_st16(taddr + CWA, b16);
                             }
                             dev::tmem_wait_st();
+                            dev::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+                            epi_store<EK, NPAD, 0>(v, a, sslope, o, x, inw);
+                        } else {
+                            dev::tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                         }
-                        dev::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
-                        if (h == 0) epi_store<EK, NPAD, 0>(v, a, sslope, o, x, inw);
-                    } else {
-                        __syncwarp();
-                        if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
                     }
+                    rin.push(nin);
+                    rinw.push(ninw);
                 }
-                rin.push(nin);
-                rinw.push(ninw);
             }
-        }
+        };
+        if (h == 0)
+            run_half(std::integral_constant<int, CWA>{}, std::integral_constant<int, 0>{});
+        else
+            run_half(std::integral_constant<int, CWB>{}, std::integral_constant<int, CWA>{});
       }
     } else {
         // ================= MMA issuer (one thread). It takes a stage of RP rows per wait and

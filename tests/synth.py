@@ -27,7 +27,9 @@ def p010_frame(seed, w=1920, h=1080):
     u = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
     v = np.rint(value_noise(rng, h // 2, w // 2, 64, 940)).astype(np.uint16) << 6
     uv = np.stack([u, v], axis=-1).reshape(h // 2, w)
-    return y, uv
+    # the bilinear blend leaves a Fortran-ordered array: callers hand the planes' memory to the
+    # engine, which reads rows
+    return np.ascontiguousarray(y), np.ascontiguousarray(uv)
 
 
 def rgb8_image(seed, w=2048, h=2048):
