@@ -18,6 +18,8 @@
 #include <new>
 
 #include "colour_math.cuh"
+#include "feature_map.cuh"
+#include "plan.h"
 #include "resample.h"
 #include "../../include/aji_b200.h"
 
@@ -99,9 +101,19 @@ __device__ __forceinline__ float quantize(float v, float qdiv, float qinv, float
 constexpr int kPreTW = 64, kPreTH = 16, kPreRows = 24;
 constexpr int kPreMaxTaps = 8;  // taps per pass the kernel holds (plans with more are refused)
 
-template <typename T>
+// The head conv's input, written by the pre pass as well when it is fused with it (PACK): the
+// fp16 RGB of each pixel, normalised as the conv's input ((x - mean) * scale, rounded to fp16)
+// when the model asks for it, as chunk 0 {r, g, b, 0 x 5} of an 8-channel strip-chunked map —
+// the bytes the executor's own pack of the NCHW input (conv.cu, k_pack_input) writes.
+struct PreMap {
+    __half *map;
+    int nstrips, in_norm;
+    float mean[3], scale[3];
+};
+
+template <typename T, bool PACK>
 __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
-                                             DevPass ph, DevPass pv, aji_csp csp, __half *dst, int w, int h)
+                                             DevPass ph, DevPass pv, aji_csp csp, __half *dst, int w, int h, PreMap pm)
 {
     __shared__ float2 uvh[kPreRows][kPreTW];  // horizontally resampled (u, v) per staged chroma row
     const int x0 = blockIdx.x * kPreTW, y0 = blockIdx.y * kPreTH;
@@ -204,9 +216,18 @@ __global__ void __launch_bounds__(256) k_pre(const uint8_t *yp, ptrdiff_t ys, co
         const float b = __fmaf_rn(cb, U, Y);
         const float g = __fsub_rn(Y, __fdiv_rn(__fmaf_rn(gb, U, __fmul_rn(gr, V)), kg));
         const size_t idx = (size_t)y * w + x;
-        dst[idx] = __float2half_rn(r);
-        dst[plane + idx] = __float2half_rn(g);
-        dst[2 * plane + idx] = __float2half_rn(b);
+        const __half hr = __float2half_rn(r), hg = __float2half_rn(g), hb = __float2half_rn(b);
+        dst[idx] = hr;
+        dst[plane + idx] = hg;
+        dst[2 * plane + idx] = hb;
+        if constexpr (PACK) {
+            float v[3] = {__half2float(hr), __half2float(hg), __half2float(hb)};
+            if (pm.in_norm) {
+#pragma unroll
+                for (int c = 0; c < 3; c++) v[c] = (v[c] - pm.mean[c]) * pm.scale[c];
+            }
+            store_px(pm.map, y, x, 0, pm.nstrips, 1, make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u));
+        }
     }
 }
 
@@ -640,20 +661,57 @@ extern "C" int ajib_plan_table(const aji_plan *p, int which, int *start, float *
     return t.taps;
 }
 
+namespace {
+
+int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
+               const aji_csp *csp, void *dst_f16, const PreMap *pm, cudaStream_t s)
+{
+    const dim3 grid((p->w + kPreTW - 1) / kPreTW, (p->h + kPreTH - 1) / kPreTH);
+    const PreMap m = pm ? *pm : PreMap{};
+    const uint8_t *yp = (const uint8_t *)y_plane, *uvp = (const uint8_t *)uv_plane;
+    __half *dst = (__half *)dst_f16;
+    if (p->format == AJI_FMT_NV12) {
+        if (pm)
+            k_pre<uint8_t, true><<<grid, 256, 0, s>>>(yp, y_stride, uvp, uv_stride, p->ph, p->pv, *csp, dst, p->w, p->h, m);
+        else
+            k_pre<uint8_t, false><<<grid, 256, 0, s>>>(yp, y_stride, uvp, uv_stride, p->ph, p->pv, *csp, dst, p->w, p->h, m);
+    } else {
+        if (pm)
+            k_pre<uint16_t, true><<<grid, 256, 0, s>>>(yp, y_stride, uvp, uv_stride, p->ph, p->pv, *csp, dst, p->w, p->h, m);
+        else
+            k_pre<uint16_t, false><<<grid, 256, 0, s>>>(yp, y_stride, uvp, uv_stride, p->ph, p->pv, *csp, dst, p->w, p->h, m);
+    }
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
 extern "C" int aji_run_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane,
                            ptrdiff_t uv_stride, const aji_csp *csp, void *dst_f16, void *stream)
 {
     if (!p || p->kind != aji_plan::PRE || !y_plane || !uv_plane || !csp || !dst_f16) return (int)cudaErrorInvalidValue;
-    const dim3 grid((p->w + kPreTW - 1) / kPreTW, (p->h + kPreTH - 1) / kPreTH);
-    cudaStream_t s = (cudaStream_t)stream;
-    if (p->format == AJI_FMT_NV12)
-        k_pre<uint8_t><<<grid, 256, 0, s>>>((const uint8_t *)y_plane, y_stride, (const uint8_t *)uv_plane, uv_stride, p->ph,
-                                            p->pv, *csp, (__half *)dst_f16, p->w, p->h);
-    else
-        k_pre<uint16_t><<<grid, 256, 0, s>>>((const uint8_t *)y_plane, y_stride, (const uint8_t *)uv_plane, uv_stride,
-                                             p->ph, p->pv, *csp, (__half *)dst_f16, p->w, p->h);
-    return (int)cudaGetLastError();
+    return launch_pre(p, y_plane, y_stride, uv_plane, uv_stride, csp, dst_f16, nullptr, (cudaStream_t)stream);
 }
+
+namespace ajib {
+
+int run_pre_packed(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
+                   const aji_csp *csp, void *dst_f16, const InputPack &pk, cudaStream_t s)
+{
+    if (!p || p->kind != aji_plan::PRE || !y_plane || !uv_plane || !csp || !dst_f16 || !pk.map) return (int)cudaErrorInvalidValue;
+    if (((uintptr_t)pk.map & 15) != 0) return (int)cudaErrorInvalidValue;
+    PreMap m{};
+    m.map = (__half *)pk.map;
+    m.nstrips = feature_strips(p->w);
+    m.in_norm = pk.in_norm ? 1 : 0;
+    for (int c = 0; c < 3; c++) {
+        m.mean[c] = pk.mean[c];
+        m.scale[c] = pk.scale[c];
+    }
+    return launch_pre(p, y_plane, y_stride, uv_plane, uv_stride, csp, dst_f16, &m, s);
+}
+
+}  // namespace ajib
 
 extern "C" int aji_run_post(aji_plan *p, const void *src_f16, const aji_csp *csp, void *y_plane, ptrdiff_t y_stride,
                             void *uv_plane, ptrdiff_t uv_stride, void *stream)

@@ -57,11 +57,11 @@
 
 #include <type_traits>
 
+#include "feature_map.cuh"
 #include "sm100.cuh"
 
 namespace ajib {
 
-constexpr int kTileM = 128;        // output pixels per tile (the MMA's M)
 constexpr int kHalo = kTileM + 2;  // staged input pixels per row
 constexpr int kTmemCols = 512;     // the whole TMEM: the accumulator ring
 constexpr int kProdWarps = 4;      // producer warps (all of them convert an NCHW model input)
@@ -116,28 +116,6 @@ __device__ __forceinline__ void segment_rows(int ya, int yb, int img_h, int &r0,
 {
     r0 = (ya % img_h == 0) ? ya : ya - 1;
     r1 = (yb % img_h == 0) ? yb - 1 : yb;
-}
-
-// Strip-chunked feature maps: 128-pixel strips per row, and columns per strip (the strip and a
-// halo column on each side).
-constexpr int kStripW = kTileM + 2;
-__host__ __device__ constexpr int feature_strips(int W) { return (W + kTileM - 1) / kTileM; }
-
-// Half index of column u (0 .. 129) of chunk `chunk` of strip `strip` of row y in a map of cc
-// chunks and nstrips strips per row.
-__device__ __forceinline__ size_t map_at(int y, int strip, int chunk, int u, int nstrips, int cc)
-{
-    return ((((size_t)y * nstrips + strip) * cc + chunk) * kStripW + u) * 8;
-}
-
-// Store one pixel's 8-channel chunk (pixel x < W of row y) at its column and, at a strip edge, into
-// the neighbouring strip's halo column.
-__device__ __forceinline__ void store_px(__half *map, int y, int x, int chunk, int nstrips, int cc, uint4 v)
-{
-    const int s = x >> 7, u = (x & (kTileM - 1)) + 1;
-    *reinterpret_cast<uint4 *>(map + map_at(y, s, chunk, u, nstrips, cc)) = v;
-    if (u == 1 && s > 0) *reinterpret_cast<uint4 *>(map + map_at(y, s - 1, chunk, kStripW - 1, nstrips, cc)) = v;
-    if (u == kTileM && s + 1 < nstrips) *reinterpret_cast<uint4 *>(map + map_at(y, s + 1, chunk, 0, nstrips, cc)) = v;
 }
 
 template <int KPAD, int NPAD, bool ATT = false, bool SKIP = false>
@@ -207,11 +185,6 @@ struct SegIter {
     }
 };
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b)
-{
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
 
 // Depth-to-space by R into NCHW [3][R*H][R*W] (PixelShuffle / DepthToSpace CRD: channel
 // c*R*R + ry*R + rx -> [c][R*y + ry][R*x + rx]), plus the nearest-upsampled model input when
@@ -525,6 +498,51 @@ __device__ __forceinline__ void issue_plan(uint64_t adesc0, uint64_t bdesc0, con
         issue_taps<1, DX0, DX1, KS, KC, NG, LBO_A>(adesc0, bdesc0, p);
     else
         issue_taps<2, DX0, DX1, KS, KC, NG, LBO_A>(adesc0, bdesc0, p);
+}
+
+// TMEM columns [C0, C0 + CW) of this warp's lanes from taddr (a slot's base) in runs of 16 at
+// 16-column boundaries and runs of 8 elsewhere, so every access is aligned to its own width (a
+// 48-column slot splits 24 + 24 between its two epilogue warps).
+template <int CW, int C0>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[CW])
+{
+#pragma unroll
+    for (int c = 0; c < CW;) {
+        if ((C0 + c) % 16 == 0 && c + 16 <= CW) {
+            float t[16];
+            dev::tmem_ld16(taddr + C0 + c, t);
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[c + j] = t[j];
+            c += 16;
+        } else {
+            float t[8];
+            dev::tmem_ld8(taddr + C0 + c, t);
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[c + j] = t[j];
+            c += 8;
+        }
+    }
+}
+
+template <int CW, int C0>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&w)[CW])
+{
+#pragma unroll
+    for (int c = 0; c < CW;) {
+        if ((C0 + c) % 16 == 0 && c + 16 <= CW) {
+            uint32_t t[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) t[j] = w[c + j];
+            dev::tmem_st16(taddr + C0 + c, t);
+            c += 16;
+        } else {
+            uint32_t t[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) t[j] = w[c + j];
+            dev::tmem_st8(taddr + C0 + c, t);
+            c += 8;
+        }
+    }
 }
 
 template <int KPAD, int NPAD, int EK, int IN>
@@ -935,11 +953,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         // it completes, while the other group works on its own row.
         const int q = warp & 3, g = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
-        // each group zeroes its share of every slot's columns, 16 at a 16-column boundary
-        constexpr int ZA = NPAD == 48 ? 32 : NPAD / 2;
-        const int zc0 = g == 0 ? 0 : ZA, zcw = g == 0 ? ZA : NPAD - ZA;
-        for (int sl = 0; sl < S; sl++)
-            for (int c = 0; c < zcw; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + zc0 + c));
+        // group g zeroes the slots of parity g, whole (16 columns at a 16-column boundary)
+        for (int sl = g; sl < S; sl += 2)
+#pragma unroll
+            for (int c = 0; c < NPAD; c += 16) dev::tmem_zero16(tmem + lanes + (uint32_t)(sl * NPAD + c));
         dev::tmem_wait_st();
         dev::tc_fence_before();
         dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
@@ -1052,13 +1069,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     } else if (warp < kMmaWarp) {
       if constexpr (!ATT) {
         // ================= epilogue: warp (q, h) takes TMEM lanes 32q.. (pixels) and half h of
-        // each slot's columns (NPAD / 2 each; at 48 channels 32 + 16, so that every TMEM access is
-        // 16 columns at a 16-column boundary); depth-to-space by 3 (groups of 3 channels across the
-        // halves) has half 0 take the whole slot
+        // each slot's columns (NPAD / 2: 16, 24 or 32); depth-to-space by 3 (groups of 3 channels
+        // across the halves) has half 0 take the whole slot
         const int q = warp & 3, h = (warp - kProdWarps) >> 2;
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const bool whole = EK == kEpiD2S && a.R == 3;
-        constexpr int CWA = NPAD == 48 ? 32 : NPAD / 2, CWB = NPAD - CWA;
+        constexpr int CWA = NPAD / 2, CWB = NPAD - CWA;
         auto run_half = [&](auto cw_tag, auto c0_tag) {
             constexpr int CW = decltype(cw_tag)::value, C0 = decltype(c0_tag)::value;
             // every accumulator starts from its channel's bias, so the epilogue adds none: this warp's
@@ -1067,16 +1083,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
             uint32_t bz[CW];
 #pragma unroll
             for (int c = 0; c < CW; c++) bz[c] = __float_as_uint(sbias[C0 + c]);
-            auto fill_bias = [&](uint32_t taddr) {
-#pragma unroll
-                for (int c = 0; c < CW; c += 16) {
-                    uint32_t b16[16];
-#pragma unroll
-                    for (int j = 0; j < 16; j++) b16[j] = bz[c + j];
-                    dev::tmem_st16(taddr + c, b16);
-                }
-            };
-            for (int sl = 0; sl < S; sl++) fill_bias(tmem + lanes + (uint32_t)(sl * NPAD + C0));
+            // taddr: a slot's base (the warp's lanes)
+            auto fill_bias = [&](uint32_t taddr) { tmem_st_cols<CW, C0>(taddr, bz); };
+            for (int sl = 0; sl < S; sl++) fill_bias(tmem + lanes + (uint32_t)(sl * NPAD));
             dev::tmem_wait_st();
             dev::tc_fence_before();
             dev::named_bar_sync(1, (kEpiWarps + 1) * 32);
@@ -1130,16 +1139,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     const uint32_t taddr = tmem + lanes + (uint32_t)(slot * NPAD);
                     if (!whole) {
                         float v[CW];
-#pragma unroll
-                        for (int c = 0; c < CW; c += 16) {
-                            float t[16];
-                            dev::tmem_ld16(taddr + C0 + c, t);
-#pragma unroll
-                            for (int j = 0; j < 16; j++) v[c + j] = t[j];
-                        }
+                        tmem_ld_cols<CW, C0>(taddr, v);
                         dev::tmem_wait_ld();
                         // hand the columns back holding the bias: the MMAs accumulate onto it
-                        fill_bias(taddr + C0);
+                        fill_bias(taddr);
                         dev::tmem_wait_st();
                         dev::tc_fence_before();
                         __syncwarp();
@@ -1160,10 +1163,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                             // both halves back to the bias (the other half's from shared memory)
                             fill_bias(taddr);
                             {
-                                uint32_t b16[16];
+                                uint32_t bo[CWB];
 #pragma unroll
-                                for (int j = 0; j < 16; j++) b16[j] = __float_as_uint(sbias[CWA + j]);
-                                dev::tmem_st16(taddr + CWA, b16);
+                                for (int j = 0; j < CWB; j++) bo[j] = __float_as_uint(sbias[CWA + j]);
+                                tmem_st_cols<CWB, CWA>(taddr, bo);
                             }
                             dev::tmem_wait_st();
                             dev::tc_fence_before();

@@ -36,6 +36,11 @@ int Executor::launches_per_run() const
     return n * bands_;
 }
 
+int Executor::launches_per_run_packed() const
+{
+    return launches_per_run() - (input_pack(nullptr) ? bands_ : 0);
+}
+
 std::unique_ptr<Executor> Executor::create(const Plan &plan, int in_w, int in_h, std::string *why)
 {
     auto fail = [&](const std::string &m) -> std::unique_ptr<Executor> {
@@ -227,9 +232,37 @@ int Executor::profile_read(double *ms, int *counts, int nsteps) const
 
 int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const { return run_images(in, out, w, h, 1, s); }
 
-int Executor::launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1,
-                     cudaStream_t s) const
+bool Executor::input_pack(InputPack *pk) const
 {
+    if (steps_.empty() || !steps_[0].pack || steps_[0].unshuffle) return false;
+    const Step &st = steps_[0];
+    if (pk) {
+        pk->map = st.pack_buf;
+        pk->in_norm = st.in_norm;
+        for (int c = 0; c < 3; c++) {
+            pk->mean[c] = st.in_mean[c];
+            pk->scale[c] = st.in_scale[c];
+        }
+    }
+    return true;
+}
+
+int Executor::run_packed(const void *in, void *out, cudaStream_t s) const
+{
+    // the map was written for the whole frame at the created size; a run at another width would
+    // first clear the maps (run_images), erasing it
+    if (!input_pack(nullptr) || last_w_ != W_) return AJIB_ERR_ARGS;
+    return run_steps(in, out, W_ * U_, H_ * U_, 1, s, true);
+}
+
+int Executor::launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1,
+                     cudaStream_t s, bool packed) const
+{
+    if (st.pack && packed) {
+        // the producer of the input wrote the head's map already
+        return ajib_conv3x3_launch_images(&st.op, st.pack_buf, nullptr, const_cast<void *>(ptr(st.dst, in, out)), nimg,
+                                          img_h, w, r0, r1, s);
+    }
     if (st.pack) {
         // the input rows the head's rows [r0, r1) read: one-row halos
         const int H = nimg * img_h;
@@ -250,6 +283,11 @@ int Executor::launch(const Step &st, const void *in, void *out, int nimg, int im
 }
 
 int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const
+{
+    return run_steps(in, out, w, img_h, nimg, s, false);
+}
+
+int Executor::run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed) const
 {
     if (w < 1 || img_h < 1 || nimg < 1 || w % U_ || img_h % U_ || !in || !out) return AJIB_ERR_ARGS;
     // the conv resolution
@@ -274,7 +312,7 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
         for (int k = 0; k < ns; k++) {
             const Step &st = steps_[k];
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2], s);
-            const int rc = launch(st, in, out, nimg, img_h, w, 0, h, s);
+            const int rc = launch(st, in, out, nimg, img_h, w, 0, h, s, packed);
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2 + 1], s);
             if (rc != AJIB_OK) return rc;
         }
@@ -291,7 +329,7 @@ int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, 
             const Step &st = steps_[k];
             int r0 = nb == 1 ? 0 : std::max(0, B0 - k), r1 = nb == 1 ? h : std::min(h, B1 - k);
             if (r0 >= r1) continue;
-            const int rc = launch(st, in, out, nimg, img_h, w, r0, r1, s);
+            const int rc = launch(st, in, out, nimg, img_h, w, r0, r1, s, packed);
             if (rc != AJIB_OK) return rc;
         }
     }

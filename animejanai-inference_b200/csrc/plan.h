@@ -28,6 +28,7 @@
 #include "../../include/aji_b200.h"
 
 struct ajib_concat_weights;
+struct aji_plan;
 
 namespace ajib {
 
@@ -78,6 +79,20 @@ double flops_per_pixel(const Plan &p);
 // The model's scale: output / input size (depth-to-space over pixel-unshuffle).
 inline int model_scale(const Plan &p) { return p.depth_to_space / (p.unshuffle > 0 ? p.unshuffle : 1); }
 
+// Where the colour pre pass writes the head conv's input when it is fused with the executor's
+// input pack (video.cpp): the head's 8-channel strip-chunked map and the model's input
+// normalisation.
+struct InputPack {
+    void *map = nullptr;
+    bool in_norm = false;
+    float mean[3] = {0.f, 0.f, 0.f}, scale[3] = {1.f, 1.f, 1.f};
+};
+
+// The NV12 / P010 pre pass (aji_run_pre) writing, besides the NCHW fp16 RGB dst [3][h][w], the
+// head's input map pk.map of the same pixels (colour.cu). Returns 0 or a cudaError_t.
+int run_pre_packed(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
+                   const aji_csp *csp, void *dst_f16, const InputPack &pk, cudaStream_t s);
+
 // The NCHW fp16 model input [3][H][W] (pixel-unshuffled by 2: [3][2H][2W]) of conv rows
 // [row_begin, row_end) as a strip-chunked map at H x W of 8 channels {r, g, b, 0...} (16: the 12
 // unshuffled channels, then zeros), normalised if in_norm; pad columns untouched (conv.cu).
@@ -100,6 +115,8 @@ public:
     size_t device_bytes() const { return bytes_; }
     size_t weight_bytes() const { return weight_bytes_; }
     int launches_per_run() const;
+    // launches per run_packed (the head's input pack left to the producer of the input)
+    int launches_per_run_packed() const;
     // bands <= 1: one launch per step over the whole frame; else the banded schedule.
     void set_bands(int bands) { bands_ = bands < 1 ? 1 : bands; }
     int bands() const { return bands_; }
@@ -110,6 +127,13 @@ public:
     // nimg images of img_h rows each, stacked along H (nimg * img_h <= in_h()), each convolved on
     // its own: in [3][nimg * img_h][w], out [3][scale * nimg * img_h][scale * w].
     int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const;
+    // The head's input map, when the head reads the plain NCHW RGB model input (not
+    // pixel-unshuffled): a producer that writes it (run_pre_packed) lets run_packed skip the
+    // head's own pack launch. False for other heads.
+    bool input_pack(InputPack *pk) const;
+    // run() at the created size with the head's input map already written from `in` (the NCHW
+    // input stays needed: a depth-to-space tail adds it).
+    int run_packed(const void *in, void *out, cudaStream_t s) const;
     // Step timing: while enabled, every launch is bracketed by CUDA events on its stream (a ring of
     // kProfRuns runs); profile_read synchronises and returns per-step summed milliseconds and
     // counts of the runs recorded since enabling.
@@ -134,7 +158,9 @@ private:
         int srcs[4] = {-1, -1, -1, -1};
     };
     const void *ptr(int t, const void *in, void *out) const;
-    int launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1, cudaStream_t s) const;
+    int launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1, cudaStream_t s,
+               bool packed = false) const;
+    int run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed) const;
     static constexpr int kProfRuns = 64;
     mutable std::vector<cudaEvent_t> prof_ev_;  // [kProfRuns][steps][2]
     mutable int prof_runs_ = 0;

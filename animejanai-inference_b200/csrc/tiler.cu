@@ -40,29 +40,112 @@ __global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *o
 // out[Y - Y0][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
 // multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134),
 // for output rows [Y0, Y0 + gridDim.y * blockDim.y) clipped to Y1; the tiles buffer holds tiles
-// [k0, k0 + ntiles) of the image's row-major tile order
-__global__ void k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx, const int *ox, const int *oy,
-                          const float *wx, const float *wy, int cols, int rows, const int2 *cx, const int2 *cy, int s,
-                          int co, int OW, int Y0, int Y1, uint8_t *out)
+// [k0, k0 + ntiles) of the image's row-major tile order. A thread takes four adjacent output
+// pixels of one row: the row's covering tiles and weights are looked up once, each (pixel, tile)
+// weight once for all channels, and where the four pixels share their covering tiles at a
+// 4-aligned tile column the tile values are read 8 bytes at a time and the 8-bit output written
+// 4 bytes at a time. Per pixel and channel the arithmetic is the same in either path.
+constexpr int kComposeQ = 4;  // output pixels per thread
+
+__device__ __forceinline__ uint8_t to_u8(float b)
 {
-    const int X = blockIdx.x * blockDim.x + threadIdx.x, Y = Y0 + blockIdx.y * blockDim.y + threadIdx.y;
-    if (X >= OW || Y >= Y1) return;
-    const int2 rx = cx[X], ry = cy[Y];
+    const float f = __fadd_rn(__fmul_rn(b, 255.0f), 0.5f);
+    return f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
+}
+
+__global__ void __launch_bounds__(256) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
+                                                 const int *ox, const int *oy, const float *wx, const float *wy, int cols,
+                                                 int rows, const int2 *cx, const int2 *cy, int s, int co, int OW, int Y0,
+                                                 int Y1, uint8_t *out)
+{
+    const int X0 = (blockIdx.x * blockDim.x + threadIdx.x) * kComposeQ, Y = Y0 + blockIdx.y * blockDim.y + threadIdx.y;
+    if (X0 >= OW || Y >= Y1) return;
+    const int2 ry = cy[Y];
     const size_t plane = (size_t)ntiles * toh * tow;
-    for (int c = 0; c < co; c++) {
-        float b = 0.0f;
-        for (int jj = 0; jj < ry.y; jj++) {
-            const int j = ry.x + jj, v = Y - oy[j] * s;
-            const float wv = wy[(size_t)j * rows + v];
-            for (int ii = 0; ii < rx.y; ii++) {
-                const int i = rx.x + ii, u = X - ox[i] * s, k = j * nx + i - k0;
-                const float w = __fmul_rn(wv, wx[(size_t)i * cols + u]);
-                const float t = __half2float(tiles[(co == 1 ? 0 : c) * plane + ((size_t)k * toh + v) * tow + u]);
-                b = __fadd_rn(b, __fmul_rn(w, t));
+    const int nq = min(kComposeQ, OW - X0);
+    int2 rx[kComposeQ];
+    bool same = nq == kComposeQ;
+#pragma unroll
+    for (int q = 0; q < kComposeQ; q++) {
+        rx[q] = q < nq ? cx[X0 + q] : make_int2(0, 0);
+        same = same && rx[q].x == rx[0].x && rx[q].y == rx[0].y;
+    }
+    // the vector path: every covering tile's column of X0 is 4-aligned, and so are the tile rows
+    // and the weight rows (16-byte weight and 8-byte tile loads)
+    same = same && (tow & 3) == 0 && (cols & 3) == 0;
+    if (same) {
+        for (int ii = 0; ii < rx[0].y; ii++) same = same && (((X0 - ox[rx[0].x + ii] * s) & 3) == 0);
+    }
+    float b[3][kComposeQ];
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int q = 0; q < kComposeQ; q++) b[c][q] = 0.0f;
+    for (int jj = 0; jj < ry.y; jj++) {
+        const int j = ry.x + jj, v = Y - oy[j] * s;
+        const float wv = wy[(size_t)j * rows + v];
+        if (same) {
+            for (int ii = 0; ii < rx[0].y; ii++) {
+                const int i = rx[0].x + ii, u = X0 - ox[i] * s, k = j * nx + i - k0;
+                const float4 wq = *reinterpret_cast<const float4 *>(wx + (size_t)i * cols + u);
+                const float w[4] = {__fmul_rn(wv, wq.x), __fmul_rn(wv, wq.y), __fmul_rn(wv, wq.z), __fmul_rn(wv, wq.w)};
+                const size_t at = ((size_t)k * toh + v) * tow + u;
+#pragma unroll
+                for (int c = 0; c < 3; c++) {
+                    if (c >= co) break;
+                    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(tiles + (co == 1 ? 0 : c) * plane + at));
+                    const float2 t01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                    const float2 t23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                    b[c][0] = __fadd_rn(b[c][0], __fmul_rn(w[0], t01.x));
+                    b[c][1] = __fadd_rn(b[c][1], __fmul_rn(w[1], t01.y));
+                    b[c][2] = __fadd_rn(b[c][2], __fmul_rn(w[2], t23.x));
+                    b[c][3] = __fadd_rn(b[c][3], __fmul_rn(w[3], t23.y));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < kComposeQ; q++) {
+                if (q >= nq) break;
+                const int X = X0 + q;
+                for (int ii = 0; ii < rx[q].y; ii++) {
+                    const int i = rx[q].x + ii, u = X - ox[i] * s, k = j * nx + i - k0;
+                    const float w = __fmul_rn(wv, wx[(size_t)i * cols + u]);
+                    const size_t at = ((size_t)k * toh + v) * tow + u;
+#pragma unroll
+                    for (int c = 0; c < 3; c++) {
+                        if (c >= co) break;
+                        b[c][q] = __fadd_rn(b[c][q], __fmul_rn(w, __half2float(tiles[(co == 1 ? 0 : c) * plane + at])));
+                    }
+                }
             }
         }
-        const float f = __fadd_rn(__fmul_rn(b, 255.0f), 0.5f);
-        out[((size_t)(Y - Y0) * OW + X) * co + c] = f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
+    }
+    uint8_t *o = out + ((size_t)(Y - Y0) * OW + X0) * co;
+    if (nq == kComposeQ && co == 3 && (OW & 3) == 0) {
+        // 12 bytes: pixel-major r, g, b of the four pixels, as three 4-byte words
+        uint32_t w3[3];
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            uint32_t wd = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int flat = 4 * k + e, q = flat / 3, c = flat % 3;
+                wd |= (uint32_t)to_u8(b[c][q]) << (8 * e);
+            }
+            w3[k] = wd;
+        }
+        uint32_t *o4 = reinterpret_cast<uint32_t *>(o);
+        o4[0] = w3[0];
+        o4[1] = w3[1];
+        o4[2] = w3[2];
+    } else if (nq == kComposeQ && co == 1 && (OW & 3) == 0) {
+        uint32_t wd = 0;
+#pragma unroll
+        for (int q = 0; q < kComposeQ; q++) wd |= (uint32_t)to_u8(b[0][q]) << (8 * q);
+        *reinterpret_cast<uint32_t *>(o) = wd;
+    } else {
+        for (int q = 0; q < nq; q++)
+            for (int c = 0; c < co; c++) o[q * co + c] = to_u8(b[c][q]);
     }
 }
 
@@ -133,7 +216,8 @@ cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int
     const int s = g_.scale, OW = g_.W * s;
     if (Y1 <= Y0) return cudaSuccess;
     const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
-    const dim3 block(64, 4), grid((OW + 63) / 64, (Y1 - Y0 + 3) / 4);
+    const int px = 64 * kComposeQ;  // output columns per block row
+    const dim3 block(64, 4), grid((OW + px - 1) / px, (Y1 - Y0 + 3) / 4);
     k_compose<<<grid, block, 0, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
                                       d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
     return cudaGetLastError();
@@ -229,7 +313,7 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
                 return AJIB_ERR_CUDA;
         }
         const int OW = g.W * s, OH = g.H * s;
-        const dim3 block(64, 4), grid((OW + 63) / 64, (OH + 3) / 4);
+        const dim3 block(64, 4), grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + 3) / 4);
         k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
                                           (const int *)(base + o_ox), (const int *)(base + o_oy),
                                           (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,

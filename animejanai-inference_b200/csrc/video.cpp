@@ -117,8 +117,10 @@ namespace {
 bool supported_in(int f) { return f == AJI_FMT_NV12 || f == AJI_FMT_P010 || aji_format_is_444(f); }
 
 // in (NV12 / P010 / 4:4:4) -> fp16 NCHW RGB dst at the frame's size; *plan / key cache the
-// 4:2:0 filter plan per format, size and siting
-int run_pre(aji_ctx *c, const aji_frame *in, void *dst, aji_plan **plan, int *key, cudaStream_t s)
+// 4:2:0 filter plan per format, size and siting. With pk (4:2:0 only), the pass also writes the
+// first model's head input map (the executor's own input pack, fused into this pass).
+int run_pre(aji_ctx *c, const aji_frame *in, void *dst, aji_plan **plan, int *key, cudaStream_t s,
+            const InputPack *pk = nullptr)
 {
     const aji_csp csp = aji_make_csp(in->format, in->matrix, in->range);
     int e;
@@ -136,7 +138,8 @@ int run_pre(aji_ctx *c, const aji_frame *in, void *dst, aji_plan **plan, int *ke
             }
             std::memcpy(key, k, sizeof(k));
         }
-        e = aji_run_pre(*plan, in->plane[0], in->stride[0], in->plane[1], in->stride[1], &csp, dst, s);
+        e = pk ? run_pre_packed(*plan, in->plane[0], in->stride[0], in->plane[1], in->stride[1], &csp, dst, *pk, s)
+               : aji_run_pre(*plan, in->plane[0], in->stride[0], in->plane[1], in->stride[1], &csp, dst, s);
     }
     if (e) {
         c->set_error("pre-kernel failed: %s", cudaGetErrorString((cudaError_t)e));
@@ -431,13 +434,20 @@ extern "C" int aji_infer(aji_ctx *c, const aji_frame *in, const aji_frame *out, 
         return AJI_ERR_CUDA;
     }
     cudaStream_t s = (cudaStream_t)cu_stream;
-    int rc = run_pre(c, in, c->buf[0], &c->pre, c->pre_key, s);
+    // a chain that starts with a model whose head reads the plain NCHW input: the 4:2:0 pre pass
+    // writes that head's input map as well, so the executor skips its own pack launch
+    InputPack pk;
+    const bool fused = !c->steps.empty() && !c->steps[0].resize && !aji_format_is_444(in->format) &&
+                       c->steps[0].exec->input_pack(&pk);
+    int rc = run_pre(c, in, c->buf[0], &c->pre, c->pre_key, s, fused ? &pk : nullptr);
     if (rc != AJI_OK) return rc;
     // the chain's steps, ping-ponging between the two buffers
     for (size_t i = 0; i < c->steps.size(); i++) {
         const ChainStep &st = c->steps[i];
         void *src = c->buf[i % 2], *dst = c->buf[(i + 1) % 2];
-        const int e = st.resize ? aji_run_resize(st.rs, src, dst, s) : st.exec->run(src, dst, s);
+        const int e = st.resize             ? aji_run_resize(st.rs, src, dst, s)
+                      : (i == 0 && fused) ? st.exec->run_packed(src, dst, s)
+                                          : st.exec->run(src, dst, s);
         if (e != 0) {
             c->set_error("%s failed (%d)", st.resize ? "resize kernel" : "native kernels", e);
             return AJI_ERR_CUDA;

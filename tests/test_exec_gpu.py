@@ -115,3 +115,50 @@ def test_video_p010_chain():
     assert vid.infer(bad, fout, 0) == -2
     assert "do not match" in vid.error()
     vid.close()
+
+
+@pytest.mark.parametrize("fmt,norm", [(2, False), (1, False), (2, True)])
+def test_fused_pre_pack_matches_separate_passes(fmt, norm):
+    """aji_infer fuses the first net's input pack into the colour pre pass (the pre pass writes the
+    head's strip-chunked map as well as the NCHW RGB). Its output must equal, bit for bit, the
+    unfused chain: aji_run_pre, the executor with its own pack, aji_run_post, on the same frame."""
+    import ctypes as C
+    import ajib
+    w, h = 200, 72
+    plan = ajib.compact_plan(41, body=3)
+    if norm:
+        plan["steps"][0]["in_norm"] = ((0.45, 0.5, 0.4), (2.0, 1.9, 2.1))
+    d = tempfile.mkdtemp()
+    path = os.path.join(d, "m.ajnm")
+    with open(path, "wb") as f:
+        f.write(ajib.model_bytes(plan))
+    vid = ajib.Video(path, w, h)
+    ow, oh = vid.configure(w, h)
+    rng = np.random.default_rng(fmt * 10 + norm)
+    y, uv = yuv420_frame(rng, w, h, fmt)
+    es = 2 if fmt == 2 else 1
+    tdt = torch.int16 if fmt == 2 else torch.uint8
+    view = np.int16 if fmt == 2 else np.uint8
+    dy, duv = torch.from_numpy(y.view(view)).cuda(), torch.from_numpy(uv.view(view)).cuda()
+    oy, ouv = torch.empty((oh, ow), dtype=tdt, device="cuda"), torch.empty((oh // 2, ow), dtype=tdt, device="cuda")
+    fin = ajib.frame(w, h, fmt, [dy.data_ptr(), duv.data_ptr()], [w * es, w * es])
+    fout = ajib.frame(ow, oh, fmt, [oy.data_ptr(), ouv.data_ptr()], [ow * es, ow * es])
+    assert vid.infer(fin, fout, 0) == 0, vid.error()
+    torch.cuda.synchronize()
+    vid.close()
+    # the same three passes, unfused
+    csp = ajib.lib.aji_make_csp(fmt, ajib.MATRIX_BT709, ajib.RANGE_LIMITED)
+    pre = ajib.lib.aji_pre_plan_create(fmt, w, h, ajib.SITING_LEFT, 0)
+    rgb = torch.empty((3, h, w), dtype=torch.float16, device="cuda")
+    assert ajib.lib.aji_run_pre(pre, dy.data_ptr(), w * es, duv.data_ptr(), w * es, C.byref(csp), rgb.data_ptr(), None) == 0
+    ex = ajib.Exec(ajib.Model(plan), w, h)
+    out = torch.empty((3, oh, ow), dtype=torch.float16, device="cuda")
+    assert ex.run(rgb.data_ptr(), out.data_ptr(), 0) == 0
+    post = ajib.lib.aji_post_plan_create(fmt, ow, oh, ajib.SITING_LEFT, 0)
+    py, puv = torch.empty_like(oy), torch.empty_like(ouv)
+    assert ajib.lib.aji_run_post(post, out.data_ptr(), C.byref(csp), py.data_ptr(), ow * es, puv.data_ptr(), ow * es,
+                                 None) == 0
+    torch.cuda.synchronize()
+    ajib.lib.aji_plan_destroy(pre)
+    ajib.lib.aji_plan_destroy(post)
+    assert torch.equal(oy, py) and torch.equal(ouv, puv)
