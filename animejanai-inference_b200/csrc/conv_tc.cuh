@@ -503,44 +503,42 @@ __device__ __forceinline__ void issue_plan(uint64_t adesc0, uint64_t bdesc0, con
 // TMEM columns [C0, C0 + CW) of this warp's lanes from taddr (a slot's base) in runs of 16 at
 // 16-column boundaries and runs of 8 elsewhere, so every access is aligned to its own width (a
 // 48-column slot splits 24 + 24 between its two epilogue warps).
-template <int CW, int C0>
+template <int CW, int C0, int C = 0>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[CW])
 {
-#pragma unroll
-    for (int c = 0; c < CW;) {
-        if ((C0 + c) % 16 == 0 && c + 16 <= CW) {
+    if constexpr (C < CW) {
+        if constexpr ((C0 + C) % 16 == 0 && C + 16 <= CW) {
             float t[16];
-            dev::tmem_ld16(taddr + C0 + c, t);
+            dev::tmem_ld16(taddr + C0 + C, t);
 #pragma unroll
-            for (int j = 0; j < 16; j++) v[c + j] = t[j];
-            c += 16;
+            for (int j = 0; j < 16; j++) v[C + j] = t[j];
+            tmem_ld_cols<CW, C0, C + 16>(taddr, v);
         } else {
             float t[8];
-            dev::tmem_ld8(taddr + C0 + c, t);
+            dev::tmem_ld8(taddr + C0 + C, t);
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[c + j] = t[j];
-            c += 8;
+            for (int j = 0; j < 8; j++) v[C + j] = t[j];
+            tmem_ld_cols<CW, C0, C + 8>(taddr, v);
         }
     }
 }
 
-template <int CW, int C0>
+template <int CW, int C0, int C = 0>
 __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&w)[CW])
 {
-#pragma unroll
-    for (int c = 0; c < CW;) {
-        if ((C0 + c) % 16 == 0 && c + 16 <= CW) {
+    if constexpr (C < CW) {
+        if constexpr ((C0 + C) % 16 == 0 && C + 16 <= CW) {
             uint32_t t[16];
 #pragma unroll
-            for (int j = 0; j < 16; j++) t[j] = w[c + j];
-            dev::tmem_st16(taddr + C0 + c, t);
-            c += 16;
+            for (int j = 0; j < 16; j++) t[j] = w[C + j];
+            dev::tmem_st16(taddr + C0 + C, t);
+            tmem_st_cols<CW, C0, C + 16>(taddr, w);
         } else {
             uint32_t t[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) t[j] = w[c + j];
-            dev::tmem_st8(taddr + C0 + c, t);
-            c += 8;
+            for (int j = 0; j < 8; j++) t[j] = w[C + j];
+            dev::tmem_st8(taddr + C0 + C, t);
+            tmem_st_cols<CW, C0, C + 8>(taddr, w);
         }
     }
 }
