@@ -53,7 +53,7 @@ __device__ __forceinline__ uint8_t to_u8(float b)
     return f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
 }
 
-__global__ void __launch_bounds__(256, 1) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
+__global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
                                                  const int *ox, const int *oy, const float *wx, const float *wy, int cols,
                                                  int rows, const int2 *cx, const int2 *cy, int s, int co, int OW, int Y0,
                                                  int Y1, uint8_t *out)
