@@ -39,13 +39,17 @@ __global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *o
 
 // out[Y - Y0][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
 // multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134),
-// for output rows [Y0, Y0 + gridDim.y * blockDim.y) clipped to Y1; the tiles buffer holds tiles
-// [k0, k0 + ntiles) of the image's row-major tile order. A thread takes four adjacent output
-// pixels of one row: the row's covering tiles and weights are looked up once, each (pixel, tile)
-// weight once for all channels, and where the four pixels share their covering tiles at a
-// 4-aligned tile column the tile values are read 8 bytes at a time and the 8-bit output written
-// 4 bytes at a time. Per pixel and channel the arithmetic is the same in either path.
-constexpr int kComposeQ = 4;  // output pixels per thread
+// for output rows [Y0, Y0 + gridDim.y * kComposeRows) clipped to Y1; the tiles buffer holds tiles
+// [k0, k0 + ntiles) of the image's row-major tile order. A block takes kComposeRows output rows
+// and 64 * kComposeQ columns; a thread four adjacent pixels in each of two rows, so its tile loads
+// for the two rows are in flight together. The block's rows' covering tile rows, tile-row offsets
+// and vertical weights are looked up once into shared memory; each (pixel, tile) weight is formed
+// once for all channels, and where four pixels share their covering tiles at a 4-aligned tile
+// column the tile values are read 8 bytes at a time and the 8-bit output written 4 bytes at a
+// time. Per pixel and channel the arithmetic is the same in either path.
+constexpr int kComposeQ = 4;     // output pixels per thread and row
+constexpr int kComposeRows = 8;  // output rows per block (two per thread)
+constexpr int kComposeMaxT = 8;  // tile rows covering one output row that the table holds
 
 __device__ __forceinline__ uint8_t to_u8(float b)
 {
@@ -53,41 +57,23 @@ __device__ __forceinline__ uint8_t to_u8(float b)
     return f <= 0.0f ? 0 : f >= 255.0f ? 255 : (uint8_t)f;
 }
 
-__global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
-                                                 const int *ox, const int *oy, const float *wx, const float *wy, int cols,
-                                                 int rows, const int2 *cx, const int2 *cy, int s, int co, int OW, int Y0,
-                                                 int Y1, uint8_t *out)
+// One output row's four pixels at X0 (nq of them inside the image) into b[c][q].
+__device__ __forceinline__ void compose_row(float (&b)[3][kComposeQ], const __half *tiles, size_t plane, int k0, int toh,
+                                            int tow, int nx, const int *ox, const float *wx, int cols, int s, int co,
+                                            int X0, int nq, const int2 (&rx)[kComposeQ], bool same, int nj,
+                                            const int *jrow, const int *vrow, const float *wvrow)
 {
-    const int X0 = (blockIdx.x * blockDim.x + threadIdx.x) * kComposeQ, Y = Y0 + blockIdx.y * blockDim.y + threadIdx.y;
-    if (X0 >= OW || Y >= Y1) return;
-    const int2 ry = cy[Y];
-    const size_t plane = (size_t)ntiles * toh * tow;
-    const int nq = min(kComposeQ, OW - X0);
-    int2 rx[kComposeQ];
-    bool same = nq == kComposeQ;
-#pragma unroll
-    for (int q = 0; q < kComposeQ; q++) {
-        rx[q] = q < nq ? cx[X0 + q] : make_int2(0, 0);
-        same = same && rx[q].x == rx[0].x && rx[q].y == rx[0].y;
-    }
-    // the vector path: every covering tile's column of X0 is 4-aligned, and so are the tile rows
-    // and the weight rows (16-byte weight and 8-byte tile loads)
-    same = same && (tow & 3) == 0 && (cols & 3) == 0;
-    if (same) {
-        for (int ii = 0; ii < rx[0].y; ii++) same = same && (((X0 - ox[rx[0].x + ii] * s) & 3) == 0);
-    }
-    float b[3][kComposeQ];
 #pragma unroll
     for (int c = 0; c < 3; c++)
 #pragma unroll
         for (int q = 0; q < kComposeQ; q++) b[c][q] = 0.0f;
-    for (int jj = 0; jj < ry.y; jj++) {
-        const int j = ry.x + jj, v = Y - oy[j] * s;
-        const float wv = wy[(size_t)j * rows + v];
+    for (int jj = 0; jj < nj; jj++) {
+        const int j = jrow[jj], v = vrow[jj];
+        const float wv = wvrow[jj];
         if (same) {
             for (int ii = 0; ii < rx[0].y; ii++) {
-                const int i = rx[0].x + ii, u = X0 - ox[i] * s, k = j * nx + i - k0;
-                const float4 wq = *reinterpret_cast<const float4 *>(wx + (size_t)i * cols + u);
+                const int i = rx[0].x + ii, u = X0 - __ldg(ox + i) * s, k = j * nx + i - k0;
+                const float4 wq = __ldg(reinterpret_cast<const float4 *>(wx + (size_t)i * cols + u));
                 const float w[4] = {__fmul_rn(wv, wq.x), __fmul_rn(wv, wq.y), __fmul_rn(wv, wq.z), __fmul_rn(wv, wq.w)};
                 const size_t at = ((size_t)k * toh + v) * tow + u;
 #pragma unroll
@@ -108,8 +94,8 @@ __global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0,
                 if (q >= nq) break;
                 const int X = X0 + q;
                 for (int ii = 0; ii < rx[q].y; ii++) {
-                    const int i = rx[q].x + ii, u = X - ox[i] * s, k = j * nx + i - k0;
-                    const float w = __fmul_rn(wv, wx[(size_t)i * cols + u]);
+                    const int i = rx[q].x + ii, u = X - __ldg(ox + i) * s, k = j * nx + i - k0;
+                    const float w = __fmul_rn(wv, __ldg(wx + (size_t)i * cols + u));
                     const size_t at = ((size_t)k * toh + v) * tow + u;
 #pragma unroll
                     for (int c = 0; c < 3; c++) {
@@ -120,10 +106,13 @@ __global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0,
             }
         }
     }
-    uint8_t *o = out + ((size_t)(Y - Y0) * OW + X0) * co;
+}
+
+__device__ __forceinline__ void compose_store(const float (&b)[3][kComposeQ], uint8_t *o, int nq, int co, int OW)
+{
     if (nq == kComposeQ && co == 3 && (OW & 3) == 0) {
         // 12 bytes: pixel-major r, g, b of the four pixels, as three 4-byte words
-        uint32_t w3[3];
+        uint32_t *o4 = reinterpret_cast<uint32_t *>(o);
 #pragma unroll
         for (int k = 0; k < 3; k++) {
             uint32_t wd = 0;
@@ -132,12 +121,8 @@ __global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0,
                 const int flat = 4 * k + e, q = flat / 3, c = flat % 3;
                 wd |= (uint32_t)to_u8(b[c][q]) << (8 * e);
             }
-            w3[k] = wd;
+            o4[k] = wd;
         }
-        uint32_t *o4 = reinterpret_cast<uint32_t *>(o);
-        o4[0] = w3[0];
-        o4[1] = w3[1];
-        o4[2] = w3[2];
     } else if (nq == kComposeQ && co == 1 && (OW & 3) == 0) {
         uint32_t wd = 0;
 #pragma unroll
@@ -150,6 +135,71 @@ __global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0,
             for (int c = 0; c < 3; c++)
                 if (q < nq && c < co) o[q * co + c] = to_u8(b[c][q]);
     }
+}
+
+__global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
+                                                 const int *ox, const int *oy, const float *wx, const float *wy, int cols,
+                                                 int rows, const int2 *cx, const int2 *cy, int s, int co, int OW, int Y0,
+                                                 int Y1, uint8_t *out)
+{
+    // the block's rows: covering tile rows, their row offsets and vertical weights
+    __shared__ int s_nj[kComposeRows], s_j[kComposeRows][kComposeMaxT], s_v[kComposeRows][kComposeMaxT];
+    __shared__ float s_wv[kComposeRows][kComposeMaxT];
+    const int Yb = Y0 + blockIdx.y * kComposeRows;
+    const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+    if (tid < kComposeRows) {
+        const int Y = Yb + tid;
+        int n = 0;
+        if (Y < Y1) {
+            const int2 ry = cy[Y];
+            n = min(ry.y, kComposeMaxT);
+            for (int jj = 0; jj < n; jj++) {
+                const int j = ry.x + jj, v = Y - oy[j] * s;
+                s_j[tid][jj] = j;
+                s_v[tid][jj] = v;
+                s_wv[tid][jj] = wy[(size_t)j * rows + v];
+            }
+        }
+        s_nj[tid] = n;
+    }
+    __syncthreads();
+    const int X0 = (blockIdx.x * blockDim.x + threadIdx.x) * kComposeQ;
+    if (X0 >= OW) return;
+    const size_t plane = (size_t)ntiles * toh * tow;
+    const int nq = min(kComposeQ, OW - X0);
+    int2 rx[kComposeQ];
+    bool same = nq == kComposeQ;
+#pragma unroll
+    for (int q = 0; q < kComposeQ; q++) {
+        rx[q] = q < nq ? cx[X0 + q] : make_int2(0, 0);
+        same = same && rx[q].x == rx[0].x && rx[q].y == rx[0].y;
+    }
+    // the vector path: every covering tile's column of X0 is 4-aligned, and so are the tile rows
+    // and the weight rows (16-byte weight and 8-byte tile loads)
+    same = same && (tow & 3) == 0 && (cols & 3) == 0;
+    if (same) {
+        for (int ii = 0; ii < rx[0].y; ii++) same = same && (((X0 - __ldg(ox + rx[0].x + ii) * s) & 3) == 0);
+    }
+    // rows ty and ty + blockDim.y of the block
+    const int ra = threadIdx.y, rb = threadIdx.y + blockDim.y;
+    const int Ya = Yb + ra, Yb2 = Yb + rb;
+    float ba[3][kComposeQ], bb[3][kComposeQ];
+    if (Ya < Y1)
+        compose_row(ba, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, s_nj[ra], s_j[ra], s_v[ra],
+                    s_wv[ra]);
+    if (Yb2 < Y1)
+        compose_row(bb, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, s_nj[rb], s_j[rb], s_v[rb],
+                    s_wv[rb]);
+    if (Ya < Y1) compose_store(ba, out + ((size_t)(Ya - Y0) * OW + X0) * co, nq, co, OW);
+    if (Yb2 < Y1) compose_store(bb, out + ((size_t)(Yb2 - Y0) * OW + X0) * co, nq, co, OW);
+}
+
+// the most tiles covering one output coordinate (the compose kernel holds kComposeMaxT a row)
+int max_cover(const std::vector<int2> &c)
+{
+    int m = 0;
+    for (const int2 &e : c) m = std::max(m, e.y);
+    return m;
 }
 
 // per output coordinate along one axis: the first tile covering it and how many do
@@ -193,10 +243,13 @@ bool DeviceTiler::init(const TileGeometry &g)
     g_ = g;
     const int s = g.scale;
     const int spw = std::min(g.tw, g.W), sph = std::min(g.th, g.H);
+    const std::vector<int2> cy = cover(g.oy, sph, s, g.H);
+    // an output row covered by more tile rows than the compose kernel's table holds: refuse
+    if (max_cover(cy) > kComposeMaxT) return false;
     return upload(&d_ox_, g.ox, &bytes_) && upload(&d_oy_, g.oy, &bytes_) &&
            upload(&d_wx_, axis_weights(g.ox, g.W, g.tw, s), &bytes_) &&
            upload(&d_wy_, axis_weights(g.oy, g.H, g.th, s), &bytes_) && upload(&d_cx_, cover(g.ox, spw, s, g.W), &bytes_) &&
-           upload(&d_cy_, cover(g.oy, sph, s, g.H), &bytes_);
+           upload(&d_cy_, cy, &bytes_);
 }
 
 cudaError_t DeviceTiler::extract(const uint8_t *img, int k0, int n, void *dst, cudaStream_t s) const
@@ -219,8 +272,8 @@ cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int
     const int s = g_.scale, OW = g_.W * s;
     if (Y1 <= Y0) return cudaSuccess;
     const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
-    const int px = 64 * kComposeQ;  // output columns per block row
-    const dim3 block(64, 4), grid((OW + px - 1) / px, (Y1 - Y0 + 3) / 4);
+    const int px = 64 * kComposeQ;  // output columns per block
+    const dim3 block(64, kComposeRows / 2), grid((OW + px - 1) / px, (Y1 - Y0 + kComposeRows - 1) / kComposeRows);
     k_compose<<<grid, block, 0, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
                                       d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
     return cudaGetLastError();
@@ -301,7 +354,9 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
         std::vector<unsigned char> img;
         const size_t o_ox = put(img, g.ox), o_oy = put(img, g.oy);
         const size_t o_wx = put(img, axis_weights(g.ox, g.W, g.tw, s)), o_wy = put(img, axis_weights(g.oy, g.H, g.th, s));
-        const size_t o_cx = put(img, cover(g.ox, spw, s, g.W)), o_cy = put(img, cover(g.oy, sph, s, g.H));
+        const std::vector<int2> cyv = cover(g.oy, sph, s, g.H);
+        if (max_cover(cyv) > kComposeMaxT) return AJIB_ERR_UNSUPPORTED;  // more covering tile rows than the kernel holds
+        const size_t o_cx = put(img, cover(g.ox, spw, s, g.W)), o_cy = put(img, cyv);
         if (img.size() > kStaticTableBytes) return AJIB_ERR_UNSUPPORTED;  // tables beyond the fixed area
         const cudaStream_t st = (cudaStream_t)stream;
         unsigned char *base = nullptr;
@@ -316,7 +371,8 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
                 return AJIB_ERR_CUDA;
         }
         const int OW = g.W * s, OH = g.H * s;
-        const dim3 block(64, 4), grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + 3) / 4);
+        const dim3 block(64, kComposeRows / 2),
+            grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + kComposeRows - 1) / kComposeRows);
         k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
                                           (const int *)(base + o_ox), (const int *)(base + o_oy),
                                           (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
