@@ -59,6 +59,12 @@ lib.ajib_feature_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
 lib.ajib_feature_bytes.restype = C.c_size_t
 lib.ajib_kernel_status.argtypes = [C.c_int]
 lib.ajib_kernel_status.restype = C.c_int
+lib.ajib_conv_pair_mode.argtypes = [C.c_int]
+lib.ajib_conv_pair_mode.restype = C.c_int
+lib.ajib_conv_on_pairs.argtypes = [C.POINTER(ConvOp)]
+lib.ajib_conv_on_pairs.restype = C.c_int
+lib.ajib_conv_pair_clusters.argtypes = []
+lib.ajib_conv_pair_clusters.restype = C.c_int
 lib.ajib_selftest_umma.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp]
 lib.ajib_selftest_umma.restype = C.c_int
 lib.ajib_selftest_division.argtypes = [_vp, C.c_int, _vp, _vp]
@@ -156,6 +162,17 @@ def conv3x3_images(op, src, resid, dst, nimg, img_h, W, row_begin=0, row_end=0, 
 
 def kernel_status(clear=True):
     return lib.ajib_kernel_status(1 if clear else 0)
+
+
+def pair_mode(mode=-1):
+    """Whether eligible convs run on SM pairs (ajib_conv_pair_mode): 1 / 0 sets, -1 queries;
+    returns the mode in force."""
+    return lib.ajib_conv_pair_mode(mode)
+
+
+def on_pairs(op):
+    """True when op runs on the SM-pair kernel in the current mode (ajib_conv_on_pairs)."""
+    return bool(lib.ajib_conv_on_pairs(C.byref(op)))
 
 
 # ---------------------------------------------------------------------------------------------

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "concat_tc.cuh"
+#include "conv_pair.cuh"
 #include "conv_tc.cuh"
 #include "../../include/aji_b200.h"
 
@@ -104,6 +105,16 @@ using ConvFn = cudaError_t (*)(const ConvDev &, int grid, cudaStream_t);
 // Launch with programmatic stream serialisation: the kernel's set-up (barriers, TMEM, weight fetch)
 // may run while the previous kernel in the stream drains; the kernel waits (griddepcontrol.wait)
 // before it touches that kernel's outputs.
+// AJIB_PDL=0 in the environment launches without the attribute (plain stream order)
+bool pdl_enabled()
+{
+    static const bool pdl = [] {
+        const char *e = std::getenv("AJIB_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return pdl;
+}
+
 template <typename Arg>
 cudaError_t launch_pdl(void (*kernel)(Arg), int grid, int threads, int smem, cudaStream_t s, const Arg &arg)
 {
@@ -112,17 +123,89 @@ cudaError_t launch_pdl(void (*kernel)(Arg), int grid, int threads, int smem, cud
     cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
-    // AJIB_PDL=0 in the environment launches without the attribute (plain stream order)
-    static const bool pdl = [] {
-        const char *e = std::getenv("AJIB_PDL");
-        return !(e && e[0] == '0');
-    }();
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
+// Whether strip-chunked convs run on SM pairs (k_conv3x3_pair) where a pair kernel exists: off
+// unless AJIB_PAIR=1 in the environment or ajib_conv_pair_mode(1). (Measured on one B200, the
+// 64-channel body conv: 0.138-0.147 ms on pairs against 0.129-0.134 ms on the one-SM kernel.)
+std::atomic<int> g_pair_mode{-1};
+int pair_mode()
+{
+    int m = g_pair_mode.load();
+    if (m < 0) {
+        const char *e = std::getenv("AJIB_PAIR");
+        m = (e && e[0] == '1') ? 1 : 0;
+        int expect = -1;
+        g_pair_mode.compare_exchange_strong(expect, m);
+        m = g_pair_mode.load();
+    }
+    return m;
+}
+
+using PairFn = cudaError_t (*)(const ConvDev &, long tiles, cudaStream_t);
+
+// The pair kernel on clusters of two CTAs, as many pairs as the device holds at once (one CTA per
+// SM), each pair a run of tiles.
+template <int KPAD, int NPAD, int EK>
+cudaError_t run_conv_pair(const ConvDev &p, long tiles, cudaStream_t s)
+{
+    using Cf = PairCfg<KPAD, NPAD>;
+    constexpr int smem = Cf::SMEM;
+    void (*kern)(ConvDev) = k_conv3x3_pair<KPAD, NPAD, EK>;
+    static std::atomic<uint64_t> done{0};
+    static std::atomic<int> pairs[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Cf::THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3(2 * (sm_count() / 2));
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        if (n < 1) return cudaErrorLaunchOutOfResources;
+        pairs[dev & 63].store(n);
+        done.fetch_or(bit);
+    }
+    const long grid = std::min<long>(2L * pairs[dev & 63].load(), (tiles + 1) / 2 * 2);
+    cfg.gridDim = dim3((unsigned)grid);
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// The pair kernels built: strip-chunked input and output, cin == cout at 32, 48 and 64 padded
+// channels with an activation, and at 32 and 48 with a SPAN gate (the body convs of Compact,
+// SuperUltraCompact and SPAN; a 64-channel gate variant would spill registers).
+PairFn find_pair_fn(int kpad, int npad, int ek)
+{
+#define AJIB_P(KP, NP, EK) \
+    if (kpad == KP && npad == NP && ek == EK) return &run_conv_pair<KP, NP, EK>;
+    AJIB_P(32, 32, kEpiAct)
+    AJIB_P(48, 48, kEpiAct)
+    AJIB_P(64, 64, kEpiAct)
+    AJIB_P(32, 32, kEpiGate)
+    AJIB_P(48, 48, kEpiGate)
+#undef AJIB_P
+    return nullptr;
 }
 
 template <int KPAD, int NPAD, int EK, int IN>
@@ -191,6 +274,15 @@ int in_kind(const ajib_conv *op)
 }
 
 ConvFn op_fn(const ajib_conv *op) { return find_fn(op->w->kpad, op->w->npad, epi_kind(op), in_kind(op)); }
+
+// The pair kernel for the op when pairs are on and one is built for it, else null.
+PairFn pair_fn(const ajib_conv *op)
+{
+    if (!pair_mode() || op->in != AJIB_IN_NHWC || op->out != AJIB_OUT_NHWC) return nullptr;
+    const int ek = epi_kind(op);
+    if (ek != kEpiAct && ek != kEpiGate) return nullptr;
+    return find_pair_fn(op->w->kpad, op->w->npad, ek);
+}
 
 int d2s_factor(int out) { return out == 1 ? 2 : out == 2 ? 4 : out == 3 ? 1 : out == 4 ? 3 : 0; }
 
@@ -372,10 +464,44 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     }
     const long strips = (W + kTileM - 1) / kTileM;
     const long tiles = strips * (row_end - row_begin);
-    const int grid = (int)std::min<long>(sm_count(), tiles);
-    ConvFn fn = op_fn(op);
-    const cudaError_t e = fn(p, grid, (cudaStream_t)stream);
+    cudaError_t e;
+    PairFn pf = pair_fn(op);
+    if (pf) {
+        e = pf(p, tiles, (cudaStream_t)stream);
+    } else {
+        const int grid = (int)std::min<long>(sm_count(), tiles);
+        e = op_fn(op)(p, grid, (cudaStream_t)stream);
+    }
     return e == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
+}
+
+extern "C" int ajib_conv_pair_mode(int mode)
+{
+    if (mode == 0 || mode == 1) g_pair_mode.store(mode);
+    return pair_mode();
+}
+
+extern "C" int ajib_conv_on_pairs(const ajib_conv *op) { return check(op, nullptr, 0) && pair_fn(op) ? 1 : 0; }
+
+extern "C" int ajib_conv_pair_clusters(void)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(PairCfg<64, 64>::THREADS);
+    cfg.dynamicSmemBytes = (size_t)PairCfg<64, 64>::SMEM;
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void (*kern)(ConvDev) = k_conv3x3_pair<64, 64, kEpiAct>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<64, 64>::SMEM) != cudaSuccess)
+        return AJIB_ERR_CUDA;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return AJIB_ERR_CUDA;
+    return n;
 }
 
 namespace ajib {

@@ -162,14 +162,16 @@ struct ConvCfg {
 struct SegIter {
     long L, L1;
     int rows, row_begin;
-    __device__ SegIter(int W, int row_begin_, int row_end)
+    __device__ SegIter(int W, int row_begin_, int row_end) : SegIter(W, row_begin_, row_end, blockIdx.x, gridDim.x) {}
+    // the run of CTA `cta` of `ncta`
+    __device__ SegIter(int W, int row_begin_, int row_end, int cta, int ncta)
     {
         row_begin = row_begin_;
         rows = row_end - row_begin_;
         const long strips = (W + kTileM - 1) / kTileM;
         const long T = strips * rows;
-        L = (long)blockIdx.x * T / gridDim.x;
-        L1 = (long)(blockIdx.x + 1) * T / gridDim.x;
+        L = (long)cta * T / ncta;
+        L1 = (long)(cta + 1) * T / ncta;
     }
     // next segment: strip, output rows [ya, yb)
     __device__ bool next(int &strip, int &ya, int &yb)
@@ -519,6 +521,30 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[CW])
 #pragma unroll
             for (int j = 0; j < 8; j++) v[C + j] = t[j];
             tmem_ld_cols<CW, C0, C + 8>(taddr, v);
+        }
+    }
+}
+
+// v += TMEM columns [C0, C0 + CW) of this warp's lanes from taddr, loaded and added in runs of 16
+// or 8 (few registers live beside v).
+template <int CW, int C0, int C = 0>
+__device__ __forceinline__ void tmem_add_cols(uint32_t taddr, float (&v)[CW])
+{
+    if constexpr (C < CW) {
+        if constexpr ((C0 + C) % 16 == 0 && C + 16 <= CW) {
+            float t[16];
+            dev::tmem_ld16(taddr + C0 + C, t);
+            dev::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[C + j] += t[j];
+            tmem_add_cols<CW, C0, C + 16>(taddr, v);
+        } else {
+            float t[8];
+            dev::tmem_ld8(taddr + C0 + C, t);
+            dev::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[C + j] += t[j];
+            tmem_add_cols<CW, C0, C + 8>(taddr, v);
         }
     }
 }

@@ -262,6 +262,69 @@ __device__ __forceinline__ uint32_t pack_relu_h2(float lo, float hi)
     return d;
 }
 
+// ---- CTA pairs (a cluster of two CTAs sharing one tcgen05 MMA: cta_group::2) -------------------
+
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (a shared::cluster address from peer_addr),
+// with the default release at CTA scope. (A release at cluster scope made the arriving thread wait
+// until its earlier global stores were visible cluster-wide: ~1300 cycles a call in the conv
+// epilogue, measured.) Orders what the tcgen05 fences and the bulk-copy barriers order; nothing
+// else.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Every thread of every CTA of the cluster (all warps, converged).
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMEM allocation across a CTA pair: the same warp of both CTAs executes these, with the same
+// destination offset; both CTAs get the same columns.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// The pair's MMA, issued by one thread of the even CTA: M = 256, rows 0-127 from this CTA's A and
+// TMEM lanes, rows 128-255 from the odd CTA's (the same shared-memory and TMEM addresses there);
+// B's N rows [0, N/2) come from this CTA's shared memory and [N/2, N) from the odd CTA's; each
+// CTA's D gets all N columns for its 128 rows.
+__device__ __forceinline__ void mma_f16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+                 "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Arrive once on the mbarrier at shared::cluster address `bar` (this CTA's or the other's) when
+// every pair MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ---- misc ------------------------------------------------------------------------------------
 
 __device__ __forceinline__ float tanh_fast(float x)

@@ -710,7 +710,8 @@ def run_kernel(args):
 
         def launch():
             return ajib.conv3x3(op, src.data_ptr(), 0, dst.data_ptr(), h_, w_, 0, 0, s.cuda_stream)
-        kname = "k_conv3x3_tc<64,64> (tcgen05, fp32 TMEM accumulation)"
+        kname = ("k_conv3x3_pair<64,64> (tcgen05 cta_group::2 over an SM pair, fp32 TMEM accumulation)" if ajib.on_pairs(op)
+                 else "k_conv3x3_tc<64,64> (tcgen05, fp32 TMEM accumulation)")
     else:
         # the frame's other convs: head 3->64 from NCHW planes (or from an 8-channel row-chunked
         # map, "head8"), tail 64->12 with depth-to-space 2 and the model-input skip

@@ -109,6 +109,20 @@ AJIB_EXPORT int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const 
 AJIB_EXPORT int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, const void *resid, void *dst,
                                            int nimg, int img_h, int W, int row_begin, int row_end, void *stream);
 
+/* Strip-chunked convs with cin == cout at 32, 48 or 64 padded channels and an activation, or at
+ * 32 or 48 and a SPAN gate, can run on SM pairs (one tcgen05 MMA over a cluster of two CTAs, each
+ * SM holding half of the weights) instead of the one-SM kernel. Off by default (slower on B200 as
+ * built); mode 1 / 0 turns pairs on / off for the process (the environment variable AJIB_PAIR=1
+ * sets the initial state to on); any other value only queries. Returns the mode now in force. Both
+ * kernels compute the same sums; results may differ in the last bits of the fp32 accumulation
+ * order. */
+AJIB_EXPORT int ajib_conv_pair_mode(int mode);
+/* 1 when op runs on SM pairs in the current mode, else 0. */
+AJIB_EXPORT int ajib_conv_on_pairs(const ajib_conv *op);
+/* How many SM pairs (clusters of two CTAs) of the 64-channel pair kernel the current device runs
+ * at once, or a negative AJIB_ERR_*. */
+AJIB_EXPORT int ajib_conv_pair_clusters(void);
+
 /* ---- colour passes (reference src/kernels.h:12-78; same names, arguments and semantics) ----
  * Normalisation constants in raw container units (P010 samples are 10 bits in the high bits of
  * 16, so its scales include the << 6): y = (raw - yoff) / yscale, c = (raw - coff) / cscale. */
