@@ -11,7 +11,7 @@
  *
  * The Executor (reference src/native/executor.cpp:23-127) uploads the weights, assigns feature
  * buffers with lifetime reuse (reference src/native/layout.cpp:10-77) and launches one kernel
- * per step on a stream, so a run can be captured into a CUDA graph. Unlike the reference it can
+ * per step on a stream, with no allocation or host synchronisation in a run. Unlike the reference it can
  * run the net as horizontal bands: all steps over band 0, then band 1, ..., each step's rows
  * shifted down by one per step so every row a step reads was written by the previous step of the
  * same or an earlier band. A band's activations stay in L2 between the steps.

@@ -209,8 +209,8 @@ AJIB_EXPORT void ajib_tiler_release(ajib_tiler **t);
  * fit. The caller passes the tiles and the output, both device memory.
  * Returns AJIB_OK, AJIB_ERR_ARGS for bad arguments, AJIB_ERR_UNSUPPORTED when the shape's tables
  * exceed the 1 MiB area, AJIB_ERR_CUDA on a CUDA error.
- * The first call on a device looks up the area's device address (with that device current);
- * make that first call before any stream capture. Every call on a device uses the same area and
+ * The first call on a device looks up the area's device address (with that device current).
+ * Every call on a device uses the same area and
  * leaves its tables there: calls that overlap on the GPU (other streams, or the next call before
  * this one's kernel has run on another stream) race; calls on one stream are ordered by it. Each
  * call uploads its tables by a copy from host memory inside this library, which may wait for
@@ -283,7 +283,7 @@ AJIB_EXPORT int ajib_selftest_frame_order(int ndev, int depth, int nframes, cons
  * this engine's model file (format: animejanai-inference_b200/csrc/model.cpp). An executor is
  * the model instantiated for one input size on the current device (reference
  * src/native/executor.h:21-60): weights uploaded, feature buffers allocated, run() only launches
- * kernels (capturable in a CUDA graph). */
+ * kernels (no allocation, no host synchronisation). */
 typedef struct ajib_model ajib_model;
 typedef struct ajib_exec ajib_exec;
 
