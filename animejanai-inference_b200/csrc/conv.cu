@@ -24,6 +24,7 @@
 #include "concat_tc.cuh"
 #include "conv_pair.cuh"
 #include "conv_tc.cuh"
+#include "plan.h"
 #include "../../include/aji_b200.h"
 
 struct ajib_weights {
@@ -414,6 +415,12 @@ extern "C" int ajib_conv3x3_launch(const ajib_conv *op, const void *src, const v
 extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, const void *resid, void *dst, int nimg,
                                           int img_h, int W, int row_begin, int row_end, void *stream)
 {
+    return ajib::conv3x3_launch_planes(op, src, resid, dst, nimg, img_h, W, row_begin, row_end, stream, 0);
+}
+
+int ajib::conv3x3_launch_planes(const ajib_conv *op, const void *src, const void *resid, void *dst, int nimg, int img_h,
+                                int W, int row_begin, int row_end, void *stream, size_t dst_plane)
+{
     if (!check(op, nullptr, 0)) return AJIB_ERR_UNSUPPORTED;
     if (nimg < 1 || img_h < 1 || (long)nimg * img_h > (1l << 30)) return AJIB_ERR_ARGS;
     const int H = nimg * img_h;
@@ -456,6 +463,12 @@ extern "C" int ajib_conv3x3_launch_images(const ajib_conv *op, const void *src, 
     p.img_h = img_h;
     p.skip_smem = op->out != AJIB_OUT_NHWC && resid && op->in == AJIB_IN_NHWC && W % 8 == 0 &&
                   ((uintptr_t)resid & 15) == 0;
+    if (dst_plane) {
+        // a plane stride only for depth-to-space outputs, and at least one dense plane
+        const size_t R = (size_t)p.R;
+        if (op->out == AJIB_OUT_NHWC || dst_plane < R * H * R * W) return AJIB_ERR_ARGS;
+    }
+    p.dst_plane = dst_plane;
     if (op->gate == AJIB_GATE_TANH1X1) {
         p.att_img = (const unsigned char *)op->att->img;
         p.att_bias = op->att->bias;

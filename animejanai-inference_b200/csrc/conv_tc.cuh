@@ -108,6 +108,9 @@ struct ConvDev {
     // depth-to-space with the skip: its rows reach shared memory by bulk copies (strip-chunked
     // input and W a multiple of 8, so every copy is 16-byte aligned), else the epilogue loads them
     int skip_smem;
+    // depth-to-space: elements from one output plane to the next (0: the dense [3][R*H][R*W]), so
+    // that a batch of tiles can land inside a larger stack of tiles
+    size_t dst_plane;
 };
 
 // The input rows a segment of output rows [ya, yb) reads: one-row halos that stay inside the
@@ -196,7 +199,7 @@ template <int R, int CW, int C0>
 __device__ __forceinline__ void store_d2s(const float (&v)[CW], const ConvDev &a, int o, int x, const float (&skip)[3])
 {
     const int W = a.W, H = a.H;
-    const size_t OW = (size_t)R * W, OH = (size_t)R * H;
+    const size_t OW = (size_t)R * W, OH = (size_t)R * H, plane = a.dst_plane ? a.dst_plane : OH * OW;
 #pragma unroll
     for (int c3 = 0; c3 < 3; c3++) {
         // skip the colour planes with no channel group inside [C0, C0 + CW)
@@ -206,7 +209,7 @@ __device__ __forceinline__ void store_d2s(const float (&v)[CW], const ConvDev &a
         for (int ry = 0; ry < R; ry++) {
             const int n0 = c3 * R * R + ry * R - C0;
             if (n0 < 0 || n0 + R > CW) continue;
-            __half *d = a.dst + ((size_t)c3 * OH + (size_t)R * o + ry) * OW + (size_t)R * x;
+            __half *d = a.dst + (size_t)c3 * plane + ((size_t)R * o + ry) * OW + (size_t)R * x;
             float t[R];
 #pragma unroll
             for (int rx = 0; rx < R; rx++) {

@@ -256,7 +256,7 @@ int Executor::run_packed(const void *in, void *out, cudaStream_t s) const
 }
 
 int Executor::launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1,
-                     cudaStream_t s, bool packed) const
+                     cudaStream_t s, bool packed, size_t out_plane) const
 {
     if (st.pack && packed) {
         // the producer of the input wrote the head's map already
@@ -278,16 +278,19 @@ int Executor::launch(const Step &st, const void *in, void *out, int nimg, int im
         return ajib_concat1x1_launch(st.w, st.nsrc, srcs, st.c, const_cast<void *>(ptr(st.dst, in, out)), nimg * img_h, w,
                                      r0, r1, s);
     }
-    return ajib_conv3x3_launch_images(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
-                                      const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, r0, r1, s);
+    // the model output's planes may sit inside a larger stack (run_images' out_plane)
+    return conv3x3_launch_planes(&st.op, ptr(st.src, in, out), ptr(st.resid, in, out),
+                                 const_cast<void *>(ptr(st.dst, in, out)), nimg, img_h, w, r0, r1, s,
+                                 st.dst == kModelOutput ? out_plane : 0);
 }
 
-int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const
+int Executor::run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, size_t out_plane) const
 {
-    return run_steps(in, out, w, img_h, nimg, s, false);
+    return run_steps(in, out, w, img_h, nimg, s, false, out_plane);
 }
 
-int Executor::run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed) const
+int Executor::run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed,
+                        size_t out_plane) const
 {
     if (w < 1 || img_h < 1 || nimg < 1 || w % U_ || img_h % U_ || !in || !out) return AJIB_ERR_ARGS;
     // the conv resolution
@@ -312,7 +315,7 @@ int Executor::run_steps(const void *in, void *out, int w, int img_h, int nimg, c
         for (int k = 0; k < ns; k++) {
             const Step &st = steps_[k];
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2], s);
-            const int rc = launch(st, in, out, nimg, img_h, w, 0, h, s, packed);
+            const int rc = launch(st, in, out, nimg, img_h, w, 0, h, s, packed, out_plane);
             cudaEventRecord(prof_ev_[((size_t)slot * ns + k) * 2 + 1], s);
             if (rc != AJIB_OK) return rc;
         }
@@ -329,7 +332,7 @@ int Executor::run_steps(const void *in, void *out, int w, int img_h, int nimg, c
             const Step &st = steps_[k];
             int r0 = nb == 1 ? 0 : std::max(0, B0 - k), r1 = nb == 1 ? h : std::min(h, B1 - k);
             if (r0 >= r1) continue;
-            const int rc = launch(st, in, out, nimg, img_h, w, r0, r1, s, packed);
+            const int rc = launch(st, in, out, nimg, img_h, w, r0, r1, s, packed, out_plane);
             if (rc != AJIB_OK) return rc;
         }
     }

@@ -42,6 +42,9 @@ std::mutex g_open_mu;
 int g_open[64] = {};  // open contexts per CUDA ordinal
 
 constexpr int kMaxBatch = 256;  // tiles per net launch
+// A share's tile rows run in up to kWaves waves: the output rows a wave completes are composed and
+// downloaded (on a second stream) while the next wave's tiles go through the net.
+constexpr int kWaves = 4;
 
 }  // namespace
 
@@ -51,6 +54,8 @@ struct aji_img_model;
 struct ImgDev {
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy = nullptr;      // the output bands' downloads
+    cudaEvent_t band[kWaves] = {};    // a band composed on `stream`
     uint8_t *d_img = nullptr, *d_out = nullptr;
     void *d_tin = nullptr, *d_tout = nullptr;
     size_t img_cap = 0, out_cap = 0, tin_cap = 0, tout_cap = 0;
@@ -162,10 +167,16 @@ bool open_dev(int d, ImgDev *out, const char **why)
         return false;
     }
     out->device = d;
-    if (cudaStreamCreateWithFlags(&out->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaStreamCreateWithFlags(&out->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&out->copy, cudaStreamNonBlocking) != cudaSuccess) {
         *why = "cannot create a stream";
         return false;
     }
+    for (cudaEvent_t &e : out->band)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+            *why = "cannot create an event";
+            return false;
+        }
     std::lock_guard<std::mutex> lk(g_open_mu);
     g_open[d & 63]++;
     return true;
@@ -180,7 +191,10 @@ void close_dev(ImgDev &d)
     cudaFree(d.d_tin);
     cudaFree(d.d_tout);
     if (d.stream) cudaStreamDestroy(d.stream);
-    d.stream = nullptr;
+    if (d.copy) cudaStreamDestroy(d.copy);
+    for (cudaEvent_t &e : d.band)
+        if (e) cudaEventDestroy(e);
+    d.stream = d.copy = nullptr;
     std::lock_guard<std::mutex> lk(g_open_mu);
     g_open[d.device & 63]--;
 }
@@ -374,66 +388,64 @@ int run_share(aji_img_model *m, size_t di, const Share &sh, const aji_img_buffer
     }
     const TileGeometry &g = D.tiler->geometry();
     const int nx = g.nx(), k0 = sh.j0 * nx, count = sh.tiles() * nx, tw = g.tw, th = g.th;
-    const int batch = std::min(count, kMaxBatch);
+    // waves: contiguous groups of the share's tile rows
+    const int nrows = sh.tiles(), nw = std::max(1, std::min(kWaves, nrows));
+    const int wave_tiles = (nrows + nw - 1) / nw * nx;
+    const int batch = std::min(wave_tiles, kMaxBatch);
     const size_t tile_in = (size_t)3 * tw * th * 2, tile_out = tile_in * s * s;
     const size_t OW = (size_t)W * s, rows = (size_t)(sh.Y1 - sh.Y0);
-    // with more tiles than one batch, each batch's output is staged after its input and then
-    // copied into its place in the share's stack
-    const size_t staging = batch < count ? tile_out * batch : 0;
     if (!ensure_exec(m, di, batch, why)) return AJI_IMG_ERR_NO_MEM;
     if (!grow((void **)&D.d_img, &D.img_cap, (size_t)W * H * ci) || !grow((void **)&D.d_out, &D.out_cap, OW * rows * ci) ||
-        !grow(&D.d_tin, &D.tin_cap, tile_in * batch + staging) || !grow(&D.d_tout, &D.tout_cap, tile_out * count)) {
+        !grow(&D.d_tin, &D.tin_cap, tile_in * batch) || !grow(&D.d_tout, &D.tout_cap, tile_out * count)) {
         *why = "out of device memory for the tiling buffers";
         return AJI_IMG_ERR_NO_MEM;
     }
+    // no download may still be writing the caller's buffer when this returns
+    auto fail = [&](int rc, const std::string &w) {
+        cudaStreamSynchronize(D.copy);
+        cudaStreamSynchronize(st);
+        *why = w;
+        return rc;
+    };
     // the whole input on every device (tiles reflect across the image edges)
     if (cudaMemcpy2DAsync(D.d_img, (size_t)W * ci, in->data, in->stride, (size_t)W * ci, H, cudaMemcpyHostToDevice, st) !=
-        cudaSuccess) {
-        *why = "image upload failed";
-        return AJI_IMG_ERR;
-    }
-    // the share's tiles through the net, a batch at a time; a batch's output lands in its tiles'
-    // place of the share's stack ([3][count * th * s][tw * s])
+        cudaSuccess)
+        return fail(AJI_IMG_ERR, "image upload failed");
+    // The share's tiles stack as [3][count * th * s][tw * s] (the compose's layout); each batch's
+    // net output lands in its tiles' place, its planes plane_all elements apart. After a wave,
+    // the output rows before the next tile row's first are final: composed on `stream`, then
+    // downloaded on `copy` while the next wave runs.
     Executor &ex = *m->execs[di].exec;
-    const size_t plane_all = (size_t)count * th * s * tw * s;
-    for (int b0 = 0; b0 < count; b0 += batch) {
-        const int n = std::min(batch, count - b0);
-        const bool direct = n == count;
-        void *dst = direct ? D.d_tout : (char *)D.d_tin + tile_in * batch;
-        if (D.tiler->extract(D.d_img, k0 + b0, n, D.d_tin, st) != cudaSuccess ||
-            ex.run_images(D.d_tin, dst, tw, th, n, st) != AJIB_OK) {
-            *why = "tile kernels failed";
-            return AJI_IMG_ERR;
+    const size_t plane_all = (size_t)count * th * s * tw * s, tile_elems = (size_t)th * s * tw * s;
+    uint8_t *host_rows = (uint8_t *)out->data + (ptrdiff_t)sh.Y0 * out->stride;
+    int y_done = sh.Y0, tiles_done = 0;
+    for (int w = 0; w < nw; w++) {
+        const int ja = sh.j0 + (int)((long)w * nrows / nw), jb = sh.j0 + (int)((long)(w + 1) * nrows / nw) - 1;
+        for (int b0 = ja * nx; b0 < (jb + 1) * nx; b0 += batch) {
+            const int n = std::min(batch, (jb + 1) * nx - b0);
+            if (D.tiler->extract(D.d_img, b0, n, D.d_tin, st) != cudaSuccess ||
+                ex.run_images(D.d_tin, (uint16_t *)D.d_tout + (size_t)(b0 - k0) * tile_elems, tw, th, n, st, plane_all) !=
+                    AJIB_OK)
+                return fail(AJI_IMG_ERR, "tile kernels failed");
+            tiles_done += n;
         }
-        if (!direct) {
-            const size_t plane_n = (size_t)n * th * s * tw * s;
-            for (int ch = 0; ch < 3; ch++)
-                if (cudaMemcpyAsync((uint16_t *)D.d_tout + ch * plane_all + (size_t)b0 * th * s * tw * s,
-                                    (const uint16_t *)dst + ch * plane_n, plane_n * 2, cudaMemcpyDeviceToDevice,
-                                    st) != cudaSuccess) {
-                    *why = "tile output copy failed";
-                    return AJI_IMG_ERR;
-                }
+        const int y_end = w == nw - 1 ? sh.Y1 : std::min(sh.Y1, std::max(y_done, g.oy[jb + 1] * s));
+        if (y_end > y_done) {
+            const size_t off = (size_t)(y_done - sh.Y0);
+            if (D.tiler->compose_rows(D.d_tout, k0, count, y_done, y_end, D.d_out + off * OW * ci, st) != cudaSuccess ||
+                cudaEventRecord(D.band[w], st) != cudaSuccess || cudaStreamWaitEvent(D.copy, D.band[w], 0) != cudaSuccess ||
+                cudaMemcpy2DAsync(host_rows + (ptrdiff_t)off * out->stride, out->stride, D.d_out + off * OW * ci, OW * ci,
+                                  OW * ci, (size_t)(y_end - y_done), cudaMemcpyDeviceToHost, D.copy) != cudaSuccess)
+                return fail(AJI_IMG_ERR, std::string("compose or download failed: ") + cudaGetErrorString(cudaGetLastError()));
+            y_done = y_end;
         }
         if (progress) {
-            if (cudaStreamSynchronize(st) != cudaSuccess) {
-                *why = "tile kernels failed";
-                return AJI_IMG_ERR;
-            }
-            if (progress(opaque, b0 + n, count)) {
-                *why = "cancelled";
-                return AJI_IMG_CANCELLED;
-            }
+            if (cudaStreamSynchronize(st) != cudaSuccess) return fail(AJI_IMG_ERR, "tile kernels failed");
+            if (progress(opaque, tiles_done, count)) return fail(AJI_IMG_CANCELLED, "cancelled");
         }
     }
-    uint8_t *host_rows = (uint8_t *)out->data + (ptrdiff_t)sh.Y0 * out->stride;
-    if (D.tiler->compose_rows(D.d_tout, k0, count, sh.Y0, sh.Y1, D.d_out, st) != cudaSuccess ||
-        cudaMemcpy2DAsync(host_rows, out->stride, D.d_out, OW * ci, OW * ci, rows, cudaMemcpyDeviceToHost, st) !=
-            cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess) {
-        *why = std::string("compose or download failed: ") + cudaGetErrorString(cudaGetLastError());
-        return AJI_IMG_ERR;
-    }
+    if (cudaStreamSynchronize(st) != cudaSuccess || cudaStreamSynchronize(D.copy) != cudaSuccess)
+        return fail(AJI_IMG_ERR, std::string("compose or download failed: ") + cudaGetErrorString(cudaGetLastError()));
     const int ks = ajib_kernel_status(1);
     if (ks != 0) {
         *why = "a native kernel timed out waiting on its pipeline (code " + std::to_string(ks) + ")";

@@ -99,6 +99,12 @@ int run_pre_packed(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const v
 int pack_model_input(const void *src, int H, int W, int unshuffle, bool in_norm, const float *mean, const float *scale,
                      int row_begin, int row_end, void *dst, cudaStream_t s);
 
+// ajib_conv3x3_launch_images with, for a depth-to-space output, dst_plane elements from one output
+// plane to the next (0: the dense [3][R*H][R*W]; else at least one dense plane), so that a batch
+// of tiles lands inside a larger stack of tiles (conv.cu).
+int conv3x3_launch_planes(const ajib_conv *op, const void *src, const void *resid, void *dst, int nimg, int img_h,
+                          int W, int row_begin, int row_end, void *stream, size_t dst_plane);
+
 class Executor {
 public:
     static std::unique_ptr<Executor> create(const Plan &plan, int in_w, int in_h, std::string *why);
@@ -125,8 +131,9 @@ public:
     int run(const void *in, void *out, int w, int h, cudaStream_t s) const;
     int run(const void *in, void *out, cudaStream_t s) const { return run(in, out, in_w(), in_h(), s); }
     // nimg images of img_h rows each, stacked along H (nimg * img_h <= in_h()), each convolved on
-    // its own: in [3][nimg * img_h][w], out [3][scale * nimg * img_h][scale * w].
-    int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s) const;
+    // its own: in [3][nimg * img_h][w], out [3][scale * nimg * img_h][scale * w], its planes
+    // out_plane elements apart when out_plane is not 0 (inside a larger stack of images).
+    int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, size_t out_plane = 0) const;
     // The head's input map, when the head reads the plain NCHW RGB model input (not
     // pixel-unshuffled): a producer that writes it (run_pre_packed) lets run_packed skip the
     // head's own pack launch. False for other heads.
@@ -159,8 +166,9 @@ private:
     };
     const void *ptr(int t, const void *in, void *out) const;
     int launch(const Step &st, const void *in, void *out, int nimg, int img_h, int w, int r0, int r1, cudaStream_t s,
-               bool packed = false) const;
-    int run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed) const;
+               bool packed = false, size_t out_plane = 0) const;
+    int run_steps(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, bool packed,
+                  size_t out_plane = 0) const;
     static constexpr int kProfRuns = 64;
     mutable std::vector<cudaEvent_t> prof_ev_;  // [kProfRuns][steps][2]
     mutable int prof_runs_ = 0;
