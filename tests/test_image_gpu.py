@@ -167,6 +167,47 @@ def test_even_tiles_of_changing_width():
     ctx.close()
 
 
+def test_waves_progress_and_strided_output():
+    """The image path's waves (tile rows composed and downloaded while later ones compute):
+    progress reports rise to the total and do not change the bytes; a host output with a row
+    stride wider than a row gets the same rows, its padding untouched; the result matches the
+    oracle tiler."""
+    import ajib
+    plan = ajib.compact_plan(24, c=24, body=2, scale=4)
+    path = _model_file(plan)
+    ctx = ajib.Image()
+    m = ctx.load(path, tile=32, overlap=8)
+    H, W = 150, 70  # seven tile rows: four waves of one or two
+    img = np.random.default_rng(9).integers(0, 256, size=(H, W, 3)).astype(np.uint8)
+    rc, plain = ctx.upscale(m, img, 4)
+    assert rc == 0, ctx.error()
+    seen = []
+
+    def watch(_, done, total):
+        seen.append((done, total))
+        return 0
+    rc, got = ctx.upscale(m, img, 4, progress=watch)
+    assert rc == 0, ctx.error()
+    assert np.array_equal(got, plain)
+    assert len(seen) >= 2 and all(t == seen[-1][1] for _, t in seen)
+    assert all(a < b for (a, _), (b, _) in zip(seen, seen[1:])) and seen[-1][0] == seen[-1][1]
+    # a padded host output (row stride 40 bytes wider than a row)
+    OW, OH = 4 * W, 4 * H
+    big = np.full((OH, OW * 3 + 40), 0xA5, np.uint8)
+    bi = ajib.img_buffer(np.ascontiguousarray(img))
+    bo = ajib.ImgBuffer()
+    bo.width, bo.height, bo.channels = OW, OH, 3
+    bo.stride = big.shape[1]
+    bo.data = big.ctypes.data
+    assert ajib.lib.aji_img_upscale(m, C.byref(bi), C.byref(bo), ajib.PROGRESS_FN(), None) == 0, ctx.error()
+    assert np.array_equal(big[:, :OW * 3].reshape(OH, OW, 3), plain)
+    assert (big[:, OW * 3:] == 0xA5).all()
+    want = oracle_upscale_tiled(lambda x: run_plan(plan, x.astype(np.float16).astype(np.float32)), 32, 32, 4, 8, img)
+    assert np.abs(plain.astype(int) - want.astype(int)).max() <= 3
+    ajib.lib.aji_img_release(C.byref(m))
+    ctx.close()
+
+
 def test_image_api_errors_and_progress():
     import ajib
     plan = ajib.compact_plan(22, c=24, body=2, scale=4)
