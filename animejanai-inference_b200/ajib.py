@@ -540,6 +540,8 @@ lib.aji_run_pre444.argtypes = [C.c_int, C.c_int, _vp, C.c_ssize_t, _vp, C.c_ssiz
 lib.aji_run_pre444.restype = C.c_int
 lib.ajib_plan_table.argtypes = [_vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float), C.c_int]
 lib.ajib_plan_table.restype = C.c_int
+lib.ajib_plan_kernel.argtypes = [_vp]
+lib.ajib_plan_kernel.restype = C.c_int
 lib.ajib_filter_table.argtypes = [C.c_int, C.c_int, C.c_double, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_float)]
 lib.ajib_filter_table.restype = C.c_int
 

@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -32,6 +33,15 @@ struct DevPass {
     int step2;  // start[i] = start[0] + 2 i for every output i (a 2:1 table)
 };
 
+// The streaming post pass's launch (k_post_roll): table offsets and weights (one set per
+// direction), chroma rows per block.
+struct PostRoll {
+    int w, h, cw, ch;
+    int oh, ov;  // start[0] of the horizontal and vertical tables (output i starts at o + 2 i)
+    int seg;     // chroma rows per block (a multiple of kPsG)
+    float wh[16], wv[16];
+};
+
 struct aji_plan {
     enum Kind { PRE, POST, RESIZE } kind;
     int format = 0, w = 0, h = 0;
@@ -39,6 +49,9 @@ struct aji_plan {
     FilterTable th, tv;  // host copies (tests)
     DevPass ph{}, pv{};
     int max_rows = 0, max_cols = 0;  // staged halo extents (checked against the kernel's capacity)
+    int roll_taps = 0;               // POST: k_post_roll serves the plan (its taps), else 0
+    PostRoll roll{};
+    dim3 roll_grid{};
 };
 
 extern "C" aji_csp aji_make_csp(int format, int matrix, int range)
@@ -436,6 +449,231 @@ __global__ void __launch_bounds__(256) k_post(const __half *src, int w, int h, D
     }
 }
 
+// ---------------- post, streaming form ----------------
+// For 2:1 tables whose outputs all share one set of weights (every table of a 4:2:0 post plan:
+// zimg's positions are exact in double, so each output's taps sit at the same offsets) on
+// frames whose width is a multiple of 8. The chroma plane is cut into strips of 64 columns (128
+// luma pixels) and each strip into runs of chroma rows; a block walks its run downwards, eight
+// chroma rows (sixteen luma rows) a step:
+//  - the next step's sixteen luma rows (3 planes x a 16-byte-aligned window of 152 columns
+//    around the strip's filter halo) are copied into a ring in shared memory by cp.async while
+//    this step computes;
+//  - each staged pixel's colour differences (u, v) are computed once and kept as a pair, split by
+//    column parity as in k_post; for the block's own pixels the quantised luma is stored, two
+//    pixels a store;
+//  - the horizontal pass turns each staged luma row into one row of 64 (u, v) pairs in a ring of
+//    32 rows, two adjacent outputs a thread (their taps overlap: 128-bit loads of the pairs);
+//  - the vertical pass reads the ring, two output rows a thread.
+// u and v share every tap position and weight, so each tap of both planes is one packed fp32 FMA
+// (__ffma2_rn: two IEEE fp32 FMAs, each rounded as __fmaf_rn), and so are the colour matrix and
+// the divisions of two adjacent pixels. Only the taps - 2 luma rows a run starts with are staged
+// twice. Every output keeps the reference's operation sequence (the expressions of k_post), so
+// the bytes are identical.
+constexpr int kPsCols = 64;              // chroma columns per strip
+constexpr int kPsG = 8;                  // chroma rows per step
+constexpr int kPsLW = 152;               // staged luma columns per row and plane (19 x 16 bytes)
+constexpr int kPsChunks = kPsLW / 8;     // 16-byte pieces per staged row and plane
+constexpr int kPsRaw = 32;               // luma rows in the staging ring (two steps)
+constexpr int kPsHR = 32;                // horizontally filtered rows in their ring
+constexpr int kPsNW = kPsLW / 2;         // (u, v) pairs per staged row of one parity
+
+struct PostRollSmem {
+    __half raw[kPsRaw][3][kPsLW];        // staged fp16 RGB rows
+    float2 d[2][2 * kPsG][kPsNW];        // [parity][row][word] ((b - Y) / db, (r - Y) / dr)
+    float2 hr[kPsHR][kPsCols];           // horizontally filtered (u, v)
+};
+static_assert(sizeof(PostRoll::wh) / sizeof(float) == kPostMaxTaps, "PostRoll holds the widest table");
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+// x / d for both lanes, as dev::div_by (fma(q0, -d, a) is fma(-q0, d, a): negation is exact)
+__device__ __forceinline__ float2 div_by2(float2 a, float d, float r)
+{
+    const float2 q0 = __fmul2_rn(a, f2(r));
+    const float2 e = __ffma2_rn(q0, f2(-d), a);
+    return __ffma2_rn(e, f2(r), q0);
+}
+
+// The sample bits quantize() gives for v = t * qdiv in the streaming kernel's formats (P010: 10
+// bits in the high bits of 16, qdiv 64; NV12: qdiv 1): round to nearest even with the result
+// clamped to [0, qmax] in one conversion (negative values and NaN give 0, as fmaxf(., 0) does),
+// then the shift that is the multiplication by qdiv.
+template <typename T>
+__device__ __forceinline__ uint32_t quant_bits(float t)
+{
+    uint32_t i;
+    asm("cvt.rni.u32.f32 %0, %1;" : "=r"(i) : "f"(t));
+    return sizeof(T) == 2 ? min(i, 1023u) << 6 : min(i, 255u);
+}
+
+template <typename T, int TAPS>
+__global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRoll pr, aji_csp csp, float qdiv,
+                                                      float qmax, uint8_t *yp, ptrdiff_t ys, uint8_t *uvp, ptrdiff_t uvs)
+{
+    extern __shared__ __align__(16) unsigned char ps_smem[];
+    PostRollSmem &sm = *reinterpret_cast<PostRollSmem *>(ps_smem);
+    constexpr int kPro = TAPS - 2;  // luma rows staged before the first step
+    const int tid = threadIdx.x;
+    const int w = pr.w, h = pr.h;
+    const int cx0 = blockIdx.x * kPsCols;
+    const int cya = blockIdx.y * pr.seg, cyb = min(cya + pr.seg, pr.ch);
+    const int cxl = min(cx0 + kPsCols, pr.cw) - 1;              // the strip's last real column
+    const int xlo = 2 * cx0 + pr.oh;                             // staged column 0
+    const int ncols = 2 * (cxl - cx0) + TAPS;                    // staged columns real outputs read
+    const int xa = xlo & ~7;                                     // the aligned window's first column
+    const int ylo = 2 * cya + pr.ov;                             // luma row of relative row 0
+    const int nsteps = (cyb - cya + kPsG - 1) / kPsG;
+    const size_t plane = (size_t)w * h;
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float db = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
+    const float dr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));
+    const float rdb = __frcp_rn(db), rdr = __frcp_rn(dr);
+    const float qinv = __frcp_rn(qdiv);
+    const int lx1 = min(2 * (cx0 + kPsCols), w);                 // the block's own luma columns end
+    const int ly0 = 2 * cya, ly1 = 2 * cyb;                      // and its own rows
+
+    // staging: piece (plane, 16-byte chunk) tid & 63 of rows tid >> 6, + 4, + 8, + 12
+    const int piece = tid & 63, sp = piece / kPsChunks, sj = piece - sp * kPsChunks;
+    const int scol = xa + 8 * sj;
+    const bool scopy = piece < 3 * kPsChunks && scol >= 0 && scol + 8 <= w;
+    const __half *sbase = src + (scopy ? sp * plane + scol : 0);
+    auto stage = [&](int rel0, int n) {
+        if (!scopy) return;
+        for (int r = tid >> 6; r < n; r += 4) {
+            const int rel = rel0 + r;
+            cp_async16(&sm.raw[rel & (kPsRaw - 1)][sp][8 * sj], sbase + (size_t)mirror_index(ylo + rel, h) * w);
+        }
+    };
+    // one staged pixel's colour differences (the halo columns outside the strip's own 128, and
+    // own columns past a partial strip's end): mirrored column
+    auto diff_px = [&](int r, int rel, int gx) {
+        const __half(*row)[kPsLW] = sm.raw[rel & (kPsRaw - 1)];
+        const int at = min(max(mirror_index(gx, w) - xa, 0), kPsLW - 1);
+        const float rr = __half2float(row[0][at]), gg = __half2float(row[1][at]), bb = __half2float(row[2][at]);
+        const float Y = __fmaf_rn(csp.kb, bb, __fmaf_rn(csp.kr, rr, __fmul_rn(kg, gg)));
+        const int c = gx - xlo;
+        sm.d[c & 1][r][c >> 1] = make_float2(dev::div_by(__fsub_rn(bb, Y), db, rdb), dev::div_by(__fsub_rn(rr, Y), dr, rdr));
+    };
+    // halo pixels: the columns [xlo, 2 cx0) and [2 cx0 + 128, xlo + ncols), one per thread and row
+    const int nhl = 2 * cx0 - xlo, nh = nhl + max(xlo + ncols - (2 * cx0 + 2 * kPsCols), 0);
+    const int hrow = nh ? tid / nh : 2 * kPsG, hidx = nh ? tid - hrow * nh : 0;
+    const int hgx = hidx < nhl ? xlo + hidx : 2 * cx0 + 2 * kPsCols + (hidx - nhl);
+    // own columns: the pair (2 cx0 + 2p, + 1), p = tid & 63, rows tid >> 6, + 4, + 8, + 12
+    const int pgx = 2 * cx0 + 2 * (tid & 63), pc = pgx - xlo;
+    const bool pfast = pgx + 1 < w;
+    auto differences = [&](int rel0, int n) {
+        for (int r = tid >> 6; r < n; r += 4) {
+            const int rel = rel0 + r, gy = ylo + rel;
+            if (pfast) {
+                const __half(*row)[kPsLW] = sm.raw[rel & (kPsRaw - 1)];
+                const int at = pgx - xa;
+                const float2 r2 = __half22float2(*reinterpret_cast<const __half2 *>(&row[0][at]));
+                const float2 g2 = __half22float2(*reinterpret_cast<const __half2 *>(&row[1][at]));
+                const float2 b2 = __half22float2(*reinterpret_cast<const __half2 *>(&row[2][at]));
+                const float2 Y = __ffma2_rn(f2(csp.kb), b2, __ffma2_rn(f2(csp.kr), r2, __fmul2_rn(f2(kg), g2)));
+                // b - Y as fma(Y, -1, b): the product is exact, so the one rounding is the subtraction's
+                const float2 U = div_by2(__ffma2_rn(Y, f2(-1.0f), b2), db, rdb);
+                const float2 V = div_by2(__ffma2_rn(Y, f2(-1.0f), r2), dr, rdr);
+                if (pc < ncols) sm.d[pc & 1][r][pc >> 1] = make_float2(U.x, V.x);
+                if (pc + 1 < ncols) sm.d[(pc + 1) & 1][r][(pc + 1) >> 1] = make_float2(U.y, V.y);
+                if (gy >= ly0 && gy < ly1 && pgx < lx1) {
+                    const float2 t = __fmul2_rn(__ffma2_rn(Y, f2(csp.yscale), f2(csp.yoff)), f2(qinv));
+                    const uint32_t q0 = quant_bits<T>(t.x), q1 = quant_bits<T>(t.y);
+                    T *yrow = reinterpret_cast<T *>(yp + (size_t)gy * ys);
+                    if constexpr (sizeof(T) == 2)
+                        *reinterpret_cast<uint32_t *>(yrow + pgx) = q0 | (q1 << 16);
+                    else
+                        *reinterpret_cast<uint16_t *>(yrow + pgx) = (uint16_t)(q0 | (q1 << 8));
+                }
+            } else {
+                if (pc < ncols) diff_px(r, rel, pgx);
+                if (pc + 1 < ncols) diff_px(r, rel, pgx + 1);
+            }
+        }
+        if (hrow < n) diff_px(hrow, rel0 + hrow, hgx);
+    };
+    // horizontal pass: outputs 2t and 2t + 1 of the strip (their taps start at staged columns 4t
+    // and 4t + 2: pairs 2t .. 2t + TAPS / 2 of each parity), rows tid >> 5 and + 8
+    constexpr int kW = (TAPS / 2 + 2) & ~1;  // pairs loaded per parity (two per 128-bit load)
+    const int ht = tid & 31;
+    auto horizontal = [&](int rel0, int n) {
+        for (int r = tid >> 5; r < n; r += 8) {
+            float2 e[kW], o[kW];
+#pragma unroll
+            for (int k = 0; k < kW; k += 2) {
+                const float4 pe = *reinterpret_cast<const float4 *>(&sm.d[0][r][2 * ht + k]);
+                const float4 po = *reinterpret_cast<const float4 *>(&sm.d[1][r][2 * ht + k]);
+                e[k] = make_float2(pe.x, pe.y), e[k + 1] = make_float2(pe.z, pe.w);
+                o[k] = make_float2(po.x, po.y), o[k + 1] = make_float2(po.z, po.w);
+            }
+            float2 a = make_float2(0.0f, 0.0f), b = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < TAPS; j++) {
+                a = __ffma2_rn(f2(pr.wh[j]), (j & 1) ? o[j >> 1] : e[j >> 1], a);
+                b = __ffma2_rn(f2(pr.wh[j]), (j & 1) ? o[(j >> 1) + 1] : e[(j >> 1) + 1], b);
+            }
+            *reinterpret_cast<float4 *>(&sm.hr[(rel0 + r) & (kPsHR - 1)][2 * ht]) = make_float4(a.x, a.y, b.x, b.y);
+        }
+    };
+
+    stage(0, kPro);
+    cp_async_commit();
+    stage(kPro, 2 * kPsG);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    differences(0, kPro);
+    __syncthreads();
+    horizontal(0, kPro);
+
+    // vertical pass: column tid & 63 of the strip, output rows 2 (tid >> 6) and + 1 of the step
+    const int vcol = tid & 63, vcx = cx0 + vcol, vrp = tid >> 6;
+    for (int s = 0; s < nsteps; s++) {
+        if (s + 1 < nsteps) stage(kPro + 2 * kPsG * (s + 1), 2 * kPsG);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        differences(kPro + 2 * kPsG * s, 2 * kPsG);
+        __syncthreads();
+        horizontal(kPro + 2 * kPsG * s, 2 * kPsG);
+        __syncthreads();
+        const int cyf = cya + kPsG * s + 2 * vrp;  // the first of this thread's two output rows
+        const int rel0 = 2 * (cyf - cya);
+        float2 v[2 + TAPS];
+#pragma unroll
+        for (int i = 0; i < 2 + TAPS; i++) v[i] = sm.hr[(rel0 + i) & (kPsHR - 1)][vcol];
+        if (vcx < pr.cw) {
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int j = 0; j < TAPS; j++) acc = __ffma2_rn(f2(pr.wv[j]), v[2 * k + j], acc);
+                if (cyf + k < cyb) {
+                    const float2 t = __fmul2_rn(__ffma2_rn(acc, f2(csp.cscale), f2(csp.coff)), f2(qinv));
+                    const uint32_t qu = quant_bits<T>(t.x), qv = quant_bits<T>(t.y);
+                    T *uvrow = reinterpret_cast<T *>(uvp + (size_t)(cyf + k) * uvs);
+                    if constexpr (sizeof(T) == 2)
+                        *reinterpret_cast<uint32_t *>(uvrow + 2 * vcx) = qu | (qv << 16);
+                    else
+                        *reinterpret_cast<uint16_t *>(uvrow + 2 * vcx) = (uint16_t)(qu | (qv << 8));
+                }
+            }
+        }
+    }
+}
+
 // ---------------- resize: fp16 NCHW RGB -> fp16 NCHW RGB (Spline36) ----------------
 // The reference's k_rs_h + k_rs_v (src/kernels.cu:322-354) in one kernel: a tile of 32 x 16
 // output pixels of one plane runs the horizontal pass for the (mirrored) source rows its
@@ -547,6 +785,67 @@ int span_of(const FilterTable &t, int tile)
     return m;
 }
 
+int host_mirror(int i, int n)
+{
+    i = i < 0 ? -i - 1 : i;
+    i = i >= n ? 2 * n - 1 - i : i;
+    return std::min(std::max(i, 0), n - 1);
+}
+
+// Whether k_post_roll serves a post plan: 2:1 tables of the same tap count (12 for Spline36, 4 for
+// bilinear) with one set of weights each and first taps in [2 - taps, 0] (so the staged rows and
+// columns reach every own pixel), a width that is a multiple of 8 (every 16-byte piece of a row is
+// wholly inside or outside the frame), and, for every strip, each mirrored column its real outputs
+// read inside its staged window. Sets the launch (PostRoll, grid) when it does.
+template <typename T, int TAPS>
+bool post_roll_setup(aji_plan *p)
+{
+    const FilterTable &th = p->th, &tv = p->tv;
+    if (th.taps != TAPS || tv.taps != TAPS || p->w % 8 != 0) return false;
+    for (const FilterTable *t : {&th, &tv}) {
+        if (t->start[0] > 0 || t->start[0] < 2 - TAPS) return false;
+        for (int i = 0; i < t->dst; i++) {
+            if (t->start[i] != t->start[0] + 2 * i) return false;
+            if (std::memcmp(&t->wt[(size_t)i * TAPS], t->wt.data(), TAPS * sizeof(float)) != 0) return false;
+        }
+    }
+    const int cw = p->w / 2, ch = p->h / 2;
+    for (int cx0 = 0; cx0 < cw; cx0 += kPsCols) {
+        const int cxl = std::min(cx0 + kPsCols, cw) - 1, xlo = 2 * cx0 + th.start[0], xa = xlo & ~7;
+        for (int gx = xlo; gx <= 2 * cxl + th.start[0] + TAPS - 1; gx++) {
+            const int mx = host_mirror(gx, p->w);
+            if (mx < xa || mx - xa >= kPsLW) return false;
+        }
+    }
+    // blocks: the strips times runs of chroma rows, about as many as fit on the device at once
+    int dev = 0, sms = 0, per_sm = 0;
+    const size_t smem = sizeof(PostRollSmem);
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(k_post_roll<T, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_post_roll<T, TAPS>, 256, smem) != cudaSuccess ||
+        per_sm < 1)
+        return false;
+    const int nstrips = (cw + kPsCols - 1) / kPsCols;
+    const int nseg = std::max(1, sms * per_sm / nstrips);
+    const int seg = ((ch + nseg - 1) / nseg + kPsG - 1) / kPsG * kPsG;
+    PostRoll &r = p->roll;
+    r.w = p->w;
+    r.h = p->h;
+    r.cw = cw;
+    r.ch = ch;
+    r.oh = th.start[0];
+    r.ov = tv.start[0];
+    r.seg = seg;
+    for (int j = 0; j < kPostMaxTaps; j++) {
+        r.wh[j] = j < TAPS ? th.wt[j] : 0.0f;
+        r.wv[j] = j < TAPS ? tv.wt[j] : 0.0f;
+    }
+    p->roll_grid = dim3(nstrips, (ch + seg - 1) / seg);
+    p->roll_taps = TAPS;
+    return true;
+}
+
 aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting, int filter)
 {
     if ((format != AJI_FMT_NV12 && format != AJI_FMT_P010) || w < 2 || h < 2 || (w & 1) || (h & 1)) return nullptr;
@@ -575,6 +874,11 @@ aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting,
         if (p->max_rows > kPostRows || p->max_cols > kPostCols || p->th.taps > kPostMaxTaps || p->tv.taps > kPostMaxTaps) {
             delete p;
             return nullptr;
+        }
+        if (format == AJI_FMT_P010) {
+            if (!post_roll_setup<uint16_t, 12>(p)) post_roll_setup<uint16_t, 4>(p);
+        } else {
+            if (!post_roll_setup<uint8_t, 12>(p)) post_roll_setup<uint8_t, 4>(p);
         }
     }
     if (!upload_pass(&p->ph, p->th) || !upload_pass(&p->pv, p->tv)) {
@@ -661,6 +965,12 @@ extern "C" int ajib_plan_table(const aji_plan *p, int which, int *start, float *
     return t.taps;
 }
 
+extern "C" int ajib_plan_kernel(const aji_plan *p)
+{
+    if (!p) return -1;
+    return p->roll_taps ? 1 : 0;
+}
+
 namespace {
 
 int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
@@ -723,6 +1033,23 @@ extern "C" int aji_run_post(aji_plan *p, const void *src_f16, const aji_csp *csp
     cudaStream_t s = (cudaStream_t)stream;
     const bool p010 = p->format == AJI_FMT_P010;
     const float qdiv = p010 ? 64.0f : 1.0f, qmax = p010 ? 1023.0f : 255.0f;
+    // the streaming kernel stores two samples at once and copies 16-byte pieces of the RGB rows
+    const size_t pair = p010 ? 4 : 2;
+    if (p->roll_taps && ((uintptr_t)src_f16 & 15) == 0 && ((uintptr_t)y_plane % pair) == 0 && (y_stride % pair) == 0 &&
+        ((uintptr_t)uv_plane % pair) == 0 && (uv_stride % pair) == 0 && y_stride > 0 && uv_stride > 0) {
+        const size_t smem = sizeof(PostRollSmem);
+        const __half *in = (const __half *)src_f16;
+        uint8_t *yo = (uint8_t *)y_plane, *uvo = (uint8_t *)uv_plane;
+        if (p010 && p->roll_taps == 12)
+            k_post_roll<uint16_t, 12><<<p->roll_grid, 256, smem, s>>>(in, p->roll, *csp, qdiv, qmax, yo, y_stride, uvo, uv_stride);
+        else if (p010)
+            k_post_roll<uint16_t, 4><<<p->roll_grid, 256, smem, s>>>(in, p->roll, *csp, qdiv, qmax, yo, y_stride, uvo, uv_stride);
+        else if (p->roll_taps == 12)
+            k_post_roll<uint8_t, 12><<<p->roll_grid, 256, smem, s>>>(in, p->roll, *csp, qdiv, qmax, yo, y_stride, uvo, uv_stride);
+        else
+            k_post_roll<uint8_t, 4><<<p->roll_grid, 256, smem, s>>>(in, p->roll, *csp, qdiv, qmax, yo, y_stride, uvo, uv_stride);
+        return (int)cudaGetLastError();
+    }
     cudaError_t e;
     if (p010) {
         e = cudaFuncSetAttribute(k_post<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -684,6 +684,9 @@ def run_kernel(args):
     from util import conv_weights, to_f16_bits, to_rows
     w_, h_ = (int(v) for v in args.size.split("x"))
     hbm_peak, tflops_burst, tflops_sus, peak_src = load_peaks()
+    if args.kernel in ("pre", "post"):
+        run_colour_kernel(args, torch.cuda.current_stream(), hbm_peak, peak_src)
+        return
     rng = np.random.default_rng(0)
     x = rng.uniform(-1, 1, size=(h_, w_, 64)).astype(np.float16).astype(np.float32)
     w, b, sl = conv_weights(rng, 64, 64, prelu=True)
@@ -759,6 +762,58 @@ def run_kernel(args):
                       "frac_of_burst_peak": tf / tflops_burst, "peak_source": peak_src,
                       "algorithmic_bytes": nbytes, "hbm_gbs_algorithmic": nbytes / (ms / 1000.0) / 1e9,
                       "frac_of_hbm_peak": nbytes / (ms / 1000.0) / 1e9 / hbm_peak}), flush=True)
+
+
+def run_colour_kernel(args, s, hbm_peak, peak_src):
+    """A colour pass alone, config 1's: `pre` converts a --size P010 frame (BT.709 limited, left
+    siting) to fp16 NCHW RGB, `post` converts the 2x model output (fp16 NCHW RGB at twice --size)
+    back to P010. K launches timed with CUDA events on the launching stream; algorithmic bytes are
+    the frame's planes read and written once."""
+    import torch
+    import ajib
+    w_, h_ = (int(v) for v in args.size.split("x"))
+    rng = np.random.default_rng(0)
+    fmt = 2
+    csp = ajib.lib.aji_make_csp(fmt, 2, 1)
+    if args.kernel == "pre":
+        p = ajib.lib.aji_pre_plan_create(fmt, w_, h_, 1, 0)
+        y = torch.from_numpy((rng.integers(64, 941, size=(h_, w_)).astype(np.uint16) << 6).view(np.int16)).cuda()
+        uv = torch.from_numpy((rng.integers(64, 961, size=(h_ // 2, w_)).astype(np.uint16) << 6).view(np.int16)).cuda()
+        out = torch.empty((3, h_, w_), dtype=torch.float16, device="cuda")
+
+        def launch():
+            return ajib.lib.aji_run_pre(p, y.data_ptr(), 2 * w_, uv.data_ptr(), 2 * w_, C.byref(csp), out.data_ptr(),
+                                        s.cuda_stream)
+        nbytes = 2 * w_ * h_ * 3 // 2 + 2 * 3 * w_ * h_
+    else:
+        w_, h_ = 2 * w_, 2 * h_
+        p = ajib.lib.aji_post_plan_create(fmt, w_, h_, 1, 0)
+        src = torch.from_numpy(rng.uniform(0, 1, size=(3, h_, w_)).astype(np.float16)).cuda()
+        y = torch.empty((h_, w_), dtype=torch.int16, device="cuda")
+        uv = torch.empty((h_ // 2, w_), dtype=torch.int16, device="cuda")
+
+        def launch():
+            return ajib.lib.aji_run_post(p, src.data_ptr(), C.byref(csp), y.data_ptr(), 2 * w_, uv.data_ptr(), 2 * w_,
+                                         s.cuda_stream)
+        nbytes = 2 * 3 * w_ * h_ + 2 * w_ * h_ * 3 // 2
+    assert p
+    form = ajib.lib.ajib_plan_kernel(p)
+    for _ in range(args.warmup):
+        assert launch() == 0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        assert launch() == 0
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ajib.lib.aji_plan_destroy(p)
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    print(json.dumps({"kernel": f"colour {args.kernel} ({'streaming' if form == 1 else 'tiled'} form)",
+                      "size": f"{w_}x{h_}", "ms_per_launch": ms, "algorithmic_bytes": nbytes,
+                      "hbm_gbs_algorithmic": gbs, "frac_of_hbm_peak": gbs / hbm_peak, "peak_source": peak_src}),
+          flush=True)
 
 
 IMG_TILE, IMG_OVERLAP = 512, 16
@@ -986,7 +1041,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "refgpu"])
-    ap.add_argument("--kernel", default=None, choices=[None, "conv64", "head", "head8", "tail"],
+    ap.add_argument("--kernel", default=None, choices=[None, "conv64", "head", "head8", "tail", "pre", "post"],
                     help="time the dominant kernel alone instead of the whole frame")
     ap.add_argument("--size", default="1920x1080")
     ap.add_argument("--bands", type=int, default=1)

@@ -181,6 +181,14 @@ AJIB_EXPORT int ajib_filter_table(int src, int dst, double shift, int filter, in
  * vertical. Copies up to max_dst entries of start and max_dst * taps weights; returns taps. */
 AJIB_EXPORT int ajib_plan_table(const aji_plan *p, int which, int *start, float *wt, int max_dst);
 
+/* Which kernel a colour plan's runs use (for tests and profiles; no reference counterpart, the
+ * reference has one kernel form): 1 = the streaming form (blocks walk column strips downwards,
+ * each source row staged once by asynchronous copies; chosen at plan creation when the filter
+ * tables are 2:1 with one set of weights and the width is a multiple of 8), 0 = the tiled form
+ * (serves every plan), -1 = bad plan. Each run checks its buffers' alignment again and uses the
+ * tiled form for unaligned buffers. */
+AJIB_EXPORT int ajib_plan_kernel(const aji_plan *p);
+
 /* ---- the image tiler on the GPU ----
  * Geometry of the reference's cover (src/core/tiling.cpp:17-103: tile origins flush to the far
  * edge or even tiles, reflect padding, linear blend ramps across a 16-pixel band at the centre of

@@ -39,23 +39,33 @@ def gpu_pre(fmt, y, uv, matrix, rng_, siting):
     return out.cpu().numpy().view(np.uint16)
 
 
-def gpu_post(fmt, rgb_bits, matrix, rng_, siting=1):
+def gpu_post(fmt, rgb_bits, matrix, rng_, siting=1, filt=0, pad=0, kernel=None):
+    """The post pass on the GPU; `pad` extra elements per output row (a strided frame), `kernel` the
+    form the plan must choose (ajib_plan_kernel: 1 streaming, 0 tiled; None: either)."""
     import ajib
     _, h, w = rgb_bits.shape
-    p = ajib.lib.aji_post_plan_create(fmt, w, h, siting, 0)
+    p = ajib.lib.aji_post_plan_create(fmt, w, h, siting, filt)
     assert p
+    if kernel is not None:
+        assert ajib.lib.ajib_plan_kernel(p) == kernel
     src = torch.from_numpy(rgb_bits.view(np.float16)).cuda()
     dt = torch.int16 if fmt == 2 else torch.uint8
-    oy = torch.empty((h, w), dtype=dt, device="cuda")
-    ouv = torch.empty((h // 2, w), dtype=dt, device="cuda")
+    # guard values around the planes: nothing outside the frame may be written
+    oy = torch.full((h, w + pad), 0x5A5A if fmt == 2 else 0x5A, dtype=torch.int32, device="cuda").to(dt)
+    ouv = torch.full((h // 2, w + pad), 0x5A5A if fmt == 2 else 0x5A, dtype=torch.int32, device="cuda").to(dt)
     es = 2 if fmt == 2 else 1
     csp = ajib.lib.aji_make_csp(fmt, matrix, rng_)
-    rc = ajib.lib.aji_run_post(p, src.data_ptr(), C.byref(csp), oy.data_ptr(), w * es, ouv.data_ptr(), w * es, None)
+    rc = ajib.lib.aji_run_post(p, src.data_ptr(), C.byref(csp), oy.data_ptr(), (w + pad) * es, ouv.data_ptr(),
+                               (w + pad) * es, None)
     torch.cuda.synchronize()
     ajib.lib.aji_plan_destroy(p)
     assert rc == 0
     npdt = np.uint16 if fmt == 2 else np.uint8
-    return oy.cpu().numpy().view(npdt), ouv.cpu().numpy().view(npdt)
+    y, uv = oy.cpu().numpy().view(npdt), ouv.cpu().numpy().view(npdt)
+    if pad:
+        guard = 0x5A5A if fmt == 2 else 0x5A
+        assert (y[:, w:] == guard).all() and (uv[:, w:] == guard).all(), "stores past the frame's width"
+    return y[:, :w], uv[:, :w]
 
 
 @pytest.mark.parametrize("fmt,matrix,rng_,siting,w,h", CASES)
@@ -73,6 +83,23 @@ def test_post_bit_exact(fmt, matrix, rng_, siting, w, h):
     rgb = rng.uniform(-0.1, 1.1, size=(3, h, w)).astype(np.float16).view(np.uint16)
     wy, wuv = oracle_post(fmt, rgb, matrix, rng_, siting)
     gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting)
+    assert np.array_equal(gy, wy), f"luma: {int((gy != wy).sum())} mismatches"
+    assert np.array_equal(guv, wuv), f"chroma: {int((guv != wuv).sum())} mismatches"
+
+
+# the streaming post kernel (k_post_roll): the config-1 4K output, partial strips, one-step runs,
+# every siting and matrix, both formats, bilinear tables (4 taps), strided outputs
+STREAM_CASES = [(2, 2, 1, 1, 0, 3840, 2160, 0), (1, 1, 2, 2, 0, 136, 72, 0), (2, 3, 2, 3, 0, 264, 40, 0),
+                (2, 2, 1, 1, 0, 1928, 16, 24), (1, 2, 1, 1, 0, 1280, 720, 8), (2, 1, 1, 2, 1, 520, 100, 0),
+                (1, 3, 2, 3, 1, 136, 18, 16), (2, 2, 2, 1, 0, 3848, 2, 0)]
+
+
+@pytest.mark.parametrize("fmt,matrix,rng_,siting,filt,w,h,pad", STREAM_CASES)
+def test_post_streaming_bit_exact(fmt, matrix, rng_, siting, filt, w, h, pad):
+    rng = np.random.default_rng(w * 5 + h + fmt + filt)
+    rgb = rng.uniform(-0.1, 1.1, size=(3, h, w)).astype(np.float16).view(np.uint16)
+    wy, wuv = oracle_post(fmt, rgb, matrix, rng_, siting, filt)
+    gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting, filt, pad=pad, kernel=1)
     assert np.array_equal(gy, wy), f"luma: {int((gy != wy).sum())} mismatches"
     assert np.array_equal(guv, wuv), f"chroma: {int((guv != wuv).sum())} mismatches"
 
