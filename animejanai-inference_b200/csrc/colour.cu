@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -42,6 +43,15 @@ struct PostRoll {
     float wh[16], wv[16];
 };
 
+// The streaming pre pass's launch (k_pre_roll): first taps and weights of outputs 0 and 1 of each
+// table (output 2k + i starts at s_i + k with output i's weights), luma rows per block.
+struct PreRoll {
+    int w, h, cw, ch;
+    int sh0, sh1, sv0, sv1;
+    int seg;  // a multiple of kPrG
+    float whe[8], who[8], wve[8], wvo[8];
+};
+
 struct aji_plan {
     enum Kind { PRE, POST, RESIZE } kind;
     int format = 0, w = 0, h = 0;
@@ -49,8 +59,9 @@ struct aji_plan {
     FilterTable th, tv;  // host copies (tests)
     DevPass ph{}, pv{};
     int max_rows = 0, max_cols = 0;  // staged halo extents (checked against the kernel's capacity)
-    int roll_taps = 0;               // POST: k_post_roll serves the plan (its taps), else 0
-    PostRoll roll{};
+    int roll_taps = 0;               // the streaming kernel serves the plan (its taps), else 0
+    PostRoll roll{};                 // POST: k_post_roll's launch
+    PreRoll proll{};                 // PRE: k_pre_roll's launch
     dim3 roll_grid{};
 };
 
@@ -674,6 +685,209 @@ __global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRol
     }
 }
 
+// ---------------- pre, streaming form ----------------
+// For 2x tables with period 2 (output 2k + 2 starts one source sample after output 2k and uses
+// its weights: every table of a 4:2:0 pre plan) on frames whose width is a multiple of 16. A
+// block owns a strip of 128 luma columns (one strip of the head conv's map) and a run of luma
+// rows, and walks it sixteen luma rows (eight chroma rows) a step:
+//  - the next step's luma rows and new chroma rows (a 16-byte-aligned window of 80 (u, v) pairs,
+//    mirrored at the frame's edges) are copied by cp.async while this step computes; each thread
+//    converts the chroma piece it copied to fp32 pairs;
+//  - the horizontal pass upsamples each new chroma row to the strip's 128 columns into a ring of
+//    16 rows, two adjacent outputs a thread;
+//  - the vertical pass, the colour matrix and the stores run two adjacent pixels a thread: their
+//    u and v, and the two pixels of each matrix step, are packed fp32 operations (__ffma2_rn and
+//    friends: two IEEE fp32 operations, each rounded as the scalar one), the output planes are
+//    written two pixels a store, and the head conv's map (PACK) one pixel chunk a store.
+// Only the taps - 1 (+1) chroma rows a run starts with are staged twice. Every output keeps the
+// reference's operation sequence (the expressions of k_pre), so the bytes are identical.
+constexpr int kPrCols = 128;  // luma columns per strip
+constexpr int kPrG = 16;      // luma rows per step (eight chroma rows)
+constexpr int kPrCW = 80;     // staged chroma (u, v) pairs per row
+constexpr int kPrCR = 16;     // chroma rows in the rings
+constexpr int kPrYR = 32;     // luma rows in the luma ring (two steps)
+
+template <typename T>
+struct PreRollSmem {
+    T uvraw[kPrCR][2 * kPrCW];   // staged (u, v) samples
+    float2 uvf[kPrCR][kPrCW];    // the same as fp32 pairs
+    float2 hr[kPrCR][kPrCols];   // horizontally upsampled (u, v) of each luma column
+    T yraw[kPrYR][kPrCols];      // staged luma rows
+};
+
+// Exact fp32 values of the two 16-bit samples in a word (low, high): 2^23 + v has v in its low
+// mantissa bits, and subtracting 2^23 is exact.
+__device__ __forceinline__ float2 u16x2_to_f2(uint32_t wd)
+{
+    return __fadd2_rn(make_float2(__uint_as_float(__byte_perm(wd, 0x4B00u, 0x5410)),
+                                  __uint_as_float(__byte_perm(wd, 0x4B00u, 0x5432))),
+                      f2(-8388608.0f));
+}
+// the same for bytes k and k + 1 of a word
+template <int K>
+__device__ __forceinline__ float2 u8x2_to_f2(uint32_t wd)
+{
+    return __fadd2_rn(make_float2(__uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7440 + K)),
+                                  __uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7440 + K + 1))),
+                      f2(-8388608.0f));
+}
+
+template <typename T, int TAPS, bool PACK>
+__global__ void __launch_bounds__(256, 4) k_pre_roll(const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
+                                                     PreRoll pr, aji_csp csp, __half *dst, PreMap pm)
+{
+    extern __shared__ __align__(16) unsigned char prs_smem[];
+    PreRollSmem<T> &sm = *reinterpret_cast<PreRollSmem<T> *>(prs_smem);
+    constexpr int kPpc = 16 / (2 * (int)sizeof(T));  // (u, v) pairs per 16-byte piece
+    constexpr int kUvChunks = kPrCW / kPpc;          // pieces per staged chroma row
+    constexpr int kYChunks = kPrCols * (int)sizeof(T) / 16;
+    const int tid = threadIdx.x;
+    const int w = pr.w, h = pr.h, cw = pr.cw, ch = pr.ch;
+    const int x0 = blockIdx.x * kPrCols;
+    const int ya = blockIdx.y * pr.seg, yb = min(ya + pr.seg, h);
+    const int mv = min(pr.sv0, pr.sv1);
+    const int ca = (x0 / 2 + min(pr.sh0, pr.sh1)) & ~(kPpc - 1);  // the window's first chroma column
+    const int cbase = ya / 2 + mv;                                 // chroma row of relative row 0
+    const int npro = TAPS - 1 + abs(pr.sv1 - pr.sv0);              // chroma rows staged before step 0
+    const int nsteps = (yb - ya + kPrG - 1) / kPrG;
+    const size_t plane = (size_t)w * h;
+
+    // chroma staging: piece tid % kUvChunks of new row tid / kUvChunks (eight rows a step)
+    const int ur = tid / kUvChunks, uj = tid - ur * kUvChunks, ucol = ca + uj * kPpc;
+    const bool uin = ucol >= 0 && ucol + kPpc <= cw;  // inside the frame: copied; else mirrored loads
+    auto stage_uv = [&](int crel0, int n) {
+        if (ur >= n || !uin) return;
+        const int crel = crel0 + ur;
+        const T *row = reinterpret_cast<const T *>(uvp + (size_t)mirror_index(cbase + crel, ch) * uvs);
+        cp_async16(&sm.uvraw[crel & (kPrCR - 1)][2 * uj * kPpc], row + 2 * ucol);
+    };
+    auto convert_uv = [&](int crel0, int n) {
+        if (ur >= n) return;
+        const int crel = crel0 + ur, slot = crel & (kPrCR - 1);
+        float2 f[kPpc];
+        if (uin) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(&sm.uvraw[slot][2 * uj * kPpc]);
+            if constexpr (sizeof(T) == 2) {
+                f[0] = u16x2_to_f2(q.x), f[1] = u16x2_to_f2(q.y), f[2] = u16x2_to_f2(q.z), f[3] = u16x2_to_f2(q.w);
+            } else {
+                f[0] = u8x2_to_f2<0>(q.x), f[1] = u8x2_to_f2<2>(q.x), f[2] = u8x2_to_f2<0>(q.y), f[3] = u8x2_to_f2<2>(q.y);
+                f[4] = u8x2_to_f2<0>(q.z), f[5] = u8x2_to_f2<2>(q.z), f[6] = u8x2_to_f2<0>(q.w), f[7] = u8x2_to_f2<2>(q.w);
+            }
+        } else {
+            const T *row = reinterpret_cast<const T *>(uvp + (size_t)mirror_index(cbase + crel, ch) * uvs);
+#pragma unroll
+            for (int k = 0; k < kPpc; k++) {
+                const int c = mirror_index(ucol + k, cw);
+                f[k] = make_float2((float)row[2 * c], (float)row[2 * c + 1]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kPpc; k += 2)
+            *reinterpret_cast<float4 *>(&sm.uvf[slot][uj * kPpc + k]) = make_float4(f[k].x, f[k].y, f[k + 1].x, f[k + 1].y);
+    };
+    // luma staging: piece tid % kYChunks of row tid / kYChunks of the step
+    const int yr = tid / kYChunks, yj = tid - yr * kYChunks;
+    const bool ycopy = yr < kPrG && x0 + (yj + 1) * (16 / (int)sizeof(T)) <= w;
+    auto stage_y = [&](int s) {
+        const int y = ya + kPrG * s + yr;
+        if (!ycopy || y >= h) return;
+        cp_async16(&sm.yraw[(kPrG * s + yr) & (kPrYR - 1)][yj * (16 / sizeof(T))],
+                   reinterpret_cast<const T *>(yp + (size_t)y * ys) + x0 + yj * (16 / sizeof(T)));
+    };
+    // horizontal pass: luma columns x0 + 2k and + 1 (k = tid & 63), new chroma rows tid >> 6, + 4
+    const int hk = tid & 63;
+    const int hbe = x0 / 2 + pr.sh0 + hk - ca, hbo = x0 / 2 + pr.sh1 + hk - ca;
+    auto horizontal = [&](int crel0, int n) {
+        for (int r = tid >> 6; r < n; r += 4) {
+            const int slot = (crel0 + r) & (kPrCR - 1);
+            const float2 *f = sm.uvf[slot];
+            float2 e = make_float2(0.0f, 0.0f), o = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < TAPS; j++) {
+                e = __ffma2_rn(f2(pr.whe[j]), f[hbe + j], e);
+                o = __ffma2_rn(f2(pr.who[j]), f[hbo + j], o);
+            }
+            *reinterpret_cast<float4 *>(&sm.hr[slot][2 * hk]) = make_float4(e.x, e.y, o.x, o.y);
+        }
+    };
+    // vertical pass + matrix + stores: pixels (x0 + 2k, + 1), k = tid & 63, luma rows
+    // 4 (tid >> 6) .. + 3 of the step
+    const int vk = tid & 63, vx = x0 + 2 * vk, vg = tid >> 6;
+    const float kg = __fsub_rn(__fsub_rn(1.0f, csp.kr), csp.kb);
+    const float cr = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kr));
+    const float cb = __fmul_rn(2.0f, __fsub_rn(1.0f, csp.kb));
+    const float gb = __fmul_rn(__fmul_rn(2.0f, csp.kb), __fsub_rn(1.0f, csp.kb));
+    const float gr = __fmul_rn(__fmul_rn(2.0f, csp.kr), __fsub_rn(1.0f, csp.kr));
+    const float ry = __frcp_rn(csp.yscale), rc = __frcp_rn(csp.cscale);
+    auto vertical = [&](int s) {
+        if (vx >= w) return;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int yrel = kPrG * s + 4 * vg + i, y = ya + yrel;
+            if (y >= yb) break;
+            const int c0 = ((i & 1) ? pr.sv1 : pr.sv0) - mv + (yrel >> 1);  // relative row of tap 0
+            float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < TAPS; j++) {
+                const float4 q = *reinterpret_cast<const float4 *>(&sm.hr[(c0 + j) & (kPrCR - 1)][2 * vk]);
+                const float wj = (i & 1) ? pr.wvo[j] : pr.wve[j];
+                a0 = __ffma2_rn(f2(wj), make_float2(q.x, q.y), a0);
+                a1 = __ffma2_rn(f2(wj), make_float2(q.z, q.w), a1);
+            }
+            float2 raw;
+            if constexpr (sizeof(T) == 2)
+                raw = u16x2_to_f2(*reinterpret_cast<const uint32_t *>(&sm.yraw[yrel & (kPrYR - 1)][2 * vk]));
+            else
+                raw = u8x2_to_f2<0>(*reinterpret_cast<const uint16_t *>(&sm.yraw[yrel & (kPrYR - 1)][2 * vk]));
+            const float2 Y = div_by2(__fadd2_rn(raw, f2(-csp.yoff)), csp.yscale, ry);
+            const float2 uv0 = div_by2(__fadd2_rn(a0, f2(-csp.coff)), csp.cscale, rc);  // (U, V) of pixel 0
+            const float2 uv1 = div_by2(__fadd2_rn(a1, f2(-csp.coff)), csp.cscale, rc);
+            const float2 U = make_float2(uv0.x, uv1.x), V = make_float2(uv0.y, uv1.y);
+            const float2 r = __ffma2_rn(f2(cr), V, Y);
+            const float2 b = __ffma2_rn(f2(cb), U, Y);
+            const float2 gn = __ffma2_rn(f2(gb), U, __fmul2_rn(f2(gr), V));
+            const float2 g = make_float2(__fsub_rn(Y.x, __fdiv_rn(gn.x, kg)), __fsub_rn(Y.y, __fdiv_rn(gn.y, kg)));
+            const __half2 hr = __floats2half2_rn(r.x, r.y), hg = __floats2half2_rn(g.x, g.y),
+                          hb = __floats2half2_rn(b.x, b.y);
+            const size_t idx = (size_t)y * w + vx;
+            *reinterpret_cast<__half2 *>(dst + idx) = hr;
+            *reinterpret_cast<__half2 *>(dst + plane + idx) = hg;
+            *reinterpret_cast<__half2 *>(dst + 2 * plane + idx) = hb;
+            if constexpr (PACK) {
+#pragma unroll
+                for (int p = 0; p < 2; p++) {
+                    float v[3] = {p ? __high2float(hr) : __low2float(hr), p ? __high2float(hg) : __low2float(hg),
+                                  p ? __high2float(hb) : __low2float(hb)};
+                    if (pm.in_norm) {
+#pragma unroll
+                        for (int c = 0; c < 3; c++) v[c] = (v[c] - pm.mean[c]) * pm.scale[c];
+                    }
+                    store_px(pm.map, y, vx + p, 0, pm.nstrips, 1,
+                             make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u));
+                }
+            }
+        }
+    };
+
+    stage_uv(0, npro);
+    cp_async_commit();
+    for (int s = -1;; s++) {
+        const int crel0 = s < 0 ? 0 : npro + (kPrG / 2) * s, n = s < 0 ? npro : kPrG / 2;
+        cp_async_wait<0>();
+        convert_uv(crel0, n);
+        __syncthreads();
+        if (s + 1 < nsteps) {
+            stage_uv(npro + (kPrG / 2) * (s + 1), kPrG / 2);
+            stage_y(s + 1);
+        }
+        cp_async_commit();
+        horizontal(crel0, n);
+        __syncthreads();
+        if (s >= 0) vertical(s);
+        if (s + 1 >= nsteps) break;
+    }
+}
+
 // ---------------- resize: fp16 NCHW RGB -> fp16 NCHW RGB (Spline36) ----------------
 // The reference's k_rs_h + k_rs_v (src/kernels.cu:322-354) in one kernel: a tile of 32 x 16
 // output pixels of one plane runs the horizontal pass for the (mirrored) source rows its
@@ -846,6 +1060,69 @@ bool post_roll_setup(aji_plan *p)
     return true;
 }
 
+// Whether k_pre_roll serves a pre plan: 2x tables of the same tap count (6 for Spline36, 2 for
+// bilinear) with period 2 (output i + 2 starts one sample after output i, with its weights) and
+// outputs 0 and 1 starting at most one sample apart, a width that is a multiple of 16 (every
+// 16-byte piece of a luma or chroma row is wholly inside or outside the frame), and every tap of
+// a strip's real outputs inside its staged window. Sets the launch (PreRoll, grid) when it does.
+template <typename T, int TAPS, bool PACK>
+bool pre_roll_occupancy(int *per_sm)
+{
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_pre_roll<T, TAPS, PACK>, 256,
+                                                         sizeof(PreRollSmem<T>)) == cudaSuccess;
+}
+
+template <typename T, int TAPS>
+bool pre_roll_setup(aji_plan *p)
+{
+    const FilterTable &th = p->th, &tv = p->tv;
+    if (th.taps != TAPS || tv.taps != TAPS || p->w % 16 != 0 || th.dst < 2 || tv.dst < 2) return false;
+    for (const FilterTable *t : {&th, &tv}) {
+        if (std::abs(t->start[1] - t->start[0]) > 1) return false;
+        for (int i = 2; i < t->dst; i++) {
+            if (t->start[i] != t->start[i - 2] + 1) return false;
+            if (std::memcmp(&t->wt[(size_t)i * TAPS], &t->wt[(size_t)(i - 2) * TAPS], TAPS * sizeof(float)) != 0)
+                return false;
+        }
+    }
+    constexpr int kPpc = 16 / (2 * (int)sizeof(T));
+    const int cw = p->w / 2, ch = p->h / 2;
+    for (int x0 = 0; x0 < p->w; x0 += kPrCols) {
+        const int ca = (x0 / 2 + std::min(th.start[0], th.start[1])) & ~(kPpc - 1);
+        for (int x = x0; x < std::min(x0 + kPrCols, p->w); x++)
+            if (th.start[x] < ca || th.start[x] + TAPS > ca + kPrCW) return false;
+    }
+    int dev = 0, sms = 0, per_sm = 0, per_sm_pack = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        !pre_roll_occupancy<T, TAPS, false>(&per_sm) || !pre_roll_occupancy<T, TAPS, true>(&per_sm_pack))
+        return false;
+    per_sm = std::min(per_sm, per_sm_pack);
+    if (per_sm < 1) return false;
+    const int nstrips = (p->w + kPrCols - 1) / kPrCols;
+    const int nseg = std::max(1, sms * per_sm / nstrips);
+    const int seg = ((p->h + nseg - 1) / nseg + kPrG - 1) / kPrG * kPrG;
+    PreRoll &r = p->proll;
+    r.w = p->w;
+    r.h = p->h;
+    r.cw = cw;
+    r.ch = ch;
+    r.sh0 = th.start[0];
+    r.sh1 = th.start[1];
+    r.sv0 = tv.start[0];
+    r.sv1 = tv.start[1];
+    r.seg = seg;
+    for (int j = 0; j < 8; j++) {
+        r.whe[j] = j < TAPS ? th.wt[j] : 0.0f;
+        r.who[j] = j < TAPS ? th.wt[TAPS + j] : 0.0f;
+        r.wve[j] = j < TAPS ? tv.wt[j] : 0.0f;
+        r.wvo[j] = j < TAPS ? tv.wt[TAPS + j] : 0.0f;
+    }
+    p->roll_grid = dim3(nstrips, (p->h + seg - 1) / seg);
+    p->roll_taps = TAPS;
+    return true;
+}
+
 aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting, int filter)
 {
     if ((format != AJI_FMT_NV12 && format != AJI_FMT_P010) || w < 2 || h < 2 || (w & 1) || (h & 1)) return nullptr;
@@ -865,6 +1142,11 @@ aji_plan *plan_create(aji_plan::Kind kind, int format, int w, int h, int siting,
         if (p->max_rows > kPreRows || p->th.taps > kPreMaxTaps || p->tv.taps > kPreMaxTaps) {
             delete p;
             return nullptr;
+        }
+        if (format == AJI_FMT_P010) {
+            if (!pre_roll_setup<uint16_t, 6>(p)) pre_roll_setup<uint16_t, 2>(p);
+        } else {
+            if (!pre_roll_setup<uint8_t, 6>(p)) pre_roll_setup<uint8_t, 2>(p);
         }
     } else {
         p->th = make_filter(w, cw, sx, filter);
@@ -973,6 +1255,17 @@ extern "C" int ajib_plan_kernel(const aji_plan *p)
 
 namespace {
 
+template <typename T, int TAPS>
+void launch_pre_roll(const aji_plan *p, const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
+                     const aji_csp &csp, __half *dst, const PreMap *pm, cudaStream_t s)
+{
+    const size_t smem = sizeof(PreRollSmem<T>);
+    if (pm)
+        k_pre_roll<T, TAPS, true><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, *pm);
+    else
+        k_pre_roll<T, TAPS, false><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, PreMap{});
+}
+
 int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
                const aji_csp *csp, void *dst_f16, const PreMap *pm, cudaStream_t s)
 {
@@ -980,6 +1273,17 @@ int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void 
     const PreMap m = pm ? *pm : PreMap{};
     const uint8_t *yp = (const uint8_t *)y_plane, *uvp = (const uint8_t *)uv_plane;
     __half *dst = (__half *)dst_f16;
+    // the streaming kernel copies 16-byte pieces of the luma and chroma rows and stores two
+    // pixels of each output plane at once
+    if (p->roll_taps && ((uintptr_t)y_plane & 15) == 0 && (y_stride & 15) == 0 && ((uintptr_t)uv_plane & 15) == 0 &&
+        (uv_stride & 15) == 0 && y_stride > 0 && uv_stride > 0 && ((uintptr_t)dst_f16 & 3) == 0) {
+        const bool p010 = p->format == AJI_FMT_P010;
+        if (p010 && p->roll_taps == 6) launch_pre_roll<uint16_t, 6>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
+        else if (p010) launch_pre_roll<uint16_t, 2>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
+        else if (p->roll_taps == 6) launch_pre_roll<uint8_t, 6>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
+        else launch_pre_roll<uint8_t, 2>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
+        return (int)cudaGetLastError();
+    }
     if (p->format == AJI_FMT_NV12) {
         if (pm)
             k_pre<uint8_t, true><<<grid, 256, 0, s>>>(yp, y_stride, uvp, uv_stride, p->ph, p->pv, *csp, dst, p->w, p->h, m);

@@ -23,11 +23,15 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a).view(np.int16 if a.dtype == np.uint16 else np.uint8)).cuda()
 
 
-def gpu_pre(fmt, y, uv, matrix, rng_, siting):
+def gpu_pre(fmt, y, uv, matrix, rng_, siting, filt=0, kernel=None):
+    """The pre pass on the GPU; `kernel` the form the plan must choose (ajib_plan_kernel: 1
+    streaming, 0 tiled; None: either)."""
     import ajib
     h, w = y.shape
-    p = ajib.lib.aji_pre_plan_create(fmt, w, h, siting, 0)
+    p = ajib.lib.aji_pre_plan_create(fmt, w, h, siting, filt)
     assert p
+    if kernel is not None:
+        assert ajib.lib.ajib_plan_kernel(p) == kernel
     dy, duv = dev(y), dev(uv)
     out = torch.empty((3, h, w), dtype=torch.float16, device="cuda")
     csp = ajib.lib.aji_make_csp(fmt, matrix, rng_)
@@ -85,6 +89,21 @@ def test_post_bit_exact(fmt, matrix, rng_, siting, w, h):
     gy, guv = gpu_post(fmt, rgb, matrix, rng_, siting)
     assert np.array_equal(gy, wy), f"luma: {int((gy != wy).sum())} mismatches"
     assert np.array_equal(guv, wuv), f"chroma: {int((guv != wuv).sum())} mismatches"
+
+
+# the streaming pre kernel (k_pre_roll): config 1's frame, config 4's (a partial last strip), every
+# siting, both formats, bilinear tables (2 taps), a two-row frame and a single-strip frame
+STREAM_PRE_CASES = [(2, 2, 1, 1, 0, 1920, 1080), (1, 1, 2, 2, 0, 1280, 720), (2, 3, 2, 3, 0, 960, 540),
+                    (1, 2, 1, 1, 1, 272, 18), (2, 1, 2, 2, 1, 144, 36), (2, 2, 1, 1, 0, 16, 2), (1, 3, 1, 3, 0, 48, 10)]
+
+
+@pytest.mark.parametrize("fmt,matrix,rng_,siting,filt,w,h", STREAM_PRE_CASES)
+def test_pre_streaming_bit_exact(fmt, matrix, rng_, siting, filt, w, h):
+    rng = np.random.default_rng(w * 11 + h + fmt + filt)
+    y, uv = yuv420_frame(rng, w, h, fmt)
+    want = oracle_pre(fmt, y, uv, matrix, rng_, siting, filt)
+    got = gpu_pre(fmt, y, uv, matrix, rng_, siting, filt, kernel=1)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} mismatches"
 
 
 # the streaming post kernel (k_post_roll): the config-1 4K output, partial strips, one-step runs,
