@@ -594,7 +594,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr bool bulk_in = IN == kInRows;  // strip-chunked input by bulk copies, else the NCHW RGB model input
     // strip-chunked input copied by its own warp (see the producer)
-    constexpr bool split_in = bulk_in && (EK == kEpiD2S || KPAD == 16);
+    constexpr bool split_in = bulk_in && (EK == kEpiD2S || KPAD <= 32);
     const int H = a.H, W = a.W;
 
     // ---- set-up
@@ -650,11 +650,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         // ================= producer: stages each input row and writes its MMA plan beside it,
         // after waiting for the accumulators the row starts to be free
         if constexpr (bulk_in) {
-            // Depth-to-space convs (skip rows to copy) and the head's narrow rows (a staged row's
-            // copy is 2 KB) split the producer in two warps on different SM sub-partitions,
-            // walking the same rows in the same stages: warp 0 copies, warp 2 plans. One warp doing
-            // both spends ~2000 cycles of its own a stage there, more than the stage's MMAs (tail
-            // 108 -> 96 us, head 86 -> 81 us); the body convs measured ~1 % slower split.
+            // Depth-to-space convs (skip rows to copy) and the narrow inputs (up to 32 channels:
+            // a staged row's copy is 2-8 KB) split the producer in two warps on different SM
+            // sub-partitions, walking the same rows in the same stages: warp 0 copies, warp 2
+            // plans. One warp doing both spends ~2000 cycles of its own a stage there, more than
+            // the stage's MMAs (tail 108 -> 96 us, head 86 -> 81 us, the 24-channel body 70.0 ->
+            // 64.0 us at 1080p); the 64-channel body measured the same split and the 48-channel
+            // one 6 % slower.
             if constexpr (split_in) {
                 if (warp == 0) {
                     // the copier: once a stage's buffer is free, one bulk copy per staged row, all

@@ -22,34 +22,59 @@ __device__ __forceinline__ int d_reflect(int i, int n)
     return i < n ? i : period - i;
 }
 
-// tile k0 + blockIdx.z: pixel (x, y) of the reflect-padded tile, as the net's fp16 input
-// v * (1/255) (the reference's k_extract, src/core/tiling_gpu.cu:71-96, 3-channel model)
+// tile k0 + blockIdx.z: pixels (x8 .. x8 + 7, y) of the reflect-padded tile, as the net's fp16
+// input v * (1/255) (the reference's k_extract, src/core/tiling_gpu.cu:71-96, 3-channel model).
+// Eight adjacent tile columns a thread: the row's reflection once, the columns' only where they
+// leave the image, and each plane's eight values as one 16-byte store where the tile width
+// allows (a warp reads 32 x 8 consecutive image pixels and writes 512 contiguous bytes a plane).
 __global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *ox, const int *oy, int nx, int tw,
                           int th, int k0, int n, float inv255, __half *dst)
 {
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, k = blockIdx.z;
-    if (x >= tw || y >= th) return;
+    const int x8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8, y = blockIdx.y * blockDim.y + threadIdx.y, k = blockIdx.z;
+    if (x8 >= tw || y >= th) return;
     const int t = k0 + k, i = t % nx, j = t / nx;
-    const uint8_t *p = img + ((size_t)d_reflect(oy[j] + y, H) * W + d_reflect(ox[i] + x, W)) * ci;
-    const size_t plane = (size_t)n * th * tw, at = ((size_t)k * th + y) * tw + x;
+    const uint8_t *row = img + (size_t)d_reflect(oy[j] + y, H) * W * ci;
+    const int gx0 = ox[i] + x8;
+    const size_t plane = (size_t)n * th * tw, at = ((size_t)k * th + y) * tw + x8;
     const int g = ci == 1;
+    const int nq = min(8, tw - x8);
+    const bool inside = gx0 >= 0 && gx0 + 8 <= W;
+    __half v[3][8];
 #pragma unroll
-    for (int c = 0; c < 3; c++) dst[c * plane + at] = __float2half_rn(__fmul_rn((float)p[g ? 0 : c], inv255));
+    for (int q = 0; q < 8; q++) {
+        const int gx = inside ? gx0 + q : d_reflect(gx0 + q, W);
+        const uint8_t *p = row + (size_t)gx * ci;
+#pragma unroll
+        for (int c = 0; c < 3; c++) v[c][q] = __float2half_rn(__fmul_rn((float)p[g ? 0 : c], inv255));
+    }
+    if (nq == 8 && (tw & 7) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+        for (int c = 0; c < 3; c++) *reinterpret_cast<uint4 *>(dst + c * plane + at) = *reinterpret_cast<const uint4 *>(v[c]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+            if (q < nq)
+#pragma unroll
+                for (int c = 0; c < 3; c++) dst[c * plane + at + q] = v[c][q];
+    }
 }
 
 // out[Y - Y0][X][c] = u8(sum over covering tiles, tile rows then tiles, of (wy * wx) * tile), each
 // multiply and add rounded on its own (the reference's k_blend + k_flush, tiling_gpu.cu:98-134),
-// for output rows [Y0, Y0 + gridDim.y * kComposeRows) clipped to Y1; the tiles buffer holds tiles
-// [k0, k0 + ntiles) of the image's row-major tile order. A block takes kComposeRows output rows
-// and 64 * kComposeQ columns; a thread four adjacent pixels in each of two rows, so its tile loads
-// for the two rows are in flight together. The block's rows' covering tile rows, tile-row offsets
-// and vertical weights are looked up once into shared memory; each (pixel, tile) weight is formed
-// once for all channels, and where four pixels share their covering tiles at a 4-aligned tile
-// column the tile values are read 8 bytes at a time and the 8-bit output written 4 bytes at a
-// time. Per pixel and channel the arithmetic is the same in either path.
+// for output rows [Y0, Y0 + gridDim.y * kComposeBlockRows) clipped to Y1; the tiles buffer holds
+// tiles [k0, k0 + ntiles) of the image's row-major tile order. A block takes kComposeBlockRows
+// output rows and 64 * kComposeQ columns: it looks its rows' covering tile rows, tile-row offsets
+// and vertical weights up once into shared memory, each thread looks its four adjacent columns'
+// covering tiles (and, on the vector path, their tile columns and weights) up once, and then
+// walks the rows, two at a time so that their tile loads are in flight together. (One block per
+// eight rows paid that chain of dependent table loads for every eight rows: 0.52 ms at config 2
+// against 0.46 with the loads hoisted and this.) Where four pixels share their covering tiles at a
+// 4-aligned tile column the tile values are read 8 bytes at a time and the 8-bit output written 4
+// bytes at a time. Per pixel and channel the arithmetic is the same in either path.
 constexpr int kComposeQ = 4;     // output pixels per thread and row
 constexpr int kComposeRows = 8;  // output rows per block (two per thread)
 constexpr int kComposeMaxT = 8;  // tile rows covering one output row that the table holds
+constexpr int kComposeBlockRows = 128;  // output rows per block (its row table is filled once)
 
 __device__ __forceinline__ uint8_t to_u8(float b)
 {
@@ -137,36 +162,101 @@ __device__ __forceinline__ void compose_store(const float (&b)[3][kComposeQ], ui
     }
 }
 
-__global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
+// The vector path where every pixel of the thread's columns and rows is covered by at most two
+// tiles along each axis (every cover whose overlap is under half a tile, config 2's included):
+// the thread's horizontal weights are loaded once, and all its tile loads for both rows (up to
+// 2 rows x 2 tile rows x 2 tiles x 3 channels of 4 pixels) are issued before any is summed, so
+// they are in flight together; each pixel's sum then runs in compose_row's order (tile rows, then
+// tiles, each multiply and add rounded on its own).
+constexpr int kComposeF = 2;
+
+__device__ __forceinline__ void compose_pair_f2(float (&ba)[3][kComposeQ], float (&bb)[3][kComposeQ], const __half *tiles,
+                                                size_t plane, int k0, int toh, int tow, int nx, int i0, int ni,
+                                                const int (&u)[kComposeF], const float4 (&wq)[kComposeF],
+                                                const int (&nj)[2], const int *j0, const int *v0, const float *wv0,
+                                                const int *j1, const int *v1, const float *wv1)
+{
+    uint2 t[2][kComposeF][kComposeF][3];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int *jr = r ? j1 : j0, *vr = r ? v1 : v0;
+#pragma unroll
+        for (int jj = 0; jj < kComposeF; jj++) {
+#pragma unroll
+            for (int ii = 0; ii < kComposeF; ii++) {
+                if (jj < nj[r] && ii < ni) {
+                    const int k = jr[jj] * nx + i0 + ii - k0;
+                    const size_t at = ((size_t)k * toh + vr[jj]) * tow + u[ii];
+#pragma unroll
+                    for (int c = 0; c < 3; c++) t[r][jj][ii][c] = __ldg(reinterpret_cast<const uint2 *>(tiles + c * plane + at));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        float(&b)[3][kComposeQ] = r ? bb : ba;
+        const float *wvr = r ? wv1 : wv0;
+#pragma unroll
+        for (int c = 0; c < 3; c++)
+#pragma unroll
+            for (int q = 0; q < kComposeQ; q++) b[c][q] = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < kComposeF; jj++) {
+            if (jj >= nj[r]) break;
+            const float wv = wvr[jj];
+#pragma unroll
+            for (int ii = 0; ii < kComposeF; ii++) {
+                if (ii >= ni) break;
+                const float w[4] = {__fmul_rn(wv, wq[ii].x), __fmul_rn(wv, wq[ii].y), __fmul_rn(wv, wq[ii].z),
+                                    __fmul_rn(wv, wq[ii].w)};
+#pragma unroll
+                for (int c = 0; c < 3; c++) {
+                    const uint2 raw = t[r][jj][ii][c];
+                    const float2 t01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                    const float2 t23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                    b[c][0] = __fadd_rn(b[c][0], __fmul_rn(w[0], t01.x));
+                    b[c][1] = __fadd_rn(b[c][1], __fmul_rn(w[1], t01.y));
+                    b[c][2] = __fadd_rn(b[c][2], __fmul_rn(w[2], t23.x));
+                    b[c][3] = __fadd_rn(b[c][3], __fmul_rn(w[3], t23.y));
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) k_compose(const __half *tiles, int k0, int ntiles, int toh, int tow, int nx,
                                                  const int *ox, const int *oy, const float *wx, const float *wy, int cols,
                                                  int rows, const int2 *cx, const int2 *cy, int s, int co, int OW, int Y0,
                                                  int Y1, uint8_t *out)
 {
-    // the block's rows: covering tile rows, their row offsets and vertical weights
-    __shared__ int s_nj[kComposeRows], s_j[kComposeRows][kComposeMaxT], s_v[kComposeRows][kComposeMaxT];
-    __shared__ float s_wv[kComposeRows][kComposeMaxT];
-    const int Yb = Y0 + blockIdx.y * kComposeRows;
+    // the block's rows: covering tile rows, their row offsets and vertical weights, looked up once
+    __shared__ int s_nj[kComposeBlockRows], s_j[kComposeBlockRows][kComposeMaxT], s_v[kComposeBlockRows][kComposeMaxT];
+    __shared__ float s_wv[kComposeBlockRows][kComposeMaxT];
+    const int Yblk = Y0 + blockIdx.y * kComposeBlockRows;
     const int tid = threadIdx.y * blockDim.x + threadIdx.x;
-    if (tid < kComposeRows) {
-        const int Y = Yb + tid;
+    for (int r = tid; r < kComposeBlockRows; r += blockDim.x * blockDim.y) {
+        const int Y = Yblk + r;
         int n = 0;
         if (Y < Y1) {
             const int2 ry = cy[Y];
             n = min(ry.y, kComposeMaxT);
             for (int jj = 0; jj < n; jj++) {
                 const int j = ry.x + jj, v = Y - oy[j] * s;
-                s_j[tid][jj] = j;
-                s_v[tid][jj] = v;
-                s_wv[tid][jj] = wy[(size_t)j * rows + v];
+                s_j[r][jj] = j;
+                s_v[r][jj] = v;
+                s_wv[r][jj] = wy[(size_t)j * rows + v];
             }
         }
-        s_nj[tid] = n;
+        s_nj[r] = n;
     }
     __syncthreads();
     const int X0 = (blockIdx.x * blockDim.x + threadIdx.x) * kComposeQ;
     if (X0 >= OW) return;
     const size_t plane = (size_t)ntiles * toh * tow;
     const int nq = min(kComposeQ, OW - X0);
+    // the thread's columns: their covering tiles, and for the vector path their tile columns and
+    // horizontal weights (the same for every row)
     int2 rx[kComposeQ];
     bool same = nq == kComposeQ;
 #pragma unroll
@@ -180,18 +270,39 @@ __global__ void __launch_bounds__(256, 4) k_compose(const __half *tiles, int k0,
     if (same) {
         for (int ii = 0; ii < rx[0].y; ii++) same = same && (((X0 - __ldg(ox + rx[0].x + ii) * s) & 3) == 0);
     }
-    // rows ty and ty + blockDim.y of the block
-    const int ra = threadIdx.y, rb = threadIdx.y + blockDim.y;
-    const int Ya = Yb + ra, Yb2 = Yb + rb;
-    float ba[3][kComposeQ], bb[3][kComposeQ];
-    if (Ya < Y1)
-        compose_row(ba, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, s_nj[ra], s_j[ra], s_v[ra],
-                    s_wv[ra]);
-    if (Yb2 < Y1)
-        compose_row(bb, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, s_nj[rb], s_j[rb], s_v[rb],
-                    s_wv[rb]);
-    if (Ya < Y1) compose_store(ba, out + ((size_t)(Ya - Y0) * OW + X0) * co, nq, co, OW);
-    if (Yb2 < Y1) compose_store(bb, out + ((size_t)(Yb2 - Y0) * OW + X0) * co, nq, co, OW);
+    const bool fast = same && co == 3 && rx[0].y <= kComposeF;
+    int u[kComposeF];
+    float4 wq[kComposeF];
+#pragma unroll
+    for (int ii = 0; ii < kComposeF; ii++) {
+        u[ii] = 0;
+        wq[ii] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (fast && ii < rx[0].y) {
+            u[ii] = X0 - __ldg(ox + rx[0].x + ii) * s;
+            wq[ii] = __ldg(reinterpret_cast<const float4 *>(wx + (size_t)(rx[0].x + ii) * cols + u[ii]));
+        }
+    }
+    // rows g + ty and g + ty + blockDim.y of each group of kComposeRows
+    for (int g = 0; g < kComposeBlockRows; g += kComposeRows) {
+        const int ra = g + threadIdx.y, rb = g + threadIdx.y + blockDim.y;
+        const int Ya = Yblk + ra, Yb2 = Yblk + rb;
+        if (Ya >= Y1) break;
+        float ba[3][kComposeQ], bb[3][kComposeQ];
+        const int nja = s_nj[ra], njb = Yb2 < Y1 ? s_nj[rb] : 0;
+        if (fast && nja <= kComposeF && njb <= kComposeF) {
+            const int nj[2] = {nja, njb};
+            compose_pair_f2(ba, bb, tiles, plane, k0, toh, tow, nx, rx[0].x, rx[0].y, u, wq, nj, s_j[ra], s_v[ra],
+                            s_wv[ra], s_j[rb], s_v[rb], s_wv[rb]);
+        } else {
+            compose_row(ba, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, nja, s_j[ra], s_v[ra],
+                        s_wv[ra]);
+            if (Yb2 < Y1)
+                compose_row(bb, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, njb, s_j[rb],
+                            s_v[rb], s_wv[rb]);
+        }
+        compose_store(ba, out + ((size_t)(Ya - Y0) * OW + X0) * co, nq, co, OW);
+        if (Yb2 < Y1) compose_store(bb, out + ((size_t)(Yb2 - Y0) * OW + X0) * co, nq, co, OW);
+    }
 }
 
 // the most tiles covering one output coordinate (the compose kernel holds kComposeMaxT a row)
@@ -255,7 +366,7 @@ bool DeviceTiler::init(const TileGeometry &g)
 cudaError_t DeviceTiler::extract(const uint8_t *img, int k0, int n, void *dst, cudaStream_t s) const
 {
     if (n < 1) return cudaSuccess;
-    const dim3 block(32, 8), grid((g_.tw + 31) / 32, (g_.th + 7) / 8, n);
+    const dim3 block(32, 8), grid((g_.tw + 255) / 256, (g_.th + 7) / 8, n);
     k_extract<<<grid, block, 0, s>>>(img, g_.W, g_.H, g_.ci, d_ox_, d_oy_, g_.nx(), g_.tw, g_.th, k0, n, 1.0f / 255.0f,
                                      (__half *)dst);
     return cudaGetLastError();
@@ -273,7 +384,7 @@ cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int
     if (Y1 <= Y0) return cudaSuccess;
     const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
     const int px = 64 * kComposeQ;  // output columns per block
-    const dim3 block(64, kComposeRows / 2), grid((OW + px - 1) / px, (Y1 - Y0 + kComposeRows - 1) / kComposeRows);
+    const dim3 block(64, kComposeRows / 2), grid((OW + px - 1) / px, (Y1 - Y0 + kComposeBlockRows - 1) / kComposeBlockRows);
     k_compose<<<grid, block, 0, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
                                       d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
     return cudaGetLastError();
@@ -372,7 +483,7 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
         }
         const int OW = g.W * s, OH = g.H * s;
         const dim3 block(64, kComposeRows / 2),
-            grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + kComposeRows - 1) / kComposeRows);
+            grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + kComposeBlockRows - 1) / kComposeBlockRows);
         k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
                                           (const int *)(base + o_ox), (const int *)(base + o_oy),
                                           (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,

@@ -705,6 +705,20 @@ def run_kernel(args):
             return ref.ref_conv_launch(hw, 0, 2, 0, 0, 64, 64, src.data_ptr(), None, dst.data_ptr(), h_, w_, -1,
                                        s.cuda_stream)
         kname = "reference k_conv3x3<64,64,...,PReLU> (mma.sync m16n8k16 fp16-acc) recompiled for sm_100a"
+    elif args.kernel in ("conv48", "conv24"):
+        # the SPAN (48) and SuperUltraCompact (24) body convs: same-width 3x3 with --act
+        cw = int(args.kernel[4:])
+        wk, bk, sk = conv_weights(rng, cw, cw, prelu=True)
+        wt = ajib.Weights(to_f16_bits(wk), bk, sk)
+        op = ajib.conv_op(wt, act={"none": ajib.ACT_NONE, "relu": ajib.ACT_RELU, "prelu": ajib.ACT_PRELU,
+                                    "silu": ajib.ACT_SILU}[args.act])
+        xc = rng.uniform(-1, 1, size=(h_, w_, cw)).astype(np.float16).astype(np.float32)
+        src = torch.from_numpy(to_rows(xc).astype(np.float16)).cuda()
+        dst = torch.zeros_like(src)
+
+        def launch():
+            return ajib.conv3x3(op, src.data_ptr(), 0, dst.data_ptr(), h_, w_, 0, 0, s.cuda_stream)
+        kname = f"k_conv3x3_tc<{cw},{cw}> {args.act} (tcgen05, fp32 TMEM accumulation)"
     elif args.kernel == "conv64":
         wt = ajib.Weights(to_f16_bits(w), b, sl)
         op = ajib.conv_op(wt, act=ajib.ACT_PRELU)
@@ -753,6 +767,9 @@ def run_kernel(args):
     ms = e0.elapsed_time(e1) / args.steps
     if args.kernel in ("conv64", None) or args.impl == "refgpu":
         flops, nbytes = 2.0 * 9 * 64 * 64 * w_ * h_, 2 * 2 * 64 * w_ * h_
+    elif args.kernel in ("conv48", "conv24"):
+        cw = int(args.kernel[4:])
+        flops, nbytes = 2.0 * 9 * cw * cw * w_ * h_, 2 * 2 * cw * w_ * h_
     elif args.kernel in ("head", "head8"):
         flops, nbytes = 2.0 * 9 * 3 * 64 * w_ * h_, (3 * 2 + 64 * 2) * w_ * h_
     else:
@@ -1041,9 +1058,12 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "refgpu"])
-    ap.add_argument("--kernel", default=None, choices=[None, "conv64", "head", "head8", "tail", "pre", "post"],
+    ap.add_argument("--kernel", default=None,
+                    choices=[None, "conv64", "conv48", "conv24", "head", "head8", "tail", "pre", "post"],
                     help="time the dominant kernel alone instead of the whole frame")
     ap.add_argument("--size", default="1920x1080")
+    ap.add_argument("--act", default="prelu", choices=["none", "relu", "prelu", "silu"],
+                    help="--kernel conv48 / conv24: the activation")
     ap.add_argument("--bands", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true",
