@@ -212,7 +212,7 @@ PairFn find_pair_fn(int kpad, int npad, int ek)
 template <int KPAD, int NPAD, int EK, int IN>
 cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 {
-    using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt, EK == kEpiD2S>;
+    using Cf = ConvCfg<KPAD, NPAD, EK == kEpiAtt, EK == kEpiD2S, EK == kEpiGate>;
     // at least half the SM's shared memory, so one CTA holds an SM and its whole TMEM (a second
     // CTA on the SM would only wait in its TMEM allocation)
     constexpr int smem = Cf::SMEM > 117 * 1024 ? Cf::SMEM : 117 * 1024;

@@ -121,7 +121,9 @@ __device__ __forceinline__ void segment_rows(int ya, int yb, int img_h, int &r0,
     r1 = (yb % img_h == 0) ? yb - 1 : yb;
 }
 
-template <int KPAD, int NPAD, bool ATT = false, bool SKIP = false>
+constexpr int kGateSlots = 3;  // SPAN gate: block-input rows staged ahead of the epilogue
+
+template <int KPAD, int NPAD, bool ATT = false, bool SKIP = false, bool GATE = false>
 struct ConvCfg {
     static_assert(KPAD % 16 == 0 && NPAD % 16 == 0 && KPAD <= 64 && NPAD <= 64, "padded channel counts");
     static constexpr int KC = KPAD / 8;       // 8-channel chunks per pixel
@@ -146,18 +148,24 @@ struct ConvCfg {
     // copied in by the producer's bulk copies
     static constexpr int SKIP_ROW = 3 * kTileM * 2;
     static constexpr int SKIP_BYTES = SKIP ? S * SKIP_ROW : 0;
-    static constexpr int FIXED = AOFF + ATT_BYTES + SKIP_BYTES + 3 * 64 * 4 + 1024 + 1024 + 1024;
+    // SPAN gate: the block input's (row, strip) block of each of kGateSlots outputs, halo columns
+    // included ([NPAD/8][130][8] fp16), copied in by the gate warp
+    static constexpr int GATE_ROW = NPAD / 8 * kHalo * 16;
+    static constexpr int GATE_BYTES = GATE ? kGateSlots * GATE_ROW : 0;
+    static constexpr int FIXED = AOFF + ATT_BYTES + SKIP_BYTES + GATE_BYTES + 3 * 64 * 4 + 1024 + 1024 + 1024;
     static constexpr int NS_FIT = (kMaxSmem - FIXED) / STAGE;
     static constexpr int NS = NS_FIT > 6 ? 6 : NS_FIT;  // stages of RP rows: as many as fit, up to 6
     static_assert(NS >= 2 && S >= 4, "pipeline depth");
     static constexpr int ATOFF = AOFF + NS * STAGE;  // attention B, then A tiles 0 and 1
     static constexpr int SKOFF = ATOFF + ATT_BYTES;  // skip rows [S][3][128] fp16
-    static constexpr int POFF = SKOFF + SKIP_BYTES;  // bias[64], slope[64], attention bias[64] floats
-    // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S], landed[NS]
+    static constexpr int GOFF = SKOFF + SKIP_BYTES;  // gate rows [kGateSlots][NPAD/8][130][8] fp16
+    static constexpr int POFF = GOFF + GATE_BYTES;   // bias[64], slope[64], attention bias[64] floats
+    // mbarriers: full[NS], empty[NS], accf[S], acce[S], wbar, dbar, attf[2], skipf[S], landed[NS],
+    // the TMEM address word, gatef[kGateSlots], gatee[kGateSlots]
     static constexpr int BOFF = POFF + 3 * 64 * 4;
     static constexpr int PLOFF = BOFF + 1024;       // RowPlan per staged row
     static constexpr int SMEM = BOFF + 1024 + 1024 + 1024;  // + alignment slack for the base
-    static_assert((3 * NS + 3 * S + 4) * 8 + 8 <= 1024 && NS * RP * 48 <= 1024, "barrier and plan area");
+    static_assert((3 * NS + 3 * S + 5 + 2 * kGateSlots) * 8 <= 1024 && NS * RP * 48 <= 1024, "barrier and plan area");
     static_assert(SMEM <= kMaxSmem, "shared memory budget");
 };
 
@@ -576,7 +584,8 @@ template <int KPAD, int NPAD, int EK, int IN>
 __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ ConvDev a)
 {
     constexpr bool ATT = EK == kEpiAtt;
-    using C = ConvCfg<KPAD, NPAD, ATT, EK == kEpiD2S>;
+    constexpr bool GATE = EK == kEpiGate;
+    using C = ConvCfg<KPAD, NPAD, ATT, EK == kEpiD2S, GATE>;
     constexpr int S = C::S;
     extern __shared__ unsigned char smraw[];
     // 1024-byte aligned base (bulk-copy destinations and descriptor bases)
@@ -589,6 +598,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                    acce0 = accf0 + 8 * S, wbar = acce0 + 8 * S, dbar = wbar + 8, attf0 = dbar + 8,
                    skipf0 = attf0 + 16, landed0 = skipf0 + 8 * S;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 3 * C::NS + 3 * S + 4);
+    const uint32_t gatef0 = dev::smem_u32(bars + 3 * C::NS + 3 * S + 5), gatee0 = gatef0 + 8 * kGateSlots;
     RowPlan *plans = reinterpret_cast<RowPlan *>(sm + C::PLOFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -614,6 +624,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         dev::mbar_init(dbar, 1);
         dev::mbar_init(attf0, 1);
         dev::mbar_init(attf0 + 8, 1);
+        if (GATE) {
+            for (int g = 0; g < kGateSlots; g++) {
+                dev::mbar_init(gatef0 + 8 * g, 1);
+                dev::mbar_init(gatee0 + 8 * g, kEpiWarps);
+            }
+        }
         dev::fence_mbar_init();
         // the weights were uploaded long before any kernel ran: fetch them before the wait below
         const uint32_t att_bytes = ATT ? (uint32_t)(a.att_kpad * a.att_npad * 2) : 0u;
@@ -649,7 +665,39 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     if (warp < kProdWarps) {
         // ================= producer: stages each input row and writes its MMA plan beside it,
         // after waiting for the accumulators the row starts to be free
+        static_assert(!GATE || bulk_in, "the SPAN gate reads strip-chunked maps");
         if constexpr (bulk_in) {
+            if constexpr (GATE) {
+                if (warp == 3) {
+                    // the gate warp: the block input's (row, strip) block of each output, in the
+                    // epilogue's output order, into a ring of kGateSlots slots (one bulk copy each,
+                    // completing gatef[slot]); a slot is reused once the epilogue's eight warps have
+                    // read it (gatee). Reading the block input from global memory in the epilogue
+                    // left each row waiting on DRAM latency (gate conv 157 us against 94 for the
+                    // activation conv at 1080p, 48 channels).
+                    const int ccout = a.cout / 8;
+                    const uint32_t bytes = (uint32_t)ccout * kHalo * 16;
+                    SegIter gseg(W, a.row_begin, a.row_end);
+                    uint32_t ot = 0;
+                    int strip, ya, yb;
+                    bool ok = true;
+                    while (ok && gseg.next(strip, ya, yb)) {
+                        for (int o = ya; o < yb; o++, ot++) {
+                            const uint32_t g = ot % kGateSlots, ph = (ot / kGateSlots) & 1u;
+                            if (!(ok = dev::mbar_wait_warp(gatee0 + 8 * g, ph ^ 1u, a.err, kErrProdEmpty))) break;
+                            if (lane == 0) {
+                                dev::mbar_arrive_expect_tx(gatef0 + 8 * g, bytes);
+                                dev::bulk_load(sbase + C::GOFF + g * C::GATE_ROW,
+                                               a.resid + map_at(o, strip, 0, 0, a.nstrips, ccout), bytes, gatef0 + 8 * g);
+                            }
+                            __syncwarp();
+                        }
+                    }
+                    // on an error exit, let the last copy land before the CTA can leave
+                    if (!ok && ot > 0 && lane == 0)
+                        dev::mbar_wait(gatef0 + 8 * ((ot - 1) % kGateSlots), ((ot - 1) / kGateSlots) & 1u, nullptr, 0);
+                }
+            }
             // Depth-to-space convs (skip rows to copy) and the narrow inputs (up to 32 channels:
             // a staged row's copy is 2-8 KB) split the producer in two warps on different SM
             // sub-partitions, walking the same rows in the same stages: warp 0 copies, warp 2
@@ -1133,7 +1181,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                     epi_prefetch<EK, NPAD, 0>(inw, a, o, x);
             };
             constexpr int PF = EK == kEpiD2S ? 3 : 1;
-            const bool pf_on = !(EK == kEpiD2S && a.skip_smem);  // a skip in shared memory needs no prefetch
+            // a skip or a gate input in shared memory needs no prefetch
+            const bool pf_on = !(EK == kEpiD2S && a.skip_smem) && !GATE;
             while (ok && seg.next(strip, ya, yb)) {
                 const int x0 = strip * kTileM;
                 const int x = x0 + q * 32 + lane;
@@ -1176,6 +1225,20 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         dev::tc_fence_before();
                         __syncwarp();
                         if (lane == 0) dev::mbar_arrive(acce0 + 8 * slot);
+                        if constexpr (GATE) {
+                            // the block input of this output, staged by the gate warp: this warp's
+                            // chunks of its pixel, then the slot goes back
+                            const uint32_t g = ot % kGateSlots;
+                            if (!(ok = dev::mbar_wait_warp(gatef0 + 8 * g, (ot / kGateSlots) & 1u, a.err, kErrEpiAccFull)))
+                                break;
+                            const uint4 *grow = reinterpret_cast<const uint4 *>(sm + C::GOFF + g * C::GATE_ROW);
+                            const int ccout = a.cout / 8;
+#pragma unroll
+                            for (int c = 0; c < CW / 8; c++)
+                                if (C0 / 8 + c < ccout) in.gate[c] = grow[(C0 / 8 + c) * kHalo + (x - x0) + 1];
+                            __syncwarp();
+                            if (lane == 0) dev::mbar_arrive(gatee0 + 8 * g);
+                        }
                         epi_store<EK, CW, C0>(v, a, sslope, o, x, in);
                     } else {
                         // depth-to-space by 3 only comes with 27 output channels (NPAD 32)
