@@ -38,11 +38,13 @@ struct ajib_weights {
 namespace ajib {
 
 int pad_k(int cin) { return cin <= 16 ? 16 : (cin + 15) / 16 * 16; }
-// 3x3 outputs pad to 32, 48 or 64 columns. 48 channels (SPAN, SPANF3) keep their width: a row's
-// stacked-tap MMA is then N = 144 rather than 192 (a quarter fewer tensor cycles), and the
+// 3x3 outputs pad to 16, 32, 48 or 64 columns. 48 channels (SPAN, SPANF3) keep their width: a
+// row's stacked-tap MMA is then N = 144 rather than 192 (a quarter fewer tensor cycles), and the
 // accumulator ring's slots start on 16-column TMEM boundaries, as every MMA, load and store here
-// addresses TMEM in 16-column units.
-int pad_n(int cout) { return cout <= 32 ? 32 : cout == 48 ? 48 : 64; }
+// addresses TMEM in 16-column units. Up to 16 channels (the 2x tails' 12, depth-to-space of RGB)
+// pad to 16: N = 48 stacked-tap MMAs, and both epilogue warps of a lane quarter hold real
+// channels (with 32 columns the second warp's were all padding).
+int pad_n(int cout) { return cout <= 16 ? 16 : cout <= 32 ? 32 : cout == 48 ? 48 : 64; }
 
 // The B operand image. 3x3 weights (taps == 9) are stacked by tap row so that one MMA covers all
 // three vertical taps of a horizontal tap dx: [dx][kc][ty][ng][n8][k8], B row ty * npad + n of
@@ -232,17 +234,20 @@ cudaError_t run_conv(const ConvDev &p, int grid, cudaStream_t s)
 }
 
 // The kernel instantiation for padded channel counts, epilogue kind and input mode. Built: every
-// K x N (N 32, 48 or 64) with the activation and depth-to-space epilogues; the SPAN gates and the
-// SPANF3 tanh gate (cin == cout) at the four K x N pairs that cin == cout gives; the NCHW RGB model input, plain
-// or pixel-unshuffled by 2 (K 16 both), with activation or depth-to-space.
+// K x N (N 16, 32, 48 or 64) with the activation and depth-to-space epilogues; the SPAN gates and
+// the SPANF3 tanh gate (cin == cout) at the five K x N pairs that cin == cout gives; the NCHW RGB
+// model input, plain or pixel-unshuffled by 2 (K 16 both), with activation or depth-to-space.
 ConvFn find_fn(int kpad, int npad, int ek, int in)
 {
 #define AJIB_K(KP, NP, EK, IN) \
     if (kpad == KP && npad == NP && ek == EK && in == IN) return &run_conv<KP, NP, EK, IN>;
-#define AJIB_KN(KP, EK) AJIB_K(KP, 32, EK, kInRows) AJIB_K(KP, 48, EK, kInRows) AJIB_K(KP, 64, EK, kInRows)
-#define AJIB_SQ(EK) AJIB_K(16, 32, EK, kInRows) AJIB_K(32, 32, EK, kInRows) AJIB_K(48, 48, EK, kInRows) AJIB_K(64, 64, EK, kInRows)
-#define AJIB_RGB(IN) AJIB_K(16, 32, kEpiAct, IN) AJIB_K(16, 48, kEpiAct, IN) AJIB_K(16, 64, kEpiAct, IN) \
-    AJIB_K(16, 32, kEpiD2S, IN) AJIB_K(16, 48, kEpiD2S, IN) AJIB_K(16, 64, kEpiD2S, IN)
+#define AJIB_KN(KP, EK) AJIB_K(KP, 16, EK, kInRows) AJIB_K(KP, 32, EK, kInRows) AJIB_K(KP, 48, EK, kInRows) \
+    AJIB_K(KP, 64, EK, kInRows)
+#define AJIB_SQ(EK) AJIB_K(16, 16, EK, kInRows) AJIB_K(16, 32, EK, kInRows) AJIB_K(32, 32, EK, kInRows) \
+    AJIB_K(48, 48, EK, kInRows) AJIB_K(64, 64, EK, kInRows)
+#define AJIB_RGB(IN) AJIB_K(16, 16, kEpiAct, IN) AJIB_K(16, 32, kEpiAct, IN) AJIB_K(16, 48, kEpiAct, IN) \
+    AJIB_K(16, 64, kEpiAct, IN) AJIB_K(16, 16, kEpiD2S, IN) AJIB_K(16, 32, kEpiD2S, IN) AJIB_K(16, 48, kEpiD2S, IN) \
+    AJIB_K(16, 64, kEpiD2S, IN)
     AJIB_KN(16, kEpiAct)
     AJIB_KN(32, kEpiAct)
     AJIB_KN(48, kEpiAct)
