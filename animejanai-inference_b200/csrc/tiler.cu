@@ -135,7 +135,7 @@ __device__ __forceinline__ void compose_row(float (&b)[3][kComposeQ], const __ha
 
 __device__ __forceinline__ void compose_store(const float (&b)[3][kComposeQ], uint8_t *o, int nq, int co, int OW)
 {
-    if (nq == kComposeQ && co == 3 && (OW & 3) == 0) {
+    if (nq == kComposeQ && co == 3 && (OW & 3) == 0 && (reinterpret_cast<uintptr_t>(o) & 3) == 0) {
         // 12 bytes: pixel-major r, g, b of the four pixels, as three 4-byte words
         uint32_t *o4 = reinterpret_cast<uint32_t *>(o);
 #pragma unroll
@@ -148,7 +148,7 @@ __device__ __forceinline__ void compose_store(const float (&b)[3][kComposeQ], ui
             }
             o4[k] = wd;
         }
-    } else if (nq == kComposeQ && co == 1 && (OW & 3) == 0) {
+    } else if (nq == kComposeQ && co == 1 && (OW & 3) == 0 && (reinterpret_cast<uintptr_t>(o) & 3) == 0) {
         uint32_t wd = 0;
 #pragma unroll
         for (int q = 0; q < kComposeQ; q++) wd |= (uint32_t)to_u8(b[0][q]) << (8 * q);
@@ -264,9 +264,9 @@ __global__ void __launch_bounds__(256, 2) k_compose(const __half *tiles, int k0,
         rx[q] = q < nq ? cx[X0 + q] : make_int2(0, 0);
         same = same && rx[q].x == rx[0].x && rx[q].y == rx[0].y;
     }
-    // the vector path: every covering tile's column of X0 is 4-aligned, and so are the tile rows
-    // and the weight rows (16-byte weight and 8-byte tile loads)
-    same = same && (tow & 3) == 0 && (cols & 3) == 0;
+    // the vector path: every covering tile's column of X0 is 4-aligned, and so are the tile rows,
+    // the weight rows and the tiles' base address (16-byte weight and 8-byte tile loads)
+    same = same && (tow & 3) == 0 && (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(tiles) & 7) == 0;
     if (same) {
         for (int ii = 0; ii < rx[0].y; ii++) same = same && (((X0 - __ldg(ox + rx[0].x + ii) * s) & 3) == 0);
     }

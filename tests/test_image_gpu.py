@@ -70,6 +70,32 @@ def test_tiler_extract_and_compose_bit_exact(W, H, ci, tile, ov, s):
     ajib.lib.ajib_tiler_release(C.byref(t))
 
 
+def test_tiler_compose_unaligned_buffers():
+    """ajib_tiler_compose with the tile stack one fp16 element and the output one byte past an
+    aligned address (any device pointers a caller holds): the vector loads and stores are left
+    for per-element ones, and the bytes equal the aligned call's. The geometry is one the vector
+    path serves when the buffers are aligned (4-aligned tile columns, RGB)."""
+    import ajib
+    W, H, ci, tile, ov, s = 256, 192, 3, 64, 16, 4
+    rng = np.random.default_rng(5)
+    t, nx, ny, tw, th = make_tiler(W, H, ci, s, tile, ov)
+    n = nx * ny
+    touts = rng.uniform(-0.05, 1.05, size=(3, n, th * s, tw * s)).astype(np.float16)
+    flat = np.ascontiguousarray(touts).reshape(-1)
+    nbytes = H * s * W * s * ci
+    dt = torch.from_numpy(flat).cuda()
+    dt1 = torch.empty(flat.size + 1, dtype=torch.float16, device="cuda")
+    dt1[1:] = dt
+    out = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out1 = torch.zeros(nbytes + 1, dtype=torch.uint8, device="cuda")
+    assert ajib.lib.ajib_tiler_compose(t, dt.data_ptr(), out.data_ptr(), None) == 0
+    assert ajib.lib.ajib_tiler_compose(t, dt1.data_ptr() + 2, out1.data_ptr() + 1, None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(out1.cpu().numpy()[1:], out.cpu().numpy())
+    assert int(out1[0].item()) == 0
+    ajib.lib.ajib_tiler_release(C.byref(t))
+
+
 @pytest.mark.skipif(not os.path.exists(REF_TGPU), reason="reference GPU tiler not built (oracle/_ref)")
 def test_tiler_matches_reference_gpu_kernels():
     """The reference's own extract / blend / band flush on the B200: same bytes."""
