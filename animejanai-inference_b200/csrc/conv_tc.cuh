@@ -312,11 +312,20 @@ __device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, cons
             }
         } else {
             if (a.act == 3) {
+                // SiLU v * sigmoid(v) = v * (0.5 tanh(v / 2) + 0.5), two channels per multiply and
+                // FMA (__fmul2_rn / __ffma2_rn: each lane rounded as the scalar operation)
 #pragma unroll
-                for (int n = 0; n < CW; n++) v[n] = v[n] * fmaf(0.5f, dev::tanh_fast(0.5f * v[n]), 0.5f);
+                for (int j = 0; j < CW / 2; j++) {
+                    const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
+                    const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), vv);
+                    const float2 t = make_float2(dev::tanh_fast(hv.x), dev::tanh_fast(hv.y));
+                    const float2 r = __fmul2_rn(vv, __ffma2_rn(make_float2(0.5f, 0.5f), t, make_float2(0.5f, 0.5f)));
+                    w[j] = pack_h2(r.x, r.y);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < CW / 2; j++) w[j] = pack_h2(v[2 * j], v[2 * j + 1]);
             }
-#pragma unroll
-            for (int j = 0; j < CW / 2; j++) w[j] = pack_h2(v[2 * j], v[2 * j + 1]);
         }
         // one 16-byte chunk per lane per store: 32 consecutive pixels = 512 contiguous bytes; the
         // row's address once, chunks kStripW x 8 halves apart, and the strip's edge pixels also
@@ -361,8 +370,15 @@ __device__ __forceinline__ void epi_store(float (&v)[CW], const ConvDev &a, cons
                         v[n0] = f.x + v[n0];
                         v[n0 + 1] = f.y + v[n0 + 1];
                     } else if (a.gate == 3) {
-                        v[n0] = (f.x + v[n0]) * (0.5f * dev::tanh_fast(0.5f * v[n0]));
-                        v[n0 + 1] = (f.y + v[n0 + 1]) * (0.5f * dev::tanh_fast(0.5f * v[n0 + 1]));
+                        // (x + v) * (sigmoid(v) - 0.5) = (x + v) * 0.5 tanh(v / 2), two channels per
+                        // operation (each lane rounded as the scalar one)
+                        const float2 vv = make_float2(v[n0], v[n0 + 1]);
+                        const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), vv);
+                        const float2 g = __fmul2_rn(make_float2(0.5f, 0.5f),
+                                                    make_float2(dev::tanh_fast(hv.x), dev::tanh_fast(hv.y)));
+                        const float2 r = __fmul2_rn(__fadd2_rn(f, vv), g);
+                        v[n0] = r.x;
+                        v[n0 + 1] = r.y;
                     }
                 }
             }
