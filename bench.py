@@ -97,7 +97,7 @@ def plan_scale(plan):
     return plan["depth_to_space"] // plan.get("unshuffle", 1)
 # DRAM bytes (read + write) of one body-conv launch at 1920x1080, from the ncu capture summarised
 # in profiles/conv3x3_body_64x64_1080p.txt (the roofline's "traffic")
-BODY_TRAFFIC_BYTES = 503.5e6
+BODY_TRAFFIC_BYTES = 501.0e6
 
 
 def load_peaks():
