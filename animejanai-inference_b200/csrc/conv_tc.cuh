@@ -788,11 +788,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                         dev::mbar_wait(landed0 + 8 * s, ph, nullptr, 0);
                     }
                 } else if (warp == 2) {
-                    // the planner: per staged row, waits for the accumulators the row starts to be free,
-                    // writes the row's MMA plan beside it and, for depth-to-space, bulk-copies the skip
-                    // rows into those accumulators' slots; one arrival on full[s] a stage, and after the
-                    // last row one terminator stage. Every lane walks the same rows (warp-uniform control
-                    // flow); lane 0 waits and writes.
+                    // the planner: per staged row, waits for the accumulators the row starts to be free
+                    // and writes the row's MMA plan beside it; one arrival on full[s] a stage, and after
+                    // the last row one terminator stage. Every lane walks the same rows (warp-uniform
+                    // control flow); lane 0 waits and writes.
                     RowWalk walk(W, a.row_begin, a.row_end, a.img_h);
                     uint32_t pi = 0;
                     bool ok = true;
@@ -811,23 +810,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                             if (lane == 0) good = wt.wait(a.err);
                             if (!(ok = __shfl_sync(0xffffffffu, good, 0))) break;
                             if (lane == 0) plans[s * C::RP + h] = pl;
-                            if constexpr (EK == kEpiD2S) {
-                                // the skip rows of the outputs this row starts (r + 1; r at an image's
-                                // first row), into their slots: lanes 8-10 and 11-13, one plane each
-                                if (a.skip_smem) {
-                                    const int x0 = walk.strip * kTileM;
-                                    const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
-                                    const int k = lane - 8, which = k / 3, c3 = k % 3;
-                                    const bool mine = k >= 0 && k < 6 && (which == 0 ? wt.w0 : wt.w1);
-                                    const uint32_t sl = ((which == 0 ? wt.bar0 : wt.bar1) - acce0) / 8;
-                                    const int orow = which == 0 ? walk.r + 1 : walk.r;
-                                    if ((k == 0 && wt.w0) || (k == 3 && wt.w1)) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
-                                    __syncwarp();
-                                    if (mine)
-                                        dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + c3 * (kTileM * 2),
-                                                       a.resid + ((size_t)c3 * H + orow) * W + x0, rb, skipf0 + 8 * sl);
-                                }
-                            }
                             __syncwarp();
                         }
                         // a stage short of rows (the walk's end, or a wait that gave up) marks the rest
@@ -847,6 +829,35 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                             dev::mbar_arrive(full0 + 8 * s);
                         }
                     }
+                } else if (EK == kEpiD2S && warp == 3 && a.skip_smem) {
+                    // the skip warp (depth-to-space): each output's model-input row (the
+                    // nearest-upsampled skip it adds: 3 planes x the strip's 128 pixels) bulk-copied
+                    // into its accumulator slot's skip buffer once the slot is free, in the
+                    // epilogue's output order (the epilogue reads the buffer before it frees the
+                    // slot). In the planner these copies made it the tail's slowest role (~1200
+                    // cycles of its own a row).
+                    SegIter kseg(W, a.row_begin, a.row_end);
+                    uint32_t ot = 0;
+                    int strip, ya, yb;
+                    bool ok = true;
+                    while (ok && kseg.next(strip, ya, yb)) {
+                        const int x0 = strip * kTileM;
+                        const uint32_t rb = (uint32_t)min(kTileM, W - x0) * 2;
+                        for (int o = ya; o < yb; o++, ot++) {
+                            const int sl = ring_slot<S>(ot);
+                            if (!(ok = dev::mbar_wait_warp(acce0 + 8 * sl, ring_phase<S>(ot) ^ 1u, a.err, kErrProdAccEmpty)))
+                                break;
+                            if (lane == 0) dev::mbar_arrive_expect_tx(skipf0 + 8 * sl, 3 * rb);
+                            __syncwarp();
+                            if (lane < 3)
+                                dev::bulk_load(sbase + C::SKOFF + sl * C::SKIP_ROW + lane * (kTileM * 2),
+                                               a.resid + ((size_t)lane * H + o) * W + x0, rb, skipf0 + 8 * sl);
+                            __syncwarp();
+                        }
+                    }
+                    // on an error exit, let the last copies land before the CTA can leave
+                    if (!ok && ot > 0 && lane == 0)
+                        dev::mbar_wait(skipf0 + 8 * ring_slot<S>(ot - 1), ring_phase<S>(ot - 1), nullptr, 0);
                 }
             } else {
                 if (warp == 0) {
