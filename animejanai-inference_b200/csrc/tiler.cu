@@ -66,9 +66,10 @@ __global__ void k_extract(const uint8_t *img, int W, int H, int ci, const int *o
 // output rows and 64 * kComposeQ columns: it looks its rows' covering tile rows, tile-row offsets
 // and vertical weights up once into shared memory, each thread looks its four adjacent columns'
 // covering tiles (and, on the vector path, their tile columns and weights) up once, and then
-// walks the rows, two at a time so that their tile loads are in flight together. (One block per
-// eight rows paid that chain of dependent table loads for every eight rows: 0.52 ms at config 2
-// against 0.46 with the loads hoisted and this.) Where four pixels share their covering tiles at a
+// walks the rows, two at a time; on the vector path a pair's tile loads are asynchronous copies
+// into shared memory issued while the previous pair is summed and stored. (One block per eight
+// rows paid that chain of dependent table loads for every eight rows: 0.52 ms at config 2 against
+// 0.33 with the block-wide tables, 0.31 with the copies one pair ahead.) Where four pixels share their covering tiles at a
 // 4-aligned tile column the tile values are read 8 bytes at a time and the 8-bit output written 4
 // bytes at a time. Per pixel and channel the arithmetic is the same in either path.
 constexpr int kComposeQ = 4;     // output pixels per thread and row
@@ -164,19 +165,33 @@ __device__ __forceinline__ void compose_store(const float (&b)[3][kComposeQ], ui
 
 // The vector path where every pixel of the thread's columns and rows is covered by at most two
 // tiles along each axis (every cover whose overlap is under half a tile, config 2's included):
-// the thread's horizontal weights are loaded once, and all its tile loads for both rows (up to
-// 2 rows x 2 tile rows x 2 tiles x 3 channels of 4 pixels) are issued before any is summed, so
-// they are in flight together; each pixel's sum then runs in compose_row's order (tile rows, then
-// tiles, each multiply and add rounded on its own).
+// the thread's horizontal weights are loaded once, its tile loads for a pair of rows (up to
+// 2 rows x 2 tile rows x 2 tiles x 3 channels of 4 pixels) go out together, and each pixel's sum
+// runs in compose_row's order (tile rows, then tiles, each multiply and add rounded on its own).
 constexpr int kComposeF = 2;
 
-__device__ __forceinline__ void compose_pair_f2(float (&ba)[3][kComposeQ], float (&bb)[3][kComposeQ], const __half *tiles,
-                                                size_t plane, int k0, int toh, int tow, int nx, int i0, int ni,
-                                                const int (&u)[kComposeF], const float4 (&wq)[kComposeF],
-                                                const int (&nj)[2], const int *j0, const int *v0, const float *wv0,
-                                                const int *j1, const int *v1, const float *wv1)
+// Its tile loads are asynchronous copies (cp.async, 8 bytes each) into the thread's own slots in
+// shared memory, so that a row pair's loads are in flight while the thread
+// sums and stores the previous pair (the bytes a thread keeps in flight no longer wait on
+// registers). Slot-major layout [slot][thread]: a warp's 32 slots of one kind are 256 contiguous
+// bytes. Only the issuing thread reads its slots, after its own cp.async.wait_group.
+constexpr int kComposeSlots = 2 * kComposeF * kComposeF * 3;  // per row pair
+constexpr int kComposeThreads = 256;
+constexpr size_t kComposeDynSmem = 2 * kComposeSlots * kComposeThreads * sizeof(uint2);
+
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem)
 {
-    uint2 t[2][kComposeF][kComposeF][3];
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+
+__device__ __forceinline__ int compose_slot(int r, int jj, int ii, int c) { return ((r * kComposeF + jj) * kComposeF + ii) * 3 + c; }
+
+__device__ __forceinline__ void compose_pair_issue(uint2 *stage, int tid, const __half *tiles, size_t plane, int k0, int toh,
+                                                   int tow, int nx, int i0, int ni, const int (&u)[kComposeF],
+                                                   const int (&nj)[2], const int *j0, const int *v0, const int *j1,
+                                                   const int *v1)
+{
 #pragma unroll
     for (int r = 0; r < 2; r++) {
         const int *jr = r ? j1 : j0, *vr = r ? v1 : v0;
@@ -188,11 +203,18 @@ __device__ __forceinline__ void compose_pair_f2(float (&ba)[3][kComposeQ], float
                     const int k = jr[jj] * nx + i0 + ii - k0;
                     const size_t at = ((size_t)k * toh + vr[jj]) * tow + u[ii];
 #pragma unroll
-                    for (int c = 0; c < 3; c++) t[r][jj][ii][c] = __ldg(reinterpret_cast<const uint2 *>(tiles + c * plane + at));
+                    for (int c = 0; c < 3; c++)
+                        cp_async8(&stage[compose_slot(r, jj, ii, c) * kComposeThreads + tid], tiles + c * plane + at);
                 }
             }
         }
     }
+}
+
+__device__ __forceinline__ void compose_pair_sum(float (&ba)[3][kComposeQ], float (&bb)[3][kComposeQ], const uint2 *stage,
+                                                 int tid, int ni, const float4 (&wq)[kComposeF], const int (&nj)[2],
+                                                 const float *wv0, const float *wv1)
+{
 #pragma unroll
     for (int r = 0; r < 2; r++) {
         float(&b)[3][kComposeQ] = r ? bb : ba;
@@ -212,7 +234,7 @@ __device__ __forceinline__ void compose_pair_f2(float (&ba)[3][kComposeQ], float
                                     __fmul_rn(wv, wq[ii].w)};
 #pragma unroll
                 for (int c = 0; c < 3; c++) {
-                    const uint2 raw = t[r][jj][ii][c];
+                    const uint2 raw = stage[compose_slot(r, jj, ii, c) * kComposeThreads + tid];
                     const float2 t01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
                     const float2 t23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
                     b[c][0] = __fadd_rn(b[c][0], __fmul_rn(w[0], t01.x));
@@ -282,17 +304,41 @@ __global__ void __launch_bounds__(256, 2) k_compose(const __half *tiles, int k0,
             wq[ii] = __ldg(reinterpret_cast<const float4 *>(wx + (size_t)(rx[0].x + ii) * cols + u[ii]));
         }
     }
-    // rows g + ty and g + ty + blockDim.y of each group of kComposeRows
-    for (int g = 0; g < kComposeBlockRows; g += kComposeRows) {
-        const int ra = g + threadIdx.y, rb = g + threadIdx.y + blockDim.y;
-        const int Ya = Yblk + ra, Yb2 = Yblk + rb;
-        if (Ya >= Y1) break;
-        float ba[3][kComposeQ], bb[3][kComposeQ];
-        const int nja = s_nj[ra], njb = Yb2 < Y1 ? s_nj[rb] : 0;
-        if (fast && nja <= kComposeF && njb <= kComposeF) {
+    // rows g + ty and g + ty + blockDim.y of each group of kComposeRows: pair k = g / kComposeRows
+    extern __shared__ uint2 cbuf[];  // [2 stages][kComposeSlots][kComposeThreads]
+    constexpr int kPairs = kComposeBlockRows / kComposeRows;
+    auto pair_rows = [&](int k, int &ra, int &rb, int &nja, int &njb) -> bool {
+        if (k >= kPairs) return false;  // (the prefetch of the pair after the block's last)
+        ra = k * kComposeRows + threadIdx.y;
+        rb = ra + blockDim.y;
+        if (Yblk + ra >= Y1) return false;
+        nja = s_nj[ra];
+        njb = Yblk + rb < Y1 ? s_nj[rb] : 0;
+        return true;
+    };
+    // the pair's loads go through shared memory when the vector path serves it
+    auto pair_async = [&](int nja, int njb) { return fast && nja <= kComposeF && njb <= kComposeF; };
+    auto issue = [&](int k) {
+        int ra, rb, nja, njb;
+        if (pair_rows(k, ra, rb, nja, njb) && pair_async(nja, njb)) {
             const int nj[2] = {nja, njb};
-            compose_pair_f2(ba, bb, tiles, plane, k0, toh, tow, nx, rx[0].x, rx[0].y, u, wq, nj, s_j[ra], s_v[ra],
-                            s_wv[ra], s_j[rb], s_v[rb], s_wv[rb]);
+            compose_pair_issue(cbuf + (size_t)(k & 1) * kComposeSlots * kComposeThreads, tid, tiles, plane, k0, toh, tow, nx,
+                               rx[0].x, rx[0].y, u, nj, s_j[ra], s_v[ra], s_j[rb], s_v[rb]);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(0);
+    for (int k = 0; k < kPairs; k++) {
+        int ra, rb, nja, njb;
+        if (!pair_rows(k, ra, rb, nja, njb)) break;
+        const int Ya = Yblk + ra, Yb2 = Yblk + rb;
+        issue(k + 1);
+        float ba[3][kComposeQ], bb[3][kComposeQ];
+        if (pair_async(nja, njb)) {
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            const int nj[2] = {nja, njb};
+            compose_pair_sum(ba, bb, cbuf + (size_t)(k & 1) * kComposeSlots * kComposeThreads, tid, rx[0].y, wq, nj,
+                             s_wv[ra], s_wv[rb]);
         } else {
             compose_row(ba, tiles, plane, k0, toh, tow, nx, ox, wx, cols, s, co, X0, nq, rx, same, nja, s_j[ra], s_v[ra],
                         s_wv[ra]);
@@ -303,6 +349,7 @@ __global__ void __launch_bounds__(256, 2) k_compose(const __half *tiles, int k0,
         compose_store(ba, out + ((size_t)(Ya - Y0) * OW + X0) * co, nq, co, OW);
         if (Yb2 < Y1) compose_store(bb, out + ((size_t)(Yb2 - Y0) * OW + X0) * co, nq, co, OW);
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // the most tiles covering one output coordinate (the compose kernel holds kComposeMaxT a row)
@@ -385,7 +432,9 @@ cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int
     const int cols = std::min(g_.tw, g_.W) * s, rows = std::min(g_.th, g_.H) * s;
     const int px = 64 * kComposeQ;  // output columns per block
     const dim3 block(64, kComposeRows / 2), grid((OW + px - 1) / px, (Y1 - Y0 + kComposeBlockRows - 1) / kComposeBlockRows);
-    k_compose<<<grid, block, 0, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
+    const cudaError_t ae = cudaFuncSetAttribute(k_compose, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kComposeDynSmem);
+    if (ae != cudaSuccess) return ae;
+    k_compose<<<grid, block, kComposeDynSmem, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
                                       d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
     return cudaGetLastError();
 }
@@ -484,7 +533,9 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
         const int OW = g.W * s, OH = g.H * s;
         const dim3 block(64, kComposeRows / 2),
             grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + kComposeBlockRows - 1) / kComposeBlockRows);
-        k_compose<<<grid, block, 0, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
+        if (cudaFuncSetAttribute(k_compose, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kComposeDynSmem) != cudaSuccess)
+            return AJIB_ERR_CUDA;
+        k_compose<<<grid, block, kComposeDynSmem, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
                                           (const int *)(base + o_ox), (const int *)(base + o_oy),
                                           (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
                                           (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, 0, OH, out);
