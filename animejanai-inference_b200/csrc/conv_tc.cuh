@@ -33,8 +33,10 @@
  *               or all 128 threads convert the NCHW RGB model input
  *               into the same layout; lane 0 also waits for the accumulators a row starts to be
  *               free and writes the row's MMA plan beside the staged row, and after the last row
- *               fills one terminator stage (depth-to-space and head convs: warp 2 does the waits,
- *               plans and skip rows, warp 0 only the copies);
+ *               fills one terminator stage (depth-to-space convs and inputs of up to 32 channels:
+ *               warp 2 does the waits and plans, warp 0 only the copies); warp 3 copies each
+ *               output's extra input row into shared memory ahead of the epilogue: the SPAN
+ *               gate's block input, or the depth-to-space skip (the model input);
  *   warps 4-11  epilogue: TMEM -> registers (one pixel per thread, half a slot's channels per
  *               warp), bias, activation, SPAN gate or depth-to-space with the model-input skip,
  *               fp16 store; then zero the half slot;
