@@ -128,10 +128,13 @@ constexpr int kPreMaxTaps = 8;  // taps per pass the kernel holds (plans with mo
 // The head conv's input, written by the pre pass as well when it is fused with it (PACK): the
 // fp16 RGB of each pixel, normalised as the conv's input ((x - mean) * scale, rounded to fp16)
 // when the model asks for it, as chunk 0 {r, g, b, 0 x 5} of an 8-channel strip-chunked map —
-// the bytes the executor's own pack of the NCHW input (conv.cu, k_pack_input) writes.
+// the bytes the executor's own pack of the NCHW input (conv.cu, k_pack_input) writes. With
+// unshuffle set (the streaming kernel only), the map is the 2x pixel-unshuffled input at half
+// width and height: 16 channels, c * 4 + ry * 2 + rx for colour c and the pixel's row and column
+// parity, the 12 real ones in chunk 0 and the first half of chunk 1.
 struct PreMap {
     __half *map;
-    int nstrips, in_norm;
+    int nstrips, in_norm, unshuffle;
     float mean[3], scale[3];
 };
 
@@ -732,7 +735,9 @@ __device__ __forceinline__ float2 u8x2_to_f2(uint32_t wd)
                       f2(-8388608.0f));
 }
 
-template <typename T, int TAPS, bool PACK>
+// PACK: 0 the NCHW RGB only; 1 also the head's map of the same pixels; 2 also the head's map of
+// the 2x pixel-unshuffled pixels (PreMap)
+template <typename T, int TAPS, int PACK>
 __global__ void __launch_bounds__(256, 4) k_pre_roll(const uint8_t *yp, ptrdiff_t ys, const uint8_t *uvp, ptrdiff_t uvs,
                                                      PreRoll pr, aji_csp csp, __half *dst, PreMap pm)
 {
@@ -821,6 +826,7 @@ __global__ void __launch_bounds__(256, 4) k_pre_roll(const uint8_t *yp, ptrdiff_
     const float ry = __frcp_rn(csp.yscale), rc = __frcp_rn(csp.cscale);
     auto vertical = [&](int s) {
         if (vx >= w) return;
+        __half2 er, eg, eb;  // PACK 2: the (even) upper row of the pair the odd row completes
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int yrel = kPrG * s + 4 * vg + i, y = ya + yrel;
@@ -853,7 +859,7 @@ __global__ void __launch_bounds__(256, 4) k_pre_roll(const uint8_t *yp, ptrdiff_
             *reinterpret_cast<__half2 *>(dst + idx) = hr;
             *reinterpret_cast<__half2 *>(dst + plane + idx) = hg;
             *reinterpret_cast<__half2 *>(dst + 2 * plane + idx) = hb;
-            if constexpr (PACK) {
+            if constexpr (PACK == 1) {
 #pragma unroll
                 for (int p = 0; p < 2; p++) {
                     float v[3] = {p ? __high2float(hr) : __low2float(hr), p ? __high2float(hg) : __low2float(hg),
@@ -864,6 +870,26 @@ __global__ void __launch_bounds__(256, 4) k_pre_roll(const uint8_t *yp, ptrdiff_
                     }
                     store_px(pm.map, y, vx + p, 0, pm.nstrips, 1,
                              make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], 0.f), 0u, 0u));
+                }
+            } else if constexpr (PACK == 2) {
+                // a run and every step start on an even row (seg and kPrG are even) and end on an
+                // odd one (h is even), so rows i = 0, 1 and i = 2, 3 are the two rows of the
+                // unshuffled pixel (y / 2, vx / 2): its word (c, ry) holds columns vx, vx + 1
+                if (!(i & 1)) {
+                    er = hr, eg = hg, eb = hb;
+                } else {
+                    __half2 q[6] = {er, hr, eg, hg, eb, hb};
+                    if (pm.in_norm) {
+#pragma unroll
+                        for (int j = 0; j < 6; j++) {
+                            const float2 f = __half22float2(q[j]);
+                            const float m = pm.mean[j >> 1], sc = pm.scale[j >> 1];
+                            q[j] = __floats2half2_rn((f.x - m) * sc, (f.y - m) * sc);
+                        }
+                    }
+                    const uint32_t *u = reinterpret_cast<const uint32_t *>(q);
+                    store_px(pm.map, y >> 1, vx >> 1, 0, pm.nstrips, 2, make_uint4(u[0], u[1], u[2], u[3]));
+                    store_px(pm.map, y >> 1, vx >> 1, 1, pm.nstrips, 2, make_uint4(u[4], u[5], 0u, 0u));
                 }
             }
         }
@@ -1065,7 +1091,7 @@ bool post_roll_setup(aji_plan *p)
 // outputs 0 and 1 starting at most one sample apart, a width that is a multiple of 16 (every
 // 16-byte piece of a luma or chroma row is wholly inside or outside the frame), and every tap of
 // a strip's real outputs inside its staged window. Sets the launch (PreRoll, grid) when it does.
-template <typename T, int TAPS, bool PACK>
+template <typename T, int TAPS, int PACK>
 bool pre_roll_occupancy(int *per_sm)
 {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_pre_roll<T, TAPS, PACK>, 256,
@@ -1092,12 +1118,13 @@ bool pre_roll_setup(aji_plan *p)
         for (int x = x0; x < std::min(x0 + kPrCols, p->w); x++)
             if (th.start[x] < ca || th.start[x] + TAPS > ca + kPrCW) return false;
     }
-    int dev = 0, sms = 0, per_sm = 0, per_sm_pack = 0;
+    int dev = 0, sms = 0, per_sm = 0, per_sm_pack = 0, per_sm_unsh = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        !pre_roll_occupancy<T, TAPS, false>(&per_sm) || !pre_roll_occupancy<T, TAPS, true>(&per_sm_pack))
+        !pre_roll_occupancy<T, TAPS, 0>(&per_sm) || !pre_roll_occupancy<T, TAPS, 1>(&per_sm_pack) ||
+        !pre_roll_occupancy<T, TAPS, 2>(&per_sm_unsh))
         return false;
-    per_sm = std::min(per_sm, per_sm_pack);
+    per_sm = std::min(per_sm, std::min(per_sm_pack, per_sm_unsh));
     if (per_sm < 1) return false;
     const int nstrips = (p->w + kPrCols - 1) / kPrCols;
     const int nseg = std::max(1, sms * per_sm / nstrips);
@@ -1260,10 +1287,12 @@ void launch_pre_roll(const aji_plan *p, const uint8_t *yp, ptrdiff_t ys, const u
                      const aji_csp &csp, __half *dst, const PreMap *pm, cudaStream_t s)
 {
     const size_t smem = sizeof(PreRollSmem<T>);
-    if (pm)
-        k_pre_roll<T, TAPS, true><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, *pm);
+    if (pm && pm->unshuffle)
+        k_pre_roll<T, TAPS, 2><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, *pm);
+    else if (pm)
+        k_pre_roll<T, TAPS, 1><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, *pm);
     else
-        k_pre_roll<T, TAPS, false><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, PreMap{});
+        k_pre_roll<T, TAPS, 0><<<p->roll_grid, 256, smem, s>>>(yp, ys, uvp, uvs, p->proll, csp, dst, PreMap{});
 }
 
 int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void *uv_plane, ptrdiff_t uv_stride,
@@ -1283,6 +1312,14 @@ int launch_pre(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const void 
         else if (p->roll_taps == 6) launch_pre_roll<uint8_t, 6>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
         else launch_pre_roll<uint8_t, 2>(p, yp, y_stride, uvp, uv_stride, *csp, dst, pm, s);
         return (int)cudaGetLastError();
+    }
+    if (pm && pm->unshuffle) {
+        // the tiled kernel writes no unshuffled map: the NCHW RGB, then the executor's own pack
+        const int e = launch_pre(p, y_plane, y_stride, uv_plane, uv_stride, csp, dst_f16, nullptr, s);
+        if (e != (int)cudaSuccess) return e;
+        const int rc = ajib::pack_model_input(dst_f16, p->h / 2, p->w / 2, 1, pm->in_norm != 0, pm->mean, pm->scale, 0,
+                                              p->h / 2, pm->map, s);
+        return rc == AJIB_OK ? (int)cudaSuccess : rc == AJIB_ERR_CUDA ? (int)cudaErrorLaunchFailure : (int)cudaErrorInvalidValue;
     }
     if (p->format == AJI_FMT_NV12) {
         if (pm)
@@ -1316,7 +1353,8 @@ int run_pre_packed(aji_plan *p, const void *y_plane, ptrdiff_t y_stride, const v
     if (((uintptr_t)pk.map & 15) != 0) return (int)cudaErrorInvalidValue;
     PreMap m{};
     m.map = (__half *)pk.map;
-    m.nstrips = feature_strips(p->w);
+    m.unshuffle = pk.unshuffle ? 1 : 0;
+    m.nstrips = feature_strips(pk.unshuffle ? p->w / 2 : p->w);
     m.in_norm = pk.in_norm ? 1 : 0;
     for (int c = 0; c < 3; c++) {
         m.mean[c] = pk.mean[c];

@@ -234,10 +234,11 @@ int Executor::run(const void *in, void *out, int w, int h, cudaStream_t s) const
 
 bool Executor::input_pack(InputPack *pk) const
 {
-    if (steps_.empty() || !steps_[0].pack || steps_[0].unshuffle) return false;
+    if (steps_.empty() || !steps_[0].pack) return false;
     const Step &st = steps_[0];
     if (pk) {
         pk->map = st.pack_buf;
+        pk->unshuffle = st.unshuffle != 0;
         pk->in_norm = st.in_norm;
         for (int c = 0; c < 3; c++) {
             pk->mean[c] = st.in_mean[c];

@@ -80,10 +80,11 @@ double flops_per_pixel(const Plan &p);
 inline int model_scale(const Plan &p) { return p.depth_to_space / (p.unshuffle > 0 ? p.unshuffle : 1); }
 
 // Where the colour pre pass writes the head conv's input when it is fused with the executor's
-// input pack (video.cpp): the head's 8-channel strip-chunked map and the model's input
-// normalisation.
+// input pack (video.cpp): the head's strip-chunked map (8 channels; with unshuffle, the 16 of the
+// 2x pixel-unshuffled input at half size) and the model's input normalisation.
 struct InputPack {
     void *map = nullptr;
+    bool unshuffle = false;
     bool in_norm = false;
     float mean[3] = {0.f, 0.f, 0.f}, scale[3] = {1.f, 1.f, 1.f};
 };
@@ -134,7 +135,7 @@ public:
     // its own: in [3][nimg * img_h][w], out [3][scale * nimg * img_h][scale * w], its planes
     // out_plane elements apart when out_plane is not 0 (inside a larger stack of images).
     int run_images(const void *in, void *out, int w, int img_h, int nimg, cudaStream_t s, size_t out_plane = 0) const;
-    // The head's input map, when the head reads the plain NCHW RGB model input (not
+    // The head's input map, when the head reads the NCHW RGB model input (plain or 2x
     // pixel-unshuffled): a producer that writes it (run_pre_packed) lets run_packed skip the
     // head's own pack launch. False for other heads.
     bool input_pack(InputPack *pk) const;

@@ -58,7 +58,7 @@ MODELS = {
     "span": dict(metric="frames/s 1080p->4K 2x SPAN-S 48x6 fp16 (BASELINE config 3)", w=1920, h=1080,
                  workload="BASELINE config 3: SPAN 2x video, 1920x1080 P010 BT.709 limited -> 3840x2160 P010",
                  model="SPAN 48 feat x 6 blocks (SiLU, sigmoid gates, concat 1x1), pixel_shuffle 2, random-init (seed 1)",
-                 kernel="k_conv3x3_tc<48,64> (SPAN body convs 48->48, SiLU / sigmoid gate, 1920x1080)"),
+                 kernel="k_conv3x3_tc<48,48> (SPAN body convs 48->48, SiLU / sigmoid gate, 1920x1080)"),
     "chain": dict(metric="frames/s 960x540->1080p->4K two-model Compact chain fp16 (BASELINE config 4)", w=960, h=540,
                   workload="BASELINE config 4: two Compact 2x nets chained by animejanai.conf, 960x540 P010 -> "
                            "3840x2160 P010 (a stream of frames, frame-parallel over ranks)",
@@ -75,7 +75,7 @@ MODELS = {
                    workload="SPANF3 b5f48 2x video (2x pixel-unshuffle, tanh gates), 1920x1080 P010 BT.709 limited -> "
                             "3840x2160 P010",
                    model="SPANF3 48 feat x 5 blocks, unshuffle 2, depth-to-space 4, random-init (seed 1, 0.7 He)",
-                   kernel="k_conv3x3_tc<48,64> (SPANF3 body convs 48->48, ReLU / tanh gate, 960x540)"),
+                   kernel="k_conv3x3_tc<48,48> (SPANF3 body convs 48->48, ReLU / tanh gate, 960x540)"),
 }
 
 
@@ -1031,9 +1031,11 @@ def cpu_image_sample(plan, nthreads=0):
 
 def fused_pack(plans):
     """1 when the video path fuses the first net's input pack into the colour pre pass (its head
-    reads the plain NCHW RGB input), else 0."""
+    reads the NCHW RGB input, plain or 2x pixel-unshuffled; the unshuffled map is written by the
+    streaming pre kernel, which every bench frame width, a multiple of 16, takes), else 0."""
+    import ajib
     head = plans[0]["steps"][0]
-    return 1 if head["kind"] == 0 and head.get("in_", 0) == 1 else 0
+    return 1 if head["kind"] == 0 and head.get("in_", 0) in (ajib.IN_NCHW3, ajib.IN_NCHW3_UNSHUFFLE2) else 0
 
 
 def chain_flops(plans, w, h):

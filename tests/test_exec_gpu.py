@@ -117,16 +117,20 @@ def test_video_p010_chain():
     vid.close()
 
 
-@pytest.mark.parametrize("fmt,norm,w,h", [(2, False, 200, 72), (1, False, 200, 72), (2, True, 200, 72),
-                                          (2, False, 272, 40), (1, True, 272, 40)])
-def test_fused_pre_pack_matches_separate_passes(fmt, norm, w, h):
+@pytest.mark.parametrize("net,fmt,norm,w,h", [("compact", 2, False, 200, 72), ("compact", 1, False, 200, 72),
+                                              ("compact", 2, True, 200, 72), ("compact", 2, False, 272, 40),
+                                              ("compact", 1, True, 272, 40), ("spanf3", 2, False, 272, 40),
+                                              ("spanf3", 1, True, 272, 40), ("spanf3", 2, True, 200, 72)])
+def test_fused_pre_pack_matches_separate_passes(net, fmt, norm, w, h):
     """aji_infer fuses the first net's input pack into the colour pre pass (the pre pass writes the
-    head's strip-chunked map as well as the NCHW RGB). Its output must equal, bit for bit, the
-    unfused chain: aji_run_pre, the executor with its own pack, aji_run_post, on the same frame.
-    Widths that are multiples of 16 take the streaming pre kernel, the others the tiled one."""
+    head's strip-chunked map as well as the NCHW RGB; for SPANF3's 2x pixel-unshuffled head, the
+    16-channel map at half size). Its output must equal, bit for bit, the unfused chain:
+    aji_run_pre, the executor with its own pack, aji_run_post, on the same frame. Widths that are
+    multiples of 16 take the streaming pre kernel, the others the tiled one (for the unshuffled
+    head followed by the executor's pack)."""
     import ctypes as C
     import ajib
-    plan = ajib.compact_plan(41, body=3)
+    plan = ajib.compact_plan(41, body=3) if net == "compact" else ajib.spanf3_plan(43, c=16, blocks=2, gain=0.7)
     if norm:
         plan["steps"][0]["in_norm"] = ((0.45, 0.5, 0.4), (2.0, 1.9, 2.1))
     d = tempfile.mkdtemp()
