@@ -434,8 +434,9 @@ cudaError_t DeviceTiler::compose_rows(const void *tiles, int k0, int ntiles, int
     const dim3 block(64, kComposeRows / 2), grid((OW + px - 1) / px, (Y1 - Y0 + kComposeBlockRows - 1) / kComposeBlockRows);
     const cudaError_t ae = cudaFuncSetAttribute(k_compose, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kComposeDynSmem);
     if (ae != cudaSuccess) return ae;
-    k_compose<<<grid, block, kComposeDynSmem, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(), d_ox_, d_oy_,
-                                      d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW, Y0, Y1, out);
+    k_compose<<<grid, block, kComposeDynSmem, st>>>((const __half *)tiles, k0, ntiles, g_.th * s, g_.tw * s, g_.nx(),
+                                                    d_ox_, d_oy_, d_wx_, d_wy_, cols, rows, d_cx_, d_cy_, s, g_.ci, OW,
+                                                    Y0, Y1, out);
     return cudaGetLastError();
 }
 
@@ -535,10 +536,10 @@ extern "C" int ajib_tiler_compose_static(int W, int H, int ci, int scale, int ti
             grid((OW + 64 * kComposeQ - 1) / (64 * kComposeQ), (OH + kComposeBlockRows - 1) / kComposeBlockRows);
         if (cudaFuncSetAttribute(k_compose, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kComposeDynSmem) != cudaSuccess)
             return AJIB_ERR_CUDA;
-        k_compose<<<grid, block, kComposeDynSmem, st>>>((const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(),
-                                          (const int *)(base + o_ox), (const int *)(base + o_oy),
-                                          (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
-                                          (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, 0, OH, out);
+        k_compose<<<grid, block, kComposeDynSmem, st>>>(
+            (const __half *)tiles, 0, g.count(), g.th * s, g.tw * s, g.nx(), (const int *)(base + o_ox),
+            (const int *)(base + o_oy), (const float *)(base + o_wx), (const float *)(base + o_wy), spw * s, sph * s,
+            (const int2 *)(base + o_cx), (const int2 *)(base + o_cy), s, g.ci, OW, 0, OH, out);
         return cudaGetLastError() == cudaSuccess ? AJIB_OK : AJIB_ERR_CUDA;
     } catch (...) {
         return AJIB_ERR_NO_MEM;
