@@ -539,6 +539,9 @@ __global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRol
     extern __shared__ __align__(16) unsigned char ps_smem[];
     PostRollSmem &sm = *reinterpret_cast<PostRollSmem *>(ps_smem);
     constexpr int kPro = TAPS - 2;  // luma rows staged before the first step
+    // the row loops below cover rows tid / 64 + 4 k (k < 4) and tid / 32 + 8 k (k < 2): every
+    // row of a pass of at most 2 kPsG rows
+    static_assert(kPro <= 2 * kPsG, "the prologue's rows fit the row loops");
     const int tid = threadIdx.x;
     const int w = pr.w, h = pr.h;
     const int cx0 = blockIdx.x * kPsCols;
@@ -565,7 +568,10 @@ __global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRol
     const __half *sbase = src + (scopy ? sp * plane + scol : 0);
     auto stage = [&](int rel0, int n) {
         if (!scopy) return;
-        for (int r = tid >> 6; r < n; r += 4) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int r = (tid >> 6) + 4 * k;
+            if (r >= n) break;
             const int rel = rel0 + r;
             cp_async16(&sm.raw[rel & (kPsRaw - 1)][sp][8 * sj], sbase + (size_t)mirror_index(ylo + rel, h) * w);
         }
@@ -588,7 +594,10 @@ __global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRol
     const int pgx = 2 * cx0 + 2 * (tid & 63), pc = pgx - xlo;
     const bool pfast = pgx + 1 < w;
     auto differences = [&](int rel0, int n) {
-        for (int r = tid >> 6; r < n; r += 4) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int r = (tid >> 6) + 4 * k;
+            if (r >= n) break;
             const int rel = rel0 + r, gy = ylo + rel;
             if (pfast) {
                 const __half(*row)[kPsLW] = sm.raw[rel & (kPsRaw - 1)];
@@ -623,7 +632,10 @@ __global__ void __launch_bounds__(256, 3) k_post_roll(const __half *src, PostRol
     constexpr int kW = (TAPS / 2 + 2) & ~1;  // pairs loaded per parity (two per 128-bit load)
     const int ht = tid & 31;
     auto horizontal = [&](int rel0, int n) {
-        for (int r = tid >> 5; r < n; r += 8) {
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int r = (tid >> 5) + 8 * k;
+            if (r >= n) break;
             float2 e[kW], o[kW];
 #pragma unroll
             for (int k = 0; k < kW; k += 2) {
